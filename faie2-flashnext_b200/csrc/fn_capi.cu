@@ -1,0 +1,303 @@
+// C ABI of the engine (declared in include/faie2fn.h): errors, launch settings, the model-free test / bench hooks of
+// the reference (engine/faie2fn.cu:2492-2935) and resident-weight handles for device-pointer callers.
+// Conventions of the reference are kept: int return 0 = ok, -1 = error with the message in fn_error(); the caller
+// owns every host buffer; every fn_test_* / fn_bench_* call is synchronous.
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "fn_engine.h"
+
+namespace fn {
+
+std::string &err() {
+    static std::string e;
+    return e;
+}
+int fail(const std::string &msg) {
+    err() = msg;
+    return -1;
+}
+
+Settings &settings() {
+    static Settings s;
+    return s;
+}
+
+int num_sms() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// One error word per device, in a static __device__ variable (no allocation); kernels record the first failure.
+__device__ uint32_t g_dev_err_word;
+static uint32_t *g_err_ptr[64] = {};
+
+uint32_t *dev_error_ptr() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!g_err_ptr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_dev_err_word) != cudaSuccess) return nullptr;
+        g_err_ptr[dev] = (uint32_t *)p;
+    }
+    return g_err_ptr[dev];
+}
+
+int check_dev_error(const char *where) {
+    uint32_t v = 0;
+    FN_CK(cudaMemcpyFromSymbol(&v, g_dev_err_word, sizeof(v)));
+    if (v == DEV_OK) return 0;
+    const uint32_t z = 0;
+    cudaMemcpyToSymbol(g_dev_err_word, &z, sizeof(z));
+    return fail(std::string(where) + ": device " +
+                (v == DEV_WAIT_TIMEOUT ? "wait timed out (a pipeline barrier never completed)" : "argument check failed") +
+                " (code " + std::to_string(v) + ")");
+}
+
+static int g_device = -1;  // device the test / bench hooks use (FN_DEVICE, default 0)
+static int hook_device() {
+    if (g_device < 0) {
+        const char *e = getenv("FN_DEVICE");
+        g_device = e ? atoi(e) : 0;
+    }
+    return g_device;
+}
+
+// a non-blocking stream per device for the synchronous hooks
+static cudaStream_t hook_stream() {
+    static cudaStream_t st[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!st[dev]) cudaStreamCreateWithFlags(&st[dev], cudaStreamNonBlocking);
+    return st[dev];
+}
+
+// device buffers freed when the scope ends
+struct DevBuf {
+    void *p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    template <typename T> T *as() const { return (T *)p; }
+};
+
+// ---- resident weights ------------------------------------------------------------------------------------------
+struct WeightH {
+    GemvPlan plan1, plan8;  // token capacity 1 and 8
+    uint8_t *d = nullptr;   // rows at stride plan.ldw
+    int dev = 0;
+    float *xbuf = nullptr, *ybuf = nullptr;  // device staging for host-buffer calls
+};
+static std::vector<WeightH *> g_w;
+static std::mutex g_w_mu;
+
+static WeightH *wget(int h) {
+    std::lock_guard<std::mutex> l(g_w_mu);
+    return h >= 1 && h <= (int)g_w.size() ? g_w[h - 1] : nullptr;
+}
+
+}  // namespace fn
+
+using namespace fn;
+
+FN_API const char *fn_error() { return err().c_str(); }
+
+FN_API int fn_set_device(int dev) {
+    int n = 0;
+    FN_CK(cudaGetDeviceCount(&n));
+    if (dev < 0 || dev >= n) return fail("fn_set_device: no device " + std::to_string(dev));
+    g_device = dev;
+    FN_CK(cudaSetDevice(dev));
+    return 0;
+}
+
+// ---- launch settings (engine/faie2fn.cu:2786-2807) ---------------------------------------------------------------
+FN_API void fn_pdl(int on) { settings().pdl = on != 0; }
+FN_API void fn_early(int on) { settings().early = on != 0; }
+FN_API void fn_bench_hot(int on) { settings().bench_hot = on; }
+// GEMV plan overrides for sweeps: warps per CTA, ring KiB, stage KiB, CTAs per SM (0 = keep)
+FN_API void fn_gemv_override(int warps, int ring_kb, int stage_kb, int ctas_per_sm) {
+    Settings &s = settings();
+    if (warps > 0) s.warps_per_cta = warps;
+    if (ring_kb > 0) s.ring_kb = ring_kb;
+    if (stage_kb > 0) s.stage_kb = stage_kb;
+    if (ctas_per_sm > 0) s.ctas_per_sm = ctas_per_sm;
+}
+FN_API void fn_gemv_waves(int ctas_per_sm) { settings().ctas_per_sm = ctas_per_sm > 0 ? ctas_per_sm : 1; }
+
+// plan of a weight: out = {lpr, gpl, rows per stage, ring slots, CTAs, threads, row stride bytes}
+FN_API int fn_gemv_plan(uint32_t type, int rows, int cols, int *out) {
+    if (cudaSetDevice(hook_device()) != cudaSuccess) return fail("fn_gemv_plan: no CUDA device");
+    GemvPlan p;
+    if (!plan_gemv(p, type, rows, cols, 1)) return fail("unsupported type/shape");
+    const int v[7] = {p.lpr, p.gpl, p.rps, p.slots, p.ctas, p.threads, (int)p.ldw};
+    memcpy(out, v, sizeof(v));
+    return 0;
+}
+
+// ---- model-free test hooks (engine/faie2fn.cu:2745-2782, 2914-2935) -----------------------------------------------
+
+// out[r][c] = dequant of GGUF rows W (rows x row_bytes(type, cols))
+FN_API int fn_test_dequant(uint32_t type, const uint8_t *Wh, int rows, int cols, float *outh) {
+    const uint64_t rb = row_bytes(type, cols);
+    if (!rb || cols % 32 || rows < 0) return fail("unsupported type/shape");
+    if (rows == 0) return 0;
+    FN_CK(cudaSetDevice(hook_device()));
+    cudaStream_t s = hook_stream();
+    DevBuf W, out;
+    FN_CK(cudaMalloc(&W.p, rb * rows));
+    FN_CK(cudaMalloc(&out.p, (size_t)rows * cols * 4));
+    FN_CK(cudaMemcpyAsync(W.p, Wh, rb * rows, cudaMemcpyHostToDevice, s));
+    if (launch_dequant(type, W.as<uint8_t>(), rb, rows, cols, out.as<float>(), s)) return -1;
+    FN_CK(cudaMemcpyAsync(outh, out.p, (size_t)rows * cols * 4, cudaMemcpyDeviceToHost, s));
+    FN_CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+// y[t][r] = W[r] . x[t], t < nt <= 8, on GGUF rows W: uploaded to the engine's row layout, then the engine's GEMV
+FN_API int fn_test_gemv(uint32_t type, const uint8_t *Wh, int rows, int cols, const float *xh, int nt, float *yh) {
+    GemvPlan p;
+    if (nt < 1 || nt > 8) return fail("nt out of range (1..8)");
+    FN_CK(cudaSetDevice(hook_device()));
+    if (!plan_gemv(p, type, rows, cols, nt == 1 ? 1 : 8)) return fail("unsupported type/shape");
+    cudaStream_t s = hook_stream();
+    DevBuf W, x, y;
+    FN_CK(cudaMalloc(&W.p, plan_weight_bytes(p)));
+    FN_CK(cudaMalloc(&x.p, (size_t)nt * cols * 4));
+    FN_CK(cudaMalloc(&y.p, (size_t)nt * rows * 4));
+    FN_CK(cudaMemcpy2DAsync(W.p, p.ldw, Wh, p.rb, p.rb, rows, cudaMemcpyHostToDevice, s));
+    FN_CK(cudaMemcpyAsync(x.p, xh, (size_t)nt * cols * 4, cudaMemcpyHostToDevice, s));
+    if (launch_gemv(p, W.as<uint8_t>(), x.as<float>(), cols, y.as<float>(), rows, nt, false, false, s)) return -1;
+    FN_CK(cudaMemcpyAsync(yh, y.p, (size_t)nt * rows * 4, cudaMemcpyDeviceToHost, s));
+    FN_CK(cudaStreamSynchronize(s));
+    return check_dev_error("fn_test_gemv");
+}
+
+// GEMV timing on hash-random bytes of a format with the weights cold in L2 (as in a forward, where each weight is
+// read once): `copies` rotating copies whose total exceeds twice the L2, `iters` calls captured in one CUDA graph,
+// one warm-up replay, an L2 flush, then one timed replay. ms per call (engine/faie2fn.cu:2817-2866).
+FN_API int fn_bench_gemv(uint32_t type, int rows, int cols, int nt, int iters, float *ms) {
+    GemvPlan p;
+    if (nt < 1 || nt > 8 || iters < 1) return fail("nt/iters out of range");
+    FN_CK(cudaSetDevice(hook_device()));
+    if (!plan_gemv(p, type, rows, cols, nt == 1 ? 1 : 8)) return fail("unsupported type/shape");
+    int dev = 0, l2 = 0;
+    FN_CK(cudaGetDevice(&dev));
+    FN_CK(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev));
+    const size_t wb = plan_weight_bytes(p);
+    const bool hot = settings().bench_hot != 0;
+    int copies = hot ? 1 : (int)std::min<size_t>((size_t)iters, std::max<size_t>(2, (2 * (size_t)l2) / wb + 1));
+    while (copies > 1 && wb * copies > (8ull << 30)) --copies;
+    DevBuf W, x, y, flush;
+    const size_t flush_n = 2 * (size_t)l2;
+    FN_CK(cudaMalloc(&W.p, wb * copies));
+    FN_CK(cudaMalloc(&x.p, (size_t)nt * cols * 4));
+    FN_CK(cudaMalloc(&y.p, (size_t)nt * rows * 4));
+    FN_CK(cudaMalloc(&flush.p, flush_n));
+    std::vector<uint8_t> hb(wb);
+    for (size_t i = 0; i < wb; ++i) hb[i] = (uint8_t)((i * 2654435761u) >> 13);
+    FN_CK(cudaMemcpy(W.p, hb.data(), wb, cudaMemcpyHostToDevice));
+    for (int c = 1; c < copies; ++c) FN_CK(cudaMemcpy(W.as<uint8_t>() + wb * c, W.p, wb, cudaMemcpyDeviceToDevice));
+    FN_CK(cudaMemset(x.p, 0, (size_t)nt * cols * 4));
+    cudaStream_t st = hook_stream();
+    cudaGraph_t g;
+    cudaGraphExec_t ge;
+    FN_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int rc = 0;
+    for (int i = 0; i < iters && !rc; ++i)
+        rc = launch_gemv(p, W.as<uint8_t>() + wb * (i % copies), x.as<float>(), cols, y.as<float>(), rows, nt, false, false, st);
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (rc) return -1;
+    FN_CK(ce);
+    FN_CK(cudaGraphInstantiate(&ge, g, 0));
+    cudaEvent_t a, b;
+    FN_CK(cudaEventCreate(&a));
+    FN_CK(cudaEventCreate(&b));
+    FN_CK(cudaGraphLaunch(ge, st));
+    if (!hot) FN_CK(cudaMemsetAsync(flush.p, 1, flush_n, st));
+    FN_CK(cudaEventRecord(a, st));
+    FN_CK(cudaGraphLaunch(ge, st));
+    FN_CK(cudaEventRecord(b, st));
+    FN_CK(cudaEventSynchronize(b));
+    FN_CK(cudaEventElapsedTime(ms, a, b));
+    *ms /= iters;
+    cudaGraphExecDestroy(ge);
+    cudaGraphDestroy(g);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return check_dev_error("fn_bench_gemv");
+}
+
+// ---- resident weights (device-pointer API for the bench and the engine's callers) --------------------------------
+
+// Upload GGUF rows (rows x row_bytes(type, cols), host memory) to the current device in the engine's layout.
+// Returns a handle >= 1, or -1.
+FN_API int fn_w_create(uint32_t type, const uint8_t *Wh, int rows, int cols) {
+    WeightH *w = new WeightH();
+    if (!plan_gemv(w->plan1, type, rows, cols, 1) || !plan_gemv(w->plan8, type, rows, cols, 8)) {
+        delete w;
+        return fail("fn_w_create: unsupported type/shape");
+    }
+    cudaGetDevice(&w->dev);
+    const GemvPlan &p = w->plan1;
+    if (cudaMalloc(&w->d, plan_weight_bytes(p)) != cudaSuccess ||
+        cudaMemcpy2D(w->d, p.ldw, Wh, p.rb, p.rb, rows, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMalloc(&w->xbuf, (size_t)8 * cols * 4) != cudaSuccess || cudaMalloc(&w->ybuf, (size_t)8 * rows * 4) != cudaSuccess) {
+        cudaFree(w->d);
+        cudaFree(w->xbuf);
+        delete w;
+        return fail("fn_w_create: device allocation/copy failed");
+    }
+    std::lock_guard<std::mutex> l(g_w_mu);
+    g_w.push_back(w);
+    return (int)g_w.size();
+}
+
+FN_API int fn_w_free(int h) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_free: bad handle");
+    cudaFree(w->d);
+    cudaFree(w->xbuf);
+    cudaFree(w->ybuf);
+    delete w;
+    std::lock_guard<std::mutex> l(g_w_mu);
+    g_w[h - 1] = nullptr;
+    return 0;
+}
+
+// bytes the GEMV must read per call: the GGUF weight bytes (rows x row_bytes), the padding excluded
+FN_API double fn_w_bytes(int h) {
+    WeightH *w = wget(h);
+    return w ? (double)w->plan1.rb * w->plan1.rows : -1.0;
+}
+
+// Launch y[t][r] (+acc)= W[r] . x[t] for t < nt on `stream` with device pointers (no synchronisation).
+FN_API int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int acc, void *stream) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_gemv: bad handle");
+    if (nt < 1 || nt > 8) return fail("fn_w_gemv: nt out of range (1..8)");
+    return launch_gemv(nt == 1 ? w->plan1 : w->plan8, w->d, x, xs, y, ys, nt, acc != 0, false, (cudaStream_t)stream);
+}
+
+// The same with host buffers: x (nt x cols) copied in, y (nt x rows) copied out, all on `stream` (x and y should be
+// pinned for the copies to be asynchronous). Does not synchronise; see fn_sync.
+FN_API int fn_w_gemv_host(int h, const float *xh, int nt, float *yh, void *stream) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_gemv_host: bad handle");
+    if (nt < 1 || nt > 8) return fail("fn_w_gemv_host: nt out of range (1..8)");
+    cudaStream_t s = (cudaStream_t)stream;
+    const GemvPlan &p = nt == 1 ? w->plan1 : w->plan8;
+    FN_CK(cudaMemcpyAsync(w->xbuf, xh, (size_t)nt * p.cols * 4, cudaMemcpyHostToDevice, s));
+    if (launch_gemv(p, w->d, w->xbuf, p.cols, w->ybuf, p.rows, nt, false, false, s)) return -1;
+    FN_CK(cudaMemcpyAsync(yh, w->ybuf, (size_t)nt * p.rows * 4, cudaMemcpyDeviceToHost, s));
+    return 0;
+}
+
+FN_API int fn_sync(void *stream) {
+    FN_CK(cudaStreamSynchronize((cudaStream_t)stream));
+    FN_CK(cudaGetLastError());
+    return check_dev_error("fn_sync");
+}

@@ -1,0 +1,72 @@
+// Host-side interfaces shared by the engine's translation units.
+#pragma once
+
+#include "fn_common.cuh"
+
+namespace fn {
+
+// ---------------------------------------------------------------------------------------------------------------
+// dequant-GEMV launch plan. Depends on (format, rows, cols, token capacity) only, never on the tokens of a call, so
+// a token's result is bit-identical in any batch up to the capacity.
+struct GemvPlan {
+    uint32_t type = 0;
+    int rows = 0, cols = 0;
+    uint64_t rb = 0;      // bytes of one GGUF row
+    uint32_t ldw = 0;     // device row stride: rb rounded up to 16 bytes (the bulk-copy granule)
+    int G = 0;            // 32-value groups per row
+    int lpr = 32;         // lanes per row
+    int gpl = 1;          // groups per lane (lane l of a row holds groups l, l + lpr, ...)
+    int ntcap = 1;        // tokens per call the plan serves (1: x in registers where the row fits)
+    int xreg = 0;         // 1: each lane keeps its x slice in registers
+    int rps = 0;          // rows per pipeline stage
+    int slots = 0;        // stages in the shared-memory ring
+    int ctas = 0;         // grid size (contiguous row ranges)
+    int threads = 256;
+    uint32_t stage_bytes = 0;
+    uint32_t x_off = 0, ring_off = 0, grid_off = 0;
+    size_t smem = 0;
+};
+
+bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap);
+size_t plan_weight_bytes(const GemvPlan &p);  // device bytes of the padded weight
+
+// y[t][r] (+)= W[r] . x[t] for t < nt <= p.ntcap. W: rows at stride p.ldw bytes (16-byte aligned); x, y: fp32 with
+// token strides xs, ys (x 16-byte aligned, xs a multiple of 4). early: x was complete before the previous kernel
+// started, so the GEMV does not wait for it before reading x (it waits before it exits).
+int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
+                bool early, cudaStream_t s);
+
+// dequantise rows x cols of GGUF rows (row stride rb bytes) into out[r][c] fp32
+int launch_dequant(uint32_t type, const uint8_t *W, uint64_t rb, int rows, int cols, float *out, cudaStream_t s);
+
+// global launch settings (set through the C ABI)
+struct Settings {
+    bool pdl = true;         // programmatic dependent launch
+    bool early = true;       // GEMVs marked early run beside their predecessor
+    int warps_per_cta = 8;   // GEMV consumer warps
+    int ring_kb = 72;        // GEMV shared-memory ring per CTA
+    int stage_kb = 16;       // target bytes per pipeline stage
+    int ctas_per_sm = 1;     // GEMV CTAs per SM
+    int ov_rps = 0;          // overrides (0 = automatic)
+    int bench_hot = 0;
+};
+Settings &settings();
+int num_sms();
+
+// launch with the programmatic-serialization attribute when enabled
+template <typename... P, typename... A>
+cudaError_t launch_k(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = settings().pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, ((P)args)...);
+}
+
+}  // namespace fn

@@ -1,0 +1,110 @@
+"""ctypes wrapper for libfaie2fn.so, the B200 build of the FAIE2-FlashNext decode hot path.
+
+Mirrors flashnext/fn.py of the reference (class FN over the engine's C ABI, same method names, argument meaning
+and error behaviour: a non-zero return raises RuntimeError with fn_error()). Differences: Linux CDLL instead of
+the Windows DLL; the library path comes from the FN_DLL environment variable, else the in-tree build; there is no
+fallback — if the library is missing the constructor raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+DLL = os.environ.get("FN_DLL") or os.path.join(os.path.dirname(HERE), "lib", "libfaie2fn.so")
+
+P = np.ctypeslib.ndpointer
+F32 = P(np.float32, flags="C_CONTIGUOUS")
+I32 = P(np.int32, flags="C_CONTIGUOUS")
+U8 = P(np.uint8, flags="C_CONTIGUOUS")
+
+# symbols include/faie2fn.h declares (the CPU test-suite checks that the library exports every one)
+EXPORTS = [
+    "fn_error", "fn_set_device", "fn_pdl", "fn_early", "fn_bench_hot", "fn_gemv_override", "fn_gemv_waves",
+    "fn_gemv_plan", "fn_test_dequant", "fn_test_gemv", "fn_bench_gemv", "fn_w_create", "fn_w_free", "fn_w_bytes",
+    "fn_w_gemv", "fn_w_gemv_host", "fn_sync",
+]
+
+
+class FN:
+    def __init__(self, dll: str = DLL):
+        if not os.path.exists(dll):
+            raise FileNotFoundError(f"{dll} not built (python faie2-flashnext_b200/build.py)")
+        d = self.d = C.CDLL(dll)
+        self.path = dll
+        d.fn_error.restype = C.c_char_p
+        d.fn_set_device.argtypes = [C.c_int]
+        d.fn_pdl.argtypes = [C.c_int]
+        d.fn_early.argtypes = [C.c_int]
+        d.fn_bench_hot.argtypes = [C.c_int]
+        d.fn_gemv_override.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
+        d.fn_gemv_waves.argtypes = [C.c_int]
+        d.fn_gemv_plan.argtypes = [C.c_uint32, C.c_int, C.c_int, I32]
+        d.fn_test_dequant.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32]
+        d.fn_test_gemv.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, F32]
+        d.fn_bench_gemv.argtypes = [C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float)]
+        d.fn_w_create.argtypes = [C.c_uint32, U8, C.c_int, C.c_int]
+        d.fn_w_free.argtypes = [C.c_int]
+        d.fn_w_bytes.argtypes = [C.c_int]
+        d.fn_w_bytes.restype = C.c_double
+        d.fn_w_gemv.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
+        d.fn_w_gemv_host.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        d.fn_sync.argtypes = [C.c_void_p]
+
+    def check(self, rc):
+        if rc != 0:
+            raise RuntimeError(self.d.fn_error().decode())
+
+    def set_device(self, dev: int):
+        self.check(self.d.fn_set_device(int(dev)))
+
+    # ---- the reference's unit-test hooks (flashnext/fn.py:56-66) ----
+    def dequant(self, qtype, raw, rows, cols):
+        out = np.zeros((rows, cols), np.float32)
+        self.check(self.d.fn_test_dequant(int(qtype), np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), rows, cols, out))
+        return out
+
+    def gemv(self, qtype, raw, rows, cols, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim == 1:
+            x = x[None]
+        nt = x.shape[0]
+        y = np.zeros((nt, rows), np.float32)
+        self.check(self.d.fn_test_gemv(int(qtype), np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), rows, cols,
+                                       x, nt, y))
+        return y
+
+    def gemv_plan(self, qtype, rows, cols):
+        out = np.zeros(7, np.int32)
+        self.check(self.d.fn_gemv_plan(int(qtype), rows, cols, out))
+        return dict(zip(["lpr", "gpl", "rows_per_stage", "slots", "ctas", "threads", "ldw"], out.tolist()))
+
+    def bench_gemv(self, qtype, rows, cols, nt=1, iters=50):
+        ms = C.c_float()
+        self.check(self.d.fn_bench_gemv(int(qtype), rows, cols, nt, iters, C.byref(ms)))
+        return ms.value
+
+    # ---- resident weights ----
+    def w_create(self, qtype, raw, rows, cols) -> int:
+        h = self.d.fn_w_create(int(qtype), np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), rows, cols)
+        if h < 0:
+            raise RuntimeError(self.d.fn_error().decode())
+        return h
+
+    def w_free(self, h):
+        self.check(self.d.fn_w_free(h))
+
+    def w_bytes(self, h) -> float:
+        return self.d.fn_w_bytes(h)
+
+    def w_gemv(self, h, x_ptr, xs, y_ptr, ys, nt=1, acc=0, stream=0):
+        self.check(self.d.fn_w_gemv(h, C.c_void_p(x_ptr), xs, C.c_void_p(y_ptr), ys, nt, acc, C.c_void_p(stream)))
+
+    def w_gemv_host(self, h, x_ptr, nt, y_ptr, stream=0):
+        self.check(self.d.fn_w_gemv_host(h, C.c_void_p(x_ptr), nt, C.c_void_p(y_ptr), C.c_void_p(stream)))
+
+    def sync(self, stream=0):
+        self.check(self.d.fn_sync(C.c_void_p(stream)))

@@ -1,0 +1,81 @@
+/* C ABI of libfaie2fn.so, the B200 (sm_100a) decode hot path of FAIE2-FlashNext.
+ *
+ * Every entry point mirrors one the reference exports from engine/faie2fn.cu (built there as faie2fn.dll with
+ * __declspec(dllexport), :34) and binds through the same ctypes layer (flashnext/fn.py). Conventions, as in the
+ * reference: int results are 0 on success and -1 on error, with the message in fn_error() (:114-118, :2495); the
+ * caller owns every host buffer (C-contiguous); the fn_test_* and fn_bench_* hooks are synchronous and use the device
+ * named by fn_set_device (default: env FN_DEVICE, else 0). Not thread-safe: one caller thread.
+ *
+ * Type ids are ggml's: Q4_0=2 Q4_1=3 Q5_0=6 Q5_1=7 Q8_0=8 Q2_K=10 Q3_K=11 Q4_K=12 Q5_K=13 Q6_K=14 IQ2_XXS=16
+ * IQ2_XS=17 IQ3_XXS=18 IQ4_NL=20 IQ3_S=21 IQ2_S=22 IQ4_XS=23 BF16=30 Q2_0=42.
+ */
+#ifndef FAIE2FN_H
+#define FAIE2FN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- errors and settings ---------------------------------------------------------------------------------- */
+
+/* Message of the last failed call. Replaces fn_error (engine/faie2fn.cu:2495). */
+const char *fn_error(void);
+
+/* Device used by the test / bench hooks; also made current. New: the reference hard-codes devices 0 and 1
+ * (engine/faie2fn.cu:2757, 2826). */
+int fn_set_device(int dev);
+
+/* Programmatic dependent launch on/off. Replaces fn_pdl (engine/faie2fn.cu:2800). */
+void fn_pdl(int on);
+/* GEMVs marked early run beside the kernel before them, on/off. Replaces fn_early (engine/faie2fn.cu:2802). */
+void fn_early(int on);
+/* 1: fn_bench_gemv replays one hot copy without an L2 flush. Replaces fn_bench_hot (engine/faie2fn.cu:2822). */
+void fn_bench_hot(int on);
+/* GEMV plan overrides for sweeps (0 keeps a setting): consumer warps per CTA, shared-memory ring KiB, stage KiB,
+ * CTAs per SM. Replaces fn_gemv_override(wpt, ks, tb, warps_per_sm) (engine/faie2fn.cu:2786-2791); the B200 plan
+ * has no split-K, so its knobs differ. */
+void fn_gemv_override(int warps, int ring_kb, int stage_kb, int ctas_per_sm);
+/* CTAs per SM of the GEMV grid. Replaces fn_gemv_waves (engine/faie2fn.cu:2793). */
+void fn_gemv_waves(int ctas_per_sm);
+/* Plan of a rows x cols weight: out[7] = {lanes per row, groups per lane, rows per stage, ring slots, CTAs,
+ * threads, row stride bytes}. Replaces fn_gemv_plan (engine/faie2fn.cu:2809-2815). */
+int fn_gemv_plan(uint32_t type, int rows, int cols, int *out);
+
+/* ---- model-free test / bench hooks ------------------------------------------------------------------------ */
+
+/* out[r][c] = dequant(W)[r][c]: W is rows GGUF rows of `type` (rows x row_bytes), out rows x cols fp32.
+ * Bit-identical to gguf-py 0.19.0. Replaces fn_test_dequant (engine/faie2fn.cu:2751-2782). */
+int fn_test_dequant(uint32_t type, const uint8_t *W, int rows, int cols, float *out);
+
+/* y[t][r] = sum_c dequant(W)[r][c] x[t][c] for t < nt <= 8; x nt x cols, y nt x rows, fp32.
+ * Replaces fn_test_gemv (engine/faie2fn.cu:2914-2935). */
+int fn_test_gemv(uint32_t type, const uint8_t *W, int rows, int cols, const float *x, int nt, float *y);
+
+/* ms per GEMV call, weights cold in L2 (rotating copies, L2 flushed, iters calls replayed as one CUDA graph).
+ * Replaces fn_bench_gemv (engine/faie2fn.cu:2823-2866). */
+int fn_bench_gemv(uint32_t type, int rows, int cols, int nt, int iters, float *ms);
+
+/* ---- resident weights (device-pointer interface; new, the engine-internal QW of engine/faie2fn.cu:1940-1948
+ * exposed so callers that own device memory and streams can drive the GEMV) ---------------------------------- */
+
+/* Upload GGUF rows to the current device; returns a handle >= 1 or -1. Replaces load_qw
+ * (engine/faie2fn.cu:2125-2142) for one tensor. */
+int fn_w_create(uint32_t type, const uint8_t *W, int rows, int cols);
+int fn_w_free(int h);
+/* GGUF bytes of the weight (rows x row_bytes), the bytes one GEMV must read. */
+double fn_w_bytes(int h);
+/* Launch y[t][r] (+= if acc) W[r] . x[t] for t < nt <= 8 on a CUDA stream (device pointers, token strides xs, ys
+ * in floats; x 16-byte aligned). Replaces gemv() (engine/faie2fn.cu:2250-2281). */
+int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int acc, void *stream);
+/* The same with host buffers x (nt x cols) and y (nt x rows), copied on the stream; does not synchronise. */
+int fn_w_gemv_host(int h, const float *x, int nt, float *y, void *stream);
+/* Synchronise a stream and report any device-side error (a bounded wait that ran out). */
+int fn_sync(void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FAIE2FN_H */
