@@ -1,0 +1,350 @@
+"""Benchmark of the B200 decode hot path: dequant-fused GEMV throughput (the format sweep).
+
+A step is one pass of the format sweep at batch 1: the 13 graded GGUF formats x (2048x4096, 4096x2048, 512x2048)
+(out x in) plus the Q6_K lm_head 151936x2048, 40 GEMVs, each weight read once (385 MB per step, larger than the
+126 MB L2, so every step streams its weights from HBM). Weights are seeded synthetic GGUF blocks (uniform random
+bytes, fp16 scales |N(0,1)|*1e-3), x is N(0,1): the reference's real model tensors are not shipped.
+
+  value  device-resident throughput: algorithmic bytes (GGUF weight bytes + 4*cols x + 4*rows y per GEMV) of all
+         ranks / the max over ranks of the CUDA-event time of K steps, each step one replay of the sweep captured as
+         CUDA graphs (programmatic dependent launch between the GEMVs)
+  e2e    the same metric through the C ABI with host buffers: every GEMV copies its x in from pinned memory and its y
+         out, inside the timed region
+  roofline  the dominant kernel (the lm_head GEMV): its algorithmic bytes / its mean CUDA-event duration inside the
+         timed region, against the measured HBM copy bandwidth
+  cpu_baseline  the reference's CPU path (gguf-py dequant + float64 numpy GEMV) on a bounded row sample, 1 core
+
+`--impl reference` times that CPU path with every host core instead (rank 0 only; other ranks exit 0).
+N > 1 (torchrun): every rank runs the sweep on its own GPU and weights (weak scaling; no data-path collective).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "faie2-flashnext_b200")
+for _p in (ROOT, PKG, os.path.join(PKG, "flashnext")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode tok/s (bs=1) and quant-GEMV achieved HBM GB/s vs B200 peak"
+SWEEP13 = ["Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "IQ2_XXS", "IQ3_XXS", "IQ4_XS"]
+SHAPES = [(2048, 4096), (4096, 2048), (512, 2048)]
+LM_HEAD = ("Q6_K", 151936, 2048)
+FALLBACK_HBM_GBS = 6650.0
+PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "gemv_q6k_lm_head_151936x2048.txt")
+
+
+def workload():
+    from synth import BY_NAME
+    w = [(BY_NAME[n], r, c, n) for n in SWEEP13 for (r, c) in SHAPES]
+    w.append((BY_NAME[LM_HEAD[0]], LM_HEAD[1], LM_HEAD[2], LM_HEAD[0]))
+    return w
+
+
+def alg_bytes(qtype, rows, cols):
+    from synth import row_bytes
+    return rows * row_bytes(qtype, cols) + 4 * cols + 4 * rows
+
+
+class ClockSampler:
+    """NVML SM clock, power and throttle reasons of one GPU, sampled in a thread while the timed region runs."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+               "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, torch_dev: int):
+        self.samples, self.stop_evt, self.th, self.h, self.max_mhz = [], threading.Event(), None, None, None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_dev).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode() if isinstance(uuid, str) else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # clocks are reported as unavailable, the run itself is unaffected
+            self.err = f"{type(e).__name__}: {e}"
+
+    def _loop(self):
+        while not self.stop_evt.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        if self.h is not None:
+            self.th = threading.Thread(target=self._loop, daemon=True)
+            self.th.start()
+
+    def stop(self):
+        if self.th:
+            self.stop_evt.set()
+            self.th.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": getattr(self, "err", "no samples")}
+        mhz = [s[0] for s in self.samples]
+        seen = set()
+        for _, rs in self.samples:
+            for name, bit in self.REASONS.items():
+                if rs & bit:
+                    seen.add(name)
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": sorted(seen),
+                "samples": len(mhz), "source": "nvml"}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per lm_head launch from the committed ncu summary (a 'dram_bytes_per_launch: N' line), or None."""
+    try:
+        for line in open(PROFILE_TRAFFIC):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline_sample(work, target_s=12.0, workers=1):
+    from oracle.ref_path import CPUSweep  # the checker's CPU path: baseline only
+    probe = CPUSweep([(q, r, c) for q, r, c, _ in work], 1 / 256, workers)
+    t = min(probe.step() for _ in range(2))
+    probe.close()
+    frac = min(1.0, (1 / 256) * target_s / max(t, 1e-3))
+    s = CPUSweep([(q, r, c) for q, r, c, _ in work], frac, workers)
+    dt = s.step()
+    s.close()
+    return s.bytes / dt / 1e9, frac, dt
+
+
+def run_reference(args, rank):
+    """`--impl reference`: the reference's CPU path (gguf-py dequant + float64 GEMV) on every host core."""
+    if rank != 0:
+        return
+    from oracle.ref_path import CPUSweep
+    work = workload()
+    cores = os.cpu_count() or 1
+    steps, warm = args.steps, args.warmup
+    budget = 150.0  # seconds for the whole run
+    probe = CPUSweep([(q, r, c) for q, r, c, _ in work], 1 / 512, cores)
+    t = min(probe.step() for _ in range(2))
+    probe.close()
+    per_step = max(0.02, min(3.0, budget / max(1, steps + warm)))
+    frac = min(1.0, (1 / 512) * per_step / max(t, 1e-4))
+    s = CPUSweep([(q, r, c) for q, r, c, _ in work], frac, cores)
+    for _ in range(warm):
+        s.step()
+    times = [s.step() for _ in range(steps)]
+    s.close()
+    total = sum(times)
+    gbs = s.bytes * steps / total / 1e9
+    sample = f"every GEMV of the sweep cut to {frac:.4g} of its rows ({s.bytes / 1e6:.1f} MB of GGUF weights per step)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": warm, "ms_per_step": round(1e3 * total / steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "config2 format sweep (13 formats x 3 shapes + Q6_K lm_head 151936x2048), bs=1",
+                   "path": "gguf-py 0.19.0 quants.dequantize -> float64 numpy x . W^T (flashnext/ref_fn.py:44-53, "
+                           "flashnext/test_fn_quants.py:34)"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "lm_head"],
+                    help="lm_head: only the dominant kernel (the small case the ncu capture profiles)")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+
+    from fn import FN
+    from synth import random_blocks
+
+    f = FN()
+    f.set_device(local)
+    work = workload() if args.workload == "sweep" else workload()[-1:]
+    hs, xs, ys = [], [], []
+    step_bytes = 0
+    for i, (q, r, c, name) in enumerate(work):
+        rng = np.random.default_rng(1000 * rank + i)
+        raw = random_blocks(q, r, c, rng)
+        hs.append(f.w_create(q, raw, r, c))
+        del raw
+        xs.append(torch.randn(c, device="cuda", generator=torch.Generator("cuda").manual_seed(i)))
+        ys.append(torch.empty(r, device="cuda"))
+        step_bytes += alg_bytes(q, r, c)
+    head_bytes = alg_bytes(*work[-1][:3])
+
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+
+    def launch(idx, s):
+        q, r, c, _ = work[idx]
+        f.w_gemv(hs[idx], xs[idx].data_ptr(), c, ys[idx].data_ptr(), r, 1, 0, s)
+
+    for i in range(len(work)):  # first launches outside capture (kernel attributes, error-word address)
+        launch(i, stream.cuda_stream)
+    f.sync(stream.cuda_stream)
+
+    g_small, g_head = (torch.cuda.CUDAGraph() if len(work) > 1 else None), torch.cuda.CUDAGraph()
+    if g_small is not None:
+        with torch.cuda.graph(g_small, stream=stream, capture_error_mode="thread_local"):
+            for i in range(len(work) - 1):
+                launch(i, torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.graph(g_head, stream=stream, capture_error_mode="thread_local"):
+        launch(len(work) - 1, torch.cuda.current_stream().cuda_stream)
+
+    def step():
+        if g_small is not None:
+            g_small.replay()
+        g_head.replay()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0.record(stream)
+    for k in range(K):
+        ev[k][0].record(stream)
+        if g_small is not None:
+            g_small.replay()
+        ev[k][1].record(stream)
+        g_head.replay()
+        ev[k][2].record(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    head_ms = sum(ev[k][1].elapsed_time(ev[k][2]) for k in range(K)) / K
+    small_ms = sum(ev[k][0].elapsed_time(ev[k][1]) for k in range(K)) / K
+    f.sync(stream.cuda_stream)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * step_bytes * K / (ms / 1e3) / 1e9
+
+    # e2e: through the C ABI with pinned host buffers, host<->device copies inside the timed region
+    xh = [torch.empty(w[2], dtype=torch.float32, pin_memory=True) for w in work]
+    yh = [torch.empty(w[1], dtype=torch.float32, pin_memory=True) for w in work]
+    for i, x in enumerate(xs):
+        xh[i].copy_(x.cpu())
+    h2d = sum(4 * w[2] for w in work)
+    d2h = sum(4 * w[1] for w in work)
+    Ke = max(3, min(K, 200))
+
+    def e2e_step():
+        for i in range(len(work)):
+            f.w_gemv_host(hs[i], xh[i].data_ptr(), 1, yh[i].data_ptr(), stream.cuda_stream)
+        f.sync(stream.cuda_stream)
+
+    for _ in range(3):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(Ke):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = world * step_bytes * Ke / (e2e_ms / 1e3) / 1e9
+    ok = np.isfinite(yh[-1].numpy()).all()
+
+    peak, peak_kind = measured_peak()
+    achieved = head_bytes / (head_ms / 1e3) / 1e9
+    traffic = profile_traffic()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 format sweep: 13 formats x (2048x4096, 4096x2048, 512x2048) + Q6_K lm_head "
+                               "151936x2048, bs=1, 40 GEMVs per step",
+                   "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (385 MB of weights per step, each "
+                   "read once per step)", "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "frac_of_measured_peak": round(value / world / peak, 4)},
+        "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": Ke, "outputs_finite": bool(ok)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "k_gemv<Q6_K> lm_head 151936x2048", "mean_launch_us": round(head_ms * 1e3, 2),
+                     "alg_bytes_per_launch": head_bytes},
+        "split_ms_per_step": {"39 sweep GEMVs": round(small_ms, 5), "lm_head": round(head_ms, 5)},
+        "gpu_launches": K * len(work),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, frac, dt = cpu_baseline_sample(work)
+        line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                                "sample": f"every GEMV of the sweep cut to {frac:.3g} of its rows, one pass "
+                                          f"({dt:.1f} s), gguf-py dequant + float64 numpy GEMV, 1 thread"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del g_small, g_head
+    for h in hs:
+        f.w_free(h)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

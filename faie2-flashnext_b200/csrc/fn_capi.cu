@@ -21,7 +21,11 @@ int fail(const std::string &msg) {
 }
 
 Settings &settings() {
-    static Settings s;
+    static Settings s = [] {
+        Settings v;
+        if (const char *e = getenv("FN_PDL")) v.pdl = atoi(e) != 0;  // FN_PDL=0: no programmatic launch (profiling)
+        return v;
+    }();
     return s;
 }
 

@@ -10,12 +10,15 @@
 // launch the weight stream of this GEMV overlaps the tail of the kernel before it. x is staged once per CTA into a
 // bank-conflict-free padded layout ([t][group][36] floats); for one token each lane then keeps its K-slice of x in
 // registers. Lane l of a row (lpr lanes per row) owns groups l, l + lpr, ... of 32 values: it decodes each group in
-// registers (Dec<TY>, bit-exact vs gguf-py) into four FMA chains, adds the chains, adds the group sums in group
-// order, and the row's lanes meet in a butterfly. A row never spans warps or CTAs, so there is no split-K scratch
-// and no reduce kernel; the sum order is a function of (format, cols) alone.
+// registers (Dec<TY>, bit-exact vs gguf-py) into four FMA chains, adds the chains (fp32), accumulates the group sums
+// in double in group order, and the row's lanes meet in a double butterfly; the row result is rounded to fp32 once.
+// A row never spans warps or CTAs, so there is no split-K scratch and no reduce kernel; the sum order is a function
+// of (format, cols) alone.
 #include "fn_decode.cuh"
 #include "fn_engine.h"
 #include "fn_grids.h"
+
+#include <unordered_set>
 
 namespace fn {
 
@@ -120,9 +123,9 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
                 const int row = base + sub;
                 const bool valid = row < n;
                 const uint8_t *rowp = sbuf + (size_t)row * a.ldw;
-                float acc[NT];
+                double acc[NT];  // group sums accumulate in double: one fp32 rounding per group, not per add
 #pragma unroll
-                for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+                for (int t = 0; t < NT; ++t) acc[t] = 0.0;
                 if (valid) {
                     const int ni = GPL > 0 ? GPL : gpl;
 #pragma unroll
@@ -150,13 +153,13 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
                         });
 #pragma unroll
                         for (int t = 0; t < NT; ++t)
-                            acc[t] = __fadd_rn(acc[t], __fadd_rn(__fadd_rn(c[t][0], c[t][1]), __fadd_rn(c[t][2], c[t][3])));
+                            acc[t] += (double)__fadd_rn(__fadd_rn(c[t][0], c[t][1]), __fadd_rn(c[t][2], c[t][3]));
                     }
                 }
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
 #pragma unroll
-                    for (int o = LPR / 2; o > 0; o >>= 1) acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], o));
+                    for (int o = LPR / 2; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
                 }
                 if (valid && lr == 0) {
                     const int r = rr0 + row;
@@ -164,7 +167,8 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
                     for (int t = 0; t < NT; ++t) {
                         if (NT > 1 && t >= nt) break;
                         float *o = a.y + (size_t)t * a.ys + r;
-                        *o = a.acc ? __fadd_rn(*o, acc[t]) : acc[t];
+                        const float v = __double2float_rn(acc[t]);
+                        *o = a.acc ? __fadd_rn(*o, v) : v;
                     }
                 }
             }
@@ -215,6 +219,11 @@ int launch_dequant(uint32_t type, const uint8_t *W, uint64_t rb, int rows, int c
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// dynamic shared memory of a launch of plan p with nt tokens
+static size_t gemv_smem(const GemvPlan &p, int nt) {
+    return align_up(p.x_off + (size_t)nt * p.G * XPAD * 4, 128);
+}
+
 bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     p = GemvPlan{};
     p.type = type;
@@ -222,8 +231,6 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     p.cols = cols;
     p.rb = row_bytes(type, cols);
     if (!p.rb || cols % 32 || rows < 1 || ntcap < 1 || ntcap > 8) return false;
-    int qk, tb;
-    type_info(type, qk, tb);
     p.ldw = (uint32_t)align_up(p.rb, 16);
     p.G = cols / 32;
     p.ntcap = ntcap == 1 ? 1 : 8;
@@ -233,8 +240,9 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     const Settings &S = settings();
     p.threads = 32 * std::max(1, std::min(S.warps_per_cta, 16));
     const int nw = p.threads / 32, rpw = 32 / p.lpr, pass = nw * rpw;
-    // rows per stage: whole passes of the CTA's warps, about stage_kb bytes
-    int rps = std::max(1, (int)((size_t)S.stage_kb * 1024 / p.ldw / pass)) * pass;
+    // rows per stage: about stage_kb bytes, whole passes of the CTA's warps when a pass fits
+    int rps = std::max(1, (int)((size_t)S.stage_kb * 1024 / p.ldw));
+    if (rps >= pass) rps = rps / pass * pass;
     if (S.ov_rps > 0) rps = S.ov_rps;
     const int ctas_max = std::max(1, num_sms() * std::max(1, S.ctas_per_sm));
     p.ctas = std::min(ctas_max, (rows + rpw - 1) / rpw);
@@ -244,17 +252,18 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     const int stages_per_cta = (rows_per_cta + p.rps - 1) / p.rps;
     p.slots = (int)std::max<size_t>(2, (size_t)S.ring_kb * 1024 / p.stage_bytes);
     p.slots = std::max(1, std::min(p.slots, std::min(stages_per_cta, 16)));
-    const size_t bar_bytes = 16 * 8;
-    p.ring_off = (uint32_t)align_up(bar_bytes, 128);
-    p.x_off = (uint32_t)align_up(p.ring_off + (size_t)p.slots * p.stage_bytes, 128);
-    p.grid_off = (uint32_t)align_up(p.x_off + (size_t)p.ntcap * p.G * XPAD * 4, 128);
-    p.smem = align_up(p.grid_off + (size_t)grid_words(type) * 4, 128);
+    // layout: barriers | ring | codebook | x (sized per call by its token count: gemv_smem)
+    p.ring_off = 128;
+    p.grid_off = (uint32_t)align_up(p.ring_off + (size_t)p.slots * p.stage_bytes, 128);
+    p.x_off = (uint32_t)align_up(p.grid_off + (size_t)grid_words(type) * 4, 128);
+    p.smem = gemv_smem(p, p.ntcap);
+    if (p.smem > 227 * 1024) p.smem = gemv_smem(p, 1);  // wide rows: fewer tokens per call fit (checked at launch)
     return p.smem <= 227 * 1024;
 }
 
 size_t plan_weight_bytes(const GemvPlan &p) { return (size_t)p.rows * p.ldw; }
 
-template <uint32_t TY> static cudaError_t launch_t(const GemvPlan &p, const GemvArgs &a, cudaStream_t s) {
+template <uint32_t TY> static cudaError_t launch_t(const GemvPlan &p, const GemvArgs &a, size_t smem, cudaStream_t s) {
     void (*k)(const GemvArgs) = nullptr;
     if (p.ntcap == 1) {
         if (p.xreg) {
@@ -270,14 +279,21 @@ template <uint32_t TY> static cudaError_t launch_t(const GemvPlan &p, const Gemv
         else if (p.lpr == 16) k = k_gemv<TY, 8, 16, 0, false>;
         else k = k_gemv<TY, 8, 32, 0, false>;
     }
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-    if (e != cudaSuccess) return e;
-    return launch_k(k, dim3(p.ctas), dim3(p.threads), p.smem, s, a);
+    static std::unordered_set<const void *> configured;  // one attribute call per kernel, outside graph capture
+    if (!configured.count((const void *)k)) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured.insert((const void *)k);
+    }
+    return launch_k(k, dim3(p.ctas), dim3(p.threads), smem, s, a);
 }
 
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
                 bool early, cudaStream_t s) {
     if (nt < 1 || nt > p.ntcap) return fail("gemv: nt out of range for the plan");
+    const size_t smem = gemv_smem(p, nt);
+    if (smem > 227 * 1024) return fail("gemv: " + std::to_string(nt) + " tokens of " + std::to_string(p.cols) +
+                                       " columns do not fit in shared memory");
     if (((uintptr_t)W & 15) || ((uintptr_t)x & 15) || (xs & 3)) return fail("gemv: W and x must be 16-byte aligned, xs % 4 == 0");
     GemvArgs a;
     a.W = W;
@@ -299,7 +315,7 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.early = early && settings().early && settings().pdl ? 1 : 0;
     a.err = dev_error_ptr();
     cudaError_t e = cudaSuccess;
-    const bool known = dispatch_type(p.type, [&]<uint32_t TY>() { e = launch_t<TY>(p, a, s); });
+    const bool known = dispatch_type(p.type, [&]<uint32_t TY>() { e = launch_t<TY>(p, a, smem, s); });
     if (!known) return fail("gemv: unsupported type " + std::to_string(p.type));
     if (e != cudaSuccess) return fail(std::string("gemv launch: ") + cudaGetErrorString(e));
     return 0;
