@@ -62,7 +62,7 @@ int check_dev_error(const char *where) {
 }
 
 static int g_device = -1;  // device the test / bench hooks use (FN_DEVICE, default 0)
-static int hook_device() {
+int hook_device() {
     if (g_device < 0) {
         const char *e = getenv("FN_DEVICE");
         g_device = e ? atoi(e) : 0;
@@ -71,7 +71,7 @@ static int hook_device() {
 }
 
 // a non-blocking stream per device for the synchronous hooks
-static cudaStream_t hook_stream() {
+cudaStream_t hook_stream() {
     static cudaStream_t st[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -79,14 +79,6 @@ static cudaStream_t hook_stream() {
     return st[dev];
 }
 
-// device buffers freed when the scope ends
-struct DevBuf {
-    void *p = nullptr;
-    ~DevBuf() {
-        if (p) cudaFree(p);
-    }
-    template <typename T> T *as() const { return (T *)p; }
-};
 
 // ---- resident weights ------------------------------------------------------------------------------------------
 struct WeightH {

@@ -1,0 +1,170 @@
+// C ABI of the MoE layer and the routing hook (declared in include/faie2fn.h).
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "fn_engine.h"
+#include "fn_moe.h"
+
+namespace fn {
+
+struct MoeH {
+    MoePlan p;
+    DevBuf gate, up, down, sg, su, sd, act;
+    MoeWeights w;
+};
+static std::vector<MoeH *> g_moe;
+static std::mutex g_moe_mu;
+
+static MoeH *moe_get(int h) {
+    std::lock_guard<std::mutex> l(g_moe_mu);
+    return h >= 1 && h <= (int)g_moe.size() ? g_moe[h - 1] : nullptr;
+}
+
+// upload rows GGUF rows (row bytes rb) to a padded device buffer (stride ldw)
+static int upload_rows(DevBuf &b, const uint8_t *src, uint64_t rb, uint32_t ldw, size_t rows, cudaStream_t s) {
+    FN_CK(cudaMalloc(&b.p, (size_t)ldw * rows));
+    FN_CK(cudaMemcpy2DAsync(b.p, ldw, src, rb, rb, rows, cudaMemcpyHostToDevice, s));
+    return 0;
+}
+
+static MoeH *moe_build(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
+                       const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
+                       cudaStream_t s) {
+    MoeH *m = new MoeH();
+    if (!plan_moe(m->p, gu_type, down_type, ne, k, ffe, d)) {
+        delete m;
+        fail("moe: unsupported types/shape");
+        return nullptr;
+    }
+    const MoePlan &p = m->p;
+    if (upload_rows(m->gate, Wg, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, s) ||
+        upload_rows(m->up, Wu, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, s) ||
+        upload_rows(m->down, Wd, p.rb_down, p.ldw_down, (size_t)ne * d, s) ||
+        upload_rows(m->sg, Wsg, p.rb_gu, p.ldw_gu, ffe, s) || upload_rows(m->su, Wsu, p.rb_gu, p.ldw_gu, ffe, s) ||
+        upload_rows(m->sd, Wsd, p.rb_down, p.ldw_down, d, s) ||
+        cudaMalloc(&m->act.p, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess) {
+        delete m;
+        if (err().empty()) fail("moe: device allocation failed");
+        return nullptr;
+    }
+    m->w = MoeWeights{m->gate.as<uint8_t>(), m->up.as<uint8_t>(), m->down.as<uint8_t>(),
+                      m->sg.as<uint8_t>(), m->su.as<uint8_t>(), m->sd.as<uint8_t>()};
+    return m;
+}
+
+}  // namespace fn
+
+using namespace fn;
+
+// One MoE layer on host buffers: routed experts stacked by expert (gate/up ne * ffe GGUF rows of
+// d columns, down ne * d rows of ffe columns), shared expert (ffe / d rows), logits [nt][ne + 1] (column ne: the
+// shared-gate logit), x [nt][d] -> y [nt][d]; sel / wsel [nt][k] (nullable) receive the routing.
+FN_API int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, int nt, const uint8_t *Wg,
+                       const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
+                       const float *logits, const float *x, float *y, int *sel, float *wsel) {
+    if (nt < 1 || nt > 8) return fail("fn_test_moe: nt out of range (1..8)");
+    FN_CK(cudaSetDevice(hook_device()));
+    cudaStream_t s = hook_stream();
+    MoeH *m = moe_build(gu_type, down_type, ne, k, ffe, d, Wg, Wu, Wd, Wsg, Wsu, Wsd, s);
+    if (!m) return -1;
+    DevBuf lg, xd, yd, sd, wd;
+    int rc = 0;
+    if (cudaMalloc(&lg.p, (size_t)nt * (ne + 1) * 4) != cudaSuccess || cudaMalloc(&xd.p, (size_t)nt * d * 4) != cudaSuccess ||
+        cudaMalloc(&yd.p, (size_t)nt * d * 4) != cudaSuccess || cudaMalloc(&sd.p, (size_t)nt * k * 4) != cudaSuccess ||
+        cudaMalloc(&wd.p, (size_t)nt * k * 4) != cudaSuccess)
+        rc = fail("fn_test_moe: device allocation failed");
+    if (!rc && (cudaMemcpyAsync(lg.p, logits, (size_t)nt * (ne + 1) * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+                cudaMemcpyAsync(xd.p, x, (size_t)nt * d * 4, cudaMemcpyHostToDevice, s) != cudaSuccess))
+        rc = fail("fn_test_moe: copy failed");
+    if (!rc)
+        rc = launch_moe(m->p, m->w, lg.as<float>(), ne + 1, xd.as<float>(), m->act.as<float>(), yd.as<float>(), nt, false,
+                        sd.as<int>(), wd.as<float>(), s);
+    if (!rc) {
+        cudaMemcpyAsync(y, yd.p, (size_t)nt * d * 4, cudaMemcpyDeviceToHost, s);
+        if (sel) cudaMemcpyAsync(sel, sd.p, (size_t)nt * k * 4, cudaMemcpyDeviceToHost, s);
+        if (wsel) cudaMemcpyAsync(wsel, wd.p, (size_t)nt * k * 4, cudaMemcpyDeviceToHost, s);
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) rc = fail(std::string("fn_test_moe: ") + cudaGetErrorString(e));
+    }
+    cudaStreamSynchronize(s);
+    delete m;
+    if (rc) return rc;
+    return check_dev_error("fn_test_moe");
+}
+
+// Resident MoE weights on the current device (same arguments as fn_test_moe); returns a handle >= 1 or -1.
+FN_API int fn_moe_create(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
+                         const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd) {
+    MoeH *m = moe_build(gu_type, down_type, ne, k, ffe, d, Wg, Wu, Wd, Wsg, Wsu, Wsd, 0);
+    if (!m) return -1;
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        delete m;
+        return fail("fn_moe_create: upload failed");
+    }
+    std::lock_guard<std::mutex> l(g_moe_mu);
+    g_moe.push_back(m);
+    return (int)g_moe.size();
+}
+
+FN_API int fn_moe_free(int h) {
+    MoeH *m = moe_get(h);
+    if (!m) return fail("fn_moe_free: bad handle");
+    delete m;
+    std::lock_guard<std::mutex> l(g_moe_mu);
+    g_moe[h - 1] = nullptr;
+    return 0;
+}
+
+// Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d] (+= if acc).
+FN_API int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream) {
+    MoeH *m = moe_get(h);
+    if (!m) return fail("fn_moe_run: bad handle");
+    return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), y, nt, acc != 0, nullptr, nullptr,
+                      (cudaStream_t)stream);
+}
+
+// Routing on router outputs given as split-K partials part[ks][8][528] (the reference's router + shared-gate GEMV
+// output layout: 512 router rows, row stride 528): sel / wsel [nt][10] of nt <= 8 tokens and the time per call
+// (iters calls replayed as one CUDA graph). variant: 0 or 1, both the engine's routing. Replaces fn_bench_route
+// (engine/faie2fn.cu:2873-2912).
+FN_API int fn_bench_route(int variant, int nt, int ks, const float *parth, int iters, int *selh, float *wselh, float *ms) {
+    constexpr int NE = 512, NEU = 10, MAXT = 8, RSG = 528;
+    if (variant < 0 || variant > 1 || nt < 1 || nt > MAXT || ks < 1 || iters < 1) return fail("fn_bench_route: bad arguments");
+    FN_CK(cudaSetDevice(hook_device()));
+    cudaStream_t st = hook_stream();
+    DevBuf part, sel, w;
+    const size_t np = (size_t)ks * MAXT * RSG;
+    FN_CK(cudaMalloc(&part.p, np * 4));
+    FN_CK(cudaMalloc(&sel.p, MAXT * NEU * 4));
+    FN_CK(cudaMalloc(&w.p, MAXT * NEU * 4));
+    FN_CK(cudaMemcpyAsync(part.p, parth, np * 4, cudaMemcpyHostToDevice, st));
+    FN_CK(cudaStreamSynchronize(st));
+    cudaGraph_t g;
+    cudaGraphExec_t ge;
+    FN_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int rc = 0;
+    for (int i = 0; i < iters && !rc; ++i)
+        rc = launch_route(part.as<float>(), ks, (size_t)MAXT * RSG, RSG, NE, NEU, nt, sel.as<int>(), w.as<float>(), st);
+    cudaError_t ce = cudaStreamEndCapture(st, &g);
+    if (rc) return rc;
+    FN_CK(ce);
+    FN_CK(cudaGraphInstantiate(&ge, g, 0));
+    FN_CK(cudaGraphLaunch(ge, st));
+    cudaEvent_t a, b;
+    FN_CK(cudaEventCreate(&a));
+    FN_CK(cudaEventCreate(&b));
+    FN_CK(cudaEventRecord(a, st));
+    FN_CK(cudaGraphLaunch(ge, st));
+    FN_CK(cudaEventRecord(b, st));
+    FN_CK(cudaEventSynchronize(b));
+    FN_CK(cudaEventElapsedTime(ms, a, b));
+    *ms /= iters;
+    FN_CK(cudaMemcpy(selh, sel.p, (size_t)nt * NEU * 4, cudaMemcpyDeviceToHost));
+    FN_CK(cudaMemcpy(wselh, w.p, (size_t)nt * NEU * 4, cudaMemcpyDeviceToHost));
+    cudaGraphExecDestroy(ge);
+    cudaGraphDestroy(g);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return 0;
+}

@@ -52,6 +52,19 @@ struct Settings {
 };
 Settings &settings();
 int num_sms();
+int hook_device();           // device of the synchronous test / bench hooks
+cudaStream_t hook_stream();  // their stream (one non-blocking stream per device)
+
+// device buffer freed when the scope ends
+struct DevBuf {
+    void *p = nullptr;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    template <typename T> T *as() const { return (T *)p; }
+};
 
 // launch with the programmatic-serialization attribute when enabled
 template <typename... P, typename... A>

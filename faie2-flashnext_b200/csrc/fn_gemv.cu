@@ -14,22 +14,12 @@
 // in double in group order, and the row's lanes meet in a double butterfly; the row result is rounded to fp32 once.
 // A row never spans warps or CTAs, so there is no split-K scratch and no reduce kernel; the sum order is a function
 // of (format, cols) alone.
-#include "fn_decode.cuh"
 #include "fn_engine.h"
-#include "fn_grids.h"
+#include "fn_rowdot.cuh"
 
 #include <unordered_set>
 
 namespace fn {
-
-template <uint32_t TY> __device__ __forceinline__ const uint32_t *dev_grid() {
-    if constexpr (TY == T_IQ2_XXS) return kIq2xxsGrid;
-    else if constexpr (TY == T_IQ2_XS) return kIq2xsGrid;
-    else if constexpr (TY == T_IQ2_S) return kIq2sGrid;
-    else if constexpr (TY == T_IQ3_XXS) return kIq3xxsGrid;
-    else if constexpr (TY == T_IQ3_S) return kIq3sGrid;
-    else return nullptr;
-}
 
 struct GemvArgs {
     const uint8_t *W;
@@ -44,13 +34,6 @@ struct GemvArgs {
     int acc, early;
     uint32_t *err;
 };
-
-constexpr int XPAD = 36;  // floats per staged x group (32 + 4: lanes reading consecutive groups hit distinct banks)
-
-// Bounded wait on a stage barrier by every lane of a warp; the warp agrees on the outcome.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
-    return __all_sync(0xffffffffu, mbar_wait(bar, parity, 1u << 22));
-}
 
 template <uint32_t TY, int NT, int LPR, int GPL, bool XREG>
 __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
@@ -76,40 +59,19 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
         mbar_fence_init();
         for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
     }
-    if constexpr (Dec<TY>::gridw > 0) {
-        const uint32_t *gsrc = dev_grid<TY>();
-        for (int i = tid; i < Dec<TY>::gridw; i += blockDim.x) grid[i] = gsrc[i];
-    }
+    stage_grid<TY>(grid);
 
     if (!a.early) pdl_wait();
     const float *x = after_wait(a.x);
     const int nt = a.nt;
-    for (int idx = tid; idx < nt * G * 8; idx += blockDim.x) {
-        const int t = idx / (G * 8), r = idx - t * (G * 8), g = r >> 3, q = r & 7;
-        const float4 v = *(const float4 *)(x + (size_t)t * a.xs + g * 32 + 4 * q);
-        *(float4 *)(xsm + ((size_t)t * G + g) * XPAD + 4 * q) = v;
-    }
+    stage_x(xsm, x, a.xs, nt, G);
     __syncthreads();
     pdl_trigger();
 
     constexpr int RPW = 32 / LPR;  // rows a warp works on at once
     const int lr = lane % LPR, sub = lane / LPR;
-    const int gpl = GPL > 0 ? GPL : (G + LPR - 1) / LPR;
-    [[maybe_unused]] float xr[XREG ? (GPL > 0 ? GPL : 1) : 1][XREG ? 32 : 1];
-    if constexpr (XREG) {
-#pragma unroll
-        for (int i = 0; i < GPL; ++i) {
-            const float *src = xsm + (size_t)(lr + LPR * i) * XPAD;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 v = *(const float4 *)(src + j);
-                xr[i][j] = v.x;
-                xr[i][j + 1] = v.y;
-                xr[i][j + 2] = v.z;
-                xr[i][j + 3] = v.w;
-            }
-        }
-    }
+    XReg<LPR, (GPL > 0 ? GPL : 1)> xr;
+    if constexpr (XREG) xr.load(xsm, lr);
 
     int st = 0;
     for (; st < nst; ++st) {
@@ -122,45 +84,8 @@ __global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
             for (int base = warp * RPW; base < n; base += nw * RPW) {
                 const int row = base + sub;
                 const bool valid = row < n;
-                const uint8_t *rowp = sbuf + (size_t)row * a.ldw;
-                double acc[NT];  // group sums accumulate in double: one fp32 rounding per group, not per add
-#pragma unroll
-                for (int t = 0; t < NT; ++t) acc[t] = 0.0;
-                if (valid) {
-                    const int ni = GPL > 0 ? GPL : gpl;
-#pragma unroll
-                    for (int i = 0; i < ni; ++i) {
-                        const int g = lr + LPR * i;
-                        if (GPL == 0 && g >= G) break;
-                        float c[NT][4];
-#pragma unroll
-                        for (int t = 0; t < NT; ++t) c[t][0] = c[t][1] = c[t][2] = c[t][3] = 0.0f;
-                        Dec<TY>::group(rowp, g, grid, [&](int j, float v0, float v1, float v2, float v3) {
-#pragma unroll
-                            for (int t = 0; t < NT; ++t) {
-                                if (NT > 1 && t >= nt) break;
-                                float4 xv;
-                                if constexpr (XREG) {
-                                    xv = make_float4(xr[i][j], xr[i][j + 1], xr[i][j + 2], xr[i][j + 3]);
-                                } else {
-                                    xv = *(const float4 *)(xsm + ((size_t)t * G + g) * XPAD + j);
-                                }
-                                c[t][0] = __fmaf_rn(v0, xv.x, c[t][0]);
-                                c[t][1] = __fmaf_rn(v1, xv.y, c[t][1]);
-                                c[t][2] = __fmaf_rn(v2, xv.z, c[t][2]);
-                                c[t][3] = __fmaf_rn(v3, xv.w, c[t][3]);
-                            }
-                        });
-#pragma unroll
-                        for (int t = 0; t < NT; ++t)
-                            acc[t] += (double)__fadd_rn(__fadd_rn(c[t][0], c[t][1]), __fadd_rn(c[t][2], c[t][3]));
-                    }
-                }
-#pragma unroll
-                for (int t = 0; t < NT; ++t) {
-#pragma unroll
-                    for (int o = LPR / 2; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-                }
+                double acc[NT];
+                row_dot<TY, NT, LPR, GPL, XREG>(sbuf + (size_t)row * a.ldw, grid, xr, xsm, G, lr, nt, valid, acc);
                 if (valid && lr == 0) {
                     const int r = rr0 + row;
 #pragma unroll

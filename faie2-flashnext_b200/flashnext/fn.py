@@ -25,7 +25,8 @@ U8 = P(np.uint8, flags="C_CONTIGUOUS")
 EXPORTS = [
     "fn_error", "fn_set_device", "fn_pdl", "fn_early", "fn_bench_hot", "fn_gemv_override", "fn_gemv_waves",
     "fn_gemv_plan", "fn_test_dequant", "fn_test_gemv", "fn_bench_gemv", "fn_w_create", "fn_w_free", "fn_w_bytes",
-    "fn_w_gemv", "fn_w_gemv_host", "fn_sync",
+    "fn_w_gemv", "fn_w_gemv_host", "fn_sync", "fn_test_moe", "fn_moe_create", "fn_moe_free", "fn_moe_run",
+    "fn_bench_route",
 ]
 
 
@@ -53,6 +54,13 @@ class FN:
         d.fn_w_gemv.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
         d.fn_w_gemv_host.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
         d.fn_sync.argtypes = [C.c_void_p]
+        vp = C.c_void_p
+        d.fn_test_moe.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  U8, U8, U8, U8, U8, U8, F32, F32, F32, vp, vp]
+        d.fn_moe_create.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, U8, U8, U8, U8, U8, U8]
+        d.fn_moe_free.argtypes = [C.c_int]
+        d.fn_moe_run.argtypes = [C.c_int, vp, C.c_int, vp, vp, C.c_int, C.c_int, vp]
+        d.fn_bench_route.argtypes = [C.c_int, C.c_int, C.c_int, F32, C.c_int, I32, F32, C.POINTER(C.c_float)]
 
     def check(self, rc):
         if rc != 0:
@@ -108,3 +116,41 @@ class FN:
 
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))
+
+    # ---- MoE layer (routing + routed experts + shared expert) ----
+    def moe(self, gu_type, down_type, ne, k, ffe, d, Wg, Wu, Wd, Wsg, Wsu, Wsd, logits, x):
+        """y [nt][d], sel [nt][k], w [nt][k] of one MoE layer (weights: expert-stacked GGUF rows)."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, d)
+        nt = x.shape[0]
+        logits = np.ascontiguousarray(logits, np.float32).reshape(nt, ne + 1)
+        y = np.zeros((nt, d), np.float32)
+        sel = np.zeros((nt, k), np.int32)
+        w = np.zeros((nt, k), np.float32)
+        u8 = lambda a: np.ascontiguousarray(a, np.uint8).reshape(-1)  # noqa: E731
+        self.check(self.d.fn_test_moe(int(gu_type), int(down_type), ne, k, ffe, d, nt, u8(Wg), u8(Wu), u8(Wd), u8(Wsg),
+                                      u8(Wsu), u8(Wsd), logits, x, y, sel.ctypes.data, w.ctypes.data))
+        return y, sel, w
+
+    def moe_create(self, gu_type, down_type, ne, k, ffe, d, Wg, Wu, Wd, Wsg, Wsu, Wsd) -> int:
+        u8 = lambda a: np.ascontiguousarray(a, np.uint8).reshape(-1)  # noqa: E731
+        h = self.d.fn_moe_create(int(gu_type), int(down_type), ne, k, ffe, d, u8(Wg), u8(Wu), u8(Wd), u8(Wsg), u8(Wsu),
+                                 u8(Wsd))
+        if h < 0:
+            raise RuntimeError(self.d.fn_error().decode())
+        return h
+
+    def moe_free(self, h):
+        self.check(self.d.fn_moe_free(h))
+
+    def moe_run(self, h, logits_ptr, ls, x_ptr, y_ptr, nt=1, acc=0, stream=0):
+        self.check(self.d.fn_moe_run(h, C.c_void_p(logits_ptr), ls, C.c_void_p(x_ptr), C.c_void_p(y_ptr), nt, acc,
+                                     C.c_void_p(stream)))
+
+    def bench_route(self, variant, part, nt, ks, iters=1):
+        """flashnext/route_fn.py:20-25: routing of split-K router partials part[ks][8][528]."""
+        sel = np.zeros(nt * 10, np.int32)
+        w = np.zeros(nt * 10, np.float32)
+        ms = C.c_float()
+        self.check(self.d.fn_bench_route(variant, nt, ks, np.ascontiguousarray(part, np.float32).reshape(-1), iters, sel,
+                                         w, C.byref(ms)))
+        return sel, w, ms.value

@@ -74,6 +74,28 @@ int fn_w_gemv_host(int h, const float *x, int nt, float *y, void *stream);
 /* Synchronise a stream and report any device-side error (a bounded wait that ran out). */
 int fn_sync(void *stream);
 
+/* ---- MoE layer ------------------------------------------------------------------------ */
+
+/* One MoE layer on host buffers: y[t] = sum_{s<k} w[t][s] down_e . (silu(gate_e . x[t]) * (up_e . x[t])) with
+ * (sel, w) the top-k routing of logits[t][0..ne) (probability descending, ties to the lower index, renormalised),
+ * plus sigmoid(logits[t][ne]) times the shared expert. Routed weights are expert-stacked GGUF rows (gate/up:
+ * ne * ffe rows of d columns; down: ne * d rows of ffe columns); shared: ffe (gate/up) and d (down) rows in the same
+ * formats. nt <= 8. sel / wsel ([nt][k] int32 / fp32) may be NULL. New hook with the conventions of fn_test_gemv;
+ * replaces the per-layer MoE of layer_forward (engine/faie2fn.cu:2406-2420: k_route, moe_gu, moe_down, k_hc_add). */
+int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, int nt, const uint8_t *Wg,
+                const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
+                const float *logits, const float *x, float *y, int *sel, float *wsel);
+/* Resident MoE weights on the current device (arguments as fn_test_moe); a handle >= 1 or -1. Replaces the expert
+ * loads of fn_load (engine/faie2fn.cu:2651-2668). */
+int fn_moe_create(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
+                  const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd);
+int fn_moe_free(int h);
+/* Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d] (+= if acc). */
+int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream);
+/* Routing of router outputs given as split-K partials part[ks][8][528] (512 experts, top 10): sel / wsel [nt][10],
+ * ms per call over iters graph-replayed calls. Replaces fn_bench_route (engine/faie2fn.cu:2873-2912). */
+int fn_bench_route(int variant, int nt, int ks, const float *part, int iters, int *sel, float *wsel, float *ms);
+
 #ifdef __cplusplus
 }
 #endif
