@@ -168,3 +168,51 @@ FN_API int fn_bench_route(int variant, int nt, int ks, const float *parth, int i
     cudaEventDestroy(b);
     return 0;
 }
+
+// ---- the MoE layer without any allocation --------------------------------------------------------------------------
+//
+// Some callers cannot call cudaMalloc: a host that owns all device memory through its own pool (an inference server,
+// a framework allocator) and forbids raw allocations, or code that must not pay the implicit device-wide
+// synchronisation cudaFree performs in the middle of a decode loop. fn_moe_layer_static takes every input and output
+// as a device pointer the caller already owns and keeps its only scratch, the activations passed from the gate/up
+// kernel to the down kernel, in a fixed array of device memory that is part of the library image.
+//
+// Limit: nt * (k + 1) * ffe <= FN_MOE_STATIC_ACT_FLOATS (65536 floats, 256 KiB); larger calls are rejected. Every GPU
+// that loads the library holds the array until the process exits. All calls share it, so calls whose kernels overlap
+// on the GPU (two streams, or two host threads) race on it: issue them in one stream. Nothing in it needs to start at
+// zero (the gate/up kernel writes every element the down kernel reads). The first call on a device resolves the
+// array's device address on that device (cudaGetSymbolAddress); make that first call outside stream capture.
+
+namespace fn {
+constexpr size_t kMoeStaticActFloats = 65536;
+static __device__ __align__(256) float g_moe_static_act[kMoeStaticActFloats];
+static float *g_moe_static_act_dev[64] = {};  // device address of g_moe_static_act, per device
+}  // namespace fn
+
+FN_API int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
+                               const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu,
+                               const uint8_t *Wsd, const float *logits, int ls, const float *x, float *y, int nt,
+                               void *stream) {
+    MoePlan p;
+    if (!plan_moe(p, gu_type, down_type, ne, k, ffe, d)) return fail("fn_moe_layer_static: unsupported types/shape");
+    if (nt < 1 || nt > 8) return fail("fn_moe_layer_static: nt out of range (1..8)");
+    const size_t need = (size_t)nt * (k + 1) * ffe;
+    if (need > kMoeStaticActFloats)
+        return fail("fn_moe_layer_static: nt * (k + 1) * ffe = " + std::to_string(need) +
+                    " floats exceeds the static scratch of " + std::to_string(kMoeStaticActFloats) + " floats");
+    const uint8_t *ws[6] = {Wg, Wu, Wd, Wsg, Wsu, Wsd};
+    for (const uint8_t *w : ws)
+        if (!w || ((uintptr_t)w & 15)) return fail("fn_moe_layer_static: weight pointers must be 16-byte aligned");
+    int dev = 0;
+    FN_CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail("fn_moe_layer_static: device index out of range");
+    if (!g_moe_static_act_dev[dev]) {
+        void *ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_moe_static_act);
+        if (e != cudaSuccess) return fail(std::string("fn_moe_layer_static: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_moe_static_act_dev[dev] = (float *)ptr;
+    }
+    const MoeWeights w{Wg, Wu, Wd, Wsg, Wsu, Wsd};
+    return launch_moe(p, w, logits, ls, x, g_moe_static_act_dev[dev], y, nt, false, nullptr, nullptr,
+                      (cudaStream_t)stream);
+}

@@ -26,7 +26,7 @@ EXPORTS = [
     "fn_error", "fn_set_device", "fn_pdl", "fn_early", "fn_bench_hot", "fn_gemv_override", "fn_gemv_waves",
     "fn_gemv_plan", "fn_test_dequant", "fn_test_gemv", "fn_bench_gemv", "fn_w_create", "fn_w_free", "fn_w_bytes",
     "fn_w_gemv", "fn_w_gemv_host", "fn_sync", "fn_test_moe", "fn_moe_create", "fn_moe_free", "fn_moe_run",
-    "fn_bench_route",
+    "fn_bench_route", "fn_moe_layer_static",
 ]
 
 
@@ -61,6 +61,8 @@ class FN:
         d.fn_moe_free.argtypes = [C.c_int]
         d.fn_moe_run.argtypes = [C.c_int, vp, C.c_int, vp, vp, C.c_int, C.c_int, vp]
         d.fn_bench_route.argtypes = [C.c_int, C.c_int, C.c_int, F32, C.c_int, I32, F32, C.POINTER(C.c_float)]
+        d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
+                                          vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
     def check(self, rc):
         if rc != 0:
@@ -154,3 +156,10 @@ class FN:
         self.check(self.d.fn_bench_route(variant, nt, ks, np.ascontiguousarray(part, np.float32).reshape(-1), iters, sel,
                                          w, C.byref(ms)))
         return sel, w, ms.value
+
+    def moe_layer_static(self, gu_type, down_type, ne, k, ffe, d, w_ptrs, logits_ptr, ls, x_ptr, y_ptr, nt=1, stream=0):
+        """The allocation-free MoE layer: every argument a device pointer the caller owns (w_ptrs: gate, up, down,
+        shared gate, shared up, shared down)."""
+        vp = C.c_void_p
+        self.check(self.d.fn_moe_layer_static(int(gu_type), int(down_type), ne, k, ffe, d, *[vp(p) for p in w_ptrs],
+                                              vp(logits_ptr), ls, vp(x_ptr), vp(y_ptr), nt, vp(stream)))

@@ -96,6 +96,17 @@ int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int
  * ms per call over iters graph-replayed calls. Replaces fn_bench_route (engine/faie2fn.cu:2873-2912). */
 int fn_bench_route(int variant, int nt, int ks, const float *part, int iters, int *sel, float *wsel, float *ms);
 
+/* The MoE layer of fn_moe_run for callers that cannot allocate device memory (a host whose memory is all owned by
+ * its own pool, or a decode loop that must not pay cudaFree's device synchronisation). No counterpart in the
+ * reference. Everything is a device pointer the caller owns: weights as in fn_test_moe, rows at a stride of
+ * row_bytes rounded up to 16, 16-byte aligned; logits [nt][ls] (ls >= ne + 1); x, y [nt][d]. The only scratch (the
+ * gate/up -> down activations) is a static 256 KiB device array inside the library: nt * (k + 1) * ffe <= 65536,
+ * larger calls fail. All calls share that array, so calls that overlap on the GPU race; keep them in one stream. The
+ * first call on a device resolves the array's address there; make it outside stream capture. Allocates nothing. */
+int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
+                        const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
+                        const float *logits, int ls, const float *x, float *y, int nt, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
