@@ -1,0 +1,218 @@
+// Gated-DeltaNet decode core on B200 (sm_100a): conv + silu + l2norm + gates + delta rule + gated RMSNorm for nt
+// tokens of one layer, in one kernel (16 key heads, 32 value heads, head dim 128).
+//
+// Reference behaviour: k_gdn (engine/faie2fn.cu:1349-1431); value head h reads key head h % NKH (GGUF tiled order,
+// :10-11, 1374); the norm is gated with sigmoid(z) (:1424); softplus(u) = u for u > 20 (:1411).
+//
+// B200 design: CTA h (one per value head) has 512 threads; thread (j, c) = (tid >> 2, tid & 3) owns state column j,
+// key rows [32c, 32c + 32), i.e. 32 fp32 values of S[h] held in registers across all tokens of the launch. The four
+// quarter-column partial dot products (S^T k, S^T q) meet by two xor shuffles inside a warp, in a fixed order. When
+// the caller says the state was complete before the previous kernel started (in a decode step the layer's previous
+// GDN launch is several kernels back), the state is loaded BEFORE griddepcontrol.wait, so under programmatic
+// dependent launch its HBM read overlaps the projection GEMVs before this kernel; back-to-back launches of one layer
+// load it after the wait. The step's own inputs (qkv, z, ab) are always read after the wait.
+// Conv state: the value channels keep [3][NVH*DS]; every value head keeps its own copy of its key head's q/k conv
+// state ([NVH][3][2][DS]): the value heads sharing a key head would otherwise race on it (one reading the old state
+// while another writes the new one); the copies stay equal.
+#include "fn_engine.h"
+#include "fn_gdn.h"
+
+namespace fn {
+
+constexpr int GDN_DS = 128;
+constexpr int GDN_THREADS = 4 * GDN_DS;
+constexpr int KPAD = 36;  // floats per 32-row chunk of the staged q / k (32 + 4: chunk c at bank offset 4c)
+
+struct GdnArgs {
+    const float *qkv;  // [nt][qs]: q (nkh*ds) | k (nkh*ds) | v (nvh*ds)
+    int qs;
+    const float *z;  // [nt][zs]
+    int zs;
+    const float *ab;  // [nt][abs_]: alpha (nvh) | beta (nvh)
+    int abs_;
+    const float4 *conv_w;  // [convch] taps (oldest .. current)
+    const float *dt_bias, *ssm_a, *norm_w;
+    float *S;       // [nvh][ds][ds]
+    float *cst_v;   // [3][nvh*ds]
+    float *cst_qk;  // [nvh][3][2][ds]
+    float *out;     // [nt][os]
+    int os;
+    int nkh, nvh, nt;
+    int prefetch;  // 1: the state was complete before the previous kernel started, so it is read before the wait
+};
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
+    constexpr int DS = GDN_DS;
+    __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[DS];
+    __shared__ float red_q[4], red_k[4], red_o[16];
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int j = tid >> 2, c = tid & 3;
+    const int kh = h % a.nkh, nvd = a.nvh * DS;
+    // conv roles: threads 0..127 q channel d, 128..255 k channel d, 256..383 v channel d (of this value head)
+    const int role = tid >> 7, d = tid & 127;
+    int ch = -1;
+    float *stp = nullptr;
+    int sst = 0;  // state stride between the 3 history slots
+    if (role == 0) {
+        ch = kh * DS + d;
+        stp = a.cst_qk + (size_t)h * 3 * 2 * DS + d;
+        sst = 2 * DS;
+    } else if (role == 1) {
+        ch = a.nkh * DS + kh * DS + d;
+        stp = a.cst_qk + (size_t)h * 3 * 2 * DS + DS + d;
+        sst = 2 * DS;
+    } else if (role == 2) {
+        ch = 2 * a.nkh * DS + h * DS + d;
+        stp = a.cst_v + (size_t)h * DS + d;
+        sst = nvd;
+    }
+    // ---- state, conv state, parameters: read before griddepcontrol.wait when the state was complete before the
+    // previous kernel started (prefetch), else after it (the previous kernel may be this layer's previous step)
+    float s[32];
+    float *Sh = a.S + (size_t)h * DS * DS;
+    float h0 = 0.f, h1 = 0.f, h2 = 0.f;
+    float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto load_state = [&]() {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = Sh[(size_t)(32 * c + i) * DS + j];
+        if (ch >= 0) {
+            h0 = stp[0];
+            h1 = stp[sst];
+            h2 = stp[2 * sst];
+        }
+    };
+    if (a.prefetch) load_state();
+    if (ch >= 0) w = a.conv_w[ch];
+    const float nwj = a.norm_w[j], dtb = a.dt_bias[h], sa = a.ssm_a[h];
+    pdl_wait();
+    if (!a.prefetch) {
+        Sh = after_wait(Sh);
+        if (stp) stp = after_wait(stp);
+        load_state();
+    }
+    const float *qkv = after_wait(a.qkv);
+    const float *zp = after_wait(a.z);
+    const float *abp = after_wait(a.ab);
+    pdl_trigger();
+
+    for (int t = 0; t < a.nt; ++t) {
+        // conv + silu of this thread's channel; history shifts
+        float y = 0.f;
+        if (ch >= 0) {
+            const float x = qkv[(size_t)t * a.qs + ch];
+            y = silu(__fmaf_rn(w.w, x, __fmaf_rn(w.z, h2, __fmaf_rn(w.y, h1, __fmul_rn(w.x, h0)))));
+            h0 = h1;
+            h1 = h2;
+            h2 = x;
+        }
+        // l2 norms of q (threads 0..127) and k (128..255): warp sums, then the 4 partials in order
+        const float sq = warp_sum_f(y * y);
+        if (lane == 0) {
+            if (role == 0) red_q[warp] = sq;
+            else if (role == 1) red_k[warp - 4] = sq;
+        }
+        if (role == 2) vs[d] = y;
+        __syncthreads();
+        if (role <= 1) {
+            const float* r = role == 0 ? red_q : red_k;
+            const float inv = rsqrtf(((r[0] + r[1]) + (r[2] + r[3])) + 1e-6f);
+            float *dst = role == 0 ? qn : kn;
+            dst[(d >> 5) * KPAD + (d & 31)] = y * inv;
+        }
+        // gates of this value head
+        const float beta = sigm(abp[(size_t)t * a.abs_ + a.nvh + h]);
+        const float u = abp[(size_t)t * a.abs_ + h] + dtb;
+        const float sp = u > 20.0f ? u : log1pf(expf(u));
+        const float decay = expf(sp * sa);
+        __syncthreads();
+        // kv_j = sum_i S[i][j] k_i over this thread's quarter, then the 4 quarters
+        const float *kq = kn + c * KPAD, *qq = qn + c * KPAD;
+        float kv = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 kk = *(const float4 *)(kq + i);
+            kv = __fmaf_rn(s[i], kk.x, kv);
+            kv = __fmaf_rn(s[i + 1], kk.y, kv);
+            kv = __fmaf_rn(s[i + 2], kk.z, kv);
+            kv = __fmaf_rn(s[i + 3], kk.w, kv);
+        }
+        kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+        kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+        const float delta = __fmul_rn(__fmaf_rn(-decay, kv, vs[j]), beta);
+        float o = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 kk = *(const float4 *)(kq + i), q4 = *(const float4 *)(qq + i);
+            s[i] = __fmaf_rn(decay, s[i], __fmul_rn(kk.x, delta));
+            s[i + 1] = __fmaf_rn(decay, s[i + 1], __fmul_rn(kk.y, delta));
+            s[i + 2] = __fmaf_rn(decay, s[i + 2], __fmul_rn(kk.z, delta));
+            s[i + 3] = __fmaf_rn(decay, s[i + 3], __fmul_rn(kk.w, delta));
+            o = __fmaf_rn(s[i], q4.x, o);
+            o = __fmaf_rn(s[i + 1], q4.y, o);
+            o = __fmaf_rn(s[i + 2], q4.z, o);
+            o = __fmaf_rn(s[i + 3], q4.w, o);
+        }
+        o += __shfl_xor_sync(0xffffffffu, o, 1);
+        o += __shfl_xor_sync(0xffffffffu, o, 2);
+        o *= 0.08838834764831845f;  // 1 / sqrt(128)
+        // gated RMSNorm over the head's 128 columns (one value per column: lanes with c == 0)
+        const float oo = warp_sum_f(c == 0 ? o * o : 0.f);
+        if (lane == 0) red_o[warp] = oo;
+        __syncthreads();
+        if (c == 0) {
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss += red_o[i];
+            const float r = rsqrtf(ss / DS + 1e-6f);
+            const size_t oi = (size_t)h * DS + j;
+            a.out[(size_t)t * a.os + oi] = o * r * nwj * sigm(zp[(size_t)t * a.zs + oi]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) Sh[(size_t)(32 * c + i) * DS + j] = s[i];
+    if (ch >= 0) {
+        stp[0] = h0;
+        stp[sst] = h1;
+        stp[2 * sst] = h2;
+    }
+}
+
+int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs, const float *z, int zs, const float *ab,
+               int abs_, float *out, int os, int nt, bool prefetch_state, cudaStream_t s) {
+    if (p.ds != GDN_DS) return fail("gdn: head dim must be 128");
+    if (p.nkh < 1 || p.nvh < 1 || p.nvh % p.nkh) return fail("gdn: value heads must be a multiple of key heads");
+    if (nt < 1) return fail("gdn: nt < 1");
+    if (((uintptr_t)p.conv_w & 15)) return fail("gdn: conv weights must be 16-byte aligned");
+    GdnArgs a;
+    a.qkv = qkv;
+    a.qs = qs;
+    a.z = z;
+    a.zs = zs;
+    a.ab = ab;
+    a.abs_ = abs_;
+    a.conv_w = (const float4 *)p.conv_w;
+    a.dt_bias = p.dt_bias;
+    a.ssm_a = p.ssm_a;
+    a.norm_w = p.norm_w;
+    a.S = st.S;
+    a.cst_v = st.conv_v;
+    a.cst_qk = st.conv_qk;
+    a.out = out;
+    a.os = os;
+    a.nkh = p.nkh;
+    a.nvh = p.nvh;
+    a.nt = nt;
+    a.prefetch = prefetch_state ? 1 : 0;
+    const cudaError_t e = launch_k(k_gdn, dim3(p.nvh), dim3(GDN_THREADS), 0, s, a);
+    if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
+    return 0;
+}
+
+}  // namespace fn

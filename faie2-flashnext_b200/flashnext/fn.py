@@ -26,7 +26,8 @@ EXPORTS = [
     "fn_error", "fn_set_device", "fn_pdl", "fn_early", "fn_bench_hot", "fn_gemv_override", "fn_gemv_waves",
     "fn_gemv_plan", "fn_test_dequant", "fn_test_gemv", "fn_bench_gemv", "fn_w_create", "fn_w_free", "fn_w_bytes",
     "fn_w_gemv", "fn_w_gemv_host", "fn_sync", "fn_test_moe", "fn_moe_create", "fn_moe_free", "fn_moe_run",
-    "fn_bench_route", "fn_moe_layer_static",
+    "fn_bench_route", "fn_moe_layer_static", "fn_test_gdn", "fn_gdn_create", "fn_gdn_free", "fn_gdn_run",
+    "fn_gdn_get_state",
 ]
 
 
@@ -61,6 +62,11 @@ class FN:
         d.fn_moe_free.argtypes = [C.c_int]
         d.fn_moe_run.argtypes = [C.c_int, vp, C.c_int, vp, vp, C.c_int, C.c_int, vp]
         d.fn_bench_route.argtypes = [C.c_int, C.c_int, C.c_int, F32, C.c_int, I32, F32, C.POINTER(C.c_float)]
+        d.fn_test_gdn.argtypes = [C.c_int] * 5 + [F32] * 7 + [F32, F32, F32]
+        d.fn_gdn_create.argtypes = [C.c_int, C.c_int, C.c_int] + [F32] * 6
+        d.fn_gdn_free.argtypes = [C.c_int]
+        d.fn_gdn_run.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp]
+        d.fn_gdn_get_state.argtypes = [C.c_int, vp, vp]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -163,3 +169,36 @@ class FN:
         vp = C.c_void_p
         self.check(self.d.fn_moe_layer_static(int(gu_type), int(down_type), ne, k, ffe, d, *[vp(p) for p in w_ptrs],
                                               vp(logits_ptr), ls, vp(x_ptr), vp(y_ptr), nt, vp(stream)))
+
+    # ---- gated-DeltaNet core ----
+    def gdn(self, nkh, nvh, qkv, z, ab, conv_w, dt_bias, ssm_a, norm_w, S, conv_state, tokens_per_launch=1, ds=128):
+        """nt tokens of the DeltaNet core; returns out [nt][nvh*ds], S and conv_state after the last token."""
+        f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+        qkv, z, ab = f(qkv), f(z), f(ab)
+        nt = qkv.shape[0]
+        S, cs = f(S).copy(), f(conv_state).copy()
+        out = np.zeros((nt, nvh * ds), np.float32)
+        self.check(self.d.fn_test_gdn(nkh, nvh, ds, nt, tokens_per_launch, qkv, z, ab, f(conv_w), f(dt_bias), f(ssm_a),
+                                      f(norm_w), S, cs, out))
+        return out, S, cs
+
+    def gdn_create(self, nkh, nvh, conv_w, dt_bias, ssm_a, norm_w, S0, conv0, ds=128) -> int:
+        f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+        h = self.d.fn_gdn_create(nkh, nvh, ds, f(conv_w), f(dt_bias), f(ssm_a), f(norm_w), f(S0), f(conv0))
+        if h < 0:
+            raise RuntimeError(self.d.fn_error().decode())
+        return h
+
+    def gdn_free(self, h):
+        self.check(self.d.fn_gdn_free(h))
+
+    def gdn_run(self, h, qkv_ptr, qs, z_ptr, zs, ab_ptr, abs_, out_ptr, os_, nt=1, prefetch_state=0, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_gdn_run(h, vp(qkv_ptr), qs, vp(z_ptr), zs, vp(ab_ptr), abs_, vp(out_ptr), os_, nt,
+                                     prefetch_state, vp(stream)))
+
+    def gdn_state(self, h, nkh, nvh, ds=128):
+        S = np.zeros((nvh, ds, ds), np.float32)
+        cs = np.zeros((3, 2 * nkh * ds + nvh * ds), np.float32)
+        self.check(self.d.fn_gdn_get_state(h, S.ctypes.data, cs.ctypes.data))
+        return S, cs

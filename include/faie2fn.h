@@ -96,6 +96,32 @@ int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int
  * ms per call over iters graph-replayed calls. Replaces fn_bench_route (engine/faie2fn.cu:2873-2912). */
 int fn_bench_route(int variant, int nt, int ks, const float *part, int iters, int *sel, float *wsel, float *ms);
 
+/* ---- gated-DeltaNet core ------------------------------------------------------------- */
+
+/* nt tokens of one DeltaNet layer's core on host buffers, tokens_per_launch tokens per kernel launch (1 = decode):
+ * conv (kernel 4) + silu, l2norm of q and k, beta = sigmoid(b), decay = exp(ssm_a * softplus(a + dt_bias)), the delta
+ * rule S = decay S + k ((v - decay S^T k) beta)^T, o = S^T q / sqrt(ds), out = o rsqrt(mean o^2 + 1e-6) norm_w
+ * sigmoid(z); value head h reads key head h % nkh. qkv [nt][2 nkh ds + nvh ds] (q | k | v), z [nt][nvh ds], ab
+ * [nt][2 nvh] (alpha | beta), conv_w [convch][4] (oldest input first), dt_bias, ssm_a [nvh], norm_w [ds]; S
+ * [nvh][ds][ds] and conv_state [3][convch] are read and updated in place; out [nt][nvh ds]. ds must be 128.
+ * Replaces k_gdn's per-layer use (engine/faie2fn.cu:1349-1431, 2386-2389) as a model-free hook. */
+int fn_test_gdn(int nkh, int nvh, int ds, int nt, int tokens_per_launch, const float *qkv, const float *z,
+                const float *ab, const float *conv_w, const float *dt_bias, const float *ssm_a, const float *norm_w,
+                float *S, float *conv_state, float *out);
+/* Resident DeltaNet state + parameters on the current device (arguments as fn_test_gdn; S0, conv0 initial state);
+ * a handle >= 1 or -1. Replaces the DeltaNet loads and state of fn_load / fn_reset (engine/faie2fn.cu:2617-2640,
+ * 2703-2717). */
+int fn_gdn_create(int nkh, int nvh, int ds, const float *conv_w, const float *dt_bias, const float *ssm_a,
+                  const float *norm_w, const float *S0, const float *conv0);
+int fn_gdn_free(int h);
+/* Launch nt tokens on device pointers (token strides qs, zs, abs_, os in floats); the handle's state advances.
+ * prefetch_state = 1 only when this handle's previous launch is two or more kernels back in the stream (the state is
+ * then read while the kernel before runs, under programmatic dependent launch); 0 for back-to-back launches. */
+int fn_gdn_run(int h, const float *qkv, int qs, const float *z, int zs, const float *ab, int abs_, float *out, int os,
+               int nt, int prefetch_state, void *stream);
+/* Copy the state to host (S [nvh][ds][ds], conv [3][convch]; either may be NULL); synchronises the device. */
+int fn_gdn_get_state(int h, float *S, float *conv);
+
 /* The MoE layer of fn_moe_run for callers that cannot allocate device memory (a host whose memory is all owned by
  * its own pool, or a decode loop that must not pay cudaFree's device synchronisation). No counterpart in the
  * reference. Everything is a device pointer the caller owns: weights as in fn_test_moe, rows at a stride of
