@@ -117,7 +117,7 @@ FN_API void fn_bench_hot(int on) { settings().bench_hot = on; }
 // GEMV plan overrides for sweeps: warps per CTA, ring KiB, stage KiB, CTAs per SM (0 = keep)
 FN_API void fn_gemv_override(int warps, int ring_kb, int stage_kb, int ctas_per_sm) {
     Settings &s = settings();
-    if (warps > 0) s.warps_per_cta = warps;
+    if (warps >= 0) s.warps_per_cta = warps;  // 0: automatic
     if (ring_kb > 0) s.ring_kb = ring_kb;
     if (stage_kb > 0) s.stage_kb = stage_kb;
     if (ctas_per_sm > 0) s.ctas_per_sm = ctas_per_sm;
@@ -161,10 +161,13 @@ FN_API int fn_test_gemv(uint32_t type, const uint8_t *Wh, int rows, int cols, co
     if (!plan_gemv(p, type, rows, cols, nt == 1 ? 1 : 8)) return fail("unsupported type/shape");
     cudaStream_t s = hook_stream();
     DevBuf W, x, y;
+    DevBuf raw;
     FN_CK(cudaMalloc(&W.p, plan_weight_bytes(p)));
+    FN_CK(cudaMalloc(&raw.p, (size_t)p.rb * rows));
     FN_CK(cudaMalloc(&x.p, (size_t)nt * cols * 4));
     FN_CK(cudaMalloc(&y.p, (size_t)nt * rows * 4));
-    FN_CK(cudaMemcpy2DAsync(W.p, p.ldw, Wh, p.rb, p.rb, rows, cudaMemcpyHostToDevice, s));
+    FN_CK(cudaMemcpyAsync(raw.p, Wh, (size_t)p.rb * rows, cudaMemcpyHostToDevice, s));
+    if (launch_plane_repack(type, raw.as<uint8_t>(), p.rb, W.as<uint8_t>(), p.ldw, rows, cols, s)) return -1;
     FN_CK(cudaMemcpyAsync(x.p, xh, (size_t)nt * cols * 4, cudaMemcpyHostToDevice, s));
     if (launch_gemv(p, W.as<uint8_t>(), x.as<float>(), cols, y.as<float>(), rows, nt, false, false, s)) return -1;
     FN_CK(cudaMemcpyAsync(yh, y.p, (size_t)nt * rows * 4, cudaMemcpyDeviceToHost, s));
@@ -239,8 +242,11 @@ FN_API int fn_w_create(uint32_t type, const uint8_t *Wh, int rows, int cols) {
     }
     cudaGetDevice(&w->dev);
     const GemvPlan &p = w->plan1;
-    if (cudaMalloc(&w->d, plan_weight_bytes(p)) != cudaSuccess ||
-        cudaMemcpy2D(w->d, p.ldw, Wh, p.rb, p.rb, rows, cudaMemcpyHostToDevice) != cudaSuccess ||
+    DevBuf raw;
+    if (cudaMalloc(&w->d, plan_weight_bytes(p)) != cudaSuccess || cudaMalloc(&raw.p, (size_t)p.rb * rows) != cudaSuccess ||
+        cudaMemcpy(raw.p, Wh, (size_t)p.rb * rows, cudaMemcpyHostToDevice) != cudaSuccess ||
+        launch_plane_repack(type, raw.as<uint8_t>(), p.rb, w->d, p.ldw, rows, cols, 0) != 0 ||
+        cudaDeviceSynchronize() != cudaSuccess ||
         cudaMalloc(&w->xbuf, (size_t)8 * cols * 4) != cudaSuccess || cudaMalloc(&w->ybuf, (size_t)8 * rows * 4) != cudaSuccess) {
         cudaFree(w->d);
         cudaFree(w->xbuf);

@@ -21,10 +21,15 @@ static MoeH *moe_get(int h) {
     return h >= 1 && h <= (int)g_moe.size() ? g_moe[h - 1] : nullptr;
 }
 
-// upload rows GGUF rows (row bytes rb) to a padded device buffer (stride ldw)
-static int upload_rows(DevBuf &b, const uint8_t *src, uint64_t rb, uint32_t ldw, size_t rows, cudaStream_t s) {
+// upload GGUF rows (row bytes rb) to a device buffer in the engine's layout (planes, stride ldw)
+static int upload_rows(DevBuf &b, uint32_t type, const uint8_t *src, uint64_t rb, uint32_t ldw, size_t rows, int cols,
+                       cudaStream_t s) {
+    DevBuf raw;
     FN_CK(cudaMalloc(&b.p, (size_t)ldw * rows));
-    FN_CK(cudaMemcpy2DAsync(b.p, ldw, src, rb, rb, rows, cudaMemcpyHostToDevice, s));
+    FN_CK(cudaMalloc(&raw.p, (size_t)rb * rows));
+    FN_CK(cudaMemcpyAsync(raw.p, src, (size_t)rb * rows, cudaMemcpyHostToDevice, s));
+    if (launch_plane_repack(type, raw.as<uint8_t>(), rb, b.as<uint8_t>(), ldw, (int)rows, cols, s)) return -1;
+    FN_CK(cudaStreamSynchronize(s));
     return 0;
 }
 
@@ -38,11 +43,12 @@ static MoeH *moe_build(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
         return nullptr;
     }
     const MoePlan &p = m->p;
-    if (upload_rows(m->gate, Wg, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, s) ||
-        upload_rows(m->up, Wu, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, s) ||
-        upload_rows(m->down, Wd, p.rb_down, p.ldw_down, (size_t)ne * d, s) ||
-        upload_rows(m->sg, Wsg, p.rb_gu, p.ldw_gu, ffe, s) || upload_rows(m->su, Wsu, p.rb_gu, p.ldw_gu, ffe, s) ||
-        upload_rows(m->sd, Wsd, p.rb_down, p.ldw_down, d, s) ||
+    if (upload_rows(m->gate, gu_type, Wg, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, d, s) ||
+        upload_rows(m->up, gu_type, Wu, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, d, s) ||
+        upload_rows(m->down, down_type, Wd, p.rb_down, p.ldw_down, (size_t)ne * d, ffe, s) ||
+        upload_rows(m->sg, gu_type, Wsg, p.rb_gu, p.ldw_gu, ffe, d, s) ||
+        upload_rows(m->su, gu_type, Wsu, p.rb_gu, p.ldw_gu, ffe, d, s) ||
+        upload_rows(m->sd, down_type, Wsd, p.rb_down, p.ldw_down, d, ffe, s) ||
         cudaMalloc(&m->act.p, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess) {
         delete m;
         if (err().empty()) fail("moe: device allocation failed");
@@ -79,7 +85,7 @@ FN_API int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
         rc = fail("fn_test_moe: copy failed");
     if (!rc)
         rc = launch_moe(m->p, m->w, lg.as<float>(), ne + 1, xd.as<float>(), m->act.as<float>(), yd.as<float>(), nt, false,
-                        sd.as<int>(), wd.as<float>(), s);
+                        sd.as<int>(), wd.as<float>(), true, s);
     if (!rc) {
         cudaMemcpyAsync(y, yd.p, (size_t)nt * d * 4, cudaMemcpyDeviceToHost, s);
         if (sel) cudaMemcpyAsync(sel, sd.p, (size_t)nt * k * 4, cudaMemcpyDeviceToHost, s);
@@ -120,7 +126,7 @@ FN_API int fn_moe_free(int h) {
 FN_API int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream) {
     MoeH *m = moe_get(h);
     if (!m) return fail("fn_moe_run: bad handle");
-    return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), y, nt, acc != 0, nullptr, nullptr,
+    return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), y, nt, acc != 0, nullptr, nullptr, true,
                       (cudaStream_t)stream);
 }
 
@@ -213,6 +219,6 @@ FN_API int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int
         g_moe_static_act_dev[dev] = (float *)ptr;
     }
     const MoeWeights w{Wg, Wu, Wd, Wsg, Wsu, Wsd};
-    return launch_moe(p, w, logits, ls, x, g_moe_static_act_dev[dev], y, nt, false, nullptr, nullptr,
+    return launch_moe(p, w, logits, ls, x, g_moe_static_act_dev[dev], y, nt, false, nullptr, nullptr, /*planes=*/false,
                       (cudaStream_t)stream);
 }

@@ -36,6 +36,11 @@ size_t plan_weight_bytes(const GemvPlan &p);  // device bytes of the padded weig
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
                 bool early, cudaStream_t s);
 
+// GGUF rows (stride rb) -> the engine's row layout (planes for formats with a fast path, else unchanged) at stride
+// ldw. src and dst must not overlap.
+int launch_plane_repack(uint32_t type, const uint8_t *src, uint64_t rb, uint8_t *dst, uint32_t ldw, int rows, int cols,
+                        cudaStream_t s);
+
 // dequantise rows x cols of GGUF rows (row stride rb bytes) into out[r][c] fp32
 int launch_dequant(uint32_t type, const uint8_t *W, uint64_t rb, int rows, int cols, float *out, cudaStream_t s);
 
@@ -43,8 +48,8 @@ int launch_dequant(uint32_t type, const uint8_t *W, uint64_t rb, int rows, int c
 struct Settings {
     bool pdl = true;         // programmatic dependent launch
     bool early = true;       // GEMVs marked early run beside their predecessor
-    int warps_per_cta = 8;   // GEMV consumer warps
-    int ring_kb = 72;        // GEMV shared-memory ring per CTA
+    int warps_per_cta = 0;   // GEMV warps per CTA (0: by weight size)
+    int ring_kb = 112;       // GEMV shared-memory rings per CTA (all warps)
     int stage_kb = 16;       // target bytes per pipeline stage
     int ctas_per_sm = 1;     // GEMV CTAs per SM
     int ov_rps = 0;          // overrides (0 = automatic)

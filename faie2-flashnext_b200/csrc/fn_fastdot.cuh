@@ -1,0 +1,552 @@
+// Fast group dot products of the dense GEMV and the expert kernels, on the engine's plane layout.
+//
+// Plane layout ("SoA rows"): at upload every GGUF row is byte-permuted so that each field of the format's blocks is
+// a contiguous plane: row = [field 0 of blocks 0..nb-1][field 1 of blocks 0..nb-1]..., in the field order of
+// PlaneSpec<TY>. A pure permutation of the row's bytes (nothing is converted or added), chosen so the quant planes
+// of every block start on 16-byte boundaries and a lane reads its 32-value group with 128-bit shared-memory loads
+// even for formats whose GGUF blocks are only 2-byte aligned (Q6_K 210 B, Q8_0 34 B, IQ3_XXS 98 B, ...).
+//
+// Fast<TY>::group(row, nb, g, grid, xa, nt, r) adds to r[t] the dot product of the 32-value group g of a row with
+// x[t], for t < nt (NT tokens at most). Arithmetic: the block's small integers q_j (plus a per-format bias) become
+// exact floats with one byte permute (2^23 + q as float bits) and one packed add of -(2^23 + bias); products with x
+// are accumulated by packed fp32 FMAs (__ffma2_rn) in four chains per 16-value half; each half sum is scaled by the
+// sub-block's dequantisation scale and offset once: a * sum_j q_j x_j + b * sum_j x_j (x sums precomputed when x is
+// staged). This equals the dot product with the exactly dequantised fp32 weights up to fp32 rounding of the same
+// order as the reference's own GEMV (flashnext/test_fn_quants.py:36-37 bounds it at 1e-5, the north star at 2e-7;
+// the GPU suite checks 2e-7). The result per group is one fp32 value; callers accumulate groups in double.
+#pragma once
+
+#include "fn_decode.cuh"
+
+namespace fn {
+
+// ---- plane specifications -------------------------------------------------------------------------------------
+struct Field {
+    int off, size;  // offset inside the GGUF block, bytes
+};
+template <uint32_t TY> struct PlaneSpec {
+    static constexpr int nf = 0;  // 0: no plane layout (the generic decoder reads GGUF rows)
+    static constexpr Field f[1] = {{0, 0}};
+};
+#define FN_PLANES(TY, ...)                                                   \
+    template <> struct PlaneSpec<TY> {                                       \
+        static constexpr Field f[] = {__VA_ARGS__};                          \
+        static constexpr int nf = sizeof(f) / sizeof(Field);                 \
+    };
+FN_PLANES(T_Q4_0, {2, 16}, {0, 2})
+FN_PLANES(T_Q4_1, {4, 16}, {0, 4})
+FN_PLANES(T_Q5_0, {6, 16}, {2, 4}, {0, 2})
+FN_PLANES(T_Q5_1, {8, 16}, {4, 4}, {0, 4})
+FN_PLANES(T_Q8_0, {2, 32}, {0, 2})
+FN_PLANES(T_Q2_K, {16, 64}, {0, 16}, {80, 4})
+FN_PLANES(T_Q3_K, {32, 64}, {0, 32}, {96, 12}, {108, 2})
+FN_PLANES(T_Q4_K, {16, 128}, {4, 12}, {0, 4})
+FN_PLANES(T_Q5_K, {48, 128}, {16, 32}, {4, 12}, {0, 4})
+FN_PLANES(T_Q6_K, {0, 128}, {128, 64}, {192, 16}, {208, 2})
+FN_PLANES(T_IQ2_XXS, {2, 64}, {0, 2})
+FN_PLANES(T_IQ3_XXS, {2, 64}, {66, 32}, {0, 2})
+FN_PLANES(T_IQ4_XS, {8, 128}, {4, 4}, {0, 4})
+FN_PLANES(T_IQ4_NL, {2, 16}, {0, 2})
+#undef FN_PLANES
+
+// bytes of one block's fields before field F; the byte offset of plane F of a row of nb blocks is that times nb
+template <uint32_t TY, int F> __host__ __device__ constexpr int plane_prefix() {
+    int o = 0;
+    for (int i = 0; i < F; ++i) o += PlaneSpec<TY>::f[i].size;
+    return o;
+}
+template <uint32_t TY, int F> __device__ __forceinline__ int plane_off(int nb) {
+    constexpr int P = plane_prefix<TY, F>();
+    return P * nb;
+}
+
+// ---- packed helpers --------------------------------------------------------------------------------------------
+// bytes k, k+1 of w as the floats 2^23 + byte
+__device__ __forceinline__ float2 mag2(uint32_t w, int k) {
+    return make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u + k)),
+                       __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441u + k)));
+}
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float hsum2(float2 a, float2 b) { return __fadd_rn(__fadd_rn(a.x, a.y), __fadd_rn(b.x, b.y)); }
+
+// x accessors: a lane's x for group g, token t; pairs x[j], x[j+1] (j even) and the half sums (values 0-15, 16-31)
+struct XRegA {  // one token, x of the group in registers
+    const float2 (&x)[16];
+    const float (&s)[2];
+    __device__ __forceinline__ float2 x2(int, int j) const { return x[j >> 1]; }
+    __device__ __forceinline__ float xs(int, int h) const { return s[h]; }
+};
+struct XSmA {  // tokens in shared memory: token t of the group at base + t * ts (32 values, then the 2 half sums)
+    const float *base;
+    int ts;
+    __device__ __forceinline__ float2 x2(int t, int j) const { return *(const float2 *)(base + (size_t)t * ts + j); }
+    __device__ __forceinline__ float xs(int t, int h) const { return base[(size_t)t * ts + 32 + h]; }
+};
+
+// four biased bytes q4 (value_k = byte_k - bias) times x[j + k]: chains a[t][0] (j, j+1) and a[t][1] (j+2, j+3)
+template <int NT, class XA>
+__device__ __forceinline__ void acc_word(uint32_t q4, float2 moff, const XA &xa, int j, int nt, float2 (&a)[NT][2]) {
+    const float2 v01 = __fadd2_rn(mag2(q4, 0), moff), v23 = __fadd2_rn(mag2(q4, 2), moff);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (NT > 1 && t >= nt) break;
+        a[t][0] = __ffma2_rn(v01, xa.x2(t, j), a[t][0]);
+        a[t][1] = __ffma2_rn(v23, xa.x2(t, j + 2), a[t][1]);
+    }
+}
+
+template <int NT> __device__ __forceinline__ void zero2(float2 (&a)[NT][2]) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) a[t][0] = a[t][1] = make_float2(0.f, 0.f);
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *(const uint4 *)p; }
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *(const uint2 *)p; }
+
+// 4 sign bits n -> per-byte masks 0xFF (bit set) / 0x00: bit k moves to bit 0 of byte k (n * 0x00204081 puts the
+// copies of each bit at distinct positions, so nothing carries), then * 0xFF widens each 0/1 byte
+__device__ __forceinline__ uint32_t sign_mask4(uint32_t n) { return ((n * 0x00204081u) & 0x01010101u) * 0xFFu; }
+// grid bytes g (< 128) with signs m (per byte 0xFF: negative) -> bytes 128 + (+-g)
+__device__ __forceinline__ uint32_t signed_bias128(uint32_t g, uint32_t m) {
+    return (g ^ (m & 0x7F7F7F7Fu)) + (0x80808080u ^ (m & 0x81818181u));
+}
+
+// IQ4_NL values + 128 as bytes, four per word
+constexpr uint32_t KVB0 = 0x3F2D1801u, KVB1 = 0x766A5D4Fu, KVB2 = 0xA6998D81u, KVB3 = 0xF1D9C5B5u;
+// the 8 nibbles of w (byte i: low nibble = value i, high nibble = value 16 + i) looked up: lo = bytes of values
+// 0..3, hi = values 16..19 (relative to w's first byte)
+__device__ __forceinline__ void iq4_lut(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    const uint32_t idx = w & 0x77777777u, sel = 0x32103210u | ((w & 0x88888888u) >> 1);
+    const uint32_t a0 = __byte_perm(KVB0, KVB1, idx), b0 = __byte_perm(KVB2, KVB3, idx);
+    const uint32_t a1 = __byte_perm(KVB0, KVB1, idx >> 16), b1 = __byte_perm(KVB2, KVB3, idx >> 16);
+    const uint32_t t0 = __byte_perm(a0, b0, sel), t1 = __byte_perm(a1, b1, sel >> 16);  // v0 v16 v1 v17 | v2 v18 v3 v19
+    lo = __byte_perm(t0, t1, 0x6420);
+    hi = __byte_perm(t0, t1, 0x7531);
+}
+
+__device__ __forceinline__ float h16(uint32_t w, int hi) {
+    return __half2float(__ushort_as_half((unsigned short)(hi ? (w >> 16) : (w & 0xFFFFu))));
+}
+
+constexpr float MAG = 8388608.0f;
+
+template <uint32_t TY> struct Fast {
+    static constexpr bool ok = false;
+};
+
+// ---- 32-value formats ------------------------------------------------------------------------------------------
+template <> struct Fast<T_Q4_0> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const uint4 w = lds128(row + 16 * g);
+        const float d = ldh(row + plane_off<T_Q4_0, 1>(nb) + 2 * g);
+        const float2 mo = f2(-(MAG + 8.0f));
+        float2 a[NT][2], b[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(b);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>(ws[k] & 0x0F0F0F0Fu, mo, xa, 4 * k, nt, a);
+            acc_word<NT>((ws[k] >> 4) & 0x0F0F0F0Fu, mo, xa, 16 + 4 * k, nt, b);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(d, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(b[t][0], b[t][1])));
+    }
+};
+
+template <> struct Fast<T_IQ4_NL> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const uint4 w = lds128(row + 16 * g);
+        const float d = ldh(row + plane_off<T_IQ4_NL, 1>(nb) + 2 * g);
+        const float2 mo = f2(-(MAG + 128.0f));
+        float2 a[NT][2], b[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(b);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t lo, hi;
+            iq4_lut(ws[k], lo, hi);
+            acc_word<NT>(lo, mo, xa, 4 * k, nt, a);
+            acc_word<NT>(hi, mo, xa, 16 + 4 * k, nt, b);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(d, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(b[t][0], b[t][1])));
+    }
+};
+
+template <> struct Fast<T_Q4_1> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const uint4 w = lds128(row + 16 * g);
+        const uint32_t dm = ld32a(row + plane_off<T_Q4_1, 1>(nb) + 4 * g);
+        const float d = h16(dm, 0), m = h16(dm, 1);
+        const float2 mo = f2(-MAG);
+        float2 a[NT][2], b[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(b);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>(ws[k] & 0x0F0F0F0Fu, mo, xa, 4 * k, nt, a);
+            acc_word<NT>((ws[k] >> 4) & 0x0F0F0F0Fu, mo, xa, 16 + 4 * k, nt, b);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (NT > 1 && t >= nt) break;
+            const float s = __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(b[t][0], b[t][1]));
+            r[t] = __fmaf_rn(d, s, __fmul_rn(m, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
+        }
+    }
+};
+
+// the 4 qh bits n (values i..i+3) as bit 4 of each byte
+__device__ __forceinline__ uint32_t spread4_b4(uint32_t n) { return (n * 0x02040810u) & 0x10101010u; }
+
+template <> struct Fast<T_Q5_0> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const uint4 w = lds128(row + 16 * g);
+        const uint32_t qh = ld32a(row + plane_off<T_Q5_0, 1>(nb) + 4 * g);
+        const float d = ldh(row + plane_off<T_Q5_0, 2>(nb) + 2 * g);
+        const float2 mo = f2(-(MAG + 16.0f));
+        float2 a[NT][2], b[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(b);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>((ws[k] & 0x0F0F0F0Fu) | spread4_b4((qh >> (4 * k)) & 15u), mo, xa, 4 * k, nt, a);
+            acc_word<NT>(((ws[k] >> 4) & 0x0F0F0F0Fu) | spread4_b4((qh >> (16 + 4 * k)) & 15u), mo, xa, 16 + 4 * k, nt, b);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(d, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(b[t][0], b[t][1])));
+    }
+};
+
+template <> struct Fast<T_Q5_1> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const uint4 w = lds128(row + 16 * g);
+        const uint32_t qh = ld32a(row + plane_off<T_Q5_1, 1>(nb) + 4 * g);
+        const uint32_t dm = ld32a(row + plane_off<T_Q5_1, 2>(nb) + 4 * g);
+        const float d = h16(dm, 0), m = h16(dm, 1);
+        const float2 mo = f2(-MAG);
+        float2 a[NT][2], b[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(b);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>((ws[k] & 0x0F0F0F0Fu) | spread4_b4((qh >> (4 * k)) & 15u), mo, xa, 4 * k, nt, a);
+            acc_word<NT>(((ws[k] >> 4) & 0x0F0F0F0Fu) | spread4_b4((qh >> (16 + 4 * k)) & 15u), mo, xa, 16 + 4 * k, nt, b);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (NT > 1 && t >= nt) break;
+            const float s = __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(b[t][0], b[t][1]));
+            r[t] = __fmaf_rn(d, s, __fmul_rn(m, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
+        }
+    }
+};
+
+template <> struct Fast<T_Q8_0> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const uint4 w0 = lds128(row + 32 * g), w1 = lds128(row + 32 * g + 16);
+        const float d = ldh(row + plane_off<T_Q8_0, 1>(nb) + 2 * g);
+        const float2 mo = f2(-(MAG + 128.0f));
+        float2 a[NT][2], b[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(b);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>(ws[k] ^ 0x80808080u, mo, xa, 4 * k, nt, a);
+            acc_word<NT>(ws[4 + k] ^ 0x80808080u, mo, xa, 16 + 4 * k, nt, b);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(d, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(b[t][0], b[t][1])));
+    }
+};
+
+// ---- K-quants (256-value blocks; group g = block g >> 3, sub-block g & 7) --------------------------------------
+template <> struct Fast<T_Q2_K> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7, h = ib >> 2, s = 2 * (ib & 3);
+        const uint8_t *q = row + 64 * b + 32 * h;
+        const uint4 w0 = lds128(q), w1 = lds128(q + 16);
+        const uint32_t sc = ld16(row + plane_off<T_Q2_K, 1>(nb) + 16 * b + 2 * ib);
+        const uint32_t dm = ld32a(row + plane_off<T_Q2_K, 2>(nb) + 4 * b);
+        const float d = h16(dm, 0), dmin = h16(dm, 1);
+        const float dl0 = __fmul_rn(d, u2f(sc & 15u)), ml0 = __fmul_rn(dmin, u2f((sc >> 4) & 15u));
+        const float dl1 = __fmul_rn(d, u2f((sc >> 8) & 15u)), ml1 = __fmul_rn(dmin, u2f((sc >> 12) & 15u));
+        const float2 mo = f2(-MAG);
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>((ws[k] >> s) & 0x03030303u, mo, xa, 4 * k, nt, a);
+            acc_word<NT>((ws[4 + k] >> s) & 0x03030303u, mo, xa, 16 + 4 * k, nt, c);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (NT > 1 && t >= nt) break;
+            const float h0 = __fmaf_rn(dl0, hsum2(a[t][0], a[t][1]), -__fmul_rn(ml0, xa.xs(t, 0)));
+            const float h1 = __fmaf_rn(dl1, hsum2(c[t][0], c[t][1]), -__fmul_rn(ml1, xa.xs(t, 1)));
+            r[t] = __fadd_rn(h0, h1);
+        }
+    }
+};
+
+template <> struct Fast<T_Q3_K> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7, h = ib >> 2, s = 2 * (ib & 3);
+        const uint8_t *q = row + 64 * b + 32 * h, *hm = row + plane_off<T_Q3_K, 1>(nb) + 32 * b;
+        const uint4 w0 = lds128(q), w1 = lds128(q + 16), m0 = lds128(hm), m1 = lds128(hm + 16);
+        const uint8_t *scp = row + plane_off<T_Q3_K, 2>(nb) + 12 * b;
+        const float d = ldh(row + plane_off<T_Q3_K, 3>(nb) + 2 * b);
+        float dl[2];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int k = 2 * ib + half;
+            const uint32_t lo = (scp[k & 7] >> (4 * (k >> 3))) & 15u, hi = (scp[8 + (k & 3)] >> (2 * (k >> 2))) & 3u;
+            dl[half] = __fmul_rn(d, u2f_off(lo | (hi << 4), 32.0f));
+        }
+        const float2 mo = f2(-(MAG + 4.0f));  // q = low 2 bits + 4 * hmask bit, minus 4
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t ms[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>(((ws[k] >> s) & 0x03030303u) | (((ms[k] >> ib) & 0x01010101u) << 2), mo, xa, 4 * k, nt, a);
+            acc_word<NT>(((ws[4 + k] >> s) & 0x03030303u) | (((ms[4 + k] >> ib) & 0x01010101u) << 2), mo, xa, 16 + 4 * k,
+                         nt, c);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmaf_rn(dl[1], hsum2(c[t][0], c[t][1]), __fmul_rn(dl[0], hsum2(a[t][0], a[t][1])));
+    }
+};
+
+template <> struct Fast<T_Q4_K> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7, sh = 4 * (ib & 1);
+        const uint8_t *q = row + 128 * b + 32 * (ib >> 1);
+        const uint4 w0 = lds128(q), w1 = lds128(q + 16);
+        uint32_t sc, m;
+        kscale(ib, row + plane_off<T_Q4_K, 1>(nb) + 12 * b, sc, m);
+        const uint32_t dm = ld32a(row + plane_off<T_Q4_K, 2>(nb) + 4 * b);
+        const float dl = __fmul_rn(h16(dm, 0), u2f(sc)), ml = __fmul_rn(h16(dm, 1), u2f(m));
+        const float2 mo = f2(-MAG);
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>((ws[k] >> sh) & 0x0F0F0F0Fu, mo, xa, 4 * k, nt, a);
+            acc_word<NT>((ws[4 + k] >> sh) & 0x0F0F0F0Fu, mo, xa, 16 + 4 * k, nt, c);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (NT > 1 && t >= nt) break;
+            const float s = __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1]));
+            r[t] = __fmaf_rn(dl, s, -__fmul_rn(ml, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
+        }
+    }
+};
+
+template <> struct Fast<T_Q5_K> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7, sh = 4 * (ib & 1);
+        const uint8_t *q = row + 128 * b + 32 * (ib >> 1), *qh = row + plane_off<T_Q5_K, 1>(nb) + 32 * b;
+        const uint4 w0 = lds128(q), w1 = lds128(q + 16), h0 = lds128(qh), h1 = lds128(qh + 16);
+        uint32_t sc, m;
+        kscale(ib, row + plane_off<T_Q5_K, 2>(nb) + 12 * b, sc, m);
+        const uint32_t dm = ld32a(row + plane_off<T_Q5_K, 3>(nb) + 4 * b);
+        const float dl = __fmul_rn(h16(dm, 0), u2f(sc)), ml = __fmul_rn(h16(dm, 1), u2f(m));
+        const float2 mo = f2(-MAG);
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t hs[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>(((ws[k] >> sh) & 0x0F0F0F0Fu) | (((hs[k] >> ib) & 0x01010101u) << 4), mo, xa, 4 * k, nt, a);
+            acc_word<NT>(((ws[4 + k] >> sh) & 0x0F0F0F0Fu) | (((hs[4 + k] >> ib) & 0x01010101u) << 4), mo, xa, 16 + 4 * k,
+                         nt, c);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (NT > 1 && t >= nt) break;
+            const float s = __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1]));
+            r[t] = __fmaf_rn(dl, s, -__fmul_rn(ml, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
+        }
+    }
+};
+
+template <> struct Fast<T_Q6_K> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const int b = g >> 3, j8 = g & 7, h = j8 >> 2, ls = 4 * ((j8 >> 1) & 1), hsh = 2 * (j8 & 3);
+        const uint8_t *ql = row + 128 * b + 64 * h + 32 * (j8 & 1), *qh = row + plane_off<T_Q6_K, 1>(nb) + 64 * b + 32 * h;
+        const uint4 w0 = lds128(ql), w1 = lds128(ql + 16), h0 = lds128(qh), h1 = lds128(qh + 16);
+        const uint32_t sc = ld16(row + plane_off<T_Q6_K, 2>(nb) + 16 * b + 2 * j8);
+        const float d = ldh(row + plane_off<T_Q6_K, 3>(nb) + 2 * b);
+        const float ds0 = __fmul_rn(d, (float)(int8_t)(sc & 255u)), ds1 = __fmul_rn(d, (float)(int8_t)(sc >> 8));
+        const float2 mo = f2(-(MAG + 32.0f));
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t hs[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc_word<NT>(((ws[k] >> ls) & 0x0F0F0F0Fu) | (((hs[k] >> hsh) & 0x03030303u) << 4), mo, xa, 4 * k, nt, a);
+            acc_word<NT>(((ws[4 + k] >> ls) & 0x0F0F0F0Fu) | (((hs[4 + k] >> hsh) & 0x03030303u) << 4), mo, xa,
+                         16 + 4 * k, nt, c);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmaf_rn(ds1, hsum2(c[t][0], c[t][1]), __fmul_rn(ds0, hsum2(a[t][0], a[t][1])));
+    }
+};
+
+// ---- IQ formats --------------------------------------------------------------------------------------------------
+template <> struct Fast<T_IQ4_XS> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
+                                                 float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7;
+        const uint4 w = lds128(row + 128 * b + 16 * ib);
+        const uint32_t sl = ld32a(row + plane_off<T_IQ4_XS, 1>(nb) + 4 * b);
+        const uint32_t dsh = ld32a(row + plane_off<T_IQ4_XS, 2>(nb) + 4 * b);  // d | scales_h << 16
+        const uint32_t ls = ((sl >> (4 * ib)) & 15u) | (((dsh >> (16 + 2 * ib)) & 3u) << 4);
+        const float dl = __fmul_rn(h16(dsh, 0), u2f_off(ls, 32.0f));
+        const float2 mo = f2(-(MAG + 128.0f));
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t lo, hi;
+            iq4_lut(ws[k], lo, hi);
+            acc_word<NT>(lo, mo, xa, 4 * k, nt, a);
+            acc_word<NT>(hi, mo, xa, 16 + 4 * k, nt, c);
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(dl, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1])));
+    }
+};
+
+template <> struct Fast<T_IQ2_XXS> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *grid, const XA &xa,
+                                                 int nt, float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7;
+        const uint2 w = lds64(row + 64 * b + 8 * ib);
+        const float d = ldh(row + plane_off<T_IQ2_XXS, 1>(nb) + 2 * b);
+        const float db = db_half(d, w.y >> 28, 0.25f);
+        const float2 mo = f2(-(MAG + 128.0f));
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint2 gw = *(const uint2 *)(grid + 2 * ((w.x >> (8 * l)) & 255u));
+            const uint32_t s8 = ksign((w.y >> (7 * l)) & 127u);
+            if (l < 2) {
+                acc_word<NT>(signed_bias128(gw.x, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, a);
+                acc_word<NT>(signed_bias128(gw.y, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, a);
+            } else {
+                acc_word<NT>(signed_bias128(gw.x, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, c);
+                acc_word<NT>(signed_bias128(gw.y, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, c);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(db, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1])));
+    }
+};
+
+template <> struct Fast<T_IQ3_XXS> {
+    static constexpr bool ok = true;
+    template <int NT, class XA>
+    __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *grid, const XA &xa,
+                                                 int nt, float (&r)[NT]) {
+        const int b = g >> 3, ib = g & 7;
+        const uint2 q = lds64(row + 64 * b + 8 * ib);
+        const uint32_t aux = ld32a(row + plane_off<T_IQ3_XXS, 1>(nb) + 32 * b + 4 * ib);
+        const float d = ldh(row + plane_off<T_IQ3_XXS, 2>(nb) + 2 * b);
+        const float db = db_half(d, aux >> 28, 0.5f);
+        const float2 mo = f2(-(MAG + 128.0f));
+        float2 a[NT][2], c[NT][2];
+        zero2<NT>(a);
+        zero2<NT>(c);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t qq = l < 2 ? q.x : q.y, s = 16 * (l & 1);
+            const uint32_t g0 = grid[(qq >> s) & 255u], g1 = grid[(qq >> (s + 8)) & 255u];
+            const uint32_t s8 = ksign((aux >> (7 * l)) & 127u);
+            if (l < 2) {
+                acc_word<NT>(signed_bias128(g0, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, a);
+                acc_word<NT>(signed_bias128(g1, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, a);
+            } else {
+                acc_word<NT>(signed_bias128(g0, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, c);
+                acc_word<NT>(signed_bias128(g1, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, c);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(db, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1])));
+    }
+};
+
+// ---- layout descriptor for the host (repack) ---------------------------------------------------------------------
+struct PlaneDesc {
+    int nf = 0;
+    Field f[6];
+};
+template <uint32_t TY> inline PlaneDesc plane_desc() {
+    PlaneDesc d;
+    if constexpr (Fast<TY>::ok) {
+        d.nf = PlaneSpec<TY>::nf;
+        for (int i = 0; i < d.nf; ++i) d.f[i] = PlaneSpec<TY>::f[i];
+    }
+    return d;
+}
+
+}  // namespace fn

@@ -14,100 +14,51 @@
 // in double in group order, and the row's lanes meet in a double butterfly; the row result is rounded to fp32 once.
 // A row never spans warps or CTAs, so there is no split-K scratch and no reduce kernel; the sum order is a function
 // of (format, cols) alone.
-#include "fn_engine.h"
-#include "fn_rowdot.cuh"
-
-#include <unordered_set>
+#include "fn_gemv_impl.cuh"
 
 namespace fn {
 
-struct GemvArgs {
-    const uint8_t *W;
-    uint32_t ldw;
-    int rows, G;
-    const float *x;
-    int xs;
-    float *y;
-    int ys, nt;
-    int rps, slots;
-    uint32_t stage_bytes, x_off, ring_off, grid_off;
-    int acc, early;
-    uint32_t *err;
-};
+FN_GEMV_DECL(T_Q4_0) FN_GEMV_DECL(T_Q4_1) FN_GEMV_DECL(T_Q5_0) FN_GEMV_DECL(T_Q5_1) FN_GEMV_DECL(T_Q8_0)
+FN_GEMV_DECL(T_Q2_K) FN_GEMV_DECL(T_Q3_K) FN_GEMV_DECL(T_Q4_K) FN_GEMV_DECL(T_Q5_K) FN_GEMV_DECL(T_Q6_K)
+FN_GEMV_DECL(T_IQ2_XXS) FN_GEMV_DECL(T_IQ2_XS) FN_GEMV_DECL(T_IQ2_S) FN_GEMV_DECL(T_IQ3_XXS) FN_GEMV_DECL(T_IQ3_S)
+FN_GEMV_DECL(T_IQ4_NL) FN_GEMV_DECL(T_IQ4_XS) FN_GEMV_DECL(T_BF16) FN_GEMV_DECL(T_Q2_0)
 
-template <uint32_t TY, int NT, int LPR, int GPL, bool XREG>
-__global__ void __launch_bounds__(256, 1) k_gemv(const GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    uint64_t *full = (uint64_t *)sm;
-    uint8_t *ring = sm + a.ring_off;
-    float *xsm = (float *)(sm + a.x_off);
-    uint32_t *grid = (uint32_t *)(sm + a.grid_off);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
-    const int r0 = (int)((long long)blockIdx.x * a.rows / gridDim.x);
-    const int r1 = (int)((long long)(blockIdx.x + 1) * a.rows / gridDim.x);
-    const int nst = (r1 - r0 + a.rps - 1) / a.rps;
-    const int G = a.G;
+// ---------------------------------------------------------------------------------------------------------------
+// plane repack at upload: GGUF rows (stride rb) -> plane rows (stride ldw), one thread per (row, block); formats
+// without a plane layout are copied as they are
 
-    auto issue = [&](int st) {  // thread 0: stage st of this CTA's rows into its slot
-        const int slot = st % a.slots, rr = r0 + st * a.rps, n = min(a.rps, r1 - rr);
-        const uint32_t bytes = (uint32_t)n * a.ldw;
-        mbar_arrive_tx(&full[slot], bytes);
-        bulk_g2s(ring + (size_t)slot * a.stage_bytes, a.W + (size_t)rr * a.ldw, bytes, &full[slot]);
-    };
-    if (tid == 0) {
-        for (int s = 0; s < a.slots; ++s) mbar_init(&full[s], 1);
-        mbar_fence_init();
-        for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
+__global__ void k_plane_repack(const uint8_t *__restrict__ src, uint64_t rb, uint8_t *__restrict__ dst, uint32_t ldw,
+                               int rows, int nb, int bytes, PlaneDesc pd) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * nb) return;
+    const int r = (int)(i / nb), b = (int)(i % nb);
+    const uint8_t *s = src + (size_t)r * rb + (size_t)b * bytes;
+    uint8_t *d = dst + (size_t)r * ldw;
+    if (pd.nf == 0) {
+        for (int k = 0; k < bytes; ++k) d[(size_t)b * bytes + k] = s[k];
+        return;
     }
-    stage_grid<TY>(grid);
-
-    if (!a.early) pdl_wait();
-    const float *x = after_wait(a.x);
-    const int nt = a.nt;
-    stage_x(xsm, x, a.xs, nt, G);
-    __syncthreads();
-    pdl_trigger();
-
-    constexpr int RPW = 32 / LPR;  // rows a warp works on at once
-    const int lr = lane % LPR, sub = lane / LPR;
-    XReg<LPR, (GPL > 0 ? GPL : 1)> xr;
-    if constexpr (XREG) xr.load(xsm, lr);
-
-    int st = 0;
-    for (; st < nst; ++st) {
-        const int slot = st % a.slots;
-        const uint32_t par = (uint32_t)(st / a.slots) & 1u;
-        const bool ok = warp_wait(&full[slot], par);
-        if (ok) {
-            const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes;
-            const int rr0 = r0 + st * a.rps, n = min(a.rps, r1 - rr0);
-            for (int base = warp * RPW; base < n; base += nw * RPW) {
-                const int row = base + sub;
-                const bool valid = row < n;
-                double acc[NT];
-                row_dot<TY, NT, LPR, GPL, XREG>(sbuf + (size_t)row * a.ldw, grid, xr, xsm, G, lr, nt, valid, acc);
-                if (valid && lr == 0) {
-                    const int r = rr0 + row;
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        if (NT > 1 && t >= nt) break;
-                        float *o = a.y + (size_t)t * a.ys + r;
-                        const float v = __double2float_rn(acc[t]);
-                        *o = a.acc ? __fadd_rn(*o, v) : v;
-                    }
-                }
-            }
-        }
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
-            break;
-        }
-        if (tid == 0 && st + a.slots < nst) issue(st + a.slots);
+    int plane = 0;
+    for (int f = 0; f < pd.nf; ++f) {
+        const Field fl = pd.f[f];
+        for (int k = 0; k < fl.size; ++k) d[plane + (size_t)b * fl.size + k] = s[fl.off + k];
+        plane += fl.size * nb;
     }
-    if (st < nst && tid == 0) {  // wound down early: let the copies already issued land (bounded) before exiting
-        for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
-    }
-    if (a.early) pdl_wait();
+}
+
+int launch_plane_repack(uint32_t type, const uint8_t *src, uint64_t rb, uint8_t *dst, uint32_t ldw, int rows, int cols,
+                        cudaStream_t s) {
+    int qk, bytes;
+    if (!type_info(type, qk, bytes) || cols % qk || row_bytes(type, cols) != rb) return fail("repack: bad type/shape");
+    if (rows == 0) return 0;
+    PlaneDesc pd;
+    dispatch_type(type, [&]<uint32_t TY>() { pd = plane_desc<TY>(); });
+    const int nb = cols / qk;
+    const long long n = (long long)rows * nb;
+    k_plane_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, rb, dst, ldw, rows, nb, bytes, pd);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(std::string("repack launch: ") + cudaGetErrorString(e));
+    return 0;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -163,23 +114,31 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     p.gpl = (p.G + p.lpr - 1) / p.lpr;
     p.xreg = p.ntcap == 1 && (p.G == 8 || p.G == 16 || p.G == 32 || p.G == 64);
     const Settings &S = settings();
-    p.threads = 32 * std::max(1, std::min(S.warps_per_cta, 16));
-    const int nw = p.threads / 32, rpw = 32 / p.lpr, pass = nw * rpw;
-    // rows per stage: about stage_kb bytes, whole passes of the CTA's warps when a pass fits
-    int rps = std::max(1, (int)((size_t)S.stage_kb * 1024 / p.ldw));
-    if (rps >= pass) rps = rps / pass * pass;
-    if (S.ov_rps > 0) rps = S.ov_rps;
+    const int rpw = 32 / p.lpr, ru = rpw * (p.lpr == 32 ? 2 : 1);
+    // every warp streams its own contiguous rows through its own ring of `slots` stages of ru rows
+    p.rps = ru;
+    p.stage_bytes = (uint32_t)align_up((size_t)ru * p.ldw, 128);
+    // budget: x for the token capacity (one token if the capacity does not fit) and the codebook come first
+    const size_t fixed = 1024 + (size_t)grid_words(type) * 4 + 128;
+    size_t xb = (size_t)p.ntcap * p.G * XPAD * 4;
+    if (fixed + xb + 2 * (size_t)p.stage_bytes > 227 * 1024) xb = (size_t)p.G * XPAD * 4;
+    const size_t ring_budget = std::min<size_t>((size_t)S.ring_kb * 1024, 227 * 1024 - fixed - xb);
+    // warps: the setting (S.warps_per_cta > 0), else 16 for large weights and 8 for small ones, fewer when wide rows
+    // would leave less than two stages per warp
+    int nw = S.warps_per_cta > 0 ? S.warps_per_cta : ((size_t)rows * p.rb >= (64u << 20) ? 16 : 8);
+    nw = std::max(1, std::min(nw, 16));
+    while (nw > 1 && (size_t)nw * 2 * p.stage_bytes > ring_budget) --nw;
+    if ((size_t)nw * p.stage_bytes > ring_budget) return false;
+    p.threads = 32 * nw;
     const int ctas_max = std::max(1, num_sms() * std::max(1, S.ctas_per_sm));
-    p.ctas = std::min(ctas_max, (rows + rpw - 1) / rpw);
-    const int rows_per_cta = (rows + p.ctas - 1) / p.ctas;
-    p.rps = std::max(1, std::min(rps, rows_per_cta));
-    p.stage_bytes = (uint32_t)align_up((size_t)p.rps * p.ldw, 128);
-    const int stages_per_cta = (rows_per_cta + p.rps - 1) / p.rps;
-    p.slots = (int)std::max<size_t>(2, (size_t)S.ring_kb * 1024 / p.stage_bytes);
-    p.slots = std::max(1, std::min(p.slots, std::min(stages_per_cta, 16)));
-    // layout: barriers | ring | codebook | x (sized per call by its token count: gemv_smem)
-    p.ring_off = 128;
-    p.grid_off = (uint32_t)align_up(p.ring_off + (size_t)p.slots * p.stage_bytes, 128);
+    p.ctas = std::min(ctas_max, (rows + ru - 1) / ru);
+    const int rows_per_warp = (int)((rows + (size_t)p.ctas * nw - 1) / ((size_t)p.ctas * nw));
+    const int stages_per_warp = std::max(1, (rows_per_warp + ru - 1) / ru);
+    p.slots = (int)std::max<size_t>(1, ring_budget / ((size_t)nw * p.stage_bytes));
+    p.slots = std::max(1, std::min(p.slots, std::min(stages_per_warp, 8)));
+    // layout: barriers (nw x slots) | rings | codebook | x (sized per call by its token count: gemv_smem)
+    p.ring_off = (uint32_t)align_up((size_t)nw * p.slots * 8, 128);
+    p.grid_off = (uint32_t)align_up(p.ring_off + (size_t)nw * p.slots * p.stage_bytes, 128);
     p.x_off = (uint32_t)align_up(p.grid_off + (size_t)grid_words(type) * 4, 128);
     p.smem = gemv_smem(p, p.ntcap);
     if (p.smem > 227 * 1024) p.smem = gemv_smem(p, 1);  // wide rows: fewer tokens per call fit (checked at launch)
@@ -187,31 +146,6 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
 }
 
 size_t plan_weight_bytes(const GemvPlan &p) { return (size_t)p.rows * p.ldw; }
-
-template <uint32_t TY> static cudaError_t launch_t(const GemvPlan &p, const GemvArgs &a, size_t smem, cudaStream_t s) {
-    void (*k)(const GemvArgs) = nullptr;
-    if (p.ntcap == 1) {
-        if (p.xreg) {
-            if (p.lpr == 8) k = k_gemv<TY, 1, 8, 1, true>;
-            else if (p.lpr == 16) k = k_gemv<TY, 1, 16, 1, true>;
-            else if (p.gpl == 1) k = k_gemv<TY, 1, 32, 1, true>;
-            else k = k_gemv<TY, 1, 32, 2, true>;
-        } else {
-            k = k_gemv<TY, 1, 32, 0, false>;
-        }
-    } else {
-        if (p.lpr == 8) k = k_gemv<TY, 8, 8, 0, false>;
-        else if (p.lpr == 16) k = k_gemv<TY, 8, 16, 0, false>;
-        else k = k_gemv<TY, 8, 32, 0, false>;
-    }
-    static std::unordered_set<const void *> configured;  // one attribute call per kernel, outside graph capture
-    if (!configured.count((const void *)k)) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        configured.insert((const void *)k);
-    }
-    return launch_k(k, dim3(p.ctas), dim3(p.threads), smem, s, a);
-}
 
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
                 bool early, cudaStream_t s) {
@@ -225,6 +159,9 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.ldw = p.ldw;
     a.rows = p.rows;
     a.G = p.G;
+    int qk_, bytes_;
+    type_info(p.type, qk_, bytes_);
+    a.nb = p.cols / qk_;
     a.x = x;
     a.xs = xs;
     a.y = y;
@@ -240,7 +177,7 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.early = early && settings().early && settings().pdl ? 1 : 0;
     a.err = dev_error_ptr();
     cudaError_t e = cudaSuccess;
-    const bool known = dispatch_type(p.type, [&]<uint32_t TY>() { e = launch_t<TY>(p, a, smem, s); });
+    const bool known = dispatch_type(p.type, [&]<uint32_t TY>() { e = gemv_launch_t<TY>(p, a, smem, s); });
     if (!known) return fail("gemv: unsupported type " + std::to_string(p.type));
     if (e != cudaSuccess) return fail(std::string("gemv launch: ") + cudaGetErrorString(e));
     return 0;

@@ -1,0 +1,136 @@
+// Dense GEMV kernel template and its per-format launcher (instantiated in fn_gemv_i*.cu, one group of formats per
+// translation unit so the build compiles them in parallel). See fn_gemv.cu for the design.
+#pragma once
+
+#include <unordered_set>
+
+#include "fn_engine.h"
+#include "fn_rowdot.cuh"
+
+namespace fn {
+
+struct GemvArgs {
+    const uint8_t *W;  // plane rows (GGUF rows for formats without a plane layout)
+    uint32_t ldw;
+    int rows, G, nb;
+    const float *x;
+    int xs;
+    float *y;
+    int ys, nt;
+    int rps, slots;
+    uint32_t stage_bytes, x_off, ring_off, grid_off;
+    int acc, early;
+    uint32_t *err;
+};
+
+template <uint32_t TY, int NT, int LPR, int GPL, bool XREG>
+__global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
+    constexpr int RR = LPR == 32 ? 2 : 1;  // rows per lane group per stage
+    constexpr int RPW = 32 / LPR;          // lane groups per warp
+    constexpr int RU = RR * RPW;           // rows per warp stage
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    uint64_t *full = (uint64_t *)sm + warp * a.slots;  // this warp's stage barriers
+    uint8_t *ring = sm + a.ring_off + (size_t)warp * a.slots * a.stage_bytes;
+    float *xsm = (float *)(sm + a.x_off);
+    uint32_t *grid = (uint32_t *)(sm + a.grid_off);
+    // the CTA's rows, split into one contiguous range per warp
+    const int r0 = (int)((long long)blockIdx.x * a.rows / gridDim.x);
+    const int r1 = (int)((long long)(blockIdx.x + 1) * a.rows / gridDim.x);
+    const int w0 = r0 + (int)((long long)(r1 - r0) * warp / nw), w1 = r0 + (int)((long long)(r1 - r0) * (warp + 1) / nw);
+    const int nst = (w1 - w0 + RU - 1) / RU;
+
+    auto issue = [&](int st) {  // lane 0: stage st of this warp's rows into its slot
+        const int slot = st % a.slots, rr = w0 + st * RU, n = min(RU, w1 - rr);
+        const uint32_t bytes = (uint32_t)n * a.ldw;
+        mbar_arrive_tx(&full[slot], bytes);
+        bulk_g2s(ring + (size_t)slot * a.stage_bytes, a.W + (size_t)rr * a.ldw, bytes, &full[slot]);
+    };
+    if (lane == 0) {
+        for (int s = 0; s < a.slots; ++s) mbar_init(&full[s], 1);
+        mbar_fence_init();
+        for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
+    }
+    __syncwarp();
+    stage_grid<TY>(grid);
+
+    if (!a.early) pdl_wait();
+    const float *x = after_wait(a.x);
+    const int nt = a.nt;
+    stage_x(xsm, x, a.xs, nt, a.G);
+    __syncthreads();
+    pdl_trigger();
+
+    const int lr = lane % LPR, sub = lane / LPR;
+    XReg<LPR, (GPL > 0 ? GPL : 1)> xr;
+    if constexpr (XREG) xr.load(xsm, lr);
+
+    int st = 0;
+    for (; st < nst; ++st) {
+        const int slot = st % a.slots;
+        if (!warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u)) {
+            if (lane == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
+            break;
+        }
+        const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes;
+        const int rr0 = w0 + st * RU;
+        const uint8_t *rp[RR];
+        bool valid[RR];
+        int row[RR];
+#pragma unroll
+        for (int q = 0; q < RR; ++q) {
+            row[q] = q * RPW + sub;
+            valid[q] = rr0 + row[q] < w1;
+            rp[q] = sbuf + (size_t)(valid[q] ? row[q] : 0) * a.ldw;
+        }
+        double acc[RR][NT];
+        rows_dot<TY, true, NT, LPR, GPL, XREG, RR>(rp, valid, a.nb, grid, xr, xsm, a.G, lr, nt, acc);
+        const int q = RR == 2 ? (lane >> 4) : 0;
+        if (valid[q] && (RR == 2 ? (lane & 15) == 0 : lr == 0)) {
+            const int r = rr0 + row[q];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (NT > 1 && t >= nt) break;
+                float *o = a.y + (size_t)t * a.ys + r;
+                const float v = __double2float_rn(acc[q][t]);
+                *o = a.acc ? __fadd_rn(*o, v) : v;
+            }
+        }
+        __syncwarp();  // every lane is done reading the slot
+        if (lane == 0 && st + a.slots < nst) issue(st + a.slots);
+    }
+    if (st < nst && lane == 0)  // wound down early: let the copies already issued land (bounded) before exiting
+        for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
+    if (a.early) pdl_wait();
+}
+
+template <uint32_t TY> cudaError_t gemv_launch_t(const GemvPlan &p, const GemvArgs &a, size_t smem, cudaStream_t s) {
+    void (*k)(const GemvArgs) = nullptr;
+    if (p.ntcap == 1) {
+        if (p.xreg) {
+            if (p.lpr == 8) k = k_gemv<TY, 1, 8, 1, true>;
+            else if (p.lpr == 16) k = k_gemv<TY, 1, 16, 1, true>;
+            else if (p.gpl == 1) k = k_gemv<TY, 1, 32, 1, true>;
+            else k = k_gemv<TY, 1, 32, 2, true>;
+        } else {
+            k = k_gemv<TY, 1, 32, 0, false>;
+        }
+    } else {
+        if (p.lpr == 8) k = k_gemv<TY, 8, 8, 0, false>;
+        else if (p.lpr == 16) k = k_gemv<TY, 8, 16, 0, false>;
+        else k = k_gemv<TY, 8, 32, 0, false>;
+    }
+    static std::unordered_set<const void *> configured;  // one attribute call per kernel, outside graph capture
+    if (!configured.count((const void *)k)) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured.insert((const void *)k);
+    }
+    return launch_k(k, dim3(p.ctas), dim3(p.threads), smem, s, a);
+}
+
+
+#define FN_GEMV_DECL(TY) extern template cudaError_t gemv_launch_t<TY>(const GemvPlan &, const GemvArgs &, size_t, cudaStream_t);
+#define FN_GEMV_INST(TY) template cudaError_t gemv_launch_t<TY>(const GemvPlan &, const GemvArgs &, size_t, cudaStream_t);
+
+}  // namespace fn

@@ -24,9 +24,10 @@ bool plan_moe(MoePlan &p, uint32_t gu_type, uint32_t down_type, int ne, int k, i
 
 // y[t] (+)= sum_{s<k} w[t][s] down_{sel[t][s]} . act[t][s] + sigmoid(logits[t][ne]) shared(x[t]) for t < nt <= 8, with
 // act[t][s] = silu(gate_e . x[t]) * (up_e . x[t]) and (sel, w) the top-k routing of logits[t][0..ne). logits: token
-// stride ls >= ne + 1. act: scratch of nt * (k + 1) * ffe floats. sel_out / w_out (nullable): [nt][k].
+// stride ls >= ne + 1. act: scratch of nt * (k + 1) * ffe floats. sel_out / w_out (nullable): [nt][k]. planes: the
+// weights are in the engine's plane layout (launch_plane_repack), else GGUF rows at the plan's strides.
 int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act, float *y,
-               int nt, bool acc, int *sel_out, float *w_out, cudaStream_t s);
+               int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s);
 
 // routing alone on split-K partials: logits[t][i] = sum_{j<ks} part[j * kst + t * ts + i] (split order)
 int launch_route(const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,

@@ -1,14 +1,16 @@
 // The row-dot core shared by the dense GEMV and the routed-expert kernels: x staging into shared memory, the
-// per-lane group decode + FMA chains, and the fixed-order reduction of a row's lanes.
+// per-lane group dot products, and the fixed-order reduction of a row's lanes.
 //
 // Sum order (a function of the weight's format and row length only, never of the tokens or the launch shape):
-// lane l of a row (lpr lanes per row) owns the 32-value groups l, l + lpr, l + 2 lpr, ...; each group is decoded
-// (Dec<TY>, bit-exact values) into four fp32 FMA chains over runs of four values (chain k takes values j + k), the
-// chains are added ((c0 + c1) + (c2 + c3)) in fp32, the group sums are accumulated in double in group order, and the
-// lanes meet in a double butterfly (xor lpr/2, ..., 1). The row result is rounded to fp32 once by the caller.
+// lane l of a row (lpr lanes per row) owns the 32-value groups l, l + lpr, l + 2 lpr, ...; each group's dot product
+// is one fp32 value (Fast<TY> on the plane layout, or the bit-exact generic decoder Dec<TY> reduced by four FMA
+// chains on GGUF rows); the group values are accumulated in double in group order, and the row's lanes meet in a
+// double butterfly (xor lpr/2, ..., 1; when a warp works on two rows the first step exchanges halves, which adds the
+// same pairs). The row result is rounded to fp32 once by the caller.
 #pragma once
 
 #include "fn_decode.cuh"
+#include "fn_fastdot.cuh"
 #include "fn_grids.h"
 
 namespace fn {
@@ -30,78 +32,128 @@ template <uint32_t TY> __device__ __forceinline__ void stage_grid(uint32_t *grid
     }
 }
 
-constexpr int XPAD = 36;  // floats per staged x group (32 + 4: lanes reading consecutive groups hit distinct banks)
+// the fast plane-layout path is used for TY when the weights are stored in planes
+template <uint32_t TY, bool SOA> struct UseFast {
+    static constexpr bool v = SOA && Fast<TY>::ok;
+};
 
-// x[t][c] (token stride xs floats, 16-byte aligned, xs % 4 == 0) -> xsm[(t * G + g) * XPAD + j]; every thread calls
+constexpr int XPAD = 36;  // floats per staged x group: 32 values, the two 16-value sums, 2 spare (bank spread)
+
+// x[t][c] (token stride xs floats, 16-byte aligned, xs % 4 == 0) -> xsm[(t * G + g) * XPAD + j], and the half sums
+// sum(x[16h .. 16h + 15]) (pairwise, fixed order) at + 32 + h. Every thread calls this.
 __device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int nt, int G) {
-    for (int idx = threadIdx.x; idx < nt * G * 8; idx += blockDim.x) {
-        const int t = idx / (G * 8), r = idx - t * (G * 8), g = r >> 3, q = r & 7;
-        const float4 v = *(const float4 *)(x + (size_t)t * xs + g * 32 + 4 * q);
-        *(float4 *)(xsm + ((size_t)t * G + g) * XPAD + 4 * q) = v;
+    for (int idx = threadIdx.x; idx < nt * G * 2; idx += blockDim.x) {
+        const int t = idx / (G * 2), r = idx - t * (G * 2), g = r >> 1, h = r & 1;
+        const float4 *src = (const float4 *)(x + (size_t)t * xs + g * 32 + 16 * h);
+        float *dst = xsm + ((size_t)t * G + g) * XPAD;
+        float4 v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            v[q] = src[q];
+            *(float4 *)(dst + 16 * h + 4 * q) = v[q];
+        }
+        float p[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) p[q] = __fadd_rn(__fadd_rn(v[q].x, v[q].y), __fadd_rn(v[q].z, v[q].w));
+        dst[32 + h] = __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3]));
     }
 }
 
 // a lane's x slice in registers (one token): groups lr + LPR * i, i < GPL
 template <int LPR, int GPL> struct XReg {
-    float v[GPL][32];
+    float2 v[GPL][16];
+    float s[GPL][2];
     __device__ __forceinline__ void load(const float *xsm, int lr) {
 #pragma unroll
         for (int i = 0; i < GPL; ++i) {
             const float *src = xsm + (size_t)(lr + LPR * i) * XPAD;
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 q = *(const float4 *)(src + j);
-                v[i][j] = q.x;
-                v[i][j + 1] = q.y;
-                v[i][j + 2] = q.z;
-                v[i][j + 3] = q.w;
+            for (int j = 0; j < 16; j += 2) {
+                const float4 q = *(const float4 *)(src + 2 * j);
+                v[i][j] = make_float2(q.x, q.y);
+                v[i][j + 1] = make_float2(q.z, q.w);
             }
+            s[i][0] = src[32];
+            s[i][1] = src[33];
         }
     }
 };
 
-// acc[t] = sum over the lane's groups of row . x[t] (t < nt), then the butterfly over the row's LPR lanes, so every
-// lane of the row ends with the row total. XREG: x from xr (one token); else from xsm ([t][G][XPAD]). Lanes of
-// invalid rows (valid == false) contribute zeros but still take part in the butterfly.
-template <uint32_t TY, int NT, int LPR, int GPL, bool XREG>
-__device__ __forceinline__ void row_dot(const uint8_t *rowp, const uint32_t *grid, const XReg<LPR, (GPL > 0 ? GPL : 1)> &xr,
-                                        const float *xsm, int G, int lr, int nt, bool valid, double (&acc)[NT]) {
+// one group of one row: fast path (planes) or generic (GGUF rows, bit-exact values in four FMA chains)
+template <uint32_t TY, bool SOA, int NT, class XA>
+__device__ __forceinline__ void group_dot(const uint8_t *rowp, int nb, int g, const uint32_t *grid, const XA &xa, int nt,
+                                          float (&r)[NT]) {
+    if constexpr (UseFast<TY, SOA>::v) {
+        Fast<TY>::template group<NT>(rowp, nb, g, grid, xa, nt, r);
+    } else {
+        float c[NT][4];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.0;
-    if (valid) {
-        const int ni = GPL > 0 ? GPL : (G + LPR - 1) / LPR;
+        for (int t = 0; t < NT; ++t) c[t][0] = c[t][1] = c[t][2] = c[t][3] = 0.0f;
+        Dec<TY>::group(rowp, g, grid, [&](int j, float v0, float v1, float v2, float v3) {
 #pragma unroll
-        for (int i = 0; i < ni; ++i) {
-            const int g = lr + LPR * i;
-            if (GPL == 0 && g >= G) break;
-            float c[NT][4];
+            for (int t = 0; t < NT; ++t) {
+                if (NT > 1 && t >= nt) break;
+                const float2 x01 = xa.x2(t, j), x23 = xa.x2(t, j + 2);
+                c[t][0] = __fmaf_rn(v0, x01.x, c[t][0]);
+                c[t][1] = __fmaf_rn(v1, x01.y, c[t][1]);
+                c[t][2] = __fmaf_rn(v2, x23.x, c[t][2]);
+                c[t][3] = __fmaf_rn(v3, x23.y, c[t][3]);
+            }
+        });
 #pragma unroll
-            for (int t = 0; t < NT; ++t) c[t][0] = c[t][1] = c[t][2] = c[t][3] = 0.0f;
-            Dec<TY>::group(rowp, g, grid, [&](int j, float v0, float v1, float v2, float v3) {
+        for (int t = 0; t < NT; ++t)
+            if (NT == 1 || t < nt) r[t] = __fadd_rn(__fadd_rn(c[t][0], c[t][1]), __fadd_rn(c[t][2], c[t][3]));
+    }
+}
+
+// RR rows (1, or 2 when LPR == 32) of one lane group: acc[rr][t] = row rr . x[t]. After the butterfly the total of
+// row rr is held by the lanes of half rr (RR == 2) or by every lane of the row (RR == 1). XREG: x from xr (one
+// token); else from xsm ([t][G][XPAD], token stride G * XPAD). Invalid rows contribute zeros.
+template <uint32_t TY, bool SOA, int NT, int LPR, int GPL, bool XREG, int RR>
+__device__ __forceinline__ void rows_dot(const uint8_t *const (&rowp)[RR], const bool (&valid)[RR], int nb,
+                                         const uint32_t *grid, const XReg<LPR, (GPL > 0 ? GPL : 1)> &xr,
+                                         const float *xsm, int G, int lr, int nt, double (&acc)[RR][NT]) {
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (NT > 1 && t >= nt) break;
-                    float4 xv;
-                    if constexpr (XREG) {
-                        xv = make_float4(xr.v[i][j], xr.v[i][j + 1], xr.v[i][j + 2], xr.v[i][j + 3]);
-                    } else {
-                        xv = *(const float4 *)(xsm + ((size_t)t * G + g) * XPAD + j);
-                    }
-                    c[t][0] = __fmaf_rn(v0, xv.x, c[t][0]);
-                    c[t][1] = __fmaf_rn(v1, xv.y, c[t][1]);
-                    c[t][2] = __fmaf_rn(v2, xv.z, c[t][2]);
-                    c[t][3] = __fmaf_rn(v3, xv.w, c[t][3]);
-                }
-            });
+    for (int q = 0; q < RR; ++q)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[q][t] = 0.0;
+    const int ni = GPL > 0 ? GPL : (G + LPR - 1) / LPR;
+#pragma unroll
+    for (int i = 0; i < ni; ++i) {
+        const int g = lr + LPR * i;
+        if (GPL == 0 && g >= G) break;
+#pragma unroll
+        for (int q = 0; q < RR; ++q) {
+            if (!valid[q]) continue;
+            float r[NT];
+            if constexpr (XREG) {
+                const XRegA xa{xr.v[i], xr.s[i]};
+                group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
+            } else {
+                const XSmA xa{xsm + (size_t)g * XPAD, G * XPAD};
+                group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
+            }
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-                acc[t] += (double)__fadd_rn(__fadd_rn(c[t][0], c[t][1]), __fadd_rn(c[t][2], c[t][3]));
+                if (NT == 1 || t < nt) acc[q][t] += (double)r[t];
         }
     }
+    const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
+        if constexpr (RR == 2) {  // lanes 0-15 keep row 0, lanes 16-31 row 1
+            const bool up = lane & 16;
+            const double send = up ? acc[0][t] : acc[1][t];
+            double keep = up ? acc[1][t] : acc[0][t];
+            keep += __shfl_xor_sync(0xffffffffu, send, 16);
 #pragma unroll
-        for (int o = LPR / 2; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+            for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+            acc[0][t] = keep;
+            acc[1][t] = keep;
+        } else {
+#pragma unroll
+            for (int o = LPR / 2; o > 0; o >>= 1) acc[0][t] += __shfl_xor_sync(0xffffffffu, acc[0][t], o);
+        }
     }
 }
 

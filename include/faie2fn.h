@@ -33,9 +33,10 @@ void fn_pdl(int on);
 void fn_early(int on);
 /* 1: fn_bench_gemv replays one hot copy without an L2 flush. Replaces fn_bench_hot (engine/faie2fn.cu:2822). */
 void fn_bench_hot(int on);
-/* GEMV plan overrides for sweeps (0 keeps a setting): consumer warps per CTA, shared-memory ring KiB, stage KiB,
- * CTAs per SM. Replaces fn_gemv_override(wpt, ks, tb, warps_per_sm) (engine/faie2fn.cu:2786-2791); the B200 plan
- * has no split-K, so its knobs differ. */
+/* GEMV plan overrides for sweeps: warps per CTA (0: automatic by weight size, < 0 keeps), shared-memory ring KiB
+ * (all warps' rings), stage KiB (unused by the per-warp rings; kept for the signature), CTAs per SM (> 0 sets).
+ * Replaces fn_gemv_override(wpt, ks, tb, warps_per_sm) (engine/faie2fn.cu:2786-2791); the B200 plan has no split-K,
+ * so its knobs differ. */
 void fn_gemv_override(int warps, int ring_kb, int stage_kb, int ctas_per_sm);
 /* CTAs per SM of the GEMV grid. Replaces fn_gemv_waves (engine/faie2fn.cu:2793). */
 void fn_gemv_waves(int ctas_per_sm);
