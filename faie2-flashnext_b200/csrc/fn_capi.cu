@@ -276,12 +276,16 @@ FN_API double fn_w_bytes(int h) {
     return w ? (double)w->plan1.rb * w->plan1.rows : -1.0;
 }
 
-// Launch y[t][r] (+acc)= W[r] . x[t] for t < nt on `stream` with device pointers (no synchronisation).
-FN_API int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int acc, void *stream) {
+// Launch y[t][r] (+)= W[r] . x[t] for t < nt on `stream` with device pointers (no synchronisation). flags: bit 0 = add
+// into y; bit 1 = early: x was complete before the previous kernel in the stream started, so the GEMV reads it without
+// waiting and waits for the previous kernel only before it exits (engine/faie2fn.cu:2247-2249); y must not be read by
+// the previous kernel.
+FN_API int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int flags, void *stream) {
     WeightH *w = wget(h);
     if (!w) return fail("fn_w_gemv: bad handle");
     if (nt < 1 || nt > 8) return fail("fn_w_gemv: nt out of range (1..8)");
-    return launch_gemv(nt == 1 ? w->plan1 : w->plan8, w->d, x, xs, y, ys, nt, acc != 0, false, (cudaStream_t)stream);
+    return launch_gemv(nt == 1 ? w->plan1 : w->plan8, w->d, x, xs, y, ys, nt, (flags & 1) != 0, (flags & 2) != 0,
+                       (cudaStream_t)stream);
 }
 
 // The same with host buffers: x (nt x cols) copied in, y (nt x rows) copied out, all on `stream` (x and y should be

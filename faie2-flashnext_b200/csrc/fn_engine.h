@@ -1,6 +1,8 @@
 // Host-side interfaces shared by the engine's translation units.
 #pragma once
 
+#include <unordered_set>
+
 #include "fn_common.cuh"
 
 namespace fn {
@@ -49,7 +51,7 @@ struct Settings {
     bool pdl = true;         // programmatic dependent launch
     bool early = true;       // GEMVs marked early run beside their predecessor
     int warps_per_cta = 0;   // GEMV warps per CTA (0: by weight size)
-    int ring_kb = 112;       // GEMV shared-memory rings per CTA (all warps)
+    int ring_kb = 128;       // GEMV shared-memory rings per CTA (all warps)
     int stage_kb = 16;       // target bytes per pipeline stage
     int ctas_per_sm = 1;     // GEMV CTAs per SM
     int ov_rps = 0;          // overrides (0 = automatic)
@@ -70,6 +72,18 @@ struct DevBuf {
     }
     template <typename T> T *as() const { return (T *)p; }
 };
+
+// allow a kernel the largest dynamic shared memory the SM grants next to its static shared memory (once per kernel)
+template <typename K> cudaError_t allow_max_dynamic_smem(K *k) {
+    static std::unordered_set<const void *> done;
+    if (done.count((const void *)k)) return cudaSuccess;
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227 * 1024 - fa.sharedSizeBytes));
+    if (e == cudaSuccess) done.insert((const void *)k);
+    return e;
+}
 
 // launch with the programmatic-serialization attribute when enabled
 template <typename... P, typename... A>

@@ -70,23 +70,43 @@ __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 __device__ __forceinline__ float hsum2(float2 a, float2 b) { return __fadd_rn(__fadd_rn(a.x, a.y), __fadd_rn(b.x, b.y)); }
 
 // x accessors: a lane's x for group g, token t; pairs x[j], x[j+1] (j even) and the half sums (values 0-15, 16-31)
+// x2: pairs x[j], x[j+1] (j even), scaled by 2^K_t for the formats that convert bytes as denormals (Denorm<TY>);
+// xs: half sums of the unscaled x; inv: 2^(149 - K_t), which turns a sum of denormal products back to q . x
 struct XRegA {  // one token, x of the group in registers
     const float2 (&x)[16];
     const float (&s)[2];
+    float iv;
     __device__ __forceinline__ float2 x2(int, int j) const { return x[j >> 1]; }
     __device__ __forceinline__ float xs(int, int h) const { return s[h]; }
+    __device__ __forceinline__ float inv(int) const { return iv; }
 };
-struct XSmA {  // tokens in shared memory: token t of the group at base + t * ts (32 values, then the 2 half sums)
+struct XSmA {  // tokens in shared memory: token t of the group at base + t * ts (32 values, 2 half sums, inv)
     const float *base;
     int ts;
     __device__ __forceinline__ float2 x2(int t, int j) const { return *(const float2 *)(base + (size_t)t * ts + j); }
     __device__ __forceinline__ float xs(int t, int h) const { return base[(size_t)t * ts + 32 + h]; }
+    __device__ __forceinline__ float inv(int t) const { return base[(size_t)t * ts + 34]; }
 };
 
 // four biased bytes q4 (value_k = byte_k - bias) times x[j + k]: chains a[t][0] (j, j+1) and a[t][1] (j+2, j+3)
 template <int NT, class XA>
 __device__ __forceinline__ void acc_word(uint32_t q4, float2 moff, const XA &xa, int j, int nt, float2 (&a)[NT][2]) {
     const float2 v01 = __fadd2_rn(mag2(q4, 0), moff), v23 = __fadd2_rn(mag2(q4, 2), moff);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (NT > 1 && t >= nt) break;
+        a[t][0] = __ffma2_rn(v01, xa.x2(t, j), a[t][0]);
+        a[t][1] = __ffma2_rn(v23, xa.x2(t, j + 2), a[t][1]);
+    }
+}
+
+// four unsigned bytes q4 as the exact denormals q * 2^-149 (no conversion instruction beyond the byte permute), times
+// the scaled x (x * 2^K): the products q x 2^(K - 149) are formed exactly by the FMA, in the normal range for the K
+// the staging chose; chains as acc_word
+template <int NT, class XA>
+__device__ __forceinline__ void acc_word_dn(uint32_t q4, const XA &xa, int j, int nt, float2 (&a)[NT][2]) {
+    const float2 v01 = make_float2(__uint_as_float(__byte_perm(q4, 0, 0x4440u)), __uint_as_float(__byte_perm(q4, 0, 0x4441u)));
+    const float2 v23 = make_float2(__uint_as_float(__byte_perm(q4, 0, 0x4442u)), __uint_as_float(__byte_perm(q4, 0, 0x4443u)));
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
         if (NT > 1 && t >= nt) break;
@@ -132,6 +152,13 @@ constexpr float MAG = 8388608.0f;
 
 template <uint32_t TY> struct Fast {
     static constexpr bool ok = false;
+};
+// formats whose quant planes are re-encoded at upload (Encoded) and whose bytes become denormals (Denorm)
+template <uint32_t TY> struct Encoded {
+    static constexpr bool v = TY == T_Q4_K || TY == T_Q5_K || TY == T_Q6_K;
+};
+template <uint32_t TY> struct Denorm {
+    static constexpr bool v = TY == T_Q4_K || TY == T_Q5_K;
 };
 
 // ---- 32-value formats ------------------------------------------------------------------------------------------
@@ -353,77 +380,78 @@ template <> struct Fast<T_Q3_K> {
 };
 
 template <> struct Fast<T_Q4_K> {
+    // encoded quant plane: 16 bytes per 32-value group, byte i = q[i] | q[16 + i] << 4 (encode_block<T_Q4_K>)
     static constexpr bool ok = true;
     template <int NT, class XA>
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
-        const int b = g >> 3, ib = g & 7, sh = 4 * (ib & 1);
-        const uint8_t *q = row + 128 * b + 32 * (ib >> 1);
-        const uint4 w0 = lds128(q), w1 = lds128(q + 16);
+        const int b = g >> 3, ib = g & 7;
+        const uint4 w = lds128(row + 16 * g);
         uint32_t sc, m;
         kscale(ib, row + plane_off<T_Q4_K, 1>(nb) + 12 * b, sc, m);
         const uint32_t dm = ld32a(row + plane_off<T_Q4_K, 2>(nb) + 4 * b);
         const float dl = __fmul_rn(h16(dm, 0), u2f(sc)), ml = __fmul_rn(h16(dm, 1), u2f(m));
-        const float2 mo = f2(-MAG);
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
-        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            acc_word<NT>((ws[k] >> sh) & 0x0F0F0F0Fu, mo, xa, 4 * k, nt, a);
-            acc_word<NT>((ws[4 + k] >> sh) & 0x0F0F0F0Fu, mo, xa, 16 + 4 * k, nt, c);
+            acc_word_dn<NT>(ws[k] & 0x0F0F0F0Fu, xa, 4 * k, nt, a);
+            acc_word_dn<NT>((ws[k] >> 4) & 0x0F0F0F0Fu, xa, 16 + 4 * k, nt, c);
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             if (NT > 1 && t >= nt) break;
-            const float s = __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1]));
-            r[t] = __fmaf_rn(dl, s, -__fmul_rn(ml, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
+            const float sq = __fmul_rn(__fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1])), xa.inv(t));
+            r[t] = __fmaf_rn(dl, sq, -__fmul_rn(ml, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
         }
     }
 };
 
 template <> struct Fast<T_Q5_K> {
+    // encoded planes: 16 bytes of low nibbles per group as Q4_K, and a 4-byte word per group whose byte i bit m is
+    // bit 4 of q[4m + i] (encode_block<T_Q5_K>)
     static constexpr bool ok = true;
     template <int NT, class XA>
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
-        const int b = g >> 3, ib = g & 7, sh = 4 * (ib & 1);
-        const uint8_t *q = row + 128 * b + 32 * (ib >> 1), *qh = row + plane_off<T_Q5_K, 1>(nb) + 32 * b;
-        const uint4 w0 = lds128(q), w1 = lds128(q + 16), h0 = lds128(qh), h1 = lds128(qh + 16);
+        const int b = g >> 3, ib = g & 7;
+        const uint4 w = lds128(row + 16 * g);
+        const uint32_t H = ld32a(row + plane_off<T_Q5_K, 1>(nb) + 4 * g);
         uint32_t sc, m;
         kscale(ib, row + plane_off<T_Q5_K, 2>(nb) + 12 * b, sc, m);
         const uint32_t dm = ld32a(row + plane_off<T_Q5_K, 3>(nb) + 4 * b);
         const float dl = __fmul_rn(h16(dm, 0), u2f(sc)), ml = __fmul_rn(h16(dm, 1), u2f(m));
-        const float2 mo = f2(-MAG);
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
-        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const uint32_t hs[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            acc_word<NT>(((ws[k] >> sh) & 0x0F0F0F0Fu) | (((hs[k] >> ib) & 0x01010101u) << 4), mo, xa, 4 * k, nt, a);
-            acc_word<NT>(((ws[4 + k] >> sh) & 0x0F0F0F0Fu) | (((hs[4 + k] >> ib) & 0x01010101u) << 4), mo, xa, 16 + 4 * k,
-                         nt, c);
+            const uint32_t tl = (H << (4 - k)) & 0x10101010u, th = (k < 4 ? (H >> k) : 0u) & 0x10101010u;
+            acc_word_dn<NT>((ws[k] & 0x0F0F0F0Fu) | tl, xa, 4 * k, nt, a);
+            acc_word_dn<NT>(((ws[k] >> 4) & 0x0F0F0F0Fu) | th, xa, 16 + 4 * k, nt, c);
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             if (NT > 1 && t >= nt) break;
-            const float s = __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1]));
-            r[t] = __fmaf_rn(dl, s, -__fmul_rn(ml, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
+            const float sq = __fmul_rn(__fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1])), xa.inv(t));
+            r[t] = __fmaf_rn(dl, sq, -__fmul_rn(ml, __fadd_rn(xa.xs(t, 0), xa.xs(t, 1))));
         }
     }
 };
 
 template <> struct Fast<T_Q6_K> {
+    // encoded planes: 16 bytes of low nibbles per group (byte i = lo[i] | lo[16 + i] << 4), and 8 bytes of the 2-bit
+    // highs per group: word A byte i bits 2m..2m+1 = hi[4m + i], word B the same for values 16.. (encode_block<T_Q6_K>)
     static constexpr bool ok = true;
     template <int NT, class XA>
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
-        const int b = g >> 3, j8 = g & 7, h = j8 >> 2, ls = 4 * ((j8 >> 1) & 1), hsh = 2 * (j8 & 3);
-        const uint8_t *ql = row + 128 * b + 64 * h + 32 * (j8 & 1), *qh = row + plane_off<T_Q6_K, 1>(nb) + 64 * b + 32 * h;
-        const uint4 w0 = lds128(ql), w1 = lds128(ql + 16), h0 = lds128(qh), h1 = lds128(qh + 16);
+        const int b = g >> 3, j8 = g & 7;
+        const uint4 w = lds128(row + 16 * g);
+        const uint2 hb = lds64(row + plane_off<T_Q6_K, 1>(nb) + 8 * g);
         const uint32_t sc = ld16(row + plane_off<T_Q6_K, 2>(nb) + 16 * b + 2 * j8);
         const float d = ldh(row + plane_off<T_Q6_K, 3>(nb) + 2 * b);
         const float ds0 = __fmul_rn(d, (float)(int8_t)(sc & 255u)), ds1 = __fmul_rn(d, (float)(int8_t)(sc >> 8));
@@ -431,16 +459,18 @@ template <> struct Fast<T_Q6_K> {
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
-        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const uint32_t hs[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            acc_word<NT>(((ws[k] >> ls) & 0x0F0F0F0Fu) | (((hs[k] >> hsh) & 0x03030303u) << 4), mo, xa, 4 * k, nt, a);
-            acc_word<NT>(((ws[4 + k] >> ls) & 0x0F0F0F0Fu) | (((hs[4 + k] >> hsh) & 0x03030303u) << 4), mo, xa,
-                         16 + 4 * k, nt, c);
+            // bits 2k..2k+1 of every byte moved to bits 4..5
+            const uint32_t ta = (k < 2 ? (hb.x << (4 - 2 * k)) : (hb.x >> (2 * k - 4))) & 0x30303030u;
+            const uint32_t tb = (k < 2 ? (hb.y << (4 - 2 * k)) : (hb.y >> (2 * k - 4))) & 0x30303030u;
+            acc_word<NT>((ws[k] & 0x0F0F0F0Fu) | ta, mo, xa, 4 * k, nt, a);
+            acc_word<NT>(((ws[k] >> 4) & 0x0F0F0F0Fu) | tb, mo, xa, 16 + 4 * k, nt, c);
         }
 #pragma unroll
-        for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmaf_rn(ds1, hsum2(c[t][0], c[t][1]), __fmul_rn(ds0, hsum2(a[t][0], a[t][1])));
+        for (int t = 0; t < NT; ++t)
+            if (NT == 1 || t < nt) r[t] = __fmaf_rn(ds1, hsum2(c[t][0], c[t][1]), __fmul_rn(ds0, hsum2(a[t][0], a[t][1])));
     }
 };
 
@@ -534,6 +564,63 @@ template <> struct Fast<T_IQ3_XXS> {
         for (int t = 0; t < NT; ++t) if (NT == 1 || t < nt) r[t] = __fmul_rn(db, __fadd_rn(hsum2(a[t][0], a[t][1]), hsum2(c[t][0], c[t][1])));
     }
 };
+
+// ---- re-encoding of the quant planes at upload (a lossless reorder of the same bits; same byte count) -------------
+// q values of one GGUF block (256), as the integers gguf-py decodes (quants.py Q4_K/Q5_K/Q6_K)
+__device__ __forceinline__ int q4k_q(const uint8_t *blk, int n) {
+    const int j = n >> 5, i = n & 31;
+    return (blk[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15;
+}
+__device__ __forceinline__ int q5k_q(const uint8_t *blk, int n) {
+    const int j = n >> 5, i = n & 31;
+    return ((blk[48 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15) | (((blk[16 + i] >> j) & 1) << 4);
+}
+__device__ __forceinline__ int q6k_q(const uint8_t *blk, int n) {
+    const int j = n >> 5, i = n & 31, h = j >> 2;
+    const int lo = (blk[64 * h + 32 * (j & 1) + i] >> (4 * ((j >> 1) & 1))) & 15;
+    const int hi = (blk[128 + 32 * h + i] >> (2 * (j & 3))) & 3;
+    return lo | (hi << 4);
+}
+// write block b (GGUF bytes blk) of a row of nb blocks into the encoded planes of dst (the row start)
+template <uint32_t TY> __device__ void encode_block(const uint8_t *blk, uint8_t *dst, int b, int nb) {
+    if constexpr (TY == T_Q4_K || TY == T_Q5_K) {
+        const int so = TY == T_Q4_K ? 128 * nb : 160 * nb, mo = so + 12 * nb;  // scale and d/dmin planes
+        for (int g = 0; g < 8; ++g) {
+            for (int i = 0; i < 16; ++i) {
+                const int lo = TY == T_Q4_K ? q4k_q(blk, 32 * g + i) : q5k_q(blk, 32 * g + i);
+                const int hi = TY == T_Q4_K ? q4k_q(blk, 32 * g + 16 + i) : q5k_q(blk, 32 * g + 16 + i);
+                dst[128 * b + 16 * g + i] = (uint8_t)((lo & 15) | ((hi & 15) << 4));
+            }
+            if constexpr (TY == T_Q5_K) {
+                uint32_t H = 0;
+                for (int m = 0; m < 8; ++m)
+                    for (int i = 0; i < 4; ++i) H |= (uint32_t)((q5k_q(blk, 32 * g + 4 * m + i) >> 4) & 1) << (8 * i + m);
+                for (int k = 0; k < 4; ++k) dst[128 * nb + 32 * b + 4 * g + k] = (uint8_t)(H >> (8 * k));
+            }
+        }
+        for (int k = 0; k < 12; ++k) dst[so + 12 * b + k] = blk[4 + k];
+        for (int k = 0; k < 4; ++k) dst[mo + 4 * b + k] = blk[k];
+    } else if constexpr (TY == T_Q6_K) {
+        for (int g = 0; g < 8; ++g) {
+            uint32_t A = 0, B = 0;
+            for (int i = 0; i < 16; ++i) {
+                const int lo = q6k_q(blk, 32 * g + i), hi = q6k_q(blk, 32 * g + 16 + i);
+                dst[128 * b + 16 * g + i] = (uint8_t)((lo & 15) | ((hi & 15) << 4));
+            }
+            for (int m = 0; m < 4; ++m)
+                for (int i = 0; i < 4; ++i) {
+                    A |= (uint32_t)(q6k_q(blk, 32 * g + 4 * m + i) >> 4) << (8 * i + 2 * m);
+                    B |= (uint32_t)(q6k_q(blk, 32 * g + 16 + 4 * m + i) >> 4) << (8 * i + 2 * m);
+                }
+            for (int k = 0; k < 4; ++k) {
+                dst[128 * nb + 64 * b + 8 * g + k] = (uint8_t)(A >> (8 * k));
+                dst[128 * nb + 64 * b + 8 * g + 4 + k] = (uint8_t)(B >> (8 * k));
+            }
+        }
+        for (int k = 0; k < 16; ++k) dst[192 * nb + 16 * b + k] = blk[192 + k];
+        for (int k = 0; k < 2; ++k) dst[208 * nb + 2 * b + k] = blk[208 + k];
+    }
+}
 
 // ---- layout descriptor for the host (repack) ---------------------------------------------------------------------
 struct PlaneDesc {

@@ -46,16 +46,34 @@ __global__ void k_plane_repack(const uint8_t *__restrict__ src, uint64_t rb, uin
     }
 }
 
+// formats with re-encoded quant planes: one thread per (row, block) writes the block's encoded planes
+template <uint32_t TY>
+__global__ void k_encode(const uint8_t *__restrict__ src, uint64_t rb, uint8_t *__restrict__ dst, uint32_t ldw, int rows,
+                         int nb, int bytes) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * nb) return;
+    const int r = (int)(i / nb), b = (int)(i % nb);
+    encode_block<TY>(src + (size_t)r * rb + (size_t)b * bytes, dst + (size_t)r * ldw, b, nb);
+}
+
 int launch_plane_repack(uint32_t type, const uint8_t *src, uint64_t rb, uint8_t *dst, uint32_t ldw, int rows, int cols,
                         cudaStream_t s) {
     int qk, bytes;
     if (!type_info(type, qk, bytes) || cols % qk || row_bytes(type, cols) != rb) return fail("repack: bad type/shape");
     if (rows == 0) return 0;
     PlaneDesc pd;
-    dispatch_type(type, [&]<uint32_t TY>() { pd = plane_desc<TY>(); });
+    bool enc = false;
     const int nb = cols / qk;
     const long long n = (long long)rows * nb;
-    k_plane_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, rb, dst, ldw, rows, nb, bytes, pd);
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    dispatch_type(type, [&]<uint32_t TY>() {
+        pd = plane_desc<TY>();
+        if constexpr (Encoded<TY>::v) {
+            enc = true;
+            k_encode<TY><<<blocks, 256, 0, s>>>(src, rb, dst, ldw, rows, nb, bytes);
+        }
+    });
+    if (!enc) k_plane_repack<<<blocks, 256, 0, s>>>(src, rb, dst, ldw, rows, nb, bytes, pd);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(std::string("repack launch: ") + cudaGetErrorString(e));
     return 0;

@@ -57,8 +57,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     if (!a.early) pdl_wait();
     const float *x = after_wait(a.x);
     const int nt = a.nt;
-    stage_x(xsm, x, a.xs, nt, a.G);
-    __syncthreads();
+    stage_x(xsm, x, a.xs, nt, a.G, ScaleX<TY, true>::v);
     pdl_trigger();
 
     const int lr = lane % LPR, sub = lane / LPR;
@@ -120,12 +119,8 @@ template <uint32_t TY> cudaError_t gemv_launch_t(const GemvPlan &p, const GemvAr
         else if (p.lpr == 16) k = k_gemv<TY, 8, 16, 0, false>;
         else k = k_gemv<TY, 8, 32, 0, false>;
     }
-    static std::unordered_set<const void *> configured;  // one attribute call per kernel, outside graph capture
-    if (!configured.count((const void *)k)) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        configured.insert((const void *)k);
-    }
+    const cudaError_t e = allow_max_dynamic_smem(k);
+    if (e != cudaSuccess) return e;
     return launch_k(k, dim3(p.ctas), dim3(p.threads), smem, s, a);
 }
 

@@ -87,7 +87,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
     if (nt < 1 || nt > 8) return fail("moe: nt out of range (1..8)");
     if (ls < p.ne + 1) return fail("moe: logits stride must hold ne + 1 columns (router + shared gate)");
     if (((uintptr_t)x & 15) || ((uintptr_t)act & 15) || (p.d & 3) || (p.ffe & 3)) return fail("moe: x/act alignment");
-    const int ks = p.k + 1, threads = 256;
+    const int ks = p.k + 1;
     // ---- gate / up
     {
         MoeGuArgs a;

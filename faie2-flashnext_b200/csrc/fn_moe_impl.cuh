@@ -170,8 +170,7 @@ __global__ void __launch_bounds__(256, 1) k_moe_gu(const MoeGuArgs a) {
         a.sel_out[t * a.k + i] = sel[t * 16 + i];
         a.w_out[t * a.k + i] = wsel[t * 16 + i];
     }
-    stage_x(xsm, x, a.d, a.nt, G);
-    __syncthreads();
+    stage_x(xsm, x, a.d, a.nt, G, ScaleX<TY, SOA>::v);
     pdl_trigger();
 
     auto rows_ptr = [&](long long u, const uint8_t *&g, const uint8_t *&up) {
@@ -308,8 +307,7 @@ __global__ void __launch_bounds__(256, 1) k_moe_down(const MoeDownArgs a) {
     stage_grid<TY>(grid);
     pdl_wait();
     const float *act = after_wait(a.act);
-    stage_x(xsm, act + (size_t)t * ks * a.ffe, a.ffe, ks, G);
-    __syncthreads();
+    stage_x(xsm, act + (size_t)t * ks * a.ffe, a.ffe, ks, G, ScaleX<TY, SOA>::v);
     pdl_trigger();
 
     constexpr int RPW = 32 / LPR;
@@ -365,12 +363,8 @@ cudaError_t moe_gu_launch_t(const MoeGuArgs &a, bool planes, int nt, int G, int 
     void (*k)(const MoeGuArgs) = nullptr;
     if (planes) k = nt == 1 && G == 64 ? k_moe_gu<TY, 32, 2, true, true> : k_moe_gu<TY, 32, 0, false, true>;
     else k = nt == 1 && G == 64 ? k_moe_gu<TY, 32, 2, true, false> : k_moe_gu<TY, 32, 0, false, false>;
-    static std::unordered_set<const void *> done;
-    if (!done.count((const void *)k)) {
-        const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        done.insert((const void *)k);
-    }
+    const cudaError_t e = allow_max_dynamic_smem(k);
+    if (e != cudaSuccess) return e;
     return launch_k(k, dim3(ctas), dim3(256), smem, s, a);
 }
 
@@ -379,12 +373,8 @@ cudaError_t moe_down_launch_t(const MoeDownArgs &a, bool planes, int lpr, dim3 g
     void (*k)(const MoeDownArgs) = nullptr;
     if (planes) k = lpr == 16 ? k_moe_down<TY, 16, true> : k_moe_down<TY, 32, true>;
     else k = lpr == 16 ? k_moe_down<TY, 16, false> : k_moe_down<TY, 32, false>;
-    static std::unordered_set<const void *> done;
-    if (!done.count((const void *)k)) {
-        const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        done.insert((const void *)k);
-    }
+    const cudaError_t e = allow_max_dynamic_smem(k);
+    if (e != cudaSuccess) return e;
     return launch_k(k, grid, dim3(256), smem, s, a);
 }
 

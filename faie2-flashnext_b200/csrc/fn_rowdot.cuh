@@ -36,34 +36,64 @@ template <uint32_t TY> __device__ __forceinline__ void stage_grid(uint32_t *grid
 template <uint32_t TY, bool SOA> struct UseFast {
     static constexpr bool v = SOA && Fast<TY>::ok;
 };
+// x is staged scaled (stage_x denorm) when the fast path converts TY's bytes as denormals
+template <uint32_t TY, bool SOA> struct ScaleX {
+    static constexpr bool v = UseFast<TY, SOA>::v && Denorm<TY>::v;
+};
 
 constexpr int XPAD = 36;  // floats per staged x group: 32 values, the two 16-value sums, 2 spare (bank spread)
 
-// x[t][c] (token stride xs floats, 16-byte aligned, xs % 4 == 0) -> xsm[(t * G + g) * XPAD + j], and the half sums
-// sum(x[16h .. 16h + 15]) (pairwise, fixed order) at + 32 + h. Every thread calls this.
-__device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int nt, int G) {
+// x[t][c] (token stride xs floats, 16-byte aligned, xs % 4 == 0) -> xsm[(t * G + g) * XPAD + j], the half sums
+// sum(x[16h .. 16h + 15]) (pairwise, fixed order, unscaled) at + 32 + h, and for formats that convert bytes as
+// denormals (denorm) the values scaled by 2^K_t with K_t = 124 - exponent(max_c |x[t][c]|) clamped to [22, 127]
+// (an exact power-of-two scaling; the products q * 2^-149 * x * 2^K_t then stay in the normal range) and
+// 2^(149 - K_t) at + 34. nt <= 32. Every thread calls this; it ends with a __syncthreads.
+__device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int nt, int G, bool denorm) {
+    __shared__ int s_xmax[32];
+    if (denorm) {
+        if ((int)threadIdx.x < nt) s_xmax[threadIdx.x] = 0;
+        __syncthreads();
+    }
     for (int idx = threadIdx.x; idx < nt * G * 2; idx += blockDim.x) {
         const int t = idx / (G * 2), r = idx - t * (G * 2), g = r >> 1, h = r & 1;
         const float4 *src = (const float4 *)(x + (size_t)t * xs + g * 32 + 16 * h);
         float *dst = xsm + ((size_t)t * G + g) * XPAD;
         float4 v[4];
+        float mx = 0.0f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             v[q] = src[q];
             *(float4 *)(dst + 16 * h + 4 * q) = v[q];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w))));
         }
         float p[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) p[q] = __fadd_rn(__fadd_rn(v[q].x, v[q].y), __fadd_rn(v[q].z, v[q].w));
         dst[32 + h] = __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3]));
+        if (denorm) atomicMax(&s_xmax[t], __float_as_int(mx));  // non-negative floats order like their bits
     }
+    __syncthreads();
+    if (!denorm) return;
+    for (int idx = threadIdx.x; idx < nt * G * 2; idx += blockDim.x) {
+        const int t = idx / (G * 2), r = idx - t * (G * 2), g = r >> 1, h = r & 1;
+        const int e = ((s_xmax[t] >> 23) & 255) - 127;  // exponent of the largest |x| (0 -> -127)
+        const int K = max(22, min(127, 124 - e));
+        const float sc = __int_as_float((K + 127) << 23);
+        float *dst = xsm + ((size_t)t * G + g) * XPAD;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) dst[16 * h + q] = __fmul_rn(dst[16 * h + q], sc);
+        if (h == 0) dst[34] = __int_as_float((149 - K + 127) << 23);
+    }
+    __syncthreads();
 }
 
 // a lane's x slice in registers (one token): groups lr + LPR * i, i < GPL
 template <int LPR, int GPL> struct XReg {
     float2 v[GPL][16];
     float s[GPL][2];
+    float iv = 1.0f;
     __device__ __forceinline__ void load(const float *xsm, int lr) {
+        iv = xsm[34];
 #pragma unroll
         for (int i = 0; i < GPL; ++i) {
             const float *src = xsm + (size_t)(lr + LPR * i) * XPAD;
@@ -127,7 +157,7 @@ __device__ __forceinline__ void rows_dot(const uint8_t *const (&rowp)[RR], const
             if (!valid[q]) continue;
             float r[NT];
             if constexpr (XREG) {
-                const XRegA xa{xr.v[i], xr.s[i]};
+                const XRegA xa{xr.v[i], xr.s[i], xr.iv};
                 group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
             } else {
                 const XSmA xa{xsm + (size_t)g * XPAD, G * XPAD};

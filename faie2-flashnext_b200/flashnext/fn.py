@@ -116,8 +116,9 @@ class FN:
     def w_bytes(self, h) -> float:
         return self.d.fn_w_bytes(h)
 
-    def w_gemv(self, h, x_ptr, xs, y_ptr, ys, nt=1, acc=0, stream=0):
-        self.check(self.d.fn_w_gemv(h, C.c_void_p(x_ptr), xs, C.c_void_p(y_ptr), ys, nt, acc, C.c_void_p(stream)))
+    def w_gemv(self, h, x_ptr, xs, y_ptr, ys, nt=1, flags=0, stream=0):
+        """flags: 1 = add into y, 2 = early (x complete before the previous kernel started)."""
+        self.check(self.d.fn_w_gemv(h, C.c_void_p(x_ptr), xs, C.c_void_p(y_ptr), ys, nt, flags, C.c_void_p(stream)))
 
     def w_gemv_host(self, h, x_ptr, nt, y_ptr, stream=0):
         self.check(self.d.fn_w_gemv_host(h, C.c_void_p(x_ptr), nt, C.c_void_p(y_ptr), C.c_void_p(stream)))

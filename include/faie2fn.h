@@ -67,9 +67,12 @@ int fn_w_create(uint32_t type, const uint8_t *W, int rows, int cols);
 int fn_w_free(int h);
 /* GGUF bytes of the weight (rows x row_bytes), the bytes one GEMV must read. */
 double fn_w_bytes(int h);
-/* Launch y[t][r] (+= if acc) W[r] . x[t] for t < nt <= 8 on a CUDA stream (device pointers, token strides xs, ys
- * in floats; x 16-byte aligned). Replaces gemv() (engine/faie2fn.cu:2250-2281). */
-int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int acc, void *stream);
+/* Launch y[t][r] (+)= W[r] . x[t] for t < nt <= 8 on a CUDA stream (device pointers, token strides xs, ys in
+ * floats; x 16-byte aligned). flags: bit 0 adds into y; bit 1 = early (x was complete before the previous kernel in
+ * the stream started, and the previous kernel does not read y: read x without waiting, wait for the previous kernel
+ * before exiting). Replaces gemv()
+ * (engine/faie2fn.cu:2250-2281) and its acc / early arguments. */
+int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int flags, void *stream);
 /* The same with host buffers x (nt x cols) and y (nt x rows), copied on the stream; does not synchronise. */
 int fn_w_gemv_host(int h, const float *x, int nt, float *y, void *stream);
 /* Synchronise a stream and report any device-side error (a bounded wait that ran out). */

@@ -132,3 +132,24 @@ def test_plan_is_batch_independent(fn):
     p = fn.gemv_plan(12, 4096, 2048)
     assert p["ldw"] == 1152 and p["lpr"] == 32 and p["gpl"] == 2
     assert p["ctas"] >= 1 and p["rows_per_stage"] >= 1
+
+
+@pytest.mark.parametrize("qtype", [BY_NAME[n] for n in ("Q4_K", "Q5_K", "Q6_K", "Q4_1", "Q2_K")])
+@pytest.mark.parametrize("scale", [1e-30, 1e-12, 1e12, 1e28])
+def test_gemv_activation_scale_extremes(fn, qtype, scale):
+    """The fast paths scale x by a per-token power of two (exact) so byte values can enter the FMAs as denormals:
+    results must keep full relative accuracy for tiny and huge activations, in a batch whose tokens differ by 40
+    orders of magnitude, and every token must match its own single-token result bit for bit."""
+    rows, cols = 300, 2048
+    rng = np.random.default_rng(int(np.log10(scale)) + 100)
+    raw = random_blocks(qtype, rows, cols, rng)
+    x = random_x(3, cols, rng)
+    x[0] *= np.float32(scale)
+    x[2] *= np.float32(1e-10)
+    y = fn.gemv(qtype, raw, rows, cols, x)
+    W = O.dequant_rows(raw, qtype, rows, cols)
+    for t in range(3):
+        y64 = O.gemv64(W, x[t:t + 1])
+        assert O.gemv_rel_err(y[t:t + 1], y64) <= GEMV_TOL, f"token {t}"
+        y1 = fn.gemv(qtype, raw, rows, cols, x[t:t + 1])
+        assert np.array_equal(bits(y1), bits(y[t:t + 1]))
