@@ -224,9 +224,16 @@ def main():
 
     # the GEMVs of a step are independent, so each is launched early: it reads its x without waiting for the kernel
     # before it and waits for that kernel only before it exits (the reference's early-GEMV protocol)
+    # the lm_head (last) carries the fused argmax, as in a decode step (lm_head GEMV + k_argmax)
+    amax_d = torch.zeros(8, dtype=torch.int32, device="cuda")
+
     def launch(idx, s, early=True):
         q, r, c, _ = work[idx]
-        f.w_gemv(hs[idx], xs[idx].data_ptr(), c, ys[idx].data_ptr(), r, 1, 2 if early else 0, s)
+        if idx == len(work) - 1:
+            f.w_gemv_argmax(hs[idx], xs[idx].data_ptr(), c, ys[idx].data_ptr(), r, 1, 2 if early else 0, 0,
+                            amax_d.data_ptr(), 0, s)
+        else:
+            f.w_gemv(hs[idx], xs[idx].data_ptr(), c, ys[idx].data_ptr(), r, 1, 2 if early else 0, s)
 
     for i in range(len(work)):  # first launches outside capture (kernel attributes, error-word address)
         launch(i, stream.cuda_stream, early=False)
@@ -280,17 +287,20 @@ def main():
     value = world * step_bytes * K / (ms / 1e3) / 1e9
 
     # e2e: through the C ABI with pinned host buffers, host<->device copies inside the timed region
+    # (the lm_head returns its token id, as a decode step does; the other GEMVs their outputs)
     xh = [torch.empty(w[2], dtype=torch.float32, pin_memory=True) for w in work]
-    yh = [torch.empty(w[1], dtype=torch.float32, pin_memory=True) for w in work]
+    yh = [torch.empty(w[1], dtype=torch.float32, pin_memory=True) for w in work[:-1]]
+    ih = torch.zeros(1, dtype=torch.int32, pin_memory=True)
     for i, x in enumerate(xs):
         xh[i].copy_(x.cpu())
     h2d = sum(4 * w[2] for w in work)
-    d2h = sum(4 * w[1] for w in work)
+    d2h = sum(4 * w[1] for w in work[:-1]) + 4
     Ke = max(3, min(K, 200))
 
     def e2e_step():
-        for i in range(len(work)):
+        for i in range(len(work) - 1):
             f.w_gemv_host(hs[i], xh[i].data_ptr(), 1, yh[i].data_ptr(), stream.cuda_stream)
+        f.w_gemv_argmax_host(hs[-1], xh[-1].data_ptr(), 1, 0, ih.data_ptr(), stream.cuda_stream)
         f.sync(stream.cuda_stream)
 
     for _ in range(3):
@@ -309,7 +319,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = world * step_bytes * Ke / (e2e_ms / 1e3) / 1e9
-    ok = np.isfinite(yh[-1].numpy()).all()
+    ok = bool(all(np.isfinite(y.numpy()).all() for y in yh)) and 0 <= int(ih[0]) < work[-1][1]
+    ok = ok and int(ih[0]) == int(amax_d[0].item())  # same x: the host-path token equals the graph's
 
     peak, peak_kind = measured_peak()
     achieved = head_bytes / (head_ms / 1e3) / 1e9
@@ -319,7 +330,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "config2 format sweep: 13 formats x (2048x4096, 4096x2048, 512x2048) + Q6_K lm_head "
-                               "151936x2048, bs=1, 40 GEMVs per step",
+                               "151936x2048 with fused argmax, bs=1, 40 GEMVs per step (e2e: the lm_head returns its token id)",
                    "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (385 MB of weights per step, each "
                    "read once per step)", "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
                    "frac_of_measured_peak": round(value / world / peak, 4)},
@@ -327,7 +338,7 @@ def main():
                 "steps": Ke, "outputs_finite": bool(ok)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "k_gemv<Q6_K> lm_head 151936x2048", "mean_launch_us": round(head_ms * 1e3, 2),
+                     "kernel": "k_gemv<Q6_K> lm_head 151936x2048 + fused argmax", "mean_launch_us": round(head_ms * 1e3, 2),
                      "alg_bytes_per_launch": head_bytes},
         "split_ms_per_step": {"39 sweep GEMVs": round(small_ms, 5), "lm_head": round(head_ms, 5)},
         "gpu_launches": K * len(work),

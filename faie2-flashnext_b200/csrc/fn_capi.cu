@@ -86,6 +86,9 @@ struct WeightH {
     uint8_t *d = nullptr;   // rows at stride plan.ldw
     int dev = 0;
     float *xbuf = nullptr, *ybuf = nullptr;  // device staging for host-buffer calls
+    unsigned long long *kacc = nullptr;      // fused-argmax key maxima [8] and ticket (zero between launches)
+    unsigned int *ticket = nullptr;
+    int *ibuf = nullptr;                     // device staging of host-buffer argmax calls [8]
 };
 static std::vector<WeightH *> g_w;
 static std::mutex g_w_mu;
@@ -247,9 +250,16 @@ FN_API int fn_w_create(uint32_t type, const uint8_t *Wh, int rows, int cols) {
         cudaMemcpy(raw.p, Wh, (size_t)p.rb * rows, cudaMemcpyHostToDevice) != cudaSuccess ||
         launch_plane_repack(type, raw.as<uint8_t>(), p.rb, w->d, p.ldw, rows, cols, 0) != 0 ||
         cudaDeviceSynchronize() != cudaSuccess ||
-        cudaMalloc(&w->xbuf, (size_t)8 * cols * 4) != cudaSuccess || cudaMalloc(&w->ybuf, (size_t)8 * rows * 4) != cudaSuccess) {
+        cudaMalloc(&w->xbuf, (size_t)8 * cols * 4) != cudaSuccess || cudaMalloc(&w->ybuf, (size_t)8 * rows * 4) != cudaSuccess ||
+        cudaMalloc(&w->kacc, 256) != cudaSuccess || cudaMemset(w->kacc, 0, 256) != cudaSuccess ||
+        cudaMalloc(&w->ticket, 256) != cudaSuccess || cudaMemset(w->ticket, 0, 256) != cudaSuccess ||
+        cudaMalloc(&w->ibuf, 8 * sizeof(int)) != cudaSuccess) {
         cudaFree(w->d);
         cudaFree(w->xbuf);
+        cudaFree(w->ybuf);
+        cudaFree(w->kacc);
+        cudaFree(w->ticket);
+        cudaFree(w->ibuf);
         delete w;
         return fail("fn_w_create: device allocation/copy failed");
     }
@@ -264,6 +274,9 @@ FN_API int fn_w_free(int h) {
     cudaFree(w->d);
     cudaFree(w->xbuf);
     cudaFree(w->ybuf);
+    cudaFree(w->kacc);
+    cudaFree(w->ticket);
+    cudaFree(w->ibuf);
     delete w;
     std::lock_guard<std::mutex> l(g_w_mu);
     g_w[h - 1] = nullptr;
@@ -286,6 +299,106 @@ FN_API int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, in
     if (nt < 1 || nt > 8) return fail("fn_w_gemv: nt out of range (1..8)");
     return launch_gemv(nt == 1 ? w->plan1 : w->plan8, w->d, x, xs, y, ys, nt, (flags & 1) != 0, (flags & 2) != 0,
                        (cudaStream_t)stream);
+}
+
+// The lm_head GEMV with the fused argmax (k_argmax, engine/faie2fn.cu:1910-1935, folded into the GEMV's last CTA):
+// y (nullable: logits not written) as fn_w_gemv; index[t] (nullable) = the lowest global row index of the largest
+// value for token t, global index = row0 + local row; keys[t] (nullable, may be a peer GPU's memory) = the 64-bit
+// ordering key of that winner, for combining the keys of a row-split lm_head by max (fn_argmax_keys). One such call at
+// a time per handle (the key maxima and the ticket belong to the handle).
+FN_API int fn_w_gemv_argmax(int h, const float *x, int xs, float *y, int ys, int nt, int flags, int row0, int *index,
+                            unsigned long long *keys, void *stream) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_gemv_argmax: bad handle");
+    if (nt < 1 || nt > 8) return fail("fn_w_gemv_argmax: nt out of range (1..8)");
+    GemvArgmax am;
+    am.row0 = row0;
+    am.index = index;
+    am.key = keys;
+    am.kacc = w->kacc;
+    am.ticket = w->ticket;
+    return launch_gemv(nt == 1 ? w->plan1 : w->plan8, w->d, x, xs, y, ys, nt, (flags & 1) != 0, (flags & 2) != 0,
+                       (cudaStream_t)stream, &am);
+}
+
+// The same with host buffers: x_host [nt][cols] in, y_host (nullable) [nt][rows] and index_host [nt] out, copies on
+// `stream` (asynchronous; pinned buffers make the copies asynchronous to the host).
+FN_API int fn_w_gemv_argmax_host(int h, const float *xh, int nt, float *yh, int *ih, void *stream) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_gemv_argmax_host: bad handle");
+    if (nt < 1 || nt > 8) return fail("fn_w_gemv_argmax_host: nt out of range (1..8)");
+    cudaStream_t s = (cudaStream_t)stream;
+    const GemvPlan &p = nt == 1 ? w->plan1 : w->plan8;
+    GemvArgmax am;
+    am.index = w->ibuf;
+    am.kacc = w->kacc;
+    am.ticket = w->ticket;
+    FN_CK(cudaMemcpyAsync(w->xbuf, xh, (size_t)nt * p.cols * 4, cudaMemcpyHostToDevice, s));
+    if (launch_gemv(p, w->d, w->xbuf, p.cols, yh ? w->ybuf : nullptr, p.rows, nt, false, false, s, &am)) return -1;
+    if (yh) FN_CK(cudaMemcpyAsync(yh, w->ybuf, (size_t)nt * p.rows * 4, cudaMemcpyDeviceToHost, s));
+    FN_CK(cudaMemcpyAsync(ih, w->ibuf, (size_t)nt * sizeof(int), cudaMemcpyDeviceToHost, s));
+    return 0;
+}
+
+// argmax of logits[t][0..n) (token stride ls, device pointers) into out[t], on `stream` (engine/faie2fn.cu:1910-1935)
+FN_API int fn_argmax(const float *logits, int ls, int n, int nt, int *out, void *stream) {
+    return launch_argmax(logits, ls, n, nt, out, (cudaStream_t)stream);
+}
+
+// out[t] = the winning index among the keys [nranks][nt] of a row-split lm_head (device pointers, on `stream`)
+FN_API int fn_argmax_keys(const unsigned long long *keys, int nranks, int nt, int *out, void *stream) {
+    return launch_argmax_keys(keys, nranks, nt, out, (cudaStream_t)stream);
+}
+
+// synchronous hook: argmax of host logits [nt][n] -> host out [nt]
+FN_API int fn_test_argmax(const float *lh, int n, int nt, int *oh) {
+    if (n < 1 || nt < 1 || nt > 65535) return fail("fn_test_argmax: bad shape");
+    FN_CK(cudaSetDevice(hook_device()));
+    cudaStream_t s = hook_stream();
+    DevBuf l, o;
+    FN_CK(cudaMalloc(&l.p, (size_t)nt * n * 4));
+    FN_CK(cudaMalloc(&o.p, (size_t)nt * 4));
+    FN_CK(cudaMemcpyAsync(l.p, lh, (size_t)nt * n * 4, cudaMemcpyHostToDevice, s));
+    if (launch_argmax(l.as<float>(), n, n, nt, o.as<int>(), s)) return -1;
+    FN_CK(cudaMemcpyAsync(oh, o.p, (size_t)nt * 4, cudaMemcpyDeviceToHost, s));
+    FN_CK(cudaStreamSynchronize(s));
+    return check_dev_error("fn_test_argmax");
+}
+
+// synchronous hook: the lm_head GEMV with fused argmax on GGUF rows (as fn_test_gemv), y_host nullable
+FN_API int fn_test_gemv_argmax(uint32_t type, const uint8_t *Wh, int rows, int cols, const float *xh, int nt, float *yh,
+                               int *ih) {
+    GemvPlan p;
+    if (nt < 1 || nt > 8) return fail("nt out of range (1..8)");
+    FN_CK(cudaSetDevice(hook_device()));
+    if (!plan_gemv(p, type, rows, cols, nt == 1 ? 1 : 8)) return fail("unsupported type/shape");
+    cudaStream_t s = hook_stream();
+    DevBuf W, raw, x, y, idx, kacc, ticket;
+    FN_CK(cudaMalloc(&W.p, plan_weight_bytes(p)));
+    FN_CK(cudaMalloc(&raw.p, (size_t)p.rb * rows));
+    FN_CK(cudaMalloc(&x.p, (size_t)nt * cols * 4));
+    FN_CK(cudaMalloc(&y.p, (size_t)nt * rows * 4));
+    FN_CK(cudaMalloc(&idx.p, 8 * sizeof(int)));
+    FN_CK(cudaMalloc(&kacc.p, 256));
+    FN_CK(cudaMalloc(&ticket.p, 256));
+    FN_CK(cudaMemsetAsync(kacc.p, 0, 256, s));
+    FN_CK(cudaMemsetAsync(ticket.p, 0, 256, s));
+    FN_CK(cudaMemcpyAsync(raw.p, Wh, (size_t)p.rb * rows, cudaMemcpyHostToDevice, s));
+    if (launch_plane_repack(type, raw.as<uint8_t>(), p.rb, W.as<uint8_t>(), p.ldw, rows, cols, s)) return -1;
+    FN_CK(cudaMemcpyAsync(x.p, xh, (size_t)nt * cols * 4, cudaMemcpyHostToDevice, s));
+    GemvArgmax am;
+    am.index = idx.as<int>();
+    am.kacc = kacc.as<unsigned long long>();
+    am.ticket = ticket.as<unsigned int>();
+    // twice: the second launch finds the key maxima and the ticket the first one cleared
+    for (int rep = 0; rep < 2; ++rep)
+        if (launch_gemv(p, W.as<uint8_t>(), x.as<float>(), cols, yh ? y.as<float>() : nullptr, rows, nt, false, false, s,
+                        &am))
+            return -1;
+    if (yh) FN_CK(cudaMemcpyAsync(yh, y.p, (size_t)nt * rows * 4, cudaMemcpyDeviceToHost, s));
+    FN_CK(cudaMemcpyAsync(ih, idx.p, (size_t)nt * sizeof(int), cudaMemcpyDeviceToHost, s));
+    FN_CK(cudaStreamSynchronize(s));
+    return check_dev_error("fn_test_gemv_argmax");
 }
 
 // The same with host buffers: x (nt x cols) copied in, y (nt x rows) copied out, all on `stream` (x and y should be

@@ -32,11 +32,31 @@ struct GemvPlan {
 bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap);
 size_t plan_weight_bytes(const GemvPlan &p);  // device bytes of the padded weight
 
+// Fused argmax epilogue of a GEMV (the lm_head): per token, the lowest global row index among the rows holding the
+// largest value (NaN never wins, -0 ranks as +0, index 0 when no value exceeds -inf), as in k_argmax
+// (engine/faie2fn.cu:1910-1935). Every CTA folds its best key into kacc[t] by an atomic max; the CTA that takes the
+// last ticket publishes the winner and clears kacc and the ticket. The key orders (value, -index); row0 is the global
+// index of the plan's row 0 (row split across GPUs: keys of the slices combine by max). One launch at a time may use
+// a given kacc / ticket.
+struct GemvArgmax {
+    int row0 = 0;
+    int *index = nullptr;                // [nt] (nullable)
+    unsigned long long *key = nullptr;   // [nt] (nullable; may be a peer GPU's memory)
+    unsigned long long *kacc = nullptr;  // [8] scratch, zero between launches
+    unsigned int *ticket = nullptr;      // zero between launches
+};
+
 // y[t][r] (+)= W[r] . x[t] for t < nt <= p.ntcap. W: rows at stride p.ldw bytes (16-byte aligned); x, y: fp32 with
 // token strides xs, ys (x 16-byte aligned, xs a multiple of 4). early: x was complete before the previous kernel
-// started, so the GEMV does not wait for it before reading x (it waits before it exits).
+// started, so the GEMV does not wait for it before reading x (it waits before it exits). y may be null when am is
+// given (no logits written).
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
-                bool early, cudaStream_t s);
+                bool early, cudaStream_t s, const GemvArgmax *am = nullptr);
+
+// argmax of logits[t][0..n) for t < nt (token stride ls): same selection rule as the fused epilogue
+int launch_argmax(const float *logits, int ls, int n, int nt, int *out, cudaStream_t s);
+// out[t] = the index of the largest key keys[r][t] over r < nranks (per-rank keys of a row-split lm_head)
+int launch_argmax_keys(const unsigned long long *keys, int nranks, int nt, int *out, cudaStream_t s);
 
 // GGUF rows (stride rb) -> the engine's row layout (planes for formats with a fast path, else unchanged) at stride
 // ldw. src and dst must not overlap.

@@ -113,6 +113,10 @@ int launch_dequant(uint32_t type, const uint8_t *W, uint64_t rb, int rows, int c
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// dynamic shared memory a GEMV may use: the SM's 227 KiB less 5 KiB for the kernel's static shared memory (x scale
+// maxima, argmax keys)
+constexpr size_t kDynSmem = 227 * 1024 - 5 * 1024;
+
 // dynamic shared memory of a launch of plan p with nt tokens
 static size_t gemv_smem(const GemvPlan &p, int nt) {
     return align_up(p.x_off + (size_t)nt * p.G * XPAD * 4, 128);
@@ -137,10 +141,10 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     p.rps = ru;
     p.stage_bytes = (uint32_t)align_up((size_t)ru * p.ldw, 128);
     // budget: x for the token capacity (one token if the capacity does not fit) and the codebook come first
-    const size_t fixed = 1024 + (size_t)grid_words(type) * 4 + 128;
+    const size_t fixed = 1024 + (size_t)grid_words(type) * 4 + 128;  // barriers, codebook
     size_t xb = (size_t)p.ntcap * p.G * XPAD * 4;
-    if (fixed + xb + 2 * (size_t)p.stage_bytes > 227 * 1024) xb = (size_t)p.G * XPAD * 4;
-    const size_t ring_budget = std::min<size_t>((size_t)S.ring_kb * 1024, 227 * 1024 - fixed - xb);
+    if (fixed + xb + 2 * (size_t)p.stage_bytes > kDynSmem) xb = (size_t)p.G * XPAD * 4;
+    const size_t ring_budget = std::min<size_t>((size_t)S.ring_kb * 1024, kDynSmem - fixed - xb);
     // warps: the setting (S.warps_per_cta > 0), else 16 for large weights and 8 for small ones, fewer when wide rows
     // would leave less than two stages per warp
     int nw = S.warps_per_cta > 0 ? S.warps_per_cta : ((size_t)rows * p.rb >= (64u << 20) ? 16 : 8);
@@ -159,17 +163,17 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     p.grid_off = (uint32_t)align_up(p.ring_off + (size_t)nw * p.slots * p.stage_bytes, 128);
     p.x_off = (uint32_t)align_up(p.grid_off + (size_t)grid_words(type) * 4, 128);
     p.smem = gemv_smem(p, p.ntcap);
-    if (p.smem > 227 * 1024) p.smem = gemv_smem(p, 1);  // wide rows: fewer tokens per call fit (checked at launch)
-    return p.smem <= 227 * 1024;
+    if (p.smem > kDynSmem) p.smem = gemv_smem(p, 1);  // wide rows: fewer tokens per call fit (checked at launch)
+    return p.smem <= kDynSmem;
 }
 
 size_t plan_weight_bytes(const GemvPlan &p) { return (size_t)p.rows * p.ldw; }
 
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
-                bool early, cudaStream_t s) {
+                bool early, cudaStream_t s, const GemvArgmax *am) {
     if (nt < 1 || nt > p.ntcap) return fail("gemv: nt out of range for the plan");
     const size_t smem = gemv_smem(p, nt);
-    if (smem > 227 * 1024) return fail("gemv: " + std::to_string(nt) + " tokens of " + std::to_string(p.cols) +
+    if (smem > kDynSmem) return fail("gemv: " + std::to_string(nt) + " tokens of " + std::to_string(p.cols) +
                                        " columns do not fit in shared memory");
     if (((uintptr_t)W & 15) || ((uintptr_t)x & 15) || (xs & 3)) return fail("gemv: W and x must be 16-byte aligned, xs % 4 == 0");
     GemvArgs a;
@@ -194,6 +198,23 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.acc = acc ? 1 : 0;
     a.early = early && settings().early && settings().pdl ? 1 : 0;
     a.err = dev_error_ptr();
+    a.amx = 0;
+    a.row0 = 0;
+    a.aidx = nullptr;
+    a.akey = a.kacc = nullptr;
+    a.ticket = nullptr;
+    if (am) {
+        if (!am->kacc || !am->ticket || (!am->index && !am->key)) return fail("gemv argmax: missing scratch or outputs");
+        if (am->row0 < 0 || (long long)am->row0 + p.rows > 0x7FFFFFFFll) return fail("gemv argmax: row0 out of range");
+        a.amx = 1;
+        a.row0 = am->row0;
+        a.aidx = am->index;
+        a.akey = am->key;
+        a.kacc = am->kacc;
+        a.ticket = am->ticket;
+    } else if (!y) {
+        return fail("gemv: y is null");
+    }
     cudaError_t e = cudaSuccess;
     const bool known = dispatch_type(p.type, [&]<uint32_t TY>() { e = gemv_launch_t<TY>(p, a, smem, s); });
     if (!known) return fail("gemv: unsupported type " + std::to_string(p.type));

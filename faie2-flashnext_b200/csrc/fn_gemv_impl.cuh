@@ -5,6 +5,7 @@
 #include <unordered_set>
 
 #include "fn_engine.h"
+#include "fn_argmax.cuh"
 #include "fn_rowdot.cuh"
 
 namespace fn {
@@ -21,7 +22,54 @@ struct GemvArgs {
     uint32_t stage_bytes, x_off, ring_off, grid_off;
     int acc, early;
     uint32_t *err;
+    // fused argmax (GemvArgmax); amx == 0: none
+    int amx, row0;
+    int *aidx;
+    unsigned long long *akey, *kacc;
+    unsigned int *ticket;
 };
+
+// Fused argmax, end of the CTA. The CTA's best key per token (a register per storing lane for one token, else
+// s_best[warp][writer][t]) goes by one relaxed atomic max into kacc[t]; then a release-acquire ticket: the CTA that
+// takes the last ticket sees every CTA's max, publishes the winner and clears kacc and the ticket for the next launch.
+// Every thread calls this.
+template <int NT>
+__device__ __forceinline__ void gemv_argmax_epilogue(unsigned long long best1, const unsigned long long (*s_best)[4][NT],
+                                                     const GemvArgs &a) {
+    __shared__ unsigned long long s_w[16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if constexpr (NT == 1) {
+        best1 = warp_kmax(best1);
+        if (lane == 0) s_w[warp] = best1;
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    for (int t = 0; t < a.nt; ++t) {  // warp 0: lane w takes warp w's keys
+        unsigned long long k = 0;
+        if (lane < nw) {
+            if constexpr (NT == 1) {
+                k = s_w[lane];
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) k = kmax(k, s_best[lane][i][t]);
+            }
+        }
+        k = warp_kmax(k);
+        if (lane == 0 && k) asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(a.kacc + t), "l"(k) : "memory");
+    }
+    if (lane != 0) return;
+    uint32_t tk;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(tk) : "l"(a.ticket) : "memory");
+    if (tk != gridDim.x - 1) return;
+    for (int t = 0; t < a.nt; ++t) {
+        unsigned long long k;
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(k) : "l"(a.kacc + t) : "memory");
+        if (a.aidx) a.aidx[t] = amax_index(k);
+        if (a.akey) a.akey[t] = k;
+        a.kacc[t] = 0ull;
+    }
+    *a.ticket = 0u;
+}
 
 template <uint32_t TY, int NT, int LPR, int GPL, bool XREG>
 __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
@@ -54,6 +102,14 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     __syncwarp();
     stage_grid<TY>(grid);
 
+    // fused argmax: best key per storing lane (one token: a register; else per (warp, writer, token) in shared
+    // memory, cleared before stage_x's barriers)
+    __shared__ unsigned long long s_best[NT == 1 ? 1 : 16][4][NT];
+    float bv = -INFINITY;  // one token: the lane's best value and its row (rows rise along a lane's stages, so a
+    int br = -1;           // strict > keeps the lowest row of equal values; NaN and -inf never enter)
+    if (NT > 1 && a.amx)
+        for (int i = tid; i < 16 * 4 * NT; i += blockDim.x) (&s_best[0][0][0])[i] = 0ull;
+
     if (!a.early) pdl_wait();
     const float *x = after_wait(a.x);
     const int nt = a.nt;
@@ -84,15 +140,31 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
         }
         double acc[RR][NT];
         rows_dot<TY, true, NT, LPR, GPL, XREG, RR>(rp, valid, a.nb, grid, xr, xsm, a.G, lr, nt, acc);
-        const int q = RR == 2 ? (lane >> 4) : 0;
-        if (valid[q] && (RR == 2 ? (lane & 15) == 0 : lr == 0)) {
-            const int r = rr0 + row[q];
+        // the lane that stores a row: lane 0 / 16 of the two halves (RR == 2), else lane 0 of each lane group; after
+        // the butterfly acc[0] holds that lane's row total (selects, not a dynamic register index, keep it in registers)
+        const bool hi = RR == 2 && (lane & 16);
+        const bool vq = hi ? valid[RR - 1] : valid[0];
+        if (vq && (RR == 2 ? (lane & 15) == 0 : lr == 0)) {
+            const int r = rr0 + (hi ? row[RR - 1] : row[0]);
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (NT > 1 && t >= nt) break;
-                float *o = a.y + (size_t)t * a.ys + r;
-                const float v = __double2float_rn(acc[q][t]);
-                *o = a.acc ? __fadd_rn(*o, v) : v;
+                const float v = __double2float_rn(acc[0][t]);
+                if (a.y) {
+                    float *o = a.y + (size_t)t * a.ys + r;
+                    *o = a.acc ? __fadd_rn(*o, v) : v;
+                }
+                if (a.amx) {
+                    if constexpr (NT == 1) {
+                        if (v > bv) {
+                            bv = v;
+                            br = r;
+                        }
+                    } else {
+                        unsigned long long &b = s_best[warp][lane / (LPR == 32 ? 16 : LPR)][t];
+                        b = kmax(b, amax_key(v, a.row0 + r));
+                    }
+                }
             }
         }
         __syncwarp();  // every lane is done reading the slot
@@ -101,6 +173,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     if (st < nst && lane == 0)  // wound down early: let the copies already issued land (bounded) before exiting
         for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
     if (a.early) pdl_wait();
+    if (a.amx) gemv_argmax_epilogue<NT>(br < 0 ? 0ull : amax_key(bv, a.row0 + br), s_best, a);
 }
 
 template <uint32_t TY> cudaError_t gemv_launch_t(const GemvPlan &p, const GemvArgs &a, size_t smem, cudaStream_t s) {

@@ -234,8 +234,9 @@ __global__ void __launch_bounds__(256, 1) k_moe_gu(const MoeGuArgs a) {
                 double acc[RR][1];
                 rows_dot<TY, SOA, 1, LPR, GPL, XREG, RR>(rp, valid, a.nb, grid, xr, xsm + (size_t)t * G * XPAD, G, lr, 1,
                                                         acc);
-                const int q = RR == 2 ? (lane >> 4) : 0;
-                if (valid[q] && (RR == 2 ? (lane & 15) == 0 : lr == 0)) res[row[q]] = __double2float_rn(acc[q][0]);
+                const bool hi = RR == 2 && (lane & 16);  // selects keep valid / row / acc in registers
+                if ((hi ? valid[RR - 1] : valid[0]) && (RR == 2 ? (lane & 15) == 0 : lr == 0))
+                    res[hi ? row[RR - 1] : row[0]] = __double2float_rn(acc[0][0]);
             }
         }
         if (__syncthreads_or(!ok)) {
@@ -333,8 +334,9 @@ __global__ void __launch_bounds__(256, 1) k_moe_down(const MoeDownArgs a) {
                 double acc[RR][1];
                 rows_dot<TY, SOA, 1, LPR, 0, false, RR>(rp, valid, a.nb, grid, xr, xsm + (size_t)s * G * XPAD, G, lr, 1,
                                                        acc);
-                const int q = RR == 2 ? (lane >> 4) : 0;
-                if (valid[q] && (RR == 2 ? (lane & 15) == 0 : lr == 0)) res[s * a.rps + row[q]] = __double2float_rn(acc[q][0]);
+                const bool hi = RR == 2 && (lane & 16);
+                if ((hi ? valid[RR - 1] : valid[0]) && (RR == 2 ? (lane & 15) == 0 : lr == 0))
+                    res[s * a.rps + (hi ? row[RR - 1] : row[0])] = __double2float_rn(acc[0][0]);
             }
         }
         if (__syncthreads_or(!ok)) {

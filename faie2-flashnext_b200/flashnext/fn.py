@@ -27,7 +27,8 @@ EXPORTS = [
     "fn_gemv_plan", "fn_test_dequant", "fn_test_gemv", "fn_bench_gemv", "fn_w_create", "fn_w_free", "fn_w_bytes",
     "fn_w_gemv", "fn_w_gemv_host", "fn_sync", "fn_test_moe", "fn_moe_create", "fn_moe_free", "fn_moe_run",
     "fn_bench_route", "fn_moe_layer_static", "fn_test_gdn", "fn_gdn_create", "fn_gdn_free", "fn_gdn_run",
-    "fn_gdn_get_state",
+    "fn_gdn_get_state", "fn_w_gemv_argmax", "fn_w_gemv_argmax_host", "fn_argmax", "fn_argmax_keys", "fn_test_argmax",
+    "fn_test_gemv_argmax",
 ]
 
 
@@ -67,6 +68,12 @@ class FN:
         d.fn_gdn_free.argtypes = [C.c_int]
         d.fn_gdn_run.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp]
         d.fn_gdn_get_state.argtypes = [C.c_int, vp, vp]
+        d.fn_w_gemv_argmax.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp]
+        d.fn_w_gemv_argmax_host.argtypes = [C.c_int, vp, C.c_int, vp, vp, vp]
+        d.fn_argmax.argtypes = [vp, C.c_int, C.c_int, C.c_int, vp, vp]
+        d.fn_argmax_keys.argtypes = [vp, C.c_int, C.c_int, vp, vp]
+        d.fn_test_argmax.argtypes = [F32, C.c_int, C.c_int, I32]
+        d.fn_test_gemv_argmax.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, vp, I32]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -92,6 +99,27 @@ class FN:
         self.check(self.d.fn_test_gemv(int(qtype), np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), rows, cols,
                                        x, nt, y))
         return y
+
+    def gemv_argmax(self, qtype, raw, rows, cols, x, logits=True):
+        """(argmax [nt], y [nt][rows] or None): the lm_head GEMV with its fused argmax on GGUF rows."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim == 1:
+            x = x[None]
+        nt = x.shape[0]
+        y = np.zeros((nt, rows), np.float32) if logits else None
+        idx = np.zeros(nt, np.int32)
+        self.check(self.d.fn_test_gemv_argmax(int(qtype), np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), rows,
+                                              cols, x, nt, y.ctypes.data if logits else None, idx))
+        return idx, y
+
+    def argmax(self, logits):
+        """argmax [nt] of host logits [nt][n] on the GPU (k_argmax semantics)."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        if lg.ndim == 1:
+            lg = lg[None]
+        out = np.zeros(lg.shape[0], np.int32)
+        self.check(self.d.fn_test_argmax(lg, lg.shape[1], lg.shape[0], out))
+        return out
 
     def gemv_plan(self, qtype, rows, cols):
         out = np.zeros(7, np.int32)
@@ -122,6 +150,22 @@ class FN:
 
     def w_gemv_host(self, h, x_ptr, nt, y_ptr, stream=0):
         self.check(self.d.fn_w_gemv_host(h, C.c_void_p(x_ptr), nt, C.c_void_p(y_ptr), C.c_void_p(stream)))
+
+    def w_gemv_argmax(self, h, x_ptr, xs, y_ptr, ys, nt=1, flags=0, row0=0, index_ptr=0, keys_ptr=0, stream=0):
+        """Device pointers (0 = null for y, index, keys)."""
+        self.check(self.d.fn_w_gemv_argmax(h, C.c_void_p(x_ptr), xs, C.c_void_p(y_ptr or None), ys, nt, flags, row0,
+                                           C.c_void_p(index_ptr or None), C.c_void_p(keys_ptr or None),
+                                           C.c_void_p(stream)))
+
+    def w_gemv_argmax_host(self, h, x_ptr, nt, y_ptr, index_ptr, stream=0):
+        self.check(self.d.fn_w_gemv_argmax_host(h, C.c_void_p(x_ptr), nt, C.c_void_p(y_ptr or None),
+                                                C.c_void_p(index_ptr), C.c_void_p(stream)))
+
+    def argmax_dev(self, logits_ptr, ls, n, nt, out_ptr, stream=0):
+        self.check(self.d.fn_argmax(C.c_void_p(logits_ptr), ls, n, nt, C.c_void_p(out_ptr), C.c_void_p(stream)))
+
+    def argmax_keys(self, keys_ptr, nranks, nt, out_ptr, stream=0):
+        self.check(self.d.fn_argmax_keys(C.c_void_p(keys_ptr), nranks, nt, C.c_void_p(out_ptr), C.c_void_p(stream)))
 
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))

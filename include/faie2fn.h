@@ -78,6 +78,30 @@ int fn_w_gemv_host(int h, const float *x, int nt, float *y, void *stream);
 /* Synchronise a stream and report any device-side error (a bounded wait that ran out). */
 int fn_sync(void *stream);
 
+/* ---- lm_head argmax (k_argmax, engine/faie2fn.cu:1910-1935; lm_head + argmax at :2446-2447) ----------------
+ * Selection rule everywhere: the largest value wins, the lowest index among equal values; NaN never wins; -0 ranks
+ * as +0; index 0 when no value exceeds -inf. */
+
+/* The lm_head GEMV with the argmax fused into its epilogue (device pointers, on a stream). y nullable (logits not
+ * written); index[t] nullable = winning global row (row0 + local row); keys[t] nullable (may be a peer GPU's memory)
+ * = the winner's 64-bit ordering key, for combining the row slices of a split lm_head by max. flags as fn_w_gemv.
+ * One such call at a time per handle. Replaces gemv(e.head) followed by k_argmax. */
+int fn_w_gemv_argmax(int h, const float *x, int xs, float *y, int ys, int nt, int flags, int row0, int *index,
+                     unsigned long long *keys, void *stream);
+/* The same with host buffers (x [nt][cols] in; y nullable [nt][rows] and index [nt] out); does not synchronise. */
+int fn_w_gemv_argmax_host(int h, const float *x, int nt, float *y, int *index, void *stream);
+/* Stand-alone argmax of logits [nt][n] (token stride ls, device pointers; nt <= 1024) into out[nt]. Replaces
+ * k_argmax. Its scratch is file-scope device memory: one stand-alone argmax at a time per device. */
+int fn_argmax(const float *logits, int ls, int n, int nt, int *out, void *stream);
+/* out[t] = winning index among keys [nranks][nt] (device pointers) of the slices of a row-split lm_head. New: the
+ * reference has no multi-GPU lm_head. */
+int fn_argmax_keys(const unsigned long long *keys, int nranks, int nt, int *out, void *stream);
+/* Synchronous hooks on host buffers: k_argmax over logits [nt][n]; the fused lm_head GEMV + argmax on GGUF rows
+ * (as fn_test_gemv; y nullable), run twice on the same scratch so the second launch checks the ticket reset. */
+int fn_test_argmax(const float *logits, int n, int nt, int *out);
+int fn_test_gemv_argmax(uint32_t type, const uint8_t *W, int rows, int cols, const float *x, int nt, float *y,
+                        int *index);
+
 /* ---- MoE layer ------------------------------------------------------------------------ */
 
 /* One MoE layer on host buffers: y[t] = sum_{s<k} w[t][s] down_e . (silu(gate_e . x[t]) * (up_e . x[t])) with
