@@ -64,6 +64,51 @@ __global__ void k_argmax_keys(const unsigned long long *__restrict__ keys, int n
     out[t] = amax_index(k);
 }
 
+// KeyExchange consumer: one warp. It first waits for the kernel before it (this rank's lm_head GEMV, whose publishing
+// CTA also counted this rank's own arrival), so it only ever waits on other GPUs. Every lane then polls the n
+// counters with acquire loads (bounded), lane t < nt reduces the n keys of token t for this call's parity, and
+// lane 0 counts the call. On a timeout the outputs are -1 and the device error word says which wait gave up.
+struct KeysCombineArgs {
+    const unsigned long long *keys;
+    const uint32_t *counters;
+    uint32_t *calls;
+    int n, nt;
+    int *out;
+    uint32_t *err;
+};
+
+__global__ void k_keys_combine(const KeysCombineArgs a) {
+    pdl_wait();
+    const int lane = threadIdx.x;
+    const uint32_t c = *after_wait(a.calls);
+    bool ok = true;
+    for (int r = 0; r < a.n && ok; ++r) ok = wait_counter_sys(a.counters + r, c + 1);
+    ok = __all_sync(0xffffffffu, ok);
+    pdl_trigger();
+    if (!ok) {
+        if (lane == 0) dev_fail(a.err, DEV_PEER_TIMEOUT);
+        if (lane < a.nt) a.out[lane] = -1;
+        return;
+    }
+    if (lane < a.nt) {
+        const int par = (int)(c & 1u);
+        unsigned long long k = 0;
+        for (int r = 0; r < a.n; ++r) k = kmax(k, a.keys[(par * MAX_RANKS + r) * 8 + lane]);
+        a.out[lane] = amax_index(k);
+    }
+    __syncwarp();
+    if (lane == 0) *a.calls = c + 1;
+}
+
+int launch_keys_combine(const unsigned long long *keys, const uint32_t *counters, uint32_t *calls, int n, int nt,
+                        int *out, cudaStream_t s) {
+    if (n < 1 || n > MAX_RANKS || nt < 1 || nt > 8) return fail("keys combine: bad shape");
+    KeysCombineArgs a{keys, counters, calls, n, nt, out, dev_error_ptr()};
+    const cudaError_t e = launch_k(k_keys_combine, dim3(1), dim3(32), 0, s, a);
+    if (e != cudaSuccess) return fail(std::string("keys combine launch: ") + cudaGetErrorString(e));
+    return 0;
+}
+
 int launch_argmax(const float *logits, int ls, int n, int nt, int *out, cudaStream_t s) {
     if (nt < 1 || nt > AMX_MAXT || n < 1 || ls < n) return fail("argmax: bad shape (1 <= nt <= 1024, n <= ls)");
     const cudaError_t e = launch_k(k_argmax, dim3((n + AMX_CHUNK - 1) / AMX_CHUNK, nt), dim3(AMX_THREADS), 0, s, logits,

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "fn_engine.h"
+#include "fn_peer.h"
 
 namespace fn {
 
@@ -57,7 +58,9 @@ int check_dev_error(const char *where) {
     const uint32_t z = 0;
     cudaMemcpyToSymbol(g_dev_err_word, &z, sizeof(z));
     return fail(std::string(where) + ": device " +
-                (v == DEV_WAIT_TIMEOUT ? "wait timed out (a pipeline barrier never completed)" : "argument check failed") +
+                (v == DEV_WAIT_TIMEOUT    ? "wait timed out (a pipeline barrier never completed)"
+                 : v == DEV_PEER_TIMEOUT ? "wait for a peer GPU timed out (a rank did not arrive)"
+                                         : "argument check failed") +
                 " (code " + std::to_string(v) + ")");
 }
 
@@ -338,6 +341,29 @@ FN_API int fn_w_gemv_argmax_host(int h, const float *xh, int nt, float *yh, int 
     if (yh) FN_CK(cudaMemcpyAsync(yh, w->ybuf, (size_t)nt * p.rows * 4, cudaMemcpyDeviceToHost, s));
     FN_CK(cudaMemcpyAsync(ih, w->ibuf, (size_t)nt * sizeof(int), cudaMemcpyDeviceToHost, s));
     return 0;
+}
+
+// Row-split lm_head on a peer group (one rank per GPU): this rank's handle holds rows [row0, row0 + rows) of the
+// vocabulary. The GEMV's fused argmax publishes this slice's winning keys to every rank over NVLink; a one-warp
+// kernel then waits (bounded) for every rank's keys of this call and writes index[t], the winner over the whole
+// vocabulary, on every rank. y (nullable) receives this rank's logit slice. Every rank makes the same calls.
+FN_API int fn_w_gemv_argmax_group(int h, int gid, const float *x, int xs, float *y, int ys, int nt, int flags, int row0,
+                                  int *index, void *stream) {
+    WeightH *w = wget(h);
+    PeerGroup *g = peer_group(gid);
+    if (!w || !g) return fail("fn_w_gemv_argmax_group: bad handle or group");
+    if (nt < 1 || nt > 8 || !index) return fail("fn_w_gemv_argmax_group: nt out of range (1..8) or no index");
+    const KeyExchange xr = key_exchange(*g);
+    GemvArgmax am;
+    am.row0 = row0;
+    am.kacc = w->kacc;
+    am.ticket = w->ticket;
+    am.xr = &xr;
+    if (launch_gemv(nt == 1 ? w->plan1 : w->plan8, w->d, x, xs, y, ys, nt, (flags & 1) != 0, (flags & 2) != 0,
+                    (cudaStream_t)stream, &am))
+        return -1;
+    return launch_keys_combine(xr.keys[g->rank], xr.counters[g->rank], g->local_calls + 1, g->n, nt, index,
+                               (cudaStream_t)stream);
 }
 
 // argmax of logits[t][0..n) (token stride ls, device pointers) into out[t], on `stream` (engine/faie2fn.cu:1910-1935)

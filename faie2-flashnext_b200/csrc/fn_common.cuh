@@ -77,7 +77,7 @@ int fail(const std::string &msg);
     } while (0)
 
 // device error word: a kernel whose bounded wait ran out records a code here and returns instead of hanging
-enum : uint32_t { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_ARG = 2 };
+enum : uint32_t { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_ARG = 2, DEV_PEER_TIMEOUT = 3 };
 // every call site that can record an error compares the word after its kernels; returns -1 with a message if set
 int check_dev_error(const char *where);
 uint32_t *dev_error_ptr();  // device address of the error word of the current device
@@ -136,6 +136,21 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 template <typename P> __device__ __forceinline__ P after_wait(P p) {
     asm volatile("" : "+l"(p));
     return p;
+}
+
+// Bounded wait until the 32-bit counter at p (in this GPU's memory, written by peer GPUs with release atomics)
+// reaches `target` (wrap-safe), polling with acquire loads at system scope; false after ~`limit` polls (about a second).
+__device__ __forceinline__ bool wait_counter_sys(const uint32_t *p, uint32_t target, uint32_t limit = 1u << 22) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if ((int32_t)(v - target) >= 0) return true;
+        __nanosleep(256);
+    }
+    return false;
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }

@@ -38,12 +38,25 @@ size_t plan_weight_bytes(const GemvPlan &p);  // device bytes of the padded weig
 // last ticket publishes the winner and clears kacc and the ticket. The key orders (value, -index); row0 is the global
 // index of the plan's row 0 (row split across GPUs: keys of the slices combine by max). One launch at a time may use
 // a given kacc / ticket.
+// Key exchange of a row-split lm_head: after the winner of this rank's slice is known, the publishing CTA stores its
+// keys into slot [call parity][this rank][t] of every rank's key area (peer memory over NVLink) and adds 1 to this
+// rank's counter in every rank's counter area with a system-scope release; the ranks' combine kernels wait for all
+// counters (launch_keys_combine).
+constexpr int MAX_RANKS = 8;
+struct KeyExchange {
+    int n = 0, rank = 0;
+    unsigned long long *keys[MAX_RANKS] = {};  // each rank's key area [2][MAX_RANKS][8]
+    uint32_t *counters[MAX_RANKS] = {};        // each rank's arrival counters [MAX_RANKS]
+    uint32_t *calls = nullptr;                 // this rank's count of publishing launches (local)
+};
+
 struct GemvArgmax {
     int row0 = 0;
     int *index = nullptr;                // [nt] (nullable)
     unsigned long long *key = nullptr;   // [nt] (nullable; may be a peer GPU's memory)
     unsigned long long *kacc = nullptr;  // [8] scratch, zero between launches
     unsigned int *ticket = nullptr;      // zero between launches
+    const KeyExchange *xr = nullptr;     // row-split lm_head: publish the keys to every rank
 };
 
 // y[t][r] (+)= W[r] . x[t] for t < nt <= p.ntcap. W: rows at stride p.ldw bytes (16-byte aligned); x, y: fp32 with
@@ -57,6 +70,10 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
 int launch_argmax(const float *logits, int ls, int n, int nt, int *out, cudaStream_t s);
 // out[t] = the index of the largest key keys[r][t] over r < nranks (per-rank keys of a row-split lm_head)
 int launch_argmax_keys(const unsigned long long *keys, int nranks, int nt, int *out, cudaStream_t s);
+// the consumer side of a KeyExchange on this rank: wait (bounded) until every rank's counter here reaches this rank's
+// consumer call count + 1, then out[t] = the winner among the n ranks' keys of that call; counts the call
+int launch_keys_combine(const unsigned long long *keys, const uint32_t *counters, uint32_t *calls, int n, int nt,
+                        int *out, cudaStream_t s);
 
 // GGUF rows (stride rb) -> the engine's row layout (planes for formats with a fast path, else unchanged) at stride
 // ldw. src and dst must not overlap.

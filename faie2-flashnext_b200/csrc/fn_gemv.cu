@@ -203,8 +203,10 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.aidx = nullptr;
     a.akey = a.kacc = nullptr;
     a.ticket = nullptr;
+    a.xr = KeyExchange{};
     if (am) {
-        if (!am->kacc || !am->ticket || (!am->index && !am->key)) return fail("gemv argmax: missing scratch or outputs");
+        if (!am->kacc || !am->ticket || (!am->index && !am->key && !am->xr))
+            return fail("gemv argmax: missing scratch or outputs");
         if (am->row0 < 0 || (long long)am->row0 + p.rows > 0x7FFFFFFFll) return fail("gemv argmax: row0 out of range");
         a.amx = 1;
         a.row0 = am->row0;
@@ -212,6 +214,13 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
         a.akey = am->key;
         a.kacc = am->kacc;
         a.ticket = am->ticket;
+        if (am->xr) {
+            const KeyExchange &x = *am->xr;
+            if (x.n < 1 || x.n > MAX_RANKS || x.rank < 0 || x.rank >= x.n || !x.calls) return fail("gemv argmax: bad key exchange");
+            for (int r = 0; r < x.n; ++r)
+                if (!x.keys[r] || !x.counters[r]) return fail("gemv argmax: key exchange without peer memory");
+            a.xr = x;
+        }
     } else if (!y) {
         return fail("gemv: y is null");
     }

@@ -27,6 +27,7 @@ struct GemvArgs {
     int *aidx;
     unsigned long long *akey, *kacc;
     unsigned int *ticket;
+    KeyExchange xr;  // xr.n == 0: no exchange
 };
 
 // Fused argmax, end of the CTA. The CTA's best key per token (a register per storing lane for one token, else
@@ -61,14 +62,22 @@ __device__ __forceinline__ void gemv_argmax_epilogue(unsigned long long best1, c
     uint32_t tk;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(tk) : "l"(a.ticket) : "memory");
     if (tk != gridDim.x - 1) return;
+    unsigned long long kt[8];
     for (int t = 0; t < a.nt; ++t) {
-        unsigned long long k;
-        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(k) : "l"(a.kacc + t) : "memory");
-        if (a.aidx) a.aidx[t] = amax_index(k);
-        if (a.akey) a.akey[t] = k;
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(kt[t]) : "l"(a.kacc + t) : "memory");
+        if (a.aidx) a.aidx[t] = amax_index(kt[t]);
+        if (a.akey) a.akey[t] = kt[t];
         a.kacc[t] = 0ull;
     }
     *a.ticket = 0u;
+    if (a.xr.n > 0) {  // row-split lm_head: keys to every rank, then one release-add on each rank's counter
+        const uint32_t c = *a.xr.calls;
+        *a.xr.calls = c + 1;
+        const int slot = ((int)(c & 1u) * MAX_RANKS + a.xr.rank) * 8;
+        for (int p = 0; p < a.xr.n; ++p)
+            for (int t = 0; t < a.nt; ++t) a.xr.keys[p][slot + t] = kt[t];
+        for (int p = 0; p < a.xr.n; ++p) red_release_sys_add(a.xr.counters[p] + a.xr.rank, 1u);
+    }
 }
 
 template <uint32_t TY, int NT, int LPR, int GPL, bool XREG>

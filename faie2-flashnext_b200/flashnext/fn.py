@@ -28,7 +28,8 @@ EXPORTS = [
     "fn_w_gemv", "fn_w_gemv_host", "fn_sync", "fn_test_moe", "fn_moe_create", "fn_moe_free", "fn_moe_run",
     "fn_bench_route", "fn_moe_layer_static", "fn_test_gdn", "fn_gdn_create", "fn_gdn_free", "fn_gdn_run",
     "fn_gdn_get_state", "fn_w_gemv_argmax", "fn_w_gemv_argmax_host", "fn_argmax", "fn_argmax_keys", "fn_test_argmax",
-    "fn_test_gemv_argmax",
+    "fn_test_gemv_argmax", "fn_ipc_alloc", "fn_ipc_open", "fn_ipc_close", "fn_ipc_free", "fn_group_create",
+    "fn_group_free", "fn_w_gemv_argmax_group",
 ]
 
 
@@ -74,6 +75,14 @@ class FN:
         d.fn_argmax_keys.argtypes = [vp, C.c_int, C.c_int, vp, vp]
         d.fn_test_argmax.argtypes = [F32, C.c_int, C.c_int, I32]
         d.fn_test_gemv_argmax.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, vp, I32]
+        d.fn_ipc_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p), C.c_char_p]
+        d.fn_ipc_open.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+        d.fn_ipc_close.argtypes = [vp]
+        d.fn_ipc_free.argtypes = [vp]
+        d.fn_group_create.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_void_p), C.c_size_t]
+        d.fn_group_free.argtypes = [C.c_int]
+        d.fn_w_gemv_argmax_group.argtypes = [C.c_int, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp,
+                                             vp]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -166,6 +175,39 @@ class FN:
 
     def argmax_keys(self, keys_ptr, nranks, nt, out_ptr, stream=0):
         self.check(self.d.fn_argmax_keys(C.c_void_p(keys_ptr), nranks, nt, C.c_void_p(out_ptr), C.c_void_p(stream)))
+
+    # ---- peer-memory groups (one process per GPU) ----
+    def ipc_alloc(self, nbytes):
+        """(device pointer, 64-byte handle) of a new zeroed buffer on the current device."""
+        p = C.c_void_p()
+        h = C.create_string_buffer(64)
+        self.check(self.d.fn_ipc_alloc(nbytes, C.byref(p), h))
+        return p.value, h.raw
+
+    def ipc_open(self, handle: bytes):
+        p = C.c_void_p()
+        self.check(self.d.fn_ipc_open(handle, C.byref(p)))
+        return p.value
+
+    def ipc_close(self, ptr):
+        self.check(self.d.fn_ipc_close(C.c_void_p(ptr)))
+
+    def ipc_free(self, ptr):
+        self.check(self.d.fn_ipc_free(C.c_void_p(ptr)))
+
+    def group_create(self, rank, n, bases, nbytes):
+        arr = (C.c_void_p * n)(*bases)
+        g = self.d.fn_group_create(rank, n, arr, nbytes)
+        if g < 1:
+            raise RuntimeError(self.d.fn_error().decode())
+        return g
+
+    def group_free(self, g):
+        self.check(self.d.fn_group_free(g))
+
+    def w_gemv_argmax_group(self, h, g, x_ptr, xs, y_ptr, ys, nt, flags, row0, index_ptr, stream=0):
+        self.check(self.d.fn_w_gemv_argmax_group(h, g, C.c_void_p(x_ptr), xs, C.c_void_p(y_ptr or None), ys, nt, flags,
+                                                 row0, C.c_void_p(index_ptr), C.c_void_p(stream)))
 
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))

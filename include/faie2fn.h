@@ -96,6 +96,25 @@ int fn_argmax(const float *logits, int ls, int n, int nt, int *out, void *stream
 /* out[t] = winning index among keys [nranks][nt] (device pointers) of the slices of a row-split lm_head. New: the
  * reference has no multi-GPU lm_head. */
 int fn_argmax_keys(const unsigned long long *keys, int nranks, int nt, int *out, void *stream);
+/* ---- multi-GPU: peer-memory groups (one process per GPU, CUDA IPC over NVLink) -------------------------------
+ * New: the reference runs on at most two GPUs with host-staged copies. Setup per rank: fn_ipc_alloc (this rank's
+ * buffer + a 64-byte handle), exchange the handles between the ranks' processes, fn_ipc_open every peer handle,
+ * fn_group_create(rank, n, bases) with bases[rank] = the own buffer. Teardown: fn_group_free, a barrier between the
+ * processes, fn_ipc_close the peers, fn_ipc_free the own buffer. */
+int fn_ipc_alloc(size_t bytes, void **ptr, uint8_t *handle64);
+int fn_ipc_open(const uint8_t *handle64, void **ptr);
+int fn_ipc_close(void *ptr);
+int fn_ipc_free(void *ptr);
+int fn_group_create(int rank, int n, void *const *bases, size_t bytes);
+int fn_group_free(int group);
+/* Row-split lm_head (vocabulary rows [row0, row0 + rows of h) on this rank): the GEMV with fused argmax publishes the
+ * slice's winning keys into every rank's buffer and counts its arrival with a release atomic; a one-warp kernel waits
+ * (bounded, ~1 s; a timeout gives index -1 and an error at fn_sync) for all ranks and writes the vocabulary-wide
+ * winner to index[t] on every rank. y nullable (the rank's logit slice). Every rank makes the same calls in the
+ * same order. Replaces gemv(e.head) + k_argmax (engine/faie2fn.cu:2446-2447) when the lm_head is split by rows. */
+int fn_w_gemv_argmax_group(int h, int group, const float *x, int xs, float *y, int ys, int nt, int flags, int row0,
+                           int *index, void *stream);
+
 /* Synchronous hooks on host buffers: k_argmax over logits [nt][n]; the fused lm_head GEMV + argmax on GGUF rows
  * (as fn_test_gemv; y nullable), run twice on the same scratch so the second launch checks the ticket reset. */
 int fn_test_argmax(const float *logits, int n, int nt, int *out);

@@ -35,3 +35,22 @@ def argmax_fast(logits: np.ndarray) -> np.ndarray:
     idx = np.argmax(clean, axis=1)
     # rows whose maximum is -inf (every element -inf or NaN): index 0
     return np.where(clean[np.arange(lg.shape[0]), idx] > -np.inf, idx, 0).astype(np.int64)
+
+
+def amax_key(v: np.ndarray, rows: np.ndarray) -> np.ndarray:
+    """The ordering key of (value, global row) the B200 kernels combine by max: the order-preserving bits of v (with
+    -0 as +0) above (2^32 - 1 - row); 0 for NaN and -inf (never a winner). Restated here so that the partition logic
+    can be checked on the CPU: max over keys == argmax_ref of the concatenated rows."""
+    v = np.asarray(v, np.float32).copy()
+    v[v == 0] = 0.0
+    u = v.view(np.uint32).astype(np.uint64)
+    o = np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000).astype(np.uint64)
+    k = (o << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.asarray(rows, np.uint64))
+    return np.where(np.asarray(v) > -np.inf, k, np.uint64(0)).astype(np.uint64)
+
+
+def slice_key(logits_slice: np.ndarray, row0: int) -> np.ndarray:
+    """Max key per token [nt] of one rank's logit slice [nt][r] whose first row is global row row0."""
+    lg = np.atleast_2d(np.asarray(logits_slice, np.float32))
+    rows = row0 + np.arange(lg.shape[1], dtype=np.uint64)
+    return np.array([amax_key(r, rows).max(initial=np.uint64(0)) for r in lg], np.uint64)
