@@ -5,13 +5,16 @@
 
 #include "fn_engine.h"
 #include "fn_moe.h"
+#include "fn_peer.h"
 
 namespace fn {
 
 struct MoeH {
     MoePlan p;
-    DevBuf gate, up, down, sg, su, sd, act;
+    DevBuf gate, up, down, sg, su, sd, act, route;
     MoeWeights w;
+    int group = 0;  // expert parallel: the peer group (0: one GPU)
+    int e0 = 0;
 };
 static std::vector<MoeH *> g_moe;
 static std::mutex g_moe_mu;
@@ -33,9 +36,11 @@ static int upload_rows(DevBuf &b, uint32_t type, const uint8_t *src, uint64_t rb
     return 0;
 }
 
+// ne_local: experts held here (all ne on one GPU; an expert-parallel rank's slice otherwise)
 static MoeH *moe_build(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
                        const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
-                       cudaStream_t s) {
+                       cudaStream_t s, int ne_local = -1) {
+    if (ne_local < 0) ne_local = ne;
     MoeH *m = new MoeH();
     if (!plan_moe(m->p, gu_type, down_type, ne, k, ffe, d)) {
         delete m;
@@ -43,13 +48,15 @@ static MoeH *moe_build(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
         return nullptr;
     }
     const MoePlan &p = m->p;
-    if (upload_rows(m->gate, gu_type, Wg, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, d, s) ||
-        upload_rows(m->up, gu_type, Wu, p.rb_gu, p.ldw_gu, (size_t)ne * ffe, d, s) ||
-        upload_rows(m->down, down_type, Wd, p.rb_down, p.ldw_down, (size_t)ne * d, ffe, s) ||
+    if (upload_rows(m->gate, gu_type, Wg, p.rb_gu, p.ldw_gu, (size_t)ne_local * ffe, d, s) ||
+        upload_rows(m->up, gu_type, Wu, p.rb_gu, p.ldw_gu, (size_t)ne_local * ffe, d, s) ||
+        upload_rows(m->down, down_type, Wd, p.rb_down, p.ldw_down, (size_t)ne_local * d, ffe, s) ||
         upload_rows(m->sg, gu_type, Wsg, p.rb_gu, p.ldw_gu, ffe, d, s) ||
         upload_rows(m->su, gu_type, Wsu, p.rb_gu, p.ldw_gu, ffe, d, s) ||
         upload_rows(m->sd, down_type, Wsd, p.rb_down, p.ldw_down, d, ffe, s) ||
-        cudaMalloc(&m->act.p, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess) {
+        cudaMalloc(&m->act.p, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess ||
+        cudaMemset(m->act.p, 0, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess ||
+        cudaMalloc(&m->route.p, MOE_ROUTE_WORDS * 4) != cudaSuccess) {
         delete m;
         if (err().empty()) fail("moe: device allocation failed");
         return nullptr;
@@ -84,8 +91,8 @@ FN_API int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
                 cudaMemcpyAsync(xd.p, x, (size_t)nt * d * 4, cudaMemcpyHostToDevice, s) != cudaSuccess))
         rc = fail("fn_test_moe: copy failed");
     if (!rc)
-        rc = launch_moe(m->p, m->w, lg.as<float>(), ne + 1, xd.as<float>(), m->act.as<float>(), yd.as<float>(), nt, false,
-                        sd.as<int>(), wd.as<float>(), true, s);
+        rc = launch_moe(m->p, m->w, lg.as<float>(), ne + 1, xd.as<float>(), m->act.as<float>(), m->route.as<uint32_t>(),
+                        yd.as<float>(), nt, false, sd.as<int>(), wd.as<float>(), true, s);
     if (!rc) {
         cudaMemcpyAsync(y, yd.p, (size_t)nt * d * 4, cudaMemcpyDeviceToHost, s);
         if (sel) cudaMemcpyAsync(sel, sd.p, (size_t)nt * k * 4, cudaMemcpyDeviceToHost, s);
@@ -122,12 +129,59 @@ FN_API int fn_moe_free(int h) {
     return 0;
 }
 
-// Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d] (+= if acc).
+// Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d]. flags: bit 0 adds
+// into y; bit 1 = x early: x was complete before the kernel before this call started (so the layer reads it without
+// waiting for that kernel, as an early GEMV does; engine/faie2fn.cu:2247-2249).
 FN_API int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream) {
     MoeH *m = moe_get(h);
     if (!m) return fail("fn_moe_run: bad handle");
-    return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), y, nt, acc != 0, nullptr, nullptr, true,
-                      (cudaStream_t)stream);
+    if (m->group) return fail("fn_moe_run: an expert-parallel handle runs with fn_moe_ep_run");
+    return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), m->route.as<uint32_t>(), y, nt, (acc & 1) != 0,
+                      nullptr, nullptr, true, (cudaStream_t)stream, nullptr, (acc & 2) != 0);
+}
+
+// Expert-parallel MoE layer on a peer group (one rank per GPU): this rank holds routed experts
+// [rank ne / n, (rank + 1) ne / n) (Wg, Wu: those experts' ffe rows each; Wd: their d rows each, GGUF rows as in
+// fn_moe_create) and the whole shared expert. Returns a handle >= 1 or -1.
+FN_API int fn_moe_ep_create(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, int group,
+                            const uint8_t *Wg, const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg,
+                            const uint8_t *Wsu, const uint8_t *Wsd) {
+    PeerGroup *g = peer_group(group);
+    if (!g) return fail("fn_moe_ep_create: bad group");
+    if ((size_t)PEER_MOE + (size_t)2 * MOE_EP_MAXT * (k + 1) * d * 4 > g->bytes)
+        return fail("fn_moe_ep_create: the group's buffers are too small for the slot outputs");
+    const int e0 = (int)((long long)g->rank * ne / g->n), e1 = (int)((long long)(g->rank + 1) * ne / g->n);
+    MoeH *m = moe_build(gu_type, down_type, ne, k, ffe, d, Wg, Wu, Wd, Wsg, Wsu, Wsd, 0, e1 - e0);
+    if (!m) return -1;
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        delete m;
+        return fail("fn_moe_ep_create: upload failed");
+    }
+    m->group = group;
+    m->e0 = e0;
+    std::lock_guard<std::mutex> l(g_moe_mu);
+    g_moe.push_back(m);
+    return (int)g_moe.size();
+}
+
+// Launch one expert-parallel MoE layer (device pointers, replicated on every rank): logits [nt][ls], x [nt][d] ->
+// y [nt][d] (+= if acc) on every rank. Every rank makes the same calls in the same order.
+FN_API int fn_moe_ep_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream) {
+    MoeH *m = moe_get(h);
+    if (!m || !m->group) return fail("fn_moe_ep_run: bad handle");
+    PeerGroup *g = peer_group(m->group);
+    if (!g) return fail("fn_moe_ep_run: the group is gone");
+    MoeEp ep;
+    ep.n = g->n;
+    ep.rank = g->rank;
+    ep.e0 = m->e0;
+    for (int r = 0; r < g->n; ++r) {
+        ep.dpart[r] = (float *)(g->base[r] + PEER_MOE);
+        ep.counters[r] = (uint32_t *)(g->base[r] + PEER_MOE_COUNTERS);
+    }
+    ep.calls = g->local_calls + 2;
+    return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), m->route.as<uint32_t>(), y, nt, (acc & 1) != 0,
+                      nullptr, nullptr, true, (cudaStream_t)stream, &ep, (acc & 2) != 0);
 }
 
 // Routing on router outputs given as split-K partials part[ks][8][528] (the reference's router + shared-gate GEMV
@@ -180,18 +234,20 @@ FN_API int fn_bench_route(int variant, int nt, int ks, const float *parth, int i
 // Some callers cannot call cudaMalloc: a host that owns all device memory through its own pool (an inference server,
 // a framework allocator) and forbids raw allocations, or code that must not pay the implicit device-wide
 // synchronisation cudaFree performs in the middle of a decode loop. fn_moe_layer_static takes every input and output
-// as a device pointer the caller already owns and keeps its only scratch, the activations passed from the gate/up
-// kernel to the down kernel, in a fixed array of device memory that is part of the library image.
+// as a device pointer the caller already owns and keeps its only scratch, the tokens' routing (written by the routing
+// kernel, read by the others) and the activations passed from the gate/up kernel to the down kernel, in a fixed array
+// of device memory that is part of the library image.
 //
 // Limit: nt * (k + 1) * ffe <= FN_MOE_STATIC_ACT_FLOATS (65536 floats, 256 KiB); larger calls are rejected. Every GPU
 // that loads the library holds the array until the process exits. All calls share it, so calls whose kernels overlap
 // on the GPU (two streams, or two host threads) race on it: issue them in one stream. Nothing in it needs to start at
-// zero (the gate/up kernel writes every element the down kernel reads). The first call on a device resolves the
-// array's device address on that device (cudaGetSymbolAddress); make that first call outside stream capture.
+// zero (each kernel writes every element the next one reads). The first call on a device resolves the array's device
+// address on that device (cudaGetSymbolAddress); make that first call outside stream capture.
 
 namespace fn {
 constexpr size_t kMoeStaticActFloats = 65536;
-static __device__ __align__(256) float g_moe_static_act[kMoeStaticActFloats];
+// activations, then the routing words
+static __device__ __align__(256) float g_moe_static_act[kMoeStaticActFloats + MOE_ROUTE_WORDS];
 static float *g_moe_static_act_dev[64] = {};  // device address of g_moe_static_act, per device
 }  // namespace fn
 
@@ -219,6 +275,7 @@ FN_API int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int
         g_moe_static_act_dev[dev] = (float *)ptr;
     }
     const MoeWeights w{Wg, Wu, Wd, Wsg, Wsu, Wsd};
-    return launch_moe(p, w, logits, ls, x, g_moe_static_act_dev[dev], y, nt, false, nullptr, nullptr, /*planes=*/false,
-                      (cudaStream_t)stream);
+    return launch_moe(p, w, logits, ls, x, g_moe_static_act_dev[dev],
+                      (uint32_t *)(g_moe_static_act_dev[dev] + kMoeStaticActFloats), y, nt, false, nullptr, nullptr,
+                      /*planes=*/false, (cudaStream_t)stream);
 }

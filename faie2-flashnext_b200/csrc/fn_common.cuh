@@ -54,13 +54,13 @@ inline uint64_t row_bytes(uint32_t t, uint64_t cols) {
     return cols / qk * b;
 }
 
-// words of the IQ codebook of a format (0 for formats without one)
+// shared-memory words of the IQ codebook of a format, with any table derived from it (0 for formats without one)
 inline int grid_words(uint32_t t) {
     switch (t) {
         case T_IQ2_XXS: return 512;
         case T_IQ2_XS: return 1024;
         case T_IQ2_S: return 2048;
-        case T_IQ3_XXS: return 256;
+        case T_IQ3_XXS: return 256 + 8192;  // the codebook, then its signed bf16 expansion (stage_grid)
         case T_IQ3_S: return 512;
         default: return 0;
     }

@@ -533,31 +533,49 @@ template <> struct Fast<T_IQ2_XXS> {
     }
 };
 
+// four signed values as bf16 pairs (t.x: values 0, 1; t.y: values 2, 3) times x[j + k]: chains as acc_word
+template <int NT, class XA>
+__device__ __forceinline__ void acc_bf4(uint2 t, const XA &xa, int j, int nt, float2 (&a)[NT][2]) {
+    const float2 v01 = make_float2(__uint_as_float(t.x << 16), __uint_as_float(t.x & 0xFFFF0000u));
+    const float2 v23 = make_float2(__uint_as_float(t.y << 16), __uint_as_float(t.y & 0xFFFF0000u));
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+        if (NT > 1 && tt >= nt) break;
+        a[tt][0] = __ffma2_rn(v01, xa.x2(tt, j), a[tt][0]);
+        a[tt][1] = __ffma2_rn(v23, xa.x2(tt, j + 2), a[tt][1]);
+    }
+}
+
+// IQ3_XXS: each codebook index and its 4 sign bits select one entry of the signed bf16 expansion staged after the
+// codebook (stage_grid), so a lookup yields 4 signed values ready for the FMAs; the values and the sum order are the
+// same as the byte path's (float(v) exactly), so results are unchanged
 template <> struct Fast<T_IQ3_XXS> {
     static constexpr bool ok = true;
     template <int NT, class XA>
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *grid, const XA &xa,
                                                  int nt, float (&r)[NT]) {
+        const uint2 *tab = (const uint2 *)(grid + 256);
         const int b = g >> 3, ib = g & 7;
         const uint2 q = lds64(row + 64 * b + 8 * ib);
         const uint32_t aux = ld32a(row + plane_off<T_IQ3_XXS, 1>(nb) + 32 * b + 4 * ib);
         const float d = ldh(row + plane_off<T_IQ3_XXS, 2>(nb) + 2 * b);
         const float db = db_half(d, aux >> 28, 0.5f);
-        const float2 mo = f2(-(MAG + 128.0f));
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
             const uint32_t qq = l < 2 ? q.x : q.y, s = 16 * (l & 1);
-            const uint32_t g0 = grid[(qq >> s) & 255u], g1 = grid[(qq >> (s + 8)) & 255u];
-            const uint32_t s8 = ksign((aux >> (7 * l)) & 127u);
+            const uint32_t code = (aux >> (7 * l)) & 127u;
+            const uint32_t shi = (code >> 4) | ((__popc(code) & 1u) << 3);  // signs 4..7: 3 bits and the parity
+            const uint2 t0 = tab[(((qq >> s) & 255u) << 4) | (code & 15u)];
+            const uint2 t1 = tab[(((qq >> (s + 8)) & 255u) << 4) | shi];
             if (l < 2) {
-                acc_word<NT>(signed_bias128(g0, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, a);
-                acc_word<NT>(signed_bias128(g1, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, a);
+                acc_bf4<NT>(t0, xa, 8 * l, nt, a);
+                acc_bf4<NT>(t1, xa, 8 * l + 4, nt, a);
             } else {
-                acc_word<NT>(signed_bias128(g0, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, c);
-                acc_word<NT>(signed_bias128(g1, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, c);
+                acc_bf4<NT>(t0, xa, 8 * l, nt, c);
+                acc_bf4<NT>(t1, xa, 8 * l + 4, nt, c);
             }
         }
 #pragma unroll

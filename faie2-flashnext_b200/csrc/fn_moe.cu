@@ -30,14 +30,41 @@ FN_MOE_DECL(T_IQ2_XXS) FN_MOE_DECL(T_IQ2_XS) FN_MOE_DECL(T_IQ2_S) FN_MOE_DECL(T_
 FN_MOE_DECL(T_IQ4_NL) FN_MOE_DECL(T_IQ4_XS) FN_MOE_DECL(T_BF16) FN_MOE_DECL(T_Q2_0)
 
 // ---------------------------------------------------------------------------------------------------------------
+// routing of a layer
+
+// the routing of nt tokens, one CTA (>= 8 warps) per token: sel / w [nt][16] for the MoE kernels, and the caller's
+// sel_out / w_out [nt][k] when given
+__global__ void __launch_bounds__(ROUTE_THREADS) k_moe_route(const float *logits, int ls, int ne, int k, int *rsel,
+                                                              float *rw, int *sel_out, float *w_out) {
+    __shared__ int sel[16];
+    __shared__ float w[16];
+    __shared__ __align__(16) unsigned long long keys[16 * 16];
+    __shared__ float vals[16];
+    const int t = blockIdx.x;
+    pdl_wait();
+    pdl_trigger();  // the gate/up kernel may start its prologue (codebook, weight-independent staging) now
+    const float *l = after_wait(logits) + (size_t)t * ls;
+    route_token(l, ne, k, sel, w, keys, vals);
+    if ((int)threadIdx.x < k) {
+        rsel[t * 16 + threadIdx.x] = sel[threadIdx.x];
+        rw[t * 16 + threadIdx.x] = w[threadIdx.x];
+        if (sel_out) {
+            sel_out[t * k + threadIdx.x] = sel[threadIdx.x];
+            w_out[t * k + threadIdx.x] = w[threadIdx.x];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // routing alone (fn_bench_route): logits = sum over ks split-K partials part[k][t][rsg] in split order, then route
 
-__global__ void __launch_bounds__(256) k_route(const float *part, int ks, int kst, int ts, int ne, int k, int *sel_out,
-                                               float *w_out) {
+__global__ void __launch_bounds__(ROUTE_THREADS) k_route(const float *part, int ks, int kst, int ts, int ne, int k,
+                                                         int *sel_out, float *w_out) {
     __shared__ float lg[1024];
     __shared__ int sel[16];
     __shared__ float w[16];
-    __shared__ unsigned long long keys[128];
+    __shared__ __align__(16) unsigned long long keys[16 * 16];
+    __shared__ float vals[16];
     const int t = blockIdx.x;
     pdl_wait();
     for (int i = threadIdx.x; i < ne; i += blockDim.x) {
@@ -48,10 +75,70 @@ __global__ void __launch_bounds__(256) k_route(const float *part, int ks, int ks
     }
     __syncthreads();
     pdl_trigger();
-    route_token(lg, ne, k, sel, w, keys);
+    route_token(lg, ne, k, sel, w, keys, vals);
     if (threadIdx.x < k) {
         sel_out[t * k + threadIdx.x] = sel[threadIdx.x];
         w_out[t * k + threadIdx.x] = w[threadIdx.x];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// expert-parallel combine: CTA t waits (bounded) until every rank's down kernel has delivered its slot outputs of this
+// call, then y[t] = sum_{s<k} w[s] dpart[s] in slot order + sigmoid(shared-gate logit) dpart[k], with the same fused
+// multiply-adds in the same order as the one-GPU down kernel's combine, so the result is bit-identical to it. The CTA
+// that takes the last ticket advances this rank's call count and expected arrivals.
+
+struct MoeCombineArgs {
+    const float *logits;
+    const float *rw;  // routing weights [nt][16] (k_moe_route)
+    int ls, ne, k, d, nt, n;
+    const float *dpart;         // this rank's slot-output area
+    const uint32_t *counters;   // this rank's arrival counters [n]
+    uint32_t *calls;            // [call count, expected arrivals, ticket]
+    uint32_t arrivals;          // arrivals per source rank of this call (its down kernel's CTAs)
+    float *y;
+    int acc;
+    uint32_t *err;
+};
+
+__global__ void __launch_bounds__(256) k_moe_ep_combine(const MoeCombineArgs a) {
+    __shared__ float wsel[16];
+    __shared__ int s_ok;
+    const int t = blockIdx.x, tid = threadIdx.x, ks = a.k + 1;
+    // the routing weights and logits were complete before the gate/up kernel two launches back passed its wait
+    if (tid < a.k) wsel[tid] = a.rw[t * 16 + tid];
+    pdl_wait();
+    const uint32_t *calls = after_wait(a.calls);
+    const uint32_t c = calls[0], expect = calls[1] + a.arrivals;
+    if (tid == 0) {
+        bool ok = true;
+        for (int r = 0; r < a.n && ok; ++r) ok = wait_counter_sys(a.counters + r, expect);
+        s_ok = ok;
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (s_ok) {
+        const float *dp = a.dpart + ((size_t)(c & 1u) * MOE_EP_MAXT + t) * ks * a.d;
+        const float sg = sigm(a.logits[(size_t)t * a.ls + a.ne]);
+        for (int i = tid; i < a.d; i += blockDim.x) {
+            float acc = 0.0f;
+            for (int q = 0; q < a.k; ++q) acc = __fmaf_rn(wsel[q], dp[(size_t)q * a.d + i], acc);
+            const float v = __fmaf_rn(sg, dp[(size_t)a.k * a.d + i], acc);
+            float *o = a.y + (size_t)t * a.d + i;
+            *o = a.acc ? *o + v : v;
+        }
+    } else if (tid == 0) {
+        dev_fail(a.err, DEV_PEER_TIMEOUT);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t tk;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(tk) : "l"(a.calls + 2) : "memory");
+        if (tk == gridDim.x - 1) {
+            a.calls[0] = c + 1;
+            a.calls[1] = expect;
+            a.calls[2] = 0u;
+        }
     }
 }
 
@@ -69,25 +156,50 @@ bool plan_moe(MoePlan &p, uint32_t gu_type, uint32_t down_type, int ne, int k, i
     p.ffe = ffe;
     p.d = d;
     const uint64_t rg = row_bytes(gu_type, d), rd = row_bytes(down_type, ffe);
-    if (!rg || !rd || d % 32 || ffe % 32 || ne < 1 || ne > 1024 || k < 1 || k > 16 || k > ne) return false;
+    if (!rg || !rd || d % 32 || ffe % 32 || ne < 1 || ne > 1024 || k < 1 || k > 16 || k > ne || ffe > 65536 || d > 65536)
+        return false;
     p.rb_gu = rg;
     p.rb_down = rd;
     p.ldw_gu = (uint32_t)al(rg, 16);
     p.ldw_down = (uint32_t)al(rd, 16);
     const int Gd = ffe / 32;
-    p.lpr_down = Gd == 16 ? 16 : 32;
+    // lanes per down row: about four groups per lane (fewer lanes per row, fewer butterfly levels per row)
+    p.lpr_down = Gd >= 128 ? 32 : Gd >= 64 ? 16 : Gd >= 32 ? 8 : 4;
     return true;
 }
 
 static int sm_count() { return num_sms(); }
 
+// dynamic shared memory of the MoE kernels: the SM's 227 KiB less 4 KiB for their static shared memory (routing pairs,
+// x scale maxima)
+constexpr size_t kMoeDynSmem = 227 * 1024 - 4 * 1024;
 
-int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act, float *y,
-               int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s) {
+
+int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act,
+               uint32_t *route, float *y, int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s,
+               const MoeEp *ep, bool x_early) {
     if (nt < 1 || nt > 8) return fail("moe: nt out of range (1..8)");
+    if (!route) return fail("moe: no routing scratch");
+    int *rsel = (int *)route;
+    float *rw = (float *)(route + 8 * 16);
+    const MoeEp none{};
+    const MoeEp &E = ep ? *ep : none;
+    if (ep) {
+        if (E.n < 1 || E.n > MAX_RANKS || E.rank < 0 || E.rank >= E.n || !E.calls ||
+            E.e0 != (int)((long long)E.rank * p.ne / E.n))
+            return fail("moe: bad expert-parallel group");
+        for (int r = 0; r < E.n; ++r)
+            if (!E.dpart[r] || !E.counters[r]) return fail("moe: expert parallel without peer memory");
+    }
     if (ls < p.ne + 1) return fail("moe: logits stride must hold ne + 1 columns (router + shared gate)");
     if (((uintptr_t)x & 15) || ((uintptr_t)act & 15) || (p.d & 3) || (p.ffe & 3)) return fail("moe: x/act alignment");
     const int ks = p.k + 1;
+    // ---- routing, once per layer
+    {
+        const cudaError_t e = launch_k(k_moe_route, dim3(nt), dim3(ROUTE_THREADS), 0, s, logits, ls, p.ne, p.k, rsel, rw,
+                                       sel_out, w_out);
+        if (e != cudaSuccess) return fail(std::string("moe route launch: ") + cudaGetErrorString(e));
+    }
     // ---- gate / up
     {
         MoeGuArgs a;
@@ -110,21 +222,30 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.ls = ls;
         a.x = x;
         a.act = act;
-        a.sel_out = sel_out;
-        a.w_out = w_out;
-        const long long U = (long long)nt * ks * p.ffe;
-        const int ctas = (int)std::min<long long>(sm_count(), (U + 7) / 8);
-        const int per_cta = (int)((U + ctas - 1) / ctas);
-        a.rps = std::max(1, std::min(per_cta, std::max(8, (int)(12 * 1024 / (2 * p.ldw_gu)) / 8 * 8)));
-        a.stage_bytes = (uint32_t)al((size_t)2 * a.rps * p.ldw_gu, 128);
-        a.slots = std::max(2, std::min(16, (int)(96 * 1024 / a.stage_bytes)));
-        a.ring_off = 128;
-        a.grid_off = (uint32_t)al(a.ring_off + (size_t)a.slots * a.stage_bytes, 128);
-        a.misc_off = (uint32_t)al(a.grid_off + (size_t)grid_words(p.gu_type) * 4, 128);
-        a.x_off = (uint32_t)al(a.misc_off + 8 * 16 * 8 + 128 * 8 + 2 * a.rps * 4, 128);
-        const size_t smem = al(a.x_off + (size_t)nt * (p.d / 32) * XPAD * 4, 128);
-        if (smem > 227 * 1024) return fail("moe: gate/up shared memory too large");
+        a.rsel = rsel;
+        a.x_early = x_early && settings().pdl ? 1 : 0;
+        // one unit (a gate row and its up row) per ring stage; each warp has its own ring of `slots` stages
+        constexpr int NW = MOE_THREADS / 32;
+        const long long U = (long long)nt * ks * p.ffe;  // upper bound (every slot computed here)
+        // one SM fewer than the GPU has: the routing kernel's CTA keeps an SM while the gate/up CTAs start beside it
+        // (programmatic launch), and a gate/up CTA does not fit next to it
+        const int ctas = (int)std::min<long long>(std::max(1, sm_count() - 1), (U + 7) / 8);
+        a.stage_bytes = (uint32_t)al((size_t)2 * p.ldw_gu, 128);
+        const size_t xb = (size_t)nt * (p.d / 32) * XPAD * 4, misc = 8 * 16 * 4, gw = (size_t)grid_words(p.gu_type) * 4;
+        const size_t fixed = 1024 + gw + 128 + misc + 128 + xb + 128;
+        if (fixed + (size_t)NW * a.stage_bytes > kMoeDynSmem) return fail("moe: gate/up rows too wide for shared memory");
+        const long long per_warp = (U + (long long)ctas * NW - 1) / ((long long)ctas * NW);
+        const long long fit = (long long)(std::min<size_t>(128 * 1024, kMoeDynSmem - fixed) / ((size_t)NW * a.stage_bytes));
+        a.slots = (int)std::max<long long>(1, std::min<long long>(std::min<long long>(8, per_warp), fit));
+        a.slots = std::min(a.slots, 1024 / (8 * NW));  // barriers: 1 KiB
+        a.ring_off = 1024;
+        a.grid_off = (uint32_t)al(a.ring_off + (size_t)NW * a.slots * a.stage_bytes, 128);
+        a.misc_off = (uint32_t)al(a.grid_off + gw, 128);
+        a.x_off = (uint32_t)al(a.misc_off + misc, 128);
+        const size_t smem = al(a.x_off + xb, 128);
+        if (smem > kMoeDynSmem) return fail("moe: gate/up shared memory too large");
         a.err = dev_error_ptr();
+        a.ep = E;
         const int G = p.d / 32;
         cudaError_t e = cudaSuccess;
         const bool known = dispatch_type(p.gu_type, [&]<uint32_t TY>() { e = moe_gu_launch_t<TY>(a, planes, nt, G, ctas, smem, s); });
@@ -152,25 +273,43 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.act = act;
         a.y = y;
         a.acc = acc ? 1 : 0;
-        const int chunks = std::max(1, std::min((p.d + 7) / 8, sm_count() / nt));
-        a.chunks = chunks;
-        const int rows_per = (p.d + chunks - 1) / chunks;
-        a.rps = std::max(1, std::min(rows_per, std::max(1, (int)(8 * 1024 / p.ldw_down))));
-        a.stage_bytes = (uint32_t)al((size_t)a.rps * p.ldw_down, 128);
-        a.slots = std::max(2, std::min(16, (int)(96 * 1024 / a.stage_bytes)));
-        a.ring_off = 128;
-        a.grid_off = (uint32_t)al(a.ring_off + (size_t)a.slots * a.stage_bytes, 128);
-        a.misc_off = (uint32_t)al(a.grid_off + (size_t)grid_words(p.down_type) * 4, 128);
-        a.x_off = (uint32_t)al(a.misc_off + 16 * 8 + 128 * 8 + (size_t)ks * a.rps * 4, 128);
-        const size_t smem = al(a.x_off + (size_t)ks * (p.ffe / 32) * XPAD * 4, 128);
-        if (smem > 227 * 1024) return fail("moe: down shared memory too large");
+        a.rsel = rsel;
+        a.rw = rw;
+        // CTA (chunk, t): rows [r0, r1) of token t, every computed slot's rows in shared memory at once
+        const size_t xb = (size_t)ks * (p.ffe / 32) * XPAD * 4, misc = 0,
+                     gw = (size_t)grid_words(p.down_type) * 4;
+        const size_t fixed = 256 + 128 + gw + 128 + misc + 128 + xb + 128;
+        if (fixed + (size_t)ks * (p.ldw_down + 4) > kMoeDynSmem) return fail("moe: down rows too wide for shared memory");
+        const int max_rows = (int)((kMoeDynSmem - fixed) / ((size_t)ks * (p.ldw_down + 4)));
+        int chunks = std::max(1, std::min((p.d + 7) / 8, sm_count() / nt));
+        int rows = (p.d + chunks - 1) / chunks;
+        if (rows > max_rows) {
+            rows = max_rows;
+            chunks = (p.d + rows - 1) / rows;
+        }
+        rows = (p.d + chunks - 1) / chunks;  // the largest chunk of the even split
+        a.rows = rows;
+        a.w_off = 256;
+        a.res_off = (uint32_t)al(a.w_off + (size_t)ks * rows * p.ldw_down, 128);
+        a.grid_off = (uint32_t)al(a.res_off + (size_t)ks * rows * 4, 128);
+        a.misc_off = (uint32_t)al(a.grid_off + gw, 128);
+        a.x_off = (uint32_t)al(a.misc_off + misc, 128);
+        const size_t smem = al(a.x_off + xb, 128);
+        if (smem > kMoeDynSmem) return fail("moe: down shared memory too large");
         a.err = dev_error_ptr();
+        a.ep = E;
         cudaError_t e = cudaSuccess;
         const bool known = dispatch_type(p.down_type, [&]<uint32_t TY>() {
             e = moe_down_launch_t<TY>(a, planes, p.lpr_down, dim3(chunks, nt), smem, s);
         });
         if (!known) return fail("moe: unsupported down type");
         if (e != cudaSuccess) return fail(std::string("moe down launch: ") + cudaGetErrorString(e));
+        if (ep) {  // ---- expert parallel: combine the ranks' slot outputs on every rank
+            MoeCombineArgs c{logits, rw, ls, p.ne, p.k, p.d, nt, E.n, E.dpart[E.rank], E.counters[E.rank], E.calls,
+                             (uint32_t)(chunks * nt), y, acc ? 1 : 0, dev_error_ptr()};
+            e = launch_k(k_moe_ep_combine, dim3(nt), dim3(256), 0, s, c);
+            if (e != cudaSuccess) return fail(std::string("moe combine launch: ") + cudaGetErrorString(e));
+        }
     }
     return 0;
 }
@@ -178,7 +317,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
 int launch_route(const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,
                  cudaStream_t s) {
     if (ne < 1 || ne > 1024 || k < 1 || k > 16 || k > ne || nt < 1) return fail("route: unsupported ne/k/nt");
-    cudaError_t e = launch_k(k_route, dim3(nt), dim3(256), 0, s, part, ks, (int)kst, ts, ne, k, sel, w);
+    cudaError_t e = launch_k(k_route, dim3(nt), dim3(ROUTE_THREADS), 0, s, part, ks, (int)kst, ts, ne, k, sel, w);
     if (e != cudaSuccess) return fail(std::string("route launch: ") + cudaGetErrorString(e));
     return 0;
 }

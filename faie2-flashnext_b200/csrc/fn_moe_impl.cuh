@@ -12,9 +12,12 @@ namespace fn {
 
 // ---------------------------------------------------------------------------------------------------------------
 // top-k routing
+//
+// Order: larger logit first, ties to the lower expert index (-0 and +0 tie), as a 64-bit key (order-preserving logit
+// bits above the complemented index), so every key is distinct. 16 warps each sort their 32 E keys (a bitonic network
+// in registers), the merged rank of a warp's candidate is its place in its own list plus, for every other warp, how
+// many of that warp's k best are larger (a binary search in the sorted list), and rank r < k is slot r.
 
-// order-preserving 64-bit key: larger logit first, then lower index first. -0 and +0 are the same probability
-// (a tie, won by the lower index), so -0 is keyed as +0.
 __device__ __forceinline__ unsigned long long route_key(float l, int idx) {
     uint32_t u = __float_as_uint(l == 0.0f ? 0.0f : l);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
@@ -35,20 +38,18 @@ template <int E> __device__ __forceinline__ void warp_sort_desc(unsigned long lo
                     const int i = lane * E + e;
                     const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[e], lm);
                     const bool desc = (i & size) == 0, lower = (lane & lm) == 0;
-                    const bool keep_max = desc == lower;
-                    v[e] = keep_max ? (v[e] > o ? v[e] : o) : (v[e] < o ? v[e] : o);
+                    v[e] = desc == lower ? (v[e] > o ? v[e] : o) : (v[e] < o ? v[e] : o);
                 }
             } else {
 #pragma unroll
                 for (int e = 0; e < E; ++e) {
                     const int p = e ^ j;
                     if (p > e) {
-                        const int i = lane * E + e;
-                        const bool desc = (i & size) == 0;
-                        const unsigned long long a = v[e], b = v[p];
-                        const bool sw = desc ? a < b : a > b;
-                        v[e] = sw ? b : a;
-                        v[p] = sw ? a : b;
+                        const bool desc = ((lane * E + e) & size) == 0;
+                        const unsigned long long x = v[e], y = v[p];
+                        const bool sw = desc ? x < y : x > y;
+                        v[e] = sw ? y : x;
+                        v[p] = sw ? x : y;
                     }
                 }
             }
@@ -56,68 +57,100 @@ template <int E> __device__ __forceinline__ void warp_sort_desc(unsigned long lo
     }
 }
 
-template <int E>
-__device__ __forceinline__ void warp_topk_keys(const float *logits, int lo, int hi, int k, unsigned long long *out,
-                                               int lane) {
-    unsigned long long v[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const int idx = lo + lane * E + e;
-        v[e] = idx < hi ? route_key(logits[idx], idx) : 0ull;
-    }
-    warp_sort_desc<E>(v, lane);
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const int i = lane * E + e;
-        if (i < k) out[i] = v[e];
-    }
-}
+constexpr int ROUTE_THREADS = 512;  // 16 warps
 
-// Route one token: the k best of logits[0, ne) into sel[k], w[k] (shared memory). Every thread of the block calls it;
-// needs 256 threads (8 warps), ne <= 1024, k <= 16, and keys[] of 8 * 16 entries in shared memory.
-__device__ __forceinline__ void route_token(const float *logits, int ne, int k, int *sel, float *w, unsigned long long *keys) {
+// Route one token: the k best of logits[0, ne) into sel[k], w[k] (shared memory). Weights as the reference:
+// v_r = expf(l_r - l_0), s = sum_r v_r in rank order, w_r = v_r / s. Every thread of a 512-thread block calls it;
+// ne <= 1024, k <= 16. keys: 16 * 16 entries, vals: 16 floats of shared memory.
+static __device__ __noinline__ void route_token(const float *logits, int ne, int k, int *sel, float *w,
+                                                unsigned long long *keys, float *vals) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int per = (ne + 7) / 8, lo = warp * per, hi = min(ne, lo + per);
-    if (per <= 32) warp_topk_keys<1>(logits, lo, hi, k, keys + warp * 16, lane);
-    else if (per <= 64) warp_topk_keys<2>(logits, lo, hi, k, keys + warp * 16, lane);
-    else warp_topk_keys<4>(logits, lo, hi, k, keys + warp * 16, lane);
+    if (ne <= 512) {
+        unsigned long long v[1];
+        const int i = warp * 32 + lane;
+        v[0] = i < ne ? route_key(logits[i], i) : 0ull;
+        warp_sort_desc<1>(v, lane);
+        if (lane < 16) keys[warp * 16 + lane] = lane < k ? v[0] : 0ull;  // each warp's k best, zero-padded to 16
+    } else {
+        unsigned long long v[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int i = warp * 64 + lane * 2 + e;
+            v[e] = i < ne ? route_key(logits[i], i) : 0ull;
+        }
+        warp_sort_desc<2>(v, lane);
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+            if (lane * 2 + e < 16) keys[warp * 16 + lane * 2 + e] = lane * 2 + e < k ? v[e] : 0ull;
+    }
     __syncthreads();
-    if (warp == 0) {
-        unsigned long long v[4];  // 8 warps x k <= 16 candidates = 128 = 32 x 4
+    // candidate c = warp c / k's rank c % k: its merged rank = the number of larger keys in all 16 lists (the keys are
+    // distinct); the k best go to sel in rank order, with their logits
+    const int c = threadIdx.x, wc = c / k;
+    if (wc < 16) {
+        const unsigned long long key = keys[wc * 16 + (c - wc * k)];
+        int rank = 0;
+#pragma unroll 4
+        for (int w2 = 0; w2 < 16; ++w2) {
+            const ulonglong2 *row = (const ulonglong2 *)(keys + w2 * 16);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int i = lane * 4 + e, wi = i / 16, j = i % 16;
-            v[e] = j < k ? keys[wi * 16 + j] : 0ull;
-        }
-        warp_sort_desc<4>(v, lane);
-        // lanes 0..3 hold ranks 0..15; rank r = lane * 4 + e
-        const float lmax = logits[key_index(__shfl_sync(0xffffffffu, v[0], 0))];
-        float ev[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int r = lane * 4 + e;
-            ev[e] = r < k ? expf(logits[key_index(v[e])] - lmax) : 0.0f;
-        }
-        // s = sum over ranks 0..k-1 in rank order (lane 0 gathers, sequential like the reference)
-        float s = 0.0f;
-        for (int r = 0; r < k; ++r) s += __shfl_sync(0xffffffffu, ev[r & 3], r >> 2);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int r = lane * 4 + e;
-            if (r < k) {
-                sel[r] = key_index(v[e]);
-                w[r] = ev[e] / s;
+            for (int j = 0; j < 8; ++j) {
+                const ulonglong2 q = row[j];
+                rank += (q.x > key) + (q.y > key);
             }
         }
+        if (rank < k && key != 0ull) {
+            const int e = key_index(key);
+            sel[rank] = e;
+            vals[rank] = logits[e];
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const float ev = lane < k ? expf(vals[lane] - vals[0]) : 0.0f;
+        float s = 0.0f;
+        for (int r = 0; r < k; ++r) s += __shfl_sync(0xffffffffu, ev, r);
+        if (lane < k) w[lane] = ev / s;
     }
     __syncthreads();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// expert parallelism: which of a token's k + 1 slots this rank computes
+
+// the rank holding expert e when ne experts are split over n ranks as [g ne / n, (g + 1) ne / n)
+__device__ __forceinline__ int expert_owner(int e, int ne, int n) {
+    int g = n - 1;
+    while (g > 0 && (int)((long long)g * ne / n) > e) --g;
+    return g;
+}
+
+// bit s set: this rank computes slot s of the token routed to sel[0..k) (slot k: the shared expert, computed by the
+// rank holding the fewest of the routed slots, the lowest such rank). One GPU (ep.n == 0): every slot.
+__device__ __forceinline__ uint32_t owned_slots(const int *sel, int k, int ne, const MoeEp &ep) {
+    if (ep.n == 0) return (2u << k) - 1u;
+    uint32_t m = 0;
+    int cnt[MAX_RANKS];
+    for (int g = 0; g < MAX_RANKS; ++g) cnt[g] = 0;
+    for (int s = 0; s < k; ++s) {
+        const int g = expert_owner(sel[s], ne, ep.n);
+        ++cnt[g];
+        if (g == ep.rank) m |= 1u << s;
+    }
+    int best = 0;
+    for (int g = 1; g < ep.n; ++g)
+        if (cnt[g] < cnt[best]) best = g;
+    if (best == ep.rank) m |= 1u << k;
+    return m;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // gate / up
 
+constexpr int MOE_THREADS = 512;  // 16 warps per CTA, one CTA per SM
+
 struct MoeGuArgs {
-    const uint8_t *Wg, *Wu, *Wsg, *Wsu;  // routed (ne * ffe rows) and shared (ffe rows), stride ldw
+    const uint8_t *Wg, *Wu, *Wsg, *Wsu;  // routed (local experts * ffe rows) and shared (ffe rows), stride ldw
     uint32_t ldw;
     int nb;  // blocks per row
     int ne, k, ffe, d, nt;
@@ -125,130 +158,150 @@ struct MoeGuArgs {
     int ls;  // logits token stride (>= ne + 1: column ne is the shared-gate logit)
     const float *x;  // [nt][d]
     float *act;      // [nt][k + 1][ffe]
-    int *sel_out;    // [nt][k] or null (written by CTA 0)
-    float *w_out;
-    int rps, slots;
+    const int *rsel;  // routing [nt][16] (k_moe_route, the kernel before this one)
+    int x_early;      // x was complete before the routing kernel started: read it before the wait
+    int slots;  // ring stages per warp; a stage is one unit: a gate row and the matching up row
     uint32_t stage_bytes, ring_off, x_off, grid_off, misc_off;
     uint32_t *err;
+    MoeEp ep;
 };
 
-template <uint32_t TY, int LPR, int GPL, bool XREG, bool SOA>
-__global__ void __launch_bounds__(256, 1) k_moe_gu(const MoeGuArgs a) {
-    constexpr int RR = LPR == 32 ? 2 : 1;
+// Units are the (token, slot, row) triples this rank computes, in (pair, row) order; CTA b takes an even share and
+// splits it into one contiguous run per warp. Each warp streams its units through its own ring of bulk copies (no
+// block barrier after the staging). A lane takes groups lane, lane + 32, .. of both rows of a unit (gate and up) in
+// one loop with a single decode body (the kernel runs once per layer: short code keeps instruction fetch off the
+// critical path); the two rows meet in one transposed butterfly, lane 0 writes act = silu(g) * u.
+// XG > 0: one token whose row of G = 32 XG groups each warp holds in registers (read from global memory by each warp,
+// no staging barrier); XG == 0: x staged in shared memory for any token count and row length.
+template <uint32_t TY, bool SOA, int XG>
+__global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    uint64_t *full = (uint64_t *)sm;
-    uint8_t *ring = sm + a.ring_off;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    uint64_t *full = (uint64_t *)sm + warp * a.slots;
+    uint8_t *ring = sm + a.ring_off + (size_t)warp * a.slots * a.stage_bytes;
     float *xsm = (float *)(sm + a.x_off);
     uint32_t *grid = (uint32_t *)(sm + a.grid_off);
-    int *sel = (int *)(sm + a.misc_off);                          // [nt][16]
-    float *wsel = (float *)(sel + 8 * 16);                          // [nt][16]
-    unsigned long long *keys = (unsigned long long *)(wsel + 8 * 16);  // [128]
-    float *res = (float *)(keys + 128);                              // [2 * rps]
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    int *sel = (int *)(sm + a.misc_off);  // [nt][16]
+    __shared__ int s_pair[MOE_EP_MAXT * 17];  // the (token, slot) pairs this rank computes, t << 5 | s, in order
+    __shared__ int s_np;
     const int G = a.d / 32, ks = a.k + 1;
-    const long long U = (long long)a.nt * ks * a.ffe;
-    const long long u0 = (long long)blockIdx.x * U / gridDim.x, u1 = (long long)(blockIdx.x + 1) * U / gridDim.x;
-    // stages: runs of <= rps consecutive units inside one (t, slot) segment
-    auto stage_span = [&](long long from, long long &to) {
-        const long long seg_end = (from / a.ffe + 1) * a.ffe;
-        to = min(min(from + a.rps, seg_end), u1);
-    };
-    int nst = 0;
-    for (long long u = u0, v; u < u1; u = v, ++nst) stage_span(u, v);
 
-    if (tid == 0) {
-        for (int s = 0; s < a.slots; ++s) mbar_init(&full[s], 1);
+    if (lane == 0) {
+        for (int q = 0; q < a.slots; ++q) mbar_init(&full[q], 1);
         mbar_fence_init();
     }
     stage_grid<TY>(grid);
+    XReg<32, (XG > 0 ? XG : 1)> xr;
+    if constexpr (XG > 0)
+        if (a.x_early) xr.load_global(a.x, lane, ScaleX<TY, SOA>::v);  // beside the routing kernel
     pdl_wait();
-    const float *logits = after_wait(a.logits);
     const float *x = after_wait(a.x);
-    for (int t = 0; t < a.nt; ++t) route_token(logits + (size_t)t * a.ls, a.ne, a.k, sel + t * 16, wsel + t * 16, keys);
-    if (blockIdx.x == 0 && a.sel_out && tid < a.nt * a.k) {
-        const int t = tid / a.k, i = tid % a.k;
-        a.sel_out[t * a.k + i] = sel[t * 16 + i];
-        a.w_out[t * a.k + i] = wsel[t * 16 + i];
+    const int *rsel = after_wait(a.rsel);
+    for (int i = tid; i < a.nt * 16; i += blockDim.x) sel[i] = rsel[i];
+    __syncthreads();
+    if (tid == 0) {
+        int np = 0;
+        for (int t = 0; t < a.nt; ++t) {
+            const uint32_t m = owned_slots(sel + t * 16, a.k, a.ne, a.ep);
+            for (int q = 0; q < ks; ++q)
+                if (m >> q & 1u) s_pair[np++] = t << 5 | q;
+        }
+        s_np = np;
     }
-    stage_x(xsm, x, a.d, a.nt, G, ScaleX<TY, SOA>::v);
-    pdl_trigger();
+    __syncthreads();
 
-    auto rows_ptr = [&](long long u, const uint8_t *&g, const uint8_t *&up) {
-        const int t = (int)(u / ((long long)ks * a.ffe)), rem = (int)(u % ((long long)ks * a.ffe));
-        const int s = rem / a.ffe, r = rem % a.ffe;
-        if (s < a.k) {
-            const int e = sel[t * 16 + s];
-            const size_t off = ((size_t)e * a.ffe + r) * a.ldw;
+    // (32-bit unit arithmetic: U <= 8 tokens * 17 slots * ffe)
+    const int U = s_np * a.ffe;
+    const int u0 = (int)((long long)blockIdx.x * U / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
+    const int w0 = u0 + (u1 - u0) * warp / nw, w1 = u0 + (u1 - u0) * (warp + 1) / nw;
+    const int nst = w1 - w0;
+    auto unit = [&](int st, int &t, int &q, int &r) {
+        const int u = w0 + st, pi = u / a.ffe;
+        const int pr = s_pair[pi];
+        t = pr >> 5;
+        q = pr & 31;
+        r = u - pi * a.ffe;
+    };
+    auto issue = [&](int st) {  // lane 0: unit st of this warp into its ring slot: the gate row, then the up row
+        int t, q, r;
+        unit(st, t, q, r);
+        const uint8_t *g, *up;
+        if (q < a.k) {
+            const size_t off = ((size_t)(sel[t * 16 + q] - a.ep.e0) * a.ffe + r) * a.ldw;
             g = a.Wg + off;
             up = a.Wu + off;
         } else {
             g = a.Wsg + (size_t)r * a.ldw;
             up = a.Wsu + (size_t)r * a.ldw;
         }
-    };
-    long long next_u = u0;
-    int issued = 0;
-    auto issue_next = [&]() {  // thread 0
-        long long to;
-        stage_span(next_u, to);
-        const int slot = issued % a.slots, n = (int)(to - next_u);
-        const uint32_t half = (uint32_t)n * a.ldw;
-        const uint8_t *g, *up;
-        rows_ptr(next_u, g, up);
+        const int slot = st % a.slots;
         uint8_t *dst = ring + (size_t)slot * a.stage_bytes;
-        mbar_arrive_tx(&full[slot], 2 * half);
-        bulk_g2s(dst, g, half, &full[slot]);
-        bulk_g2s(dst + (size_t)a.rps * a.ldw, up, half, &full[slot]);
-        next_u = to;
-        ++issued;
+        mbar_arrive_tx(&full[slot], 2 * a.ldw);
+        bulk_g2s(dst, g, a.ldw, &full[slot]);
+        bulk_g2s(dst + a.ldw, up, a.ldw, &full[slot]);
     };
-    if (tid == 0)
-        while (issued < min(nst, a.slots)) issue_next();
+    if (lane == 0)  // the weight copies fly while x is staged
+        for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
+    if constexpr (XG > 0) {
+        if (!a.x_early) xr.load_global(x, lane, ScaleX<TY, SOA>::v);
+        __syncwarp();
+    } else {
+        stage_x(xsm, x, a.d, a.nt, G, ScaleX<TY, SOA>::v);  // ends with a __syncthreads
+    }
+    pdl_trigger();
 
-    constexpr int RPW = 32 / LPR;
-    const int lr = lane % LPR, sub = lane / LPR;
-    XReg<LPR, (GPL > 0 ? GPL : 1)> xr;
-    if constexpr (XREG) xr.load(xsm, lr);  // one token (nt == 1)
-
-    long long u = u0;
+    const int ni = (G + 31) / 32;
     int st = 0;
     for (; st < nst; ++st) {
-        long long to;
-        stage_span(u, to);
-        const int n = (int)(to - u), slot = st % a.slots;
-        const int t = (int)(u / ((long long)ks * a.ffe));
-        const bool ok = warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u);
-        if (ok) {
-            const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes;
-            for (int base = warp * RPW * RR; base < 2 * n; base += nw * RPW * RR) {  // rows 0..n-1 gate, n..2n-1 up
-                const uint8_t *rp[RR];
-                bool valid[RR];
-                int row[RR];
-#pragma unroll
-                for (int q = 0; q < RR; ++q) {
-                    row[q] = base + q * RPW + sub;
-                    valid[q] = row[q] < 2 * n;
-                    const int srow = !valid[q] ? 0 : row[q] < n ? row[q] : a.rps + (row[q] - n);
-                    rp[q] = sbuf + (size_t)srow * a.ldw;
-                }
-                double acc[RR][1];
-                rows_dot<TY, SOA, 1, LPR, GPL, XREG, RR>(rp, valid, a.nb, grid, xr, xsm + (size_t)t * G * XPAD, G, lr, 1,
-                                                        acc);
-                const bool hi = RR == 2 && (lane & 16);  // selects keep valid / row / acc in registers
-                if ((hi ? valid[RR - 1] : valid[0]) && (RR == 2 ? (lane & 15) == 0 : lr == 0))
-                    res[hi ? row[RR - 1] : row[0]] = __double2float_rn(acc[0][0]);
-            }
-        }
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
+        const int slot = st % a.slots;
+        if (!warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u)) {
+            if (lane == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
             break;
         }
-        for (int i = tid; i < n; i += blockDim.x) a.act[u + i] = silu(res[i]) * res[n + i];  // act = silu(g) * u
-        __syncthreads();
-        if (tid == 0 && issued < nst) issue_next();
-        u = to;
+        int t, q, r;
+        unit(st, t, q, r);
+        const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes;
+        const float *xt = xsm + (size_t)t * G * XPAD;
+        double accg = 0.0, accu = 0.0;  // group sums of the gate and the up row, in group order
+        if constexpr (XG > 0) {
+#pragma unroll
+            for (int i = 0; i < XG; ++i) {
+                const int g = lane + 32 * i;
+                const XRegA xa{xr.v[i], xr.s[i], xr.iv};
+                float rg[1], ru[1];
+                group_dot<TY, SOA, 1>(sbuf, a.nb, g, grid, xa, 1, rg);
+                group_dot<TY, SOA, 1>(sbuf + a.ldw, a.nb, g, grid, xa, 1, ru);
+                accg += (double)rg[0];
+                accu += (double)ru[0];
+            }
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < ni; ++i) {
+                const int g = lane + 32 * i;
+                if (g >= G) break;
+                XReg<32, 1> xg;  // group g of x in registers, shared by the two rows
+                xg.load(xt, g);
+                const XRegA xa{xg.v[0], xg.s[0], xg.iv};
+                float rg[1], ru[1];
+                group_dot<TY, SOA, 1>(sbuf, a.nb, g, grid, xa, 1, rg);
+                group_dot<TY, SOA, 1>(sbuf + a.ldw, a.nb, g, grid, xa, 1, ru);
+                accg += (double)rg[0];
+                accu += (double)ru[0];
+            }
+        }
+        // lanes 0-15 keep the gate row, 16-31 the up row (the halves' exchange adds the same pairs as a full butterfly)
+        const bool uh = lane & 16;
+        double keep = uh ? accu : accg;
+        keep += __shfl_xor_sync(0xffffffffu, uh ? accg : accu, 16);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+        const float v = __double2float_rn(keep);  // lanes 0-15: the gate row, 16-31: the up row
+        const float up = __shfl_sync(0xffffffffu, v, 16);
+        if (lane == 0) a.act[((size_t)t * ks + q) * a.ffe + r] = silu(v) * up;
+        __syncwarp();  // every lane is done reading the slot
+        if (lane == 0 && st + a.slots < nst) issue(st + a.slots);
     }
-    if (st < nst && tid == 0)
+    if (st < nst && lane == 0)  // wound down early: let the copies already issued land (bounded) before exiting
         for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
 }
 
@@ -256,7 +309,7 @@ __global__ void __launch_bounds__(256, 1) k_moe_gu(const MoeGuArgs a) {
 // down + shared expert + combine
 
 struct MoeDownArgs {
-    const uint8_t *Wd, *Wsd;  // routed (ne * d rows) and shared (d rows), ffe columns, stride ldw
+    const uint8_t *Wd, *Wsd;  // routed (local experts * d rows) and shared (d rows), ffe columns, stride ldw
     uint32_t ldw;
     int nb;
     int ne, k, ffe, d, nt;
@@ -265,119 +318,141 @@ struct MoeDownArgs {
     const float *act;  // [nt][k + 1][ffe]
     float *y;          // [nt][d]
     int acc;
-    int chunks;  // row chunks per token (gridDim.x)
-    int rps, slots;
-    uint32_t stage_bytes, ring_off, x_off, grid_off, misc_off;
+    const int *rsel;   // routing [nt][16] and its weights (k_moe_route, two kernels back)
+    const float *rw;
+    int rows;  // rows per CTA at most (gridDim.x chunks of d)
+    uint32_t w_off, x_off, grid_off, res_off, misc_off;
     uint32_t *err;
+    MoeEp ep;
 };
 
+// CTA (chunk, t) owns output rows [r0, r1) of token t. Before griddepcontrol.wait it routes token t and issues one
+// bulk copy per computed slot (that slot's rows [r0, r1), all in shared memory at once, one mbarrier each), so its
+// weight stream overlaps the gate/up kernel. After the wait the warps take (slot, row group) units independently;
+// one barrier, then the slot-order combine (or, expert parallel, the stores of this rank's slot outputs).
 template <uint32_t TY, int LPR, bool SOA>
-__global__ void __launch_bounds__(256, 1) k_moe_down(const MoeDownArgs a) {
-    constexpr int RR = LPR == 32 ? 2 : 1;
+__global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_down(const MoeDownArgs a) {
+    constexpr int RR = LPR == 32 ? 2 : 1, RPW = 32 / LPR, RU = RR * RPW;
     extern __shared__ __align__(128) uint8_t sm[];
-    uint64_t *full = (uint64_t *)sm;
-    uint8_t *ring = sm + a.ring_off;
+    uint64_t *bars = (uint64_t *)sm;  // [17]
+    uint8_t *wbuf = sm + a.w_off;
     float *xsm = (float *)(sm + a.x_off);
     uint32_t *grid = (uint32_t *)(sm + a.grid_off);
-    int *sel = (int *)(sm + a.misc_off);  // [16]
-    float *wsel = (float *)(sel + 16);
-    unsigned long long *keys = (unsigned long long *)(wsel + 16);
-    float *res = (float *)(keys + 128);  // [(k + 1) * rps]
+    float *res = (float *)(sm + a.res_off);  // [k + 1][rows]
+    __shared__ int sel[16];
+    __shared__ float wsel[16];
+    __shared__ int s_fail;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const int t = blockIdx.y, G = a.ffe / 32, ks = a.k + 1;
     const int r0 = (int)((long long)blockIdx.x * a.d / gridDim.x), r1 = (int)((long long)(blockIdx.x + 1) * a.d / gridDim.x);
-    const int nchunk = (r1 - r0 + a.rps - 1) / a.rps, nst = nchunk * ks;
-
-    if (tid == 0) {
-        for (int s = 0; s < a.slots; ++s) mbar_init(&full[s], 1);
-        mbar_fence_init();
+    const int n = r1 - r0;
+    // the routing was written by k_moe_route before the previous kernel (k_moe_gu) passed its own wait, so it is
+    // complete here without waiting; the expert rows to stream follow from it
+    if (tid < a.k) {
+        sel[tid] = a.rsel[t * 16 + tid];
+        wsel[tid] = a.rw[t * 16 + tid];
     }
     __syncthreads();
-    // routing: the logits were written before the previous kernel (k_moe_gu) passed its own wait, so they are
-    // complete here without waiting; the expert rows to stream follow from them
-    route_token(a.logits + (size_t)t * a.ls, a.ne, a.k, sel, wsel, keys);
-    auto issue = [&](int st) {  // thread 0: stage st = (chunk c, slot s)
-        const int c = st / ks, s = st % ks, rr = r0 + c * a.rps, n = min(a.rps, r1 - rr), slot = st % a.slots;
-        const uint8_t *src = s < a.k ? a.Wd + ((size_t)sel[s] * a.d + rr) * a.ldw : a.Wsd + (size_t)rr * a.ldw;
-        const uint32_t bytes = (uint32_t)n * a.ldw;
-        mbar_arrive_tx(&full[slot], bytes);
-        bulk_g2s(ring + (size_t)slot * a.stage_bytes, src, bytes, &full[slot]);
+    const uint32_t own = owned_slots(sel, a.k, a.ne, a.ep);
+    const int m = __popc(own);
+    auto slot_at = [&](int j) {  // the j-th (from 0) set bit of own
+        uint32_t mm = own;
+        for (int i = 0; i < j; ++i) mm &= mm - 1u;
+        return __ffs(mm) - 1;
     };
-    if (tid == 0)
-        for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
+    const size_t wslot = (size_t)a.rows * a.ldw;  // bytes of one slot's rows
+    if (tid == 0) {
+        s_fail = 0;
+        for (int j = 0; j < m; ++j) mbar_init(&bars[j], 1);
+        mbar_fence_init();
+        for (int j = 0; j < m; ++j) {
+            const int q = slot_at(j);
+            const uint8_t *src = q < a.k ? a.Wd + ((size_t)(sel[q] - a.ep.e0) * a.d + r0) * a.ldw : a.Wsd + (size_t)r0 * a.ldw;
+            mbar_arrive_tx(&bars[j], (uint32_t)(n * a.ldw));
+            bulk_g2s(wbuf + j * wslot, src, (uint32_t)(n * a.ldw), &bars[j]);
+        }
+    }
     stage_grid<TY>(grid);
     pdl_wait();
     const float *act = after_wait(a.act);
-    stage_x(xsm, act + (size_t)t * ks * a.ffe, a.ffe, ks, G, ScaleX<TY, SOA>::v);
+    const int par = a.ep.n ? (int)(*after_wait(a.ep.calls) & 1u) : 0;  // expert parallel: this call's output parity
+    stage_x(xsm, act + (size_t)t * ks * a.ffe, a.ffe, ks, G, ScaleX<TY, SOA>::v);  // ends with a __syncthreads
     pdl_trigger();
 
-    constexpr int RPW = 32 / LPR;
     const int lr = lane % LPR, sub = lane / LPR;
-    const float sg = sigm(a.logits[(size_t)t * a.ls + a.ne]);
     XReg<LPR, 1> xr;
-    int st = 0;
-    for (; st < nst; ++st) {
-        const int c = st / ks, s = st % ks, rr = r0 + c * a.rps, n = min(a.rps, r1 - rr), slot = st % a.slots;
-        const bool ok = warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u);
-        if (ok) {
-            const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes;
-            for (int base = warp * RPW * RR; base < n; base += nw * RPW * RR) {
-                const uint8_t *rp[RR];
-                bool valid[RR];
-                int row[RR];
-#pragma unroll
-                for (int q = 0; q < RR; ++q) {
-                    row[q] = base + q * RPW + sub;
-                    valid[q] = row[q] < n;
-                    rp[q] = sbuf + (size_t)(valid[q] ? row[q] : 0) * a.ldw;
-                }
-                double acc[RR][1];
-                rows_dot<TY, SOA, 1, LPR, 0, false, RR>(rp, valid, a.nb, grid, xr, xsm + (size_t)s * G * XPAD, G, lr, 1,
-                                                       acc);
-                const bool hi = RR == 2 && (lane & 16);
-                if ((hi ? valid[RR - 1] : valid[0]) && (RR == 2 ? (lane & 15) == 0 : lr == 0))
-                    res[s * a.rps + (hi ? row[RR - 1] : row[0])] = __double2float_rn(acc[0][0]);
-            }
-        }
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
+    const int npg = (n + RU - 1) / RU;
+    for (int u = warp; u < m * npg; u += nw) {
+        const int j = u / npg, pg = u % npg, q = slot_at(j);
+        if (!warp_wait(&bars[j], 0u)) {
+            if (lane == 0) s_fail = 1;
             break;
         }
-        if (s == a.k) {  // chunk complete: combine in slot order, then the gated shared expert
-            for (int i = tid; i < n; i += blockDim.x) {
-                float m = 0.0f;
-                for (int q = 0; q < a.k; ++q) m = __fmaf_rn(wsel[q], res[q * a.rps + i], m);
-                const float v = __fmaf_rn(sg, res[a.k * a.rps + i], m);
-                float *o = a.y + (size_t)t * a.d + rr + i;
-                *o = a.acc ? *o + v : v;
-            }
-            __syncthreads();
+        const uint8_t *rp[RR];
+        bool valid[RR];
+        int row[RR];
+#pragma unroll
+        for (int h = 0; h < RR; ++h) {
+            row[h] = pg * RU + h * RPW + sub;
+            valid[h] = row[h] < n;
+            rp[h] = wbuf + j * wslot + (size_t)(valid[h] ? row[h] : 0) * a.ldw;
         }
-        if (tid == 0 && st + a.slots < nst) issue(st + a.slots);
+        double acc[RR][1];
+        rows_dot<TY, SOA, 1, LPR, 0, false, RR>(rp, valid, a.nb, grid, xr, xsm + (size_t)q * G * XPAD, G, lr, 1, acc);
+        const bool hi = RR == 2 && (lane & 16);  // selects keep valid / row / acc in registers
+        if ((hi ? valid[RR - 1] : valid[0]) && (RR == 2 ? (lane & 15) == 0 : lr == 0))
+            res[q * a.rows + (hi ? row[RR - 1] : row[0])] = __double2float_rn(acc[0][0]);
     }
-    if (st < nst && tid == 0)
-        for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
+    __syncthreads();
+    if (s_fail) {  // a copy never landed: record it, let the others land (bounded), publish nothing
+        if (tid == 0) {
+            dev_fail(a.err, DEV_WAIT_TIMEOUT);
+            for (int j = 0; j < m; ++j) mbar_wait(&bars[j], 0u, 1u << 16);
+        }
+        return;
+    }
+    const float sg = sigm(a.logits[(size_t)t * a.ls + a.ne]);
+    if (a.ep.n == 0) {  // one GPU: combine in slot order, then the gated shared expert
+        for (int i = tid; i < n; i += blockDim.x) {
+            float acc = 0.0f;
+            for (int q = 0; q < a.k; ++q) acc = __fmaf_rn(wsel[q], res[q * a.rows + i], acc);
+            const float v = __fmaf_rn(sg, res[a.k * a.rows + i], acc);
+            float *o = a.y + (size_t)t * a.d + r0 + i;
+            *o = a.acc ? *o + v : v;
+        }
+    } else {  // expert parallel: this rank's slot outputs to every rank's slot-output area, then count the arrival
+        for (int i = tid; i < m * n; i += blockDim.x) {
+            const int q = slot_at(i / n), r = i % n;
+            const float v = res[q * a.rows + r];
+            const size_t off = (((size_t)par * MOE_EP_MAXT + t) * ks + q) * a.d + r0 + r;
+            for (int p = 0; p < a.ep.n; ++p) a.ep.dpart[p][off] = v;
+        }
+        __syncthreads();  // every thread's stores, then the release
+        if (tid == 0)
+            for (int p = 0; p < a.ep.n; ++p) red_release_sys_add(a.ep.counters[p] + a.ep.rank, 1u);
+    }
 }
 
 
 template <uint32_t TY>
 cudaError_t moe_gu_launch_t(const MoeGuArgs &a, bool planes, int nt, int G, int ctas, size_t smem, cudaStream_t s) {
     void (*k)(const MoeGuArgs) = nullptr;
-    if (planes) k = nt == 1 && G == 64 ? k_moe_gu<TY, 32, 2, true, true> : k_moe_gu<TY, 32, 0, false, true>;
-    else k = nt == 1 && G == 64 ? k_moe_gu<TY, 32, 2, true, false> : k_moe_gu<TY, 32, 0, false, false>;
+    if (nt == 1 && G == 64) k = planes ? k_moe_gu<TY, true, 2> : k_moe_gu<TY, false, 2>;
+    else if (nt == 1 && G == 32) k = planes ? k_moe_gu<TY, true, 1> : k_moe_gu<TY, false, 1>;
+    else k = planes ? k_moe_gu<TY, true, 0> : k_moe_gu<TY, false, 0>;
     const cudaError_t e = allow_max_dynamic_smem(k);
     if (e != cudaSuccess) return e;
-    return launch_k(k, dim3(ctas), dim3(256), smem, s, a);
+    return launch_k(k, dim3(ctas), dim3(MOE_THREADS), smem, s, a);
 }
 
 template <uint32_t TY>
 cudaError_t moe_down_launch_t(const MoeDownArgs &a, bool planes, int lpr, dim3 grid, size_t smem, cudaStream_t s) {
     void (*k)(const MoeDownArgs) = nullptr;
-    if (planes) k = lpr == 16 ? k_moe_down<TY, 16, true> : k_moe_down<TY, 32, true>;
-    else k = lpr == 16 ? k_moe_down<TY, 16, false> : k_moe_down<TY, 32, false>;
+    if (planes) k = lpr == 4 ? k_moe_down<TY, 4, true> : lpr == 8 ? k_moe_down<TY, 8, true> : lpr == 16 ? k_moe_down<TY, 16, true> : k_moe_down<TY, 32, true>;
+    else k = lpr == 4 ? k_moe_down<TY, 4, false> : lpr == 8 ? k_moe_down<TY, 8, false> : lpr == 16 ? k_moe_down<TY, 16, false> : k_moe_down<TY, 32, false>;
     const cudaError_t e = allow_max_dynamic_smem(k);
     if (e != cudaSuccess) return e;
-    return launch_k(k, grid, dim3(256), smem, s, a);
+    return launch_k(k, grid, dim3(MOE_THREADS), smem, s, a);
 }
 
 #define FN_MOE_SIG(TY)                                                                                       \

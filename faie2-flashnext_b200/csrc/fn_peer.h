@@ -18,8 +18,8 @@ struct PeerGroup {
     int rank = 0, n = 1, dev = 0;
     size_t bytes = 0;
     uint8_t *base[MAX_RANKS] = {};  // every rank's buffer as mapped in this process (base[rank] is this rank's own)
-    uint32_t *local_calls = nullptr;  // device counters of this rank: [0] key publishes, [1] key combines, [2] MoE
-                                      // publishes, [3] MoE combines
+    uint32_t *local_calls = nullptr;  // device counters of this rank: [0] key publishes, [1] key combines, [2..4]
+                                      // MoE calls, expected MoE arrivals, MoE combine ticket
     bool mapped[MAX_RANKS] = {};      // base[r] was opened here (closed at free)
 };
 

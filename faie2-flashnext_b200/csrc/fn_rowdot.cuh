@@ -25,10 +25,18 @@ template <uint32_t TY> __device__ __forceinline__ const uint32_t *dev_grid() {
 }
 
 // copy the codebook of TY (if it has one) to shared memory; every thread of the block calls this
+// (IQ3_XXS: after the 256 codebook words, its signed expansion for the fast path: entry (i, s) holds the 4 values of
+// codebook word i with the signs of the 4 bits of s (bit j set: value j negative) as bf16, exact for |v| <= 62, two
+// per word: tab[2 (16 i + s) + h] = bf16(v[2h]) | bf16(v[2h + 1]) << 16)
 template <uint32_t TY> __device__ __forceinline__ void stage_grid(uint32_t *grid) {
     if constexpr (Dec<TY>::gridw > 0) {
         const uint32_t *g = dev_grid<TY>();
         for (int i = threadIdx.x; i < Dec<TY>::gridw; i += blockDim.x) grid[i] = g[i];
+        if constexpr (TY == T_IQ3_XXS) {  // (generated with the codebook by gen_grids.py)
+            uint4 *tab = (uint4 *)(grid + Dec<TY>::gridw);
+            const uint4 *src = (const uint4 *)kIq3xxsSigned;
+            for (int i = threadIdx.x; i < 8192 / 4; i += blockDim.x) tab[i] = src[i];
+        }
     }
 }
 
@@ -92,6 +100,46 @@ template <int LPR, int GPL> struct XReg {
     float2 v[GPL][16];
     float s[GPL][2];
     float iv = 1.0f;
+    // Straight from x in global memory (16-byte aligned), by one warp whose lanes together hold every group of the
+    // row (LPR == 32 and GPL == G / 32): the same values, half sums and power-of-two scaling (denorm) as stage_x,
+    // with the row maximum taken over the warp instead of the block, so no block barrier is needed.
+    __device__ __forceinline__ void load_global(const float *x, int lr, bool denorm) {
+        float mx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < GPL; ++i) {
+            const float4 *src = (const float4 *)(x + (size_t)(lr + LPR * i) * 32);
+            float4 q[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) q[j] = src[j];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float p[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 f = q[4 * h + u];
+                    p[u] = __fadd_rn(__fadd_rn(f.x, f.y), __fadd_rn(f.z, f.w));
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+                }
+                s[i][h] = __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3]));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                v[i][2 * j] = make_float2(q[j].x, q[j].y);
+                v[i][2 * j + 1] = make_float2(q[j].z, q[j].w);
+            }
+        }
+        if (!denorm) return;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int e = ((__float_as_int(mx) >> 23) & 255) - 127;
+        const int K = max(22, min(127, 124 - e));
+        const float sc = __int_as_float((K + 127) << 23);
+#pragma unroll
+        for (int i = 0; i < GPL; ++i)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[i][j] = make_float2(__fmul_rn(v[i][j].x, sc), __fmul_rn(v[i][j].y, sc));
+        iv = __int_as_float((149 - K + 127) << 23);
+    }
     __device__ __forceinline__ void load(const float *xsm, int lr) {
         iv = xsm[34];
 #pragma unroll
@@ -147,25 +195,42 @@ __device__ __forceinline__ void rows_dot(const uint8_t *const (&rowp)[RR], const
     for (int q = 0; q < RR; ++q)
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[q][t] = 0.0;
-    const int ni = GPL > 0 ? GPL : (G + LPR - 1) / LPR;
+    if constexpr (GPL > 0) {  // a fixed number of groups per lane (x in registers or not): unrolled
 #pragma unroll
-    for (int i = 0; i < ni; ++i) {
-        const int g = lr + LPR * i;
-        if (GPL == 0 && g >= G) break;
+        for (int i = 0; i < GPL; ++i) {
+            const int g = lr + LPR * i;
 #pragma unroll
-        for (int q = 0; q < RR; ++q) {
-            if (!valid[q]) continue;
-            float r[NT];
-            if constexpr (XREG) {
-                const XRegA xa{xr.v[i], xr.s[i], xr.iv};
-                group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
-            } else {
-                const XSmA xa{xsm + (size_t)g * XPAD, G * XPAD};
-                group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
+            for (int q = 0; q < RR; ++q) {
+                if (!valid[q]) continue;
+                float r[NT];
+                if constexpr (XREG) {
+                    const XRegA xa{xr.v[i], xr.s[i], xr.iv};
+                    group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
+                } else {
+                    const XSmA xa{xsm + (size_t)g * XPAD, G * XPAD};
+                    group_dot<TY, SOA, NT>(rowp[q], nb, g, grid, xa, nt, r);
+                }
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    if (NT == 1 || t < nt) acc[q][t] += (double)r[t];
             }
+        }
+    } else {  // any row length: one decode body in a loop over (group, row), x from shared memory
+        const int ni = (G + LPR - 1) / LPR;
+#pragma unroll 1
+        for (int it = 0; it < ni * RR; ++it) {
+            const int i = it / RR, q = it - i * RR, g = lr + LPR * i;
+            if (g >= G) break;
+            if (!(q == 0 ? valid[0] : valid[RR - 1])) continue;
+            float r[NT];
+            const XSmA xa{xsm + (size_t)g * XPAD, G * XPAD};
+            group_dot<TY, SOA, NT>(q == 0 ? rowp[0] : rowp[RR - 1], nb, g, grid, xa, nt, r);
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-                if (NT == 1 || t < nt) acc[q][t] += (double)r[t];
+                if (NT == 1 || t < nt) {
+                    if (q == 0) acc[0][t] += (double)r[t];
+                    else acc[RR - 1][t] += (double)r[t];
+                }
         }
     }
     const int lane = threadIdx.x & 31;

@@ -29,7 +29,7 @@ EXPORTS = [
     "fn_bench_route", "fn_moe_layer_static", "fn_test_gdn", "fn_gdn_create", "fn_gdn_free", "fn_gdn_run",
     "fn_gdn_get_state", "fn_w_gemv_argmax", "fn_w_gemv_argmax_host", "fn_argmax", "fn_argmax_keys", "fn_test_argmax",
     "fn_test_gemv_argmax", "fn_ipc_alloc", "fn_ipc_open", "fn_ipc_close", "fn_ipc_free", "fn_group_create",
-    "fn_group_free", "fn_w_gemv_argmax_group",
+    "fn_group_free", "fn_w_gemv_argmax_group", "fn_moe_ep_create", "fn_moe_ep_run",
 ]
 
 
@@ -83,6 +83,9 @@ class FN:
         d.fn_group_free.argtypes = [C.c_int]
         d.fn_w_gemv_argmax_group.argtypes = [C.c_int, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp,
                                              vp]
+        d.fn_moe_ep_create.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, U8, U8, U8,
+                                       U8, U8, U8]
+        d.fn_moe_ep_run.argtypes = [C.c_int, vp, C.c_int, vp, vp, C.c_int, C.c_int, vp]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -208,6 +211,19 @@ class FN:
     def w_gemv_argmax_group(self, h, g, x_ptr, xs, y_ptr, ys, nt, flags, row0, index_ptr, stream=0):
         self.check(self.d.fn_w_gemv_argmax_group(h, g, C.c_void_p(x_ptr), xs, C.c_void_p(y_ptr or None), ys, nt, flags,
                                                  row0, C.c_void_p(index_ptr), C.c_void_p(stream)))
+
+    def moe_ep_create(self, gu_type, down_type, ne, k, ffe, d, group, Wg, Wu, Wd, Wsg, Wsu, Wsd):
+        """Expert-parallel MoE weights of this rank (its expert slice of Wg / Wu / Wd, the whole shared expert)."""
+        u8 = lambda a: np.ascontiguousarray(a, dtype=np.uint8).reshape(-1)
+        h = self.d.fn_moe_ep_create(int(gu_type), int(down_type), ne, k, ffe, d, group, u8(Wg), u8(Wu), u8(Wd), u8(Wsg),
+                                    u8(Wsu), u8(Wsd))
+        if h < 1:
+            raise RuntimeError(self.d.fn_error().decode())
+        return h
+
+    def moe_ep_run(self, h, logits_ptr, ls, x_ptr, y_ptr, nt=1, acc=0, stream=0):
+        self.check(self.d.fn_moe_ep_run(h, C.c_void_p(logits_ptr), ls, C.c_void_p(x_ptr), C.c_void_p(y_ptr), nt, acc,
+                                        C.c_void_p(stream)))
 
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))

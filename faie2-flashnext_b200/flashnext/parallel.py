@@ -36,7 +36,7 @@ class PeerGroup:
     engine's group id. `all_gather(obj) -> list` exchanges a picklable object between the ranks (e.g.
     torch.distributed.all_gather_object) and `barrier()` synchronises them; both are host-side plumbing only."""
 
-    BYTES = 1 << 20
+    BYTES = 8 << 20  # key area, MoE slot outputs for k <= 16, d <= 4096, 8 tokens, two parities
 
     def __init__(self, fn, rank: int, n: int, all_gather: Callable[[object], List[object]],
                  barrier: Callable[[], None], nbytes: int = BYTES):

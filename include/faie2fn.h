@@ -115,6 +115,17 @@ int fn_group_free(int group);
 int fn_w_gemv_argmax_group(int h, int group, const float *x, int xs, float *y, int ys, int nt, int flags, int row0,
                            int *index, void *stream);
 
+/* Expert-parallel MoE layer on a peer group: rank g holds routed experts [g ne / n, (g + 1) ne / n) (Wg / Wu: their
+ * ffe GGUF rows each, Wd: their d rows each) and the whole shared expert. Every rank routes every token; a routed
+ * slot is computed by its expert's rank, the shared slot by the rank with the fewest routed slots of the token; the
+ * down kernel stores its slot outputs into every rank's buffer over NVLink and counts its arrival; a combine kernel
+ * waits (bounded) and adds the k + 1 slots in slot order, bit-identical to the one-GPU layer, on every rank.
+ * New: the reference has no expert parallelism. Run: device pointers, logits [nt][ls], x, y [nt][d] replicated;
+ * acc flags as fn_moe_run. */
+int fn_moe_ep_create(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, int group, const uint8_t *Wg,
+                     const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd);
+int fn_moe_ep_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream);
+
 /* Synchronous hooks on host buffers: k_argmax over logits [nt][n]; the fused lm_head GEMV + argmax on GGUF rows
  * (as fn_test_gemv; y nullable), run twice on the same scratch so the second launch checks the ticket reset. */
 int fn_test_argmax(const float *logits, int n, int nt, int *out);
@@ -137,7 +148,10 @@ int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, in
 int fn_moe_create(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
                   const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd);
 int fn_moe_free(int h);
-/* Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d] (+= if acc). */
+/* Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d] (three kernels:
+ * routing, gate/up, down + combine). acc flags: bit 0 adds into y; bit 1 = x early: x was complete before the kernel
+ * before this call started (e.g. the router GEMV's predecessor wrote it), so the gate/up kernel reads it beside the
+ * routing kernel, as an early GEMV does (engine/faie2fn.cu:2247-2249). */
 int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream);
 /* Routing of router outputs given as split-K partials part[ks][8][528] (512 experts, top 10): sel / wsel [nt][10],
  * ms per call over iters graph-replayed calls. Replaces fn_bench_route (engine/faie2fn.cu:2873-2912). */

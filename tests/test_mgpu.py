@@ -39,3 +39,12 @@ def test_lm_head_row_split_argmax(n):
     rc, out = _torchrun("mgpu_lm_head.py", n, "--fail-test")
     assert rc == 0, out[-4000:]
     assert '"failures": 0' in out and '"failure_test": "ok"' in out, out[-4000:]
+
+
+@pytest.mark.parametrize("n", [2])
+def test_moe_expert_parallel(n):
+    if _ngpu() < n:
+        pytest.skip(f"needs {n} GPUs")
+    rc, out = _torchrun("mgpu_moe.py", n, "--fail-test")
+    assert rc == 0, out[-4000:]
+    assert '"failures": 0' in out and '"failure_test": "ok"' in out, out[-4000:]
