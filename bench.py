@@ -16,6 +16,9 @@ bytes, fp16 scales |N(0,1)|*1e-3), x is N(0,1): the reference's real model tenso
 
 `--impl reference` times that CPU path with every host core instead (rank 0 only; other ranks exit 0).
 N > 1 (torchrun): every rank runs the sweep on its own GPU and weights (weak scaling; no data-path collective).
+`--components` (1 GPU) prints one JSON line per component instead of the bench line: every sweep GEMV alone with cold
+weights (fn_bench_gemv), the config-3 MoE layer and the config-4 DeltaNet layer step, each timed with CUDA events over
+a CUDA graph of back-to-back calls whose weights alternate between two copies (together larger than L2).
 """
 
 from __future__ import annotations
@@ -139,6 +142,117 @@ def cpu_baseline_sample(work, target_s=12.0, workers=1):
     return s.bytes / dt / 1e9, frac, dt
 
 
+def run_components():
+    """Per-component device times on GPU 0 (see the module docstring); one JSON line each on stdout."""
+    import torch
+    from fn import FN
+    from synth import BY_NAME, TYPES, random_blocks
+
+    f = FN()
+    f.set_device(0)
+    torch.cuda.set_device(0)
+
+    def emit(d):
+        print(json.dumps(d), flush=True)
+
+    for name, r, c in [(n, r, c) for n in SWEEP13 for r, c in SHAPES] + [LM_HEAD]:
+        q = BY_NAME[name]
+        ms = f.bench_gemv(q, r, c, 1, 40 if r < 100000 else 10)
+        emit({"component": "gemv", "format": name, "rows": r, "cols": c, "us": round(ms * 1e3, 2),
+              "tb_per_s": round(alg_bytes(q, r, c) / (ms / 1e3) / 1e12, 3)})
+
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    K = 200
+
+    def timed(one):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(K):
+                one(i, torch.cuda.current_stream().cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        best = 1e30
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            g.replay()
+            b.record(st)
+            torch.cuda.synchronize()
+            best = min(best, a.elapsed_time(b) / K * 1e3)
+        del g
+        return best
+
+    # config 3: 512 experts, top-10, width 512, hidden 2048, IQ3_XXS gate/up, Q4_K down, shared expert
+    gu, dn, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 512, 10, 512, 2048
+    rng = np.random.default_rng(3)
+    W = [random_blocks(gu, ne * ffe, d, rng), random_blocks(gu, ne * ffe, d, rng), random_blocks(dn, ne * d, ffe, rng),
+         random_blocks(gu, ffe, d, rng), random_blocks(gu, ffe, d, rng), random_blocks(dn, d, ffe, rng)]
+    hs = [f.moe_create(gu, dn, ne, k, ffe, d, *W) for _ in range(2)]
+    del W
+    x = torch.randn(16, d, device="cuda")
+    lg = torch.randn(16, ne + 1, device="cuda") * 2
+    y = torch.zeros(8, d, device="cuda")
+    moe_bytes = (k + 1) * (2 * ffe * row_bytes_of(gu, d) + d * row_bytes_of(dn, ffe))
+    for nt in (1, 8):
+        us = timed(lambda i, cs: f.moe_run(hs[i % 2], lg[i % 16].data_ptr(), ne + 1, x[i % 16].data_ptr(), y.data_ptr(),
+                                           nt, 2, cs))
+        emit({"component": "moe_layer_config3", "tokens": nt, "us": round(us, 2), "kernels": 3,
+              "weight_bytes_per_token": moe_bytes})
+    for h in hs:
+        f.moe_free(h)
+
+    # config 4: Q5_K in-projection 2048 -> 8192 + 4096, Q8_0 alpha/beta 2048 -> 64, the core, Q5_K out 4096 -> 2048
+    NKH, NVH, DS = 16, 32, 128
+    CONVCH = 2 * NKH * DS + NVH * DS
+    q5, q8 = BY_NAME["Q5_K"], BY_NAME["Q8_0"]
+    hw = []
+    for _ in range(2):
+        w_in = f.w_create(q5, random_blocks(q5, CONVCH + NVH * DS, d, rng), CONVCH + NVH * DS, d)
+        w_ab = f.w_create(q8, random_blocks(q8, 2 * NVH, d, rng), 2 * NVH, d)
+        w_out = f.w_create(q5, random_blocks(q5, d, NVH * DS, rng), d, NVH * DS)
+        conv_w = (rng.standard_normal((CONVCH, 4)) * 0.5).astype(np.float32)
+        hg = f.gdn_create(NKH, NVH, conv_w, (rng.standard_normal(NVH) * 0.5).astype(np.float32),
+                          (-np.exp(rng.standard_normal(NVH) * 0.5)).astype(np.float32),
+                          (1 + 0.1 * rng.standard_normal(DS)).astype(np.float32),
+                          (rng.standard_normal((NVH, DS, DS)) * 0.02).astype(np.float32),
+                          rng.standard_normal((3, CONVCH)).astype(np.float32))
+        hw.append((w_in, w_ab, w_out, hg))
+    qkvz = torch.empty(CONVCH + NVH * DS, device="cuda")
+    ab = torch.empty(2 * NVH, device="cuda")
+    core = torch.empty(NVH * DS, device="cuda")
+    yo = torch.empty(d, device="cuda")
+
+    def gdn_core(i, cs):
+        f.gdn_run(hw[i % 2][3], qkvz.data_ptr(), CONVCH, qkvz.data_ptr() + 4 * CONVCH, NVH * DS, ab.data_ptr(),
+                  2 * NVH, core.data_ptr(), NVH * DS, 1, 0, cs)
+
+    def gdn_layer(i, cs):
+        w_in, w_ab, w_out, hg = hw[i % 2]
+        xp = x[i % 16].data_ptr()
+        f.w_gemv(w_in, xp, d, qkvz.data_ptr(), CONVCH + NVH * DS, 1, 0, cs)
+        f.w_gemv(w_ab, xp, d, ab.data_ptr(), 2 * NVH, 1, 2, cs)
+        f.gdn_run(hg, qkvz.data_ptr(), CONVCH, qkvz.data_ptr() + 4 * CONVCH, NVH * DS, ab.data_ptr(), 2 * NVH,
+                  core.data_ptr(), NVH * DS, 1, 1, cs)
+        f.w_gemv(w_out, core.data_ptr(), NVH * DS, yo.data_ptr(), d, 1, 0, cs)
+
+    emit({"component": "gdn_core_config4", "tokens": 1, "us": round(timed(gdn_core), 2),
+          "state_bytes_read_and_written": 2 * NVH * DS * DS * 4})
+    emit({"component": "gdn_layer_config4", "tokens": 1, "us": round(timed(gdn_layer), 2), "kernels": 4,
+          "weight_bytes": row_bytes_of(q5, d) * (CONVCH + NVH * DS) + row_bytes_of(q8, d) * 2 * NVH
+          + row_bytes_of(q5, NVH * DS) * d})
+    for w_in, w_ab, w_out, hg in hw:
+        for h in (w_in, w_ab, w_out):
+            f.w_free(h)
+        f.gdn_free(hg)
+
+
+def row_bytes_of(qtype, cols):
+    from synth import TYPES
+    _, qk, tb = TYPES[qtype]
+    return cols // qk * tb
+
+
 def run_reference(args, rank):
     """`--impl reference`: the reference's CPU path (gguf-py dequant + float64 GEMV) on every host core."""
     if rank != 0:
@@ -181,6 +295,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--components", action="store_true",
+                    help="per-component device times (sweep GEMVs alone, config-3 MoE layer, config-4 DeltaNet layer)")
     ap.add_argument("--workload", default="sweep", choices=["sweep", "lm_head"],
                     help="lm_head: only the dominant kernel (the small case the ncu capture profiles)")
     args = ap.parse_args()
@@ -189,6 +305,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.components:
+        if rank == 0:
+            run_components()
         return
     if args.warmup < 3:
         args.warmup = 3
