@@ -110,7 +110,10 @@ struct DevBuf {
     template <typename T> T *as() const { return (T *)p; }
 };
 
-// allow a kernel the largest dynamic shared memory the SM grants next to its static shared memory (once per kernel)
+// allow a kernel the largest dynamic shared memory the SM grants next to its static shared memory, and ask for the
+// SM's largest shared-memory carveout: an SM configured with a smaller carveout for one kernel cannot take a CTA of
+// the next kernel that needs more until it drains, which would keep consecutive small kernels from overlapping under
+// programmatic dependent launch (once per kernel)
 template <typename K> cudaError_t allow_max_dynamic_smem(K *k) {
     static std::unordered_set<const void *> done;
     if (done.count((const void *)k)) return cudaSuccess;
@@ -118,6 +121,7 @@ template <typename K> cudaError_t allow_max_dynamic_smem(K *k) {
     cudaError_t e = cudaFuncGetAttributes(&fa, k);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227 * 1024 - fa.sharedSizeBytes));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess) done.insert((const void *)k);
     return e;
 }

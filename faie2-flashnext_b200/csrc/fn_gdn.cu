@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     if (ch >= 0) w = a.conv_w[ch];
     const float nwj = a.norm_w[j], dtb = a.dt_bias[h], sa = a.ssm_a[h];
     pdl_wait();
+    pdl_trigger();
     if (!a.prefetch) {
         Sh = after_wait(Sh);
         if (stp) stp = after_wait(stp);
@@ -99,7 +100,6 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     const float *qkv = after_wait(a.qkv);
     const float *zp = after_wait(a.z);
     const float *abp = after_wait(a.ab);
-    pdl_trigger();
 
     for (int t = 0; t < a.nt; ++t) {
         // conv + silu of this thread's channel; history shifts

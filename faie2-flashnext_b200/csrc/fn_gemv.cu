@@ -145,9 +145,11 @@ bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap) {
     size_t xb = (size_t)p.ntcap * p.G * XPAD * 4;
     if (fixed + xb + 2 * (size_t)p.stage_bytes > kDynSmem) xb = (size_t)p.G * XPAD * 4;
     const size_t ring_budget = std::min<size_t>((size_t)S.ring_kb * 1024, kDynSmem - fixed - xb);
-    // warps: the setting (S.warps_per_cta > 0), else 16 for large weights and 8 for small ones, fewer when wide rows
-    // would leave less than two stages per warp
-    int nw = S.warps_per_cta > 0 ? S.warps_per_cta : ((size_t)rows * p.rb >= (64u << 20) ? 16 : 8);
+    // warps: the setting (S.warps_per_cta > 0), else by weight size, fewer when wide rows would leave less than two
+    // stages per warp
+    // (small weights: 4 warps, so that the CTAs of consecutive GEMVs fit on an SM together and overlap)
+    const size_t wbytes = (size_t)rows * p.rb;
+    int nw = S.warps_per_cta > 0 ? S.warps_per_cta : wbytes >= (64u << 20) ? 16 : wbytes >= (16u << 20) ? 8 : 4;
     nw = std::max(1, std::min(nw, 16));
     while (nw > 1 && (size_t)nw * 2 * p.stage_bytes > ring_budget) --nw;
     if ((size_t)nw * p.stage_bytes > ring_budget) return false;

@@ -109,6 +109,11 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
         for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
     }
     __syncwarp();
+    // The next kernel may launch (its CTAs stage their own weights beside this one where they fit; its
+    // griddepcontrol.wait still waits for this whole grid; a dependent grid starts about 2 us after the trigger):
+    // an early GEMV triggers at once, as the reference's does (engine/faie2fn.cu:920-922); any other kernel only after
+    // its own wait, so that everything before it is complete when the kernel after it starts.
+    if (a.early) pdl_trigger();
     stage_grid<TY>(grid);
 
     // fused argmax: best key per storing lane (one token: a register; else per (warp, writer, token) in shared
@@ -119,11 +124,13 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     if (NT > 1 && a.amx)
         for (int i = tid; i < 16 * 4 * NT; i += blockDim.x) (&s_best[0][0][0])[i] = 0ull;
 
-    if (!a.early) pdl_wait();
+    if (!a.early) {
+        pdl_wait();
+        pdl_trigger();
+    }
     const float *x = after_wait(a.x);
     const int nt = a.nt;
     stage_x(xsm, x, a.xs, nt, a.G, ScaleX<TY, true>::v);
-    pdl_trigger();
 
     const int lr = lane % LPR, sub = lane / LPR;
     XReg<LPR, (GPL > 0 ? GPL : 1)> xr;

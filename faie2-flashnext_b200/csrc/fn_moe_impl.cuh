@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     if constexpr (XG > 0)
         if (a.x_early) xr.load_global(a.x, lane, ScaleX<TY, SOA>::v);  // beside the routing kernel
     pdl_wait();
+    pdl_trigger();  // after the wait: the down kernel may rely on the routing being complete before it starts
     const float *x = after_wait(a.x);
     const int *rsel = after_wait(a.rsel);
     for (int i = tid; i < a.nt * 16; i += blockDim.x) sel[i] = rsel[i];
@@ -248,7 +249,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     } else {
         stage_x(xsm, x, a.d, a.nt, G, ScaleX<TY, SOA>::v);  // ends with a __syncthreads
     }
-    pdl_trigger();
 
     const int ni = (G + 31) / 32;
     int st = 0;
@@ -374,10 +374,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_down(const MoeDownArgs a
     }
     stage_grid<TY>(grid);
     pdl_wait();
+    pdl_trigger();
     const float *act = after_wait(a.act);
     const int par = a.ep.n ? (int)(*after_wait(a.ep.calls) & 1u) : 0;  // expert parallel: this call's output parity
     stage_x(xsm, act + (size_t)t * ks * a.ffe, a.ffe, ks, G, ScaleX<TY, SOA>::v);  // ends with a __syncthreads
-    pdl_trigger();
 
     const int lr = lane % LPR, sub = lane / LPR;
     XReg<LPR, 1> xr;
