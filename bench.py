@@ -8,8 +8,9 @@ bytes, fp16 scales |N(0,1)|*1e-3), x is N(0,1): the reference's real model tenso
   value  device-resident throughput: algorithmic bytes (GGUF weight bytes + 4*cols x + 4*rows y per GEMV) of all
          ranks / the max over ranks of the CUDA-event time of K steps, each step one replay of the sweep captured as
          CUDA graphs (programmatic dependent launch between the GEMVs)
-  e2e    the same metric through the C ABI with host buffers: every GEMV copies its x in from pinned memory and its y
-         out, inside the timed region
+  e2e    the same metric through the C ABI with host buffers: one fn_w_step_host call per step copies every x in from
+         pinned memory, runs the step's GEMVs and copies every y (the lm_head: its token id) out, inside the timed
+         region
   roofline  the dominant kernel (the lm_head GEMV): its algorithmic bytes / its mean CUDA-event duration inside the
          timed region, against the measured HBM copy bandwidth
   cpu_baseline  the reference's CPU path (gguf-py dequant + float64 numpy GEMV) on a bounded row sample, 1 core
@@ -407,20 +408,17 @@ def main():
     value = world * step_bytes * K / (ms / 1e3) / 1e9
 
     # e2e: through the C ABI with pinned host buffers, host<->device copies inside the timed region
-    # (the lm_head returns its token id, as a decode step does; the other GEMVs their outputs)
-    xh = [torch.empty(w[2], dtype=torch.float32, pin_memory=True) for w in work]
-    yh = [torch.empty(w[1], dtype=torch.float32, pin_memory=True) for w in work[:-1]]
-    ih = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-    for i, x in enumerate(xs):
-        xh[i].copy_(x.cpu())
+    # one call per step (fn_w_step_host): every input copied in from pinned host memory, the step's GEMVs, every
+    # output copied out (the lm_head returns its token id, as a decode step does; the other GEMVs their outputs)
+    xh = torch.cat([x.cpu() for x in xs]).pin_memory()
+    yh = torch.empty(sum(w[1] for w in work[:-1]), dtype=torch.float32).pin_memory()
+    ih = torch.zeros(1, dtype=torch.int32).pin_memory()
     h2d = sum(4 * w[2] for w in work)
     d2h = sum(4 * w[1] for w in work[:-1]) + 4
     Ke = max(3, min(K, 200))
 
     def e2e_step():
-        for i in range(len(work) - 1):
-            f.w_gemv_host(hs[i], xh[i].data_ptr(), 1, yh[i].data_ptr(), stream.cuda_stream)
-        f.w_gemv_argmax_host(hs[-1], xh[-1].data_ptr(), 1, 0, ih.data_ptr(), stream.cuda_stream)
+        f.w_step_host(hs, xh.data_ptr(), yh.data_ptr(), len(work) - 1, ih.data_ptr(), stream.cuda_stream)
         f.sync(stream.cuda_stream)
 
     for _ in range(3):
@@ -439,7 +437,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = world * step_bytes * Ke / (e2e_ms / 1e3) / 1e9
-    ok = bool(all(np.isfinite(y.numpy()).all() for y in yh)) and 0 <= int(ih[0]) < work[-1][1]
+    ok = bool(np.isfinite(yh.numpy()).all()) and 0 <= int(ih[0]) < work[-1][1]
     ok = ok and int(ih[0]) == int(amax_d[0].item())  # same x: the host-path token equals the graph's
 
     peak, peak_kind = measured_peak()

@@ -4,6 +4,7 @@
 // owns every host buffer; every fn_test_* / fn_bench_* call is synchronous.
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -99,6 +100,62 @@ static std::mutex g_w_mu;
 static WeightH *wget(int h) {
     std::lock_guard<std::mutex> l(g_w_mu);
     return h >= 1 && h <= (int)g_w.size() ? g_w[h - 1] : nullptr;
+}
+
+// a decode step's GEMVs on host buffers (fn_w_step_host)
+struct StepPlan {
+    DevBuf x, y;  // staging: the inputs back to back, then the outputs back to back (+ one int for the argmax)
+    size_t xn = 0, yn = 0;
+    cudaGraphExec_t exec = nullptr;
+    ~StepPlan() {
+        if (exec) cudaGraphExecDestroy(exec);
+    }
+};
+static std::map<std::vector<int>, StepPlan *> g_steps;
+static std::mutex g_steps_mu;
+
+static int build_step(const std::vector<int> &key, int n, const int *handles, int head, StepPlan *sp) {
+    size_t xn = 0, yn = 0;
+    for (int i = 0; i < n; ++i) {
+        WeightH *w = wget(handles[i]);
+        if (!w) return fail("fn_w_step_host: bad handle " + std::to_string(handles[i]));
+        xn += (size_t)w->plan1.cols;
+        if (i != head) yn += (size_t)w->plan1.rows;
+    }
+    sp->xn = xn;
+    sp->yn = yn;
+    FN_CK(cudaMalloc(&sp->x.p, std::max<size_t>(xn, 1) * 4));
+    FN_CK(cudaMalloc(&sp->y.p, (yn + 4) * 4));
+    cudaStream_t cap;
+    FN_CK(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    cudaGraph_t g = nullptr;
+    int rc = 0;
+    if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) rc = fail("fn_w_step_host: capture");
+    size_t xo = 0, yo = 0;
+    for (int i = 0; i < n && !rc; ++i) {
+        WeightH *w = wget(handles[i]);
+        const GemvPlan &p = w->plan1;
+        // inputs come from the copy before the graph: every GEMV after the first may read its x before waiting
+        const bool early = i > 0;
+        if (i == head) {
+            GemvArgmax am;
+            am.index = (int *)(sp->y.as<float>() + yn);
+            am.kacc = w->kacc;
+            am.ticket = w->ticket;
+            rc = launch_gemv(p, w->d, sp->x.as<float>() + xo, p.cols, nullptr, p.rows, 1, false, early, cap, &am);
+        } else {
+            rc = launch_gemv(p, w->d, sp->x.as<float>() + xo, p.cols, sp->y.as<float>() + yo, p.rows, 1, false, early, cap);
+            yo += (size_t)p.rows;
+        }
+        xo += (size_t)p.cols;
+    }
+    const cudaError_t ce = cudaStreamEndCapture(cap, &g);
+    if (!rc && ce != cudaSuccess) rc = fail(std::string("fn_w_step_host: capture: ") + cudaGetErrorString(ce));
+    if (!rc && cudaGraphInstantiate(&sp->exec, g, 0) != cudaSuccess) rc = fail("fn_w_step_host: graph instantiate");
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(cap);
+    (void)key;
+    return rc;
 }
 
 }  // namespace fn
@@ -274,6 +331,19 @@ FN_API int fn_w_create(uint32_t type, const uint8_t *Wh, int rows, int cols) {
 FN_API int fn_w_free(int h) {
     WeightH *w = wget(h);
     if (!w) return fail("fn_w_free: bad handle");
+    {
+        std::lock_guard<std::mutex> l(g_steps_mu);
+        for (auto it = g_steps.begin(); it != g_steps.end();) {
+            bool uses = false;
+            for (size_t i = 0; i + 1 < it->first.size(); ++i) uses = uses || it->first[i] == h;
+            if (uses) {
+                delete it->second;
+                it = g_steps.erase(it);
+            } else {
+                ++it;
+            }
+        }
+    }
     cudaFree(w->d);
     cudaFree(w->xbuf);
     cudaFree(w->ybuf);
@@ -438,6 +508,43 @@ FN_API int fn_w_gemv_host(int h, const float *xh, int nt, float *yh, void *strea
     FN_CK(cudaMemcpyAsync(w->xbuf, xh, (size_t)nt * p.cols * 4, cudaMemcpyHostToDevice, s));
     if (launch_gemv(p, w->d, w->xbuf, p.cols, w->ybuf, p.rows, nt, false, false, s)) return -1;
     FN_CK(cudaMemcpyAsync(yh, w->ybuf, (size_t)nt * p.rows * 4, cudaMemcpyDeviceToHost, s));
+    return 0;
+}
+
+// ---- a decode step's GEMVs on host buffers ---------------------------------------------------------------------------
+// One host->device copy of every input, the GEMVs as one CUDA graph (built on the first call for a list of handles and
+// replayed after), one device->host copy of every output: the per-call host overhead of a step is paid once.
+
+// A decode step's GEMVs, one token each, on host buffers: x the inputs of handles[0..n) back to back (cols_i floats
+// each), y the outputs back to back (rows_i floats each, the lm_head's left out); head (-1: none) is the index in
+// handles of the lm_head, whose argmax goes to *index instead of its logits. One host->device copy, the GEMVs as one
+// CUDA graph (built on the first call for this list of handles, then replayed), one device->host copy, on `stream`
+// (pinned host buffers make the copies asynchronous); does not synchronise. New: the reference's fn_forward runs a
+// whole step per call (engine/faie2fn.cu:2733); this is that call's shape for the GEMV path alone.
+FN_API int fn_w_step_host(int n, const int *handles, const float *xh, float *yh, int head, int *index, void *stream) {
+    if (n < 1 || head >= n || (head >= 0 && !index)) return fail("fn_w_step_host: bad arguments");
+    std::vector<int> key(handles, handles + n);
+    key.push_back(head);
+    StepPlan *sp = nullptr;
+    {
+        std::lock_guard<std::mutex> l(g_steps_mu);
+        auto it = g_steps.find(key);
+        if (it != g_steps.end()) sp = it->second;
+    }
+    if (!sp) {
+        sp = new StepPlan();
+        if (build_step(key, n, handles, head, sp)) {
+            delete sp;
+            return -1;
+        }
+        std::lock_guard<std::mutex> l(g_steps_mu);
+        g_steps[key] = sp;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    FN_CK(cudaMemcpyAsync(sp->x.p, xh, sp->xn * 4, cudaMemcpyHostToDevice, s));
+    FN_CK(cudaGraphLaunch(sp->exec, s));
+    if (sp->yn) FN_CK(cudaMemcpyAsync(yh, sp->y.p, sp->yn * 4, cudaMemcpyDeviceToHost, s));
+    if (head >= 0) FN_CK(cudaMemcpyAsync(index, sp->y.as<float>() + sp->yn, 4, cudaMemcpyDeviceToHost, s));
     return 0;
 }
 

@@ -361,17 +361,16 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_down(const MoeDownArgs a
         return __ffs(mm) - 1;
     };
     const size_t wslot = (size_t)a.rows * a.ldw;  // bytes of one slot's rows
-    if (tid == 0) {
-        s_fail = 0;
-        for (int j = 0; j < m; ++j) mbar_init(&bars[j], 1);
-        mbar_fence_init();
-        for (int j = 0; j < m; ++j) {
+    if (tid == 0) s_fail = 0;
+    for (int j = warp; j < m; j += nw)  // one copy per slot, issued by different warps at once
+        if (lane == 0) {
             const int q = slot_at(j);
             const uint8_t *src = q < a.k ? a.Wd + ((size_t)(sel[q] - a.ep.e0) * a.d + r0) * a.ldw : a.Wsd + (size_t)r0 * a.ldw;
+            mbar_init(&bars[j], 1);
+            mbar_fence_init();
             mbar_arrive_tx(&bars[j], (uint32_t)(n * a.ldw));
             bulk_g2s(wbuf + j * wslot, src, (uint32_t)(n * a.ldw), &bars[j]);
         }
-    }
     stage_grid<TY>(grid);
     pdl_wait();
     pdl_trigger();

@@ -29,7 +29,7 @@ EXPORTS = [
     "fn_bench_route", "fn_moe_layer_static", "fn_test_gdn", "fn_gdn_create", "fn_gdn_free", "fn_gdn_run",
     "fn_gdn_get_state", "fn_w_gemv_argmax", "fn_w_gemv_argmax_host", "fn_argmax", "fn_argmax_keys", "fn_test_argmax",
     "fn_test_gemv_argmax", "fn_ipc_alloc", "fn_ipc_open", "fn_ipc_close", "fn_ipc_free", "fn_group_create",
-    "fn_group_free", "fn_w_gemv_argmax_group", "fn_moe_ep_create", "fn_moe_ep_run",
+    "fn_group_free", "fn_w_gemv_argmax_group", "fn_moe_ep_create", "fn_moe_ep_run", "fn_w_step_host",
 ]
 
 
@@ -86,6 +86,7 @@ class FN:
         d.fn_moe_ep_create.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, U8, U8, U8,
                                        U8, U8, U8]
         d.fn_moe_ep_run.argtypes = [C.c_int, vp, C.c_int, vp, vp, C.c_int, C.c_int, vp]
+        d.fn_w_step_host.argtypes = [C.c_int, I32, vp, vp, C.c_int, vp, vp]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -178,6 +179,13 @@ class FN:
 
     def argmax_keys(self, keys_ptr, nranks, nt, out_ptr, stream=0):
         self.check(self.d.fn_argmax_keys(C.c_void_p(keys_ptr), nranks, nt, C.c_void_p(out_ptr), C.c_void_p(stream)))
+
+    def w_step_host(self, handles, x_ptr, y_ptr, head=-1, index_ptr=0, stream=0):
+        """A decode step's GEMVs on host buffers (x / y: the inputs / outputs back to back; head: the lm_head's
+        position, its argmax to index_ptr)."""
+        hs = np.ascontiguousarray(handles, np.int32)
+        self.check(self.d.fn_w_step_host(len(hs), hs, C.c_void_p(x_ptr), C.c_void_p(y_ptr or None), head,
+                                         C.c_void_p(index_ptr or None), C.c_void_p(stream)))
 
     # ---- peer-memory groups (one process per GPU) ----
     def ipc_alloc(self, nbytes):

@@ -75,6 +75,13 @@ double fn_w_bytes(int h);
 int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int flags, void *stream);
 /* The same with host buffers x (nt x cols) and y (nt x rows), copied on the stream; does not synchronise. */
 int fn_w_gemv_host(int h, const float *x, int nt, float *y, void *stream);
+/* A decode step's GEMVs, one token each, on host buffers: x = the inputs of handles[0..n) back to back (cols_i floats
+ * each), y = the outputs back to back (rows_i floats each, the lm_head's left out); head (-1: none) = the position in
+ * handles of the lm_head, whose argmax goes to *index instead of its logits. One host->device copy, the GEMVs as one
+ * CUDA graph (built on the first call for a list of handles, then replayed), one device->host copy; does not
+ * synchronise. New: the reference's fn_forward (engine/faie2fn.cu:2733) runs a whole step per call; this is that
+ * call's shape for the GEMV path. */
+int fn_w_step_host(int n, const int *handles, const float *x, float *y, int head, int *index, void *stream);
 /* Synchronise a stream and report any device-side error (a bounded wait that ran out). */
 int fn_sync(void *stream);
 

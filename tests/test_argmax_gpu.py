@@ -107,3 +107,35 @@ def test_gemv_argmax_lm_head_handle(fn):
             assert abs(float(y[0, w]) - float(y64[0, 0])) <= 2e-7 * np.abs(y).max()
     finally:
         fn.w_free(h)
+
+
+def test_step_host_matches_single_calls(fn):
+    """fn_w_step_host (one copy in, the GEMVs as a replayed graph, one copy out) gives the same bits as one-call-per-GEMV
+    launches, twice in a row (the second call replays the cached graph), with the lm_head's argmax instead of logits."""
+    import torch
+    rng = np.random.default_rng(17)
+    specs = [("Q4_K", 4096, 2048), ("IQ3_XXS", 512, 2048), ("Q8_0", 2048, 4096), ("Q6_K", 20000, 2048)]
+    hs, raws = [], []
+    for name, r, c in specs:
+        raws.append(random_blocks(BY_NAME[name], r, c, rng))
+        hs.append(fn.w_create(BY_NAME[name], raws[-1], r, c))
+    try:
+        st = torch.cuda.current_stream().cuda_stream
+        for rep in range(2):
+            xs = [random_x(1, c, rng)[0] for _, _, c in specs]
+            xh = torch.from_numpy(np.concatenate(xs)).pin_memory()
+            yh = torch.zeros(sum(r for _, r, _ in specs[:-1]), dtype=torch.float32).pin_memory()
+            ih = torch.full((1,), -1, dtype=torch.int32).pin_memory()
+            fn.w_step_host(hs, xh.data_ptr(), yh.data_ptr(), len(hs) - 1, ih.data_ptr(), st)
+            fn.sync(st)
+            off = 0
+            for i, (name, r, c) in enumerate(specs[:-1]):
+                want = fn.gemv(BY_NAME[name], raws[i], r, c, xs[i][None])[0]
+                assert np.array_equal(yh.numpy()[off:off + r].view(np.uint32), want.view(np.uint32)), name
+                off += r
+            name, r, c = specs[-1]
+            idx, _ = fn.gemv_argmax(BY_NAME[name], raws[-1], r, c, xs[-1][None], logits=False)
+            assert int(ih[0]) == int(idx[0])
+    finally:
+        for h in hs:
+            fn.w_free(h)
