@@ -230,11 +230,16 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         // one SM fewer than the GPU has: the routing kernel's CTA keeps an SM while the gate/up CTAs start beside it
         // (programmatic launch), and a gate/up CTA does not fit next to it
         const int ctas = (int)std::min<long long>(std::max(1, sm_count() - 1), (U + 7) / 8);
-        a.stage_bytes = (uint32_t)al((size_t)2 * p.ldw_gu, 128);
+        const long long per_warp0 = (U + (long long)ctas * NW - 1) / ((long long)ctas * NW);
         const size_t xb = (size_t)nt * (p.d / 32) * XPAD * 4, misc = 8 * 16 * 4, gw = (size_t)grid_words(p.gu_type) * 4;
         const size_t fixed = 1024 + gw + 128 + misc + 128 + xb + 128;
+        // a warp's few units in one stage (one more stage where its run crosses an expert boundary); else one unit
+        // per stage; shorter runs where rows are wide
+        a.run = per_warp0 <= 4 ? (int)per_warp0 : 1;
+        while (a.run > 1 && fixed + (size_t)NW * al((size_t)2 * a.run * p.ldw_gu, 128) > kMoeDynSmem / 2) --a.run;
+        a.stage_bytes = (uint32_t)al((size_t)2 * a.run * p.ldw_gu, 128);
         if (fixed + (size_t)NW * a.stage_bytes > kMoeDynSmem) return fail("moe: gate/up rows too wide for shared memory");
-        const long long per_warp = (U + (long long)ctas * NW - 1) / ((long long)ctas * NW);
+        const long long per_warp = (per_warp0 + a.run - 1) / a.run + 1;  // stages per warp at most
         const long long fit = (long long)(std::min<size_t>(128 * 1024, kMoeDynSmem - fixed) / ((size_t)NW * a.stage_bytes));
         a.slots = (int)std::max<long long>(1, std::min<long long>(std::min<long long>(8, per_warp), fit));
         a.slots = std::min(a.slots, 1024 / (8 * NW));  // barriers: 1 KiB

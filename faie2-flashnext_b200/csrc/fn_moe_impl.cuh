@@ -160,7 +160,8 @@ struct MoeGuArgs {
     float *act;      // [nt][k + 1][ffe]
     const int *rsel;  // routing [nt][16] (k_moe_route, the kernel before this one)
     int x_early;      // x was complete before the routing kernel started: read it before the wait
-    int slots;  // ring stages per warp; a stage is one unit: a gate row and the matching up row
+    int slots;  // ring stages per warp
+    int run;    // units per stage at most: `run` consecutive gate rows of one expert, then the matching up rows
     uint32_t stage_bytes, ring_off, x_off, grid_off, misc_off;
     uint32_t *err;
     MoeEp ep;
@@ -198,16 +199,18 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     pdl_trigger();  // after the wait: the down kernel may rely on the routing being complete before it starts
     const float *x = after_wait(a.x);
     const int *rsel = after_wait(a.rsel);
-    for (int i = tid; i < a.nt * 16; i += blockDim.x) sel[i] = rsel[i];
-    __syncthreads();
-    if (tid == 0) {
-        int np = 0;
-        for (int t = 0; t < a.nt; ++t) {
-            const uint32_t m = owned_slots(sel + t * 16, a.k, a.ne, a.ep);
-            for (int q = 0; q < ks; ++q)
-                if (m >> q & 1u) s_pair[np++] = t << 5 | q;
+    if (warp == 0) {  // the routing and this rank's (token, slot) pairs, then one block barrier
+        for (int i = lane; i < a.nt * 16; i += 32) sel[i] = rsel[i];
+        __syncwarp();
+        if (lane == 0) {
+            int np = 0;
+            for (int t = 0; t < a.nt; ++t) {
+                const uint32_t m = owned_slots(sel + t * 16, a.k, a.ne, a.ep);
+                for (int q = 0; q < ks; ++q)
+                    if (m >> q & 1u) s_pair[np++] = t << 5 | q;
+            }
+            s_np = np;
         }
-        s_np = np;
     }
     __syncthreads();
 
@@ -215,17 +218,23 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     const int U = s_np * a.ffe;
     const int u0 = (int)((long long)blockIdx.x * U / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
     const int w0 = u0 + (u1 - u0) * warp / nw, w1 = u0 + (u1 - u0) * (warp + 1) / nw;
-    const int nst = w1 - w0;
-    auto unit = [&](int st, int &t, int &q, int &r) {
-        const int u = w0 + st, pi = u / a.ffe;
+    // stages: runs of at most `run` consecutive units of one pair (contiguous rows of one expert)
+    auto run_end = [&](int u) { return min(min(u + a.run, w1), (u / a.ffe + 1) * a.ffe); };
+    int nst = 0;
+    for (int u = w0; u < w1; u = run_end(u)) ++nst;
+    auto unit = [&](int u, int &t, int &q, int &r) {
+        const int pi = u / a.ffe;
         const int pr = s_pair[pi];
         t = pr >> 5;
         q = pr & 31;
         r = u - pi * a.ffe;
     };
-    auto issue = [&](int st) {  // lane 0: unit st of this warp into its ring slot: the gate row, then the up row
+    const size_t up_off = (size_t)a.run * a.ldw;  // the up rows' place in a stage
+    int u_issue = w0, n_issued = 0;
+    auto issue = [&]() {  // lane 0: the next run of this warp into its ring slot: n gate rows, then the n up rows
+        const int e1 = run_end(u_issue), n = e1 - u_issue;
         int t, q, r;
-        unit(st, t, q, r);
+        unit(u_issue, t, q, r);
         const uint8_t *g, *up;
         if (q < a.k) {
             const size_t off = ((size_t)(sel[t * 16 + q] - a.ep.e0) * a.ffe + r) * a.ldw;
@@ -235,14 +244,16 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
             g = a.Wsg + (size_t)r * a.ldw;
             up = a.Wsu + (size_t)r * a.ldw;
         }
-        const int slot = st % a.slots;
+        const int slot = n_issued % a.slots;
         uint8_t *dst = ring + (size_t)slot * a.stage_bytes;
-        mbar_arrive_tx(&full[slot], 2 * a.ldw);
-        bulk_g2s(dst, g, a.ldw, &full[slot]);
-        bulk_g2s(dst + a.ldw, up, a.ldw, &full[slot]);
+        mbar_arrive_tx(&full[slot], 2u * (uint32_t)n * a.ldw);
+        bulk_g2s(dst, g, (uint32_t)n * a.ldw, &full[slot]);
+        bulk_g2s(dst + up_off, up, (uint32_t)n * a.ldw, &full[slot]);
+        u_issue = e1;
+        ++n_issued;
     };
     if (lane == 0)  // the weight copies fly while x is staged
-        for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
+        while (n_issued < min(nst, a.slots)) issue();
     if constexpr (XG > 0) {
         if (!a.x_early) xr.load_global(x, lane, ScaleX<TY, SOA>::v);
         __syncwarp();
@@ -251,16 +262,18 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     }
 
     const int ni = (G + 31) / 32;
-    int st = 0;
+    int st = 0, u_cons = w0;
     for (; st < nst; ++st) {
         const int slot = st % a.slots;
         if (!warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u)) {
             if (lane == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
             break;
         }
+        const int e1 = run_end(u_cons);
+        for (int u = u_cons; u < e1; ++u) {
         int t, q, r;
-        unit(st, t, q, r);
-        const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes;
+        unit(u, t, q, r);
+        const uint8_t *sbuf = ring + (size_t)slot * a.stage_bytes + (size_t)(u - u_cons) * a.ldw;
         const float *xt = xsm + (size_t)t * G * XPAD;
         double accg = 0.0, accu = 0.0;  // group sums of the gate and the up row, in group order
         if constexpr (XG > 0) {
@@ -270,7 +283,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
                 const XRegA xa{xr.v[i], xr.s[i], xr.iv};
                 float rg[1], ru[1];
                 group_dot<TY, SOA, 1>(sbuf, a.nb, g, grid, xa, 1, rg);
-                group_dot<TY, SOA, 1>(sbuf + a.ldw, a.nb, g, grid, xa, 1, ru);
+                group_dot<TY, SOA, 1>(sbuf + up_off, a.nb, g, grid, xa, 1, ru);
                 accg += (double)rg[0];
                 accu += (double)ru[0];
             }
@@ -284,7 +297,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
                 const XRegA xa{xg.v[0], xg.s[0], xg.iv};
                 float rg[1], ru[1];
                 group_dot<TY, SOA, 1>(sbuf, a.nb, g, grid, xa, 1, rg);
-                group_dot<TY, SOA, 1>(sbuf + a.ldw, a.nb, g, grid, xa, 1, ru);
+                group_dot<TY, SOA, 1>(sbuf + up_off, a.nb, g, grid, xa, 1, ru);
                 accg += (double)rg[0];
                 accu += (double)ru[0];
             }
@@ -298,11 +311,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
         const float v = __double2float_rn(keep);  // lanes 0-15: the gate row, 16-31: the up row
         const float up = __shfl_sync(0xffffffffu, v, 16);
         if (lane == 0) a.act[((size_t)t * ks + q) * a.ffe + r] = silu(v) * up;
+        }
+        u_cons = e1;
         __syncwarp();  // every lane is done reading the slot
-        if (lane == 0 && st + a.slots < nst) issue(st + a.slots);
+        if (lane == 0 && n_issued < nst) issue();
     }
     if (st < nst && lane == 0)  // wound down early: let the copies already issued land (bounded) before exiting
-        for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
+        for (int s2 = st; s2 < n_issued; ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

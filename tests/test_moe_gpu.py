@@ -62,6 +62,13 @@ def test_moe_small(fn, gu, dn, nt):
     check(fn, BY_NAME[gu], BY_NAME[dn], 24, 4, 256, 512, nt, seed=nt * 7 + len(gu))
 
 
+@pytest.mark.parametrize("ne,k,nt", [(700, 8, 1), (1024, 16, 2), (513, 10, 1)])
+def test_moe_many_experts(fn, ne, k, nt):
+    """More than 512 experts (two logits per routing lane), the largest k, and an expert count that is not a multiple
+    of the routing warps' share."""
+    check(fn, BY_NAME["Q4_K"], BY_NAME["Q4_K"], ne, k, 256, 512, nt, seed=ne + k)
+
+
 def test_moe_batch_invariance(fn):
     gu, dn, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 32, 6, 256, 2048
     y4, W, logits, x = check(fn, gu, dn, ne, k, ffe, d, 4, seed=11)
