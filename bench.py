@@ -7,7 +7,8 @@ bytes, fp16 scales |N(0,1)|*1e-3), x is N(0,1): the reference's real model tenso
 
   value  device-resident throughput: algorithmic bytes (GGUF weight bytes + 4*cols x + 4*rows y per GEMV) of all
          ranks / the max over ranks of the CUDA-event time of K steps, each step one replay of the sweep captured as
-         CUDA graphs (programmatic dependent launch between the GEMVs)
+         CUDA graphs: the 39 independent sweep GEMVs as 8 concurrent chains (programmatic dependent launch inside a
+         chain), then the lm_head
   e2e    the same metric through the C ABI with host buffers: one fn_w_step_host call per step copies every x in from
          pinned memory, runs the step's GEMVs and copies every y (the lm_head: its token id) out, inside the timed
          region
@@ -360,11 +361,20 @@ def main():
         launch(i, stream.cuda_stream, early=False)
     f.sync(stream.cuda_stream)
 
+    # the 39 sweep GEMVs are independent (own weights, inputs and outputs): they run as BRANCHES concurrent chains of
+    # the graph (a fork and a join on the capture stream), so several are resident on an SM at once
+    BRANCHES = 8
+    side = [torch.cuda.Stream() for _ in range(BRANCHES)]
     g_small, g_head = (torch.cuda.CUDAGraph() if len(work) > 1 else None), torch.cuda.CUDAGraph()
     if g_small is not None:
         with torch.cuda.graph(g_small, stream=stream, capture_error_mode="thread_local"):
+            main = torch.cuda.current_stream()
+            for sd in side:
+                sd.wait_stream(main)
             for i in range(len(work) - 1):
-                launch(i, torch.cuda.current_stream().cuda_stream)
+                launch(i, side[i % BRANCHES].cuda_stream)
+            for sd in side:
+                main.wait_stream(sd)
     with torch.cuda.graph(g_head, stream=stream, capture_error_mode="thread_local"):
         launch(len(work) - 1, torch.cuda.current_stream().cuda_stream, early=False)
 

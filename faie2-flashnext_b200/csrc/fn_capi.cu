@@ -126,33 +126,53 @@ static int build_step(const std::vector<int> &key, int n, const int *handles, in
     sp->yn = yn;
     FN_CK(cudaMalloc(&sp->x.p, std::max<size_t>(xn, 1) * 4));
     FN_CK(cudaMalloc(&sp->y.p, (yn + 4) * 4));
-    cudaStream_t cap;
+    // The GEMVs are independent (inputs from the host copy, outputs to the host copy): they run as kStepBranches
+    // concurrent chains of the graph (fork from the capture stream, join back), several resident on an SM at once.
+    constexpr int kStepBranches = 8;
+    cudaStream_t cap, side[kStepBranches];
+    cudaEvent_t fork, join[kStepBranches];
     FN_CK(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    for (int b = 0; b < kStepBranches; ++b) {
+        FN_CK(cudaStreamCreateWithFlags(&side[b], cudaStreamNonBlocking));
+        FN_CK(cudaEventCreateWithFlags(&join[b], cudaEventDisableTiming));
+    }
+    FN_CK(cudaEventCreateWithFlags(&fork, cudaEventDisableTiming));
     cudaGraph_t g = nullptr;
     int rc = 0;
     if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) rc = fail("fn_w_step_host: capture");
+    if (!rc && cudaEventRecord(fork, cap) != cudaSuccess) rc = fail("fn_w_step_host: fork");
+    for (int b = 0; b < kStepBranches && !rc; ++b)
+        if (cudaStreamWaitEvent(side[b], fork, 0) != cudaSuccess) rc = fail("fn_w_step_host: fork");
     size_t xo = 0, yo = 0;
     for (int i = 0; i < n && !rc; ++i) {
         WeightH *w = wget(handles[i]);
         const GemvPlan &p = w->plan1;
-        // inputs come from the copy before the graph: every GEMV after the first may read its x before waiting
-        const bool early = i > 0;
+        cudaStream_t s = side[i % kStepBranches];
+        // inputs come from the copy before the graph: every GEMV may read its x before waiting
         if (i == head) {
             GemvArgmax am;
             am.index = (int *)(sp->y.as<float>() + yn);
             am.kacc = w->kacc;
             am.ticket = w->ticket;
-            rc = launch_gemv(p, w->d, sp->x.as<float>() + xo, p.cols, nullptr, p.rows, 1, false, early, cap, &am);
+            rc = launch_gemv(p, w->d, sp->x.as<float>() + xo, p.cols, nullptr, p.rows, 1, false, true, s, &am);
         } else {
-            rc = launch_gemv(p, w->d, sp->x.as<float>() + xo, p.cols, sp->y.as<float>() + yo, p.rows, 1, false, early, cap);
+            rc = launch_gemv(p, w->d, sp->x.as<float>() + xo, p.cols, sp->y.as<float>() + yo, p.rows, 1, false, true, s);
             yo += (size_t)p.rows;
         }
         xo += (size_t)p.cols;
     }
+    for (int b = 0; b < kStepBranches && !rc; ++b)
+        if (cudaEventRecord(join[b], side[b]) != cudaSuccess || cudaStreamWaitEvent(cap, join[b], 0) != cudaSuccess)
+            rc = fail("fn_w_step_host: join");
     const cudaError_t ce = cudaStreamEndCapture(cap, &g);
     if (!rc && ce != cudaSuccess) rc = fail(std::string("fn_w_step_host: capture: ") + cudaGetErrorString(ce));
     if (!rc && cudaGraphInstantiate(&sp->exec, g, 0) != cudaSuccess) rc = fail("fn_w_step_host: graph instantiate");
     if (g) cudaGraphDestroy(g);
+    for (int b = 0; b < kStepBranches; ++b) {
+        cudaStreamDestroy(side[b]);
+        cudaEventDestroy(join[b]);
+    }
+    cudaEventDestroy(fork);
     cudaStreamDestroy(cap);
     (void)key;
     return rc;
@@ -513,7 +533,8 @@ FN_API int fn_w_gemv_host(int h, const float *xh, int nt, float *yh, void *strea
 
 // ---- a decode step's GEMVs on host buffers ---------------------------------------------------------------------------
 // One host->device copy of every input, the GEMVs as one CUDA graph (built on the first call for a list of handles and
-// replayed after), one device->host copy of every output: the per-call host overhead of a step is paid once.
+// replayed after; the GEMVs are independent, so they run as concurrent chains), one device->host copy of every output:
+// the per-call host overhead of a step is paid once.
 
 // A decode step's GEMVs, one token each, on host buffers: x the inputs of handles[0..n) back to back (cols_i floats
 // each), y the outputs back to back (rows_i floats each, the lm_head's left out); head (-1: none) is the index in
