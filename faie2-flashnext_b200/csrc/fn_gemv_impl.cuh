@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     const int w0 = r0 + (int)((long long)(r1 - r0) * warp / nw), w1 = r0 + (int)((long long)(r1 - r0) * (warp + 1) / nw);
     const int nst = (w1 - w0 + RU - 1) / RU;
 
-    auto issue = [&](int st) {  // lane 0: stage st of this warp's rows into its slot
-        const int slot = st % a.slots, rr = w0 + st * RU, n = min(RU, w1 - rr);
+    auto issue = [&](int st, int slot) {  // lane 0: stage st of this warp's rows into ring slot `slot`
+        const int rr = w0 + st * RU, n = min(RU, w1 - rr);
         const uint32_t bytes = (uint32_t)n * a.ldw;
         mbar_arrive_tx(&full[slot], bytes);
         bulk_g2s(ring + (size_t)slot * a.stage_bytes, a.W + (size_t)rr * a.ldw, bytes, &full[slot]);
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     if (lane == 0) {
         for (int s = 0; s < a.slots; ++s) mbar_init(&full[s], 1);
         mbar_fence_init();
-        for (int st = 0; st < min(nst, a.slots); ++st) issue(st);
+        for (int st = 0; st < min(nst, a.slots); ++st) issue(st, st);
     }
     __syncwarp();
     // The next kernel may launch (its CTAs stage their own weights beside this one where they fit; its
@@ -136,10 +136,11 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     XReg<LPR, (GPL > 0 ? GPL : 1)> xr;
     if constexpr (XREG) xr.load(xsm, lr);
 
-    int st = 0;
+    // the ring position of stage st: slot = st mod slots and its phase parity, kept incrementally (no division)
+    int st = 0, slot = 0;
+    uint32_t phase = 0;
     for (; st < nst; ++st) {
-        const int slot = st % a.slots;
-        if (!warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u)) {
+        if (!warp_wait(&full[slot], phase)) {
             if (lane == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
             break;
         }
@@ -184,7 +185,11 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
             }
         }
         __syncwarp();  // every lane is done reading the slot
-        if (lane == 0 && st + a.slots < nst) issue(st + a.slots);
+        if (lane == 0 && st + a.slots < nst) issue(st + a.slots, slot);
+        if (++slot == a.slots) {
+            slot = 0;
+            phase ^= 1u;
+        }
     }
     if (st < nst && lane == 0)  // wound down early: let the copies already issued land (bounded) before exiting
         for (int s2 = st; s2 < min(nst, st + a.slots); ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);

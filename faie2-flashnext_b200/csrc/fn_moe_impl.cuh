@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
         r = u - pi * a.ffe;
     };
     const size_t up_off = (size_t)a.run * a.ldw;  // the up rows' place in a stage
-    int u_issue = w0, n_issued = 0;
+    int u_issue = w0, n_issued = 0, issue_slot = 0;
     auto issue = [&]() {  // lane 0: the next run of this warp into its ring slot: n gate rows, then the n up rows
         const int e1 = run_end(u_issue), n = e1 - u_issue;
         int t, q, r;
@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
             g = a.Wsg + (size_t)r * a.ldw;
             up = a.Wsu + (size_t)r * a.ldw;
         }
-        const int slot = n_issued % a.slots;
+        const int slot = issue_slot;
+        issue_slot = issue_slot + 1 == a.slots ? 0 : issue_slot + 1;
         uint8_t *dst = ring + (size_t)slot * a.stage_bytes;
         mbar_arrive_tx(&full[slot], 2u * (uint32_t)n * a.ldw);
         bulk_g2s(dst, g, (uint32_t)n * a.ldw, &full[slot]);
@@ -262,10 +263,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     }
 
     const int ni = (G + 31) / 32;
-    int st = 0, u_cons = w0;
+    int st = 0, u_cons = w0, slot = 0;
+    uint32_t phase = 0;  // ring position kept incrementally (no division per stage)
     for (; st < nst; ++st) {
-        const int slot = st % a.slots;
-        if (!warp_wait(&full[slot], (uint32_t)(st / a.slots) & 1u)) {
+        if (!warp_wait(&full[slot], phase)) {
             if (lane == 0) dev_fail(a.err, DEV_WAIT_TIMEOUT);
             break;
         }
@@ -315,6 +316,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
         u_cons = e1;
         __syncwarp();  // every lane is done reading the slot
         if (lane == 0 && n_issued < nst) issue();
+        if (++slot == a.slots) {
+            slot = 0;
+            phase ^= 1u;
+        }
     }
     if (st < nst && lane == 0)  // wound down early: let the copies already issued land (bounded) before exiting
         for (int s2 = st; s2 < n_issued; ++s2) mbar_wait(&full[s2 % a.slots], (uint32_t)(s2 / a.slots) & 1u, 1u << 16);
