@@ -143,6 +143,19 @@ FN_API int fn_gdn_create(int nkh, int nvh, int ds, const float *conv_w, const fl
     return (int)g_gdn.size();
 }
 
+// Zero the handle's recurrent state and conv histories (the start of a new sequence), on `stream`.
+FN_API int fn_gdn_reset(int h, void *stream) {
+    GdnH *g = gdn_get(h);
+    if (!g) return fail("fn_gdn_reset: bad handle");
+    const size_t nS = (size_t)g->p.nvh * g->p.ds * g->p.ds, nv = (size_t)3 * g->p.nvh * g->p.ds,
+                 nqk = (size_t)g->p.nvh * 3 * 2 * g->p.ds;
+    cudaStream_t s = (cudaStream_t)stream;
+    FN_CK(cudaMemsetAsync(g->st.S, 0, nS * 4, s));
+    FN_CK(cudaMemsetAsync(g->st.conv_v, 0, nv * 4, s));
+    FN_CK(cudaMemsetAsync(g->st.conv_qk, 0, nqk * 4, s));
+    return 0;
+}
+
 FN_API int fn_gdn_free(int h) {
     GdnH *g = gdn_get(h);
     if (!g) return fail("fn_gdn_free: bad handle");

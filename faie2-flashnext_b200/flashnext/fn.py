@@ -30,6 +30,7 @@ EXPORTS = [
     "fn_gdn_get_state", "fn_w_gemv_argmax", "fn_w_gemv_argmax_host", "fn_argmax", "fn_argmax_keys", "fn_test_argmax",
     "fn_test_gemv_argmax", "fn_ipc_alloc", "fn_ipc_open", "fn_ipc_close", "fn_ipc_free", "fn_group_create",
     "fn_group_free", "fn_w_gemv_argmax_group", "fn_moe_ep_create", "fn_moe_ep_run", "fn_w_step_host",
+    "fn_embed", "fn_rmsnorm", "fn_attn_decode", "fn_step_advance", "fn_gdn_reset",
 ]
 
 
@@ -87,6 +88,11 @@ class FN:
                                        U8, U8, U8]
         d.fn_moe_ep_run.argtypes = [C.c_int, vp, C.c_int, vp, vp, C.c_int, C.c_int, vp]
         d.fn_w_step_host.argtypes = [C.c_int, I32, vp, vp, C.c_int, vp, vp]
+        d.fn_embed.argtypes = [C.c_uint32, vp, C.c_int, vp, vp, vp, vp]
+        d.fn_rmsnorm.argtypes = [vp, vp, vp, C.c_int, C.c_float, vp]
+        d.fn_attn_decode.argtypes = [vp] * 11 + [C.c_int, C.c_int, C.c_int, C.c_float, vp]
+        d.fn_step_advance.argtypes = [vp, vp, vp, vp, C.c_int, vp]
+        d.fn_gdn_reset.argtypes = [C.c_int, vp]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -186,6 +192,27 @@ class FN:
         hs = np.ascontiguousarray(handles, np.int32)
         self.check(self.d.fn_w_step_host(len(hs), hs, C.c_void_p(x_ptr), C.c_void_p(y_ptr or None), head,
                                          C.c_void_p(index_ptr or None), C.c_void_p(stream)))
+
+    # ---- the rest of a decode step (device pointers) ----
+    def embed(self, qtype, E_ptr, D, tokens_ptr, pos_ptr, h_ptr, stream=0):
+        self.check(self.d.fn_embed(int(qtype), C.c_void_p(E_ptr), D, C.c_void_p(tokens_ptr), C.c_void_p(pos_ptr),
+                                   C.c_void_p(h_ptr), C.c_void_p(stream)))
+
+    def rmsnorm(self, x_ptr, w_ptr, out_ptr, D, eps=1e-6, stream=0):
+        self.check(self.d.fn_rmsnorm(C.c_void_p(x_ptr), C.c_void_p(w_ptr), C.c_void_p(out_ptr), D, eps,
+                                     C.c_void_p(stream)))
+
+    def attn_decode(self, qg, k, v, wq, wk, inv_freq, Q, Kc, Vc, out, pos, nh, nkv, max_ctx, eps=1e-6, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_attn_decode(vp(qg), vp(k), vp(v), vp(wq), vp(wk), vp(inv_freq), vp(Q), vp(Kc), vp(Vc),
+                                         vp(out), vp(pos), nh, nkv, max_ctx, eps, vp(stream)))
+
+    def step_advance(self, pos, tokens, nxt, prompt_len_ptr, max_ctx, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_step_advance(vp(pos), vp(tokens), vp(nxt), vp(prompt_len_ptr), max_ctx, vp(stream)))
+
+    def gdn_reset(self, h, stream=0):
+        self.check(self.d.fn_gdn_reset(h, C.c_void_p(stream)))
 
     # ---- peer-memory groups (one process per GPU) ----
     def ipc_alloc(self, nbytes):

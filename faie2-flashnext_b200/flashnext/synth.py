@@ -50,5 +50,83 @@ def random_blocks(qtype: int, rows: int, cols: int, rng: np.random.Generator, sc
     return raw.reshape(rows, row_bytes(qtype, cols))
 
 
+# formats whose blocks carry a min beside the scale: (scale offset, min offset, mean quant); the min written as
+# mean quant x scale makes a block's expected value zero
+CENTER = {"Q4_K": (0, 2, 7.5), "Q5_K": (0, 2, 15.5), "Q2_K": (80, 82, 1.5), "Q4_1": (0, 2, -7.5), "Q5_1": (0, 2, -15.5)}
+
+
+def model_blocks(qtype: int, rows: int, cols: int, rng: np.random.Generator, scale: float = 1e-3) -> np.ndarray:
+    """random_blocks with zero-mean blocks: a random-byte Q4_K row otherwise has a large common offset (its mins), which
+    drives every layer's output along one direction, so a model built from such rows predicts the same token and routes
+    to the same experts whatever the input."""
+    raw = random_blocks(qtype, rows, cols, rng, scale)
+    name, _, tb = TYPES[qtype]
+    if name in CENTER:
+        so, mo, k = CENTER[name]
+        r = raw.reshape(-1, tb)
+        d = r[:, so:so + 2].copy().view(np.float16).astype(np.float32)
+        r[:, mo:mo + 2] = (d * np.float32(k)).astype(np.float16).view(np.uint8)
+    return raw
+
+
 def random_x(nt: int, cols: int, rng: np.random.Generator) -> np.ndarray:
     return rng.standard_normal((nt, cols), dtype=np.float32)
+
+
+# ---- BASELINE config 5: the synthetic hybrid MoE decoder ---------------------------------------------------------------
+
+def model_config(small: bool = False) -> dict:
+    """Config 5 (48 layers, 3 gated-DeltaNet layers then 1 gated-attention layer, MoE on every layer, vocab 151936),
+    or a small model of the same structure for parity tests. Formats: a mixed Q4_K / Q6_K / IQ3_XXS recipe (expert
+    gate/up IQ3_XXS, everything else Q4_K, the lm_head Q6_K, the router BF16)."""
+    if small:
+        return dict(D=512, layers=4, pattern="GGGA", vocab=2048, eps=1e-6, nkh=2, nvh=4, nh=4, nkv=1, rope_base=1e7,
+                    ne=16, k=4, ffe=256, proj=BY_NAME["Q4_K"], gate_up=BY_NAME["IQ3_XXS"], down=BY_NAME["Q4_K"],
+                    embed=BY_NAME["Q4_K"], head=BY_NAME["Q6_K"], router=BY_NAME["BF16"])
+    return dict(D=2048, layers=48, pattern="GGGA", vocab=151936, eps=1e-6, nkh=16, nvh=32, nh=16, nkv=2, rope_base=1e7,
+                ne=512, k=10, ffe=512, proj=BY_NAME["Q4_K"], gate_up=BY_NAME["IQ3_XXS"], down=BY_NAME["Q4_K"],
+                embed=BY_NAME["Q4_K"], head=BY_NAME["Q6_K"], router=BY_NAME["BF16"])
+
+
+def layer_kind(cfg: dict, l: int) -> str:
+    return cfg["pattern"][l % len(cfg["pattern"])]
+
+
+def model_weights(cfg: dict, seed: int = 0) -> dict:
+    """Seeded synthetic weights of the config-5 model as GGUF rows (uint8, zero-mean blocks: model_blocks) and fp32
+    vectors. DeltaNet projections are stacked as in the reference's load_qw_cat: in = [q | k | v | z] (CONVCH + NVH*128
+    rows), ab = [alpha | beta]. The lm_head's scales are 1e-4 (logits of a few units, as a trained head gives)."""
+    rng = np.random.default_rng(seed)
+    D, DS, HD = cfg["D"], 128, 256
+    nkh, nvh, nh, nkv = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
+    convch = 2 * nkh * DS + nvh * DS
+    ne, ffe = cfg["ne"], cfg["ffe"]
+    P = cfg["proj"]
+    f32 = lambda a: np.asarray(a, np.float32)  # noqa: E731
+    W = dict(embed=model_blocks(cfg["embed"], cfg["vocab"], D, rng, scale=1e-2),
+             head=model_blocks(cfg["head"], cfg["vocab"], D, rng, scale=1e-4), final_norm=f32(1 + 0.1 * rng.standard_normal(D)),
+             layers=[])
+    for l in range(cfg["layers"]):
+        L = dict(kind=layer_kind(cfg, l), norm1=f32(1 + 0.1 * rng.standard_normal(D)),
+                 norm2=f32(1 + 0.1 * rng.standard_normal(D)))
+        if L["kind"] == "G":
+            L.update(w_in=model_blocks(P, convch + nvh * DS, D, rng), w_ab=model_blocks(P, 2 * nvh, D, rng),
+                     w_out=model_blocks(P, D, nvh * DS, rng), conv_w=f32(rng.standard_normal((convch, 4)) * 0.5),
+                     dt_bias=f32(rng.standard_normal(nvh) * 0.5), ssm_a=f32(-np.exp(rng.standard_normal(nvh) * 0.5)),
+                     gnorm=f32(1 + 0.1 * rng.standard_normal(DS)))
+        else:
+            L.update(w_q=model_blocks(P, nh * 2 * HD, D, rng), w_k=model_blocks(P, nkv * HD, D, rng),
+                     w_v=model_blocks(P, nkv * HD, D, rng), w_o=model_blocks(P, D, nh * HD, rng),
+                     q_norm=f32(1 + 0.1 * rng.standard_normal(HD)), k_norm=f32(1 + 0.1 * rng.standard_normal(HD)))
+        gu, dn = cfg["gate_up"], cfg["down"]
+        L.update(router=model_blocks(cfg["router"], ne + 1, D, rng),
+                 moe=[model_blocks(gu, ne * ffe, D, rng), model_blocks(gu, ne * ffe, D, rng),
+                      model_blocks(dn, ne * D, ffe, rng), model_blocks(gu, ffe, D, rng), model_blocks(gu, ffe, D, rng),
+                      model_blocks(dn, D, ffe, rng)])
+        W["layers"].append(L)
+    return W
+
+
+def rope_inv_freq(base: float, nrot: int = 64) -> np.ndarray:
+    """float32 inverse frequencies of the partial RoPE, as the reference computes them (engine/faie2fn.cu:2575)."""
+    return np.array([1.0 / base ** (2 * i / nrot) for i in range(nrot // 2)], np.float32)

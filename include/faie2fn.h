@@ -82,6 +82,22 @@ int fn_w_gemv_host(int h, const float *x, int nt, float *y, void *stream);
  * synchronise. New: the reference's fn_forward (engine/faie2fn.cu:2733) runs a whole step per call; this is that
  * call's shape for the GEMV path. */
 int fn_w_step_host(int n, const int *handles, const float *x, float *y, int head, int *index, void *stream);
+/* ---- the rest of a decode step (device pointers, on a stream) --------------------------------
+ * h = dequant(E[tokens[*pos]]) (GGUF rows). Replaces k_embed (engine/faie2fn.cu:1334-1347). */
+int fn_embed(uint32_t type, const uint8_t *E, int D, const int *tokens, const int *pos, float *h, void *stream);
+/* out = x * rsqrt(mean(x^2) + eps) * w. Replaces k_groupnorm (engine/faie2fn.cu:1222-1235) for one stream. */
+int fn_rmsnorm(const float *x, const float *w, float *out, int D, float eps, void *stream);
+/* Gated attention of one token at position *pos (head dim 256, RoPE on the first 64 dims): q / k head RMSNorm, RoPE,
+ * k / v appended to the caches [max_ctx][nkv][256], out [nh][256] = softmax(q.k / 16) v * sigmoid(gate). Replaces
+ * k_qk_norm_rope + k_attn_split + k_attn_combine (engine/faie2fn.cu:1452-1478, 1598-1690), without the QSA indexer. */
+int fn_attn_decode(const float *qg, const float *k, const float *v, const float *wq, const float *wk,
+                   const float *inv_freq, float *Q, float *Kc, float *Vc, float *out, const int *pos, int nh, int nkv,
+                   int max_ctx, float eps, void *stream);
+/* *pos += 1 and, once the prompt tokens[0..*prompt_len) is consumed, tokens[*pos] = *next (all device memory).
+ * Replaces k_advance (engine/faie2fn.cu:1905) and the host's token feedback, so a decode step replays as one CUDA
+ * graph for any prompt. */
+int fn_step_advance(int *pos, int *tokens, const int *next, const int *prompt_len, int max_ctx, void *stream);
+
 /* Synchronise a stream and report any device-side error (a bounded wait that ran out). */
 int fn_sync(void *stream);
 
@@ -181,6 +197,8 @@ int fn_test_gdn(int nkh, int nvh, int ds, int nt, int tokens_per_launch, const f
  * 2703-2717). */
 int fn_gdn_create(int nkh, int nvh, int ds, const float *conv_w, const float *dt_bias, const float *ssm_a,
                   const float *norm_w, const float *S0, const float *conv0);
+/* Zero a handle's recurrent state and conv histories (a new sequence), on a stream. */
+int fn_gdn_reset(int h, void *stream);
 int fn_gdn_free(int h);
 /* Launch nt tokens on device pointers (token strides qs, zs, abs_, os in floats); the handle's state advances.
  * prefetch_state = 1 only when this handle's previous launch is two or more kernels back in the stream (the state is
