@@ -249,6 +249,159 @@ def run_components():
         f.gdn_free(hg)
 
 
+def decode_step_bytes(cfg, ctx_mean):
+    """Algorithmic bytes of one config-5 decode step: every GGUF weight the step reads once (the embedding row, the
+    projections, the routers, k routed experts and the shared expert per layer, the lm_head), each DeltaNet state
+    read and written (fp32 [nvh][128][128]), and the attention caches read over ctx_mean positions on average."""
+    from synth import TYPES, row_bytes
+    D, ne, k, ffe = cfg["D"], cfg["ne"], cfg["k"], cfg["ffe"]
+    nkh, nvh, nh, nkv, P = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["proj"]
+    convch = 2 * nkh * 128 + nvh * 128
+    rg, rd = row_bytes(cfg["gate_up"], D), row_bytes(cfg["down"], ffe)
+    expert = 2 * ffe * rg + D * rd
+    total = row_bytes(cfg["embed"], D) + cfg["vocab"] * row_bytes(cfg["head"], D)
+    for l in range(cfg["layers"]):
+        kind = cfg["pattern"][l % len(cfg["pattern"])]
+        if kind == "G":
+            total += (convch + nvh * 128 + 2 * nvh) * row_bytes(P, D) + D * row_bytes(P, nvh * 128)
+            total += 2 * nvh * 128 * 128 * 4
+        else:
+            total += (nh * 512 + 2 * nkv * 256) * row_bytes(P, D) + D * row_bytes(P, nh * 256)
+            total += 2 * ctx_mean * nkv * 256 * 4
+        total += (ne + 1) * row_bytes(cfg["router"], D) + (k + 1) * expert
+    return int(total)
+
+
+def cpu_decode_sample(cfg, seed=0, tokens=4):
+    """The reference's CPU forward (dequantised weights, float64, ref_fn.py pattern) on one thread, on a bounded sample:
+    the model's first 4 layers (3 DeltaNet + 1 attention) at full width with a vocabulary of 8192, each token run twice
+    (the first pass dequantises the experts it selects, as the reference's load does; the second is timed). Per token
+    of the full model: 12 x (the 4 layers) + the lm_head matvec scaled to 151936 rows. Returns (tok/s, description)."""
+    from threadpoolctl import threadpool_limits
+    from oracle.model import OracleModel
+    from synth import model_weights, rope_inv_freq
+    sub = dict(cfg, layers=4, vocab=8192)
+    with threadpool_limits(1):
+        W = model_weights(sub, seed)
+        o = OracleModel(sub, W, rope_inv_freq(sub["rope_base"]))
+        toks = np.random.default_rng(seed).integers(0, sub["vocab"], tokens)
+        for t in toks:
+            o.step(int(t))
+        o.reset()
+        t0 = time.perf_counter()
+        for t in toks:
+            o.step(int(t))
+        t4 = (time.perf_counter() - t0) / tokens
+        x = np.random.default_rng(1).standard_normal(cfg["D"])
+        t0 = time.perf_counter()
+        for _ in range(5):
+            o.Hd @ x
+        th = (time.perf_counter() - t0) / 5
+    per_token = cfg["layers"] / 4 * (t4 - th) + th * cfg["vocab"] / sub["vocab"]
+    return 1.0 / per_token, (f"4 layers (GGGA) at full width, vocab 8192, {tokens} tokens, float64 numpy on 1 thread: "
+                             f"{t4 * 1e3:.0f} ms per token; x12 layers + lm_head matvec scaled to {cfg['vocab']} rows")
+
+
+def run_decode(f, args, rank, with_cpu=True):
+    """greedy decode of 256 tokens from a seeded 64-token prompt at batch 1 on the synthetic
+    48-layer hybrid MoE, one decode step = one CUDA graph replay. Returns a dict of the figures."""
+    import torch
+    from model import DecodeModel
+    from synth import model_config, model_weights
+    cfg = model_config()
+    n_prompt, n_new = 64, 256
+    t0 = time.perf_counter()
+    W = model_weights(cfg, seed=0, pooled=True)
+    m = DecodeModel(f, cfg, W, max_ctx=n_prompt + n_new)
+    del W
+    build_s = time.perf_counter() - t0
+    s = torch.cuda.Stream()
+    m.capture(s)
+    prompt = torch.from_numpy(np.random.default_rng(0).integers(0, cfg["vocab"], n_prompt).astype(np.int32)).pin_memory()
+    out = torch.zeros(n_new, dtype=torch.int32).pin_memory()
+    if args.profile_steps:  # the launch list of a few eager steps (an NVTX range "decode_steps" for ncu)
+        m.generate_host(prompt, 1, out, s)
+        f.sync(s.cuda_stream)
+        torch.cuda.nvtx.range_push("decode_steps")
+        for _ in range(args.profile_steps):
+            m.launch_step(s.cuda_stream)
+        f.sync(s.cuda_stream)
+        torch.cuda.nvtx.range_pop()
+        n = m.launches_per_step()
+        m.free()
+        return {"profile_steps": args.profile_steps, "gpu_launches_per_step": n, "build_s": round(build_s, 1)}
+    for _ in range(max(1, args.warmup // 20)):  # each warm-up generation is 319 decode steps
+        m.generate_host(prompt, n_new, out, s)
+    f.sync(s.cuda_stream)
+    reps = max(1, min(4, args.steps // n_new))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(reps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ids = []
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    for r in range(reps):
+        if r == 0:
+            e0.record(s)
+        m.generate_host(prompt, n_new, out, s, marks=ev[r])
+        if r == reps - 1:
+            e1.record(s)
+        f.sync(s.cuda_stream)
+        ids.append(out.numpy().copy())
+    clk = clocks.stop()
+    gen_ms = [ev[r][1].elapsed_time(ev[r][2]) for r in range(reps)]
+    all_ms = [ev[r][0].elapsed_time(ev[r][2]) for r in range(reps)]
+    e2e_ms = e0.elapsed_time(e1) / reps  # prompt copy in, resets, 319 steps, ids copied out
+    steps_all = n_prompt + n_new - 1
+    ms_tok = statistics.median(gen_ms) / n_new
+    ctx_mean = (n_prompt + n_new) / 2
+    nbytes = decode_step_bytes(cfg, ctx_mean)
+    peak, peak_kind = measured_peak()
+    d = {
+        "tok_s": round(1e3 / ms_tok, 2), "ms_per_token": round(ms_tok, 4),
+        "tok_s_all_steps": round(steps_all * 1e3 / statistics.median(all_ms), 2),
+        "e2e_tok_s": round(n_new * 1e3 / e2e_ms, 2), "e2e_ms_per_generation": round(e2e_ms, 3),
+        "generations": reps, "bytes_per_step": nbytes,
+        "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_tok / 1e3) / 1e9, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(nbytes / (ms_tok / 1e3) / 1e9 / peak, 4), "peak_kind": peak_kind,
+                     "scope": "whole decode step (algorithmic bytes / step time)"},
+        "ids_repeatable": bool(all(np.array_equal(ids[0], i) for i in ids)),
+        "distinct_ids": int(len(np.unique(ids[0]))),
+        "gpu_launches_per_step": m.launches_per_step(),
+        "build_s": round(build_s, 1), "clocks": clk,
+        "config": "config5: 48 layers GGGA (gated DeltaNet 16/32 heads x 128, gated attention 16/2 heads x 256, "
+                  "RoPE 1e7), MoE 512 experts top-10 + shared on every layer (IQ3_XXS gate/up, Q4_K down), Q4_K "
+                  "projections, BF16 router, Q6_K lm_head 151936 with fused argmax; 64-token prompt, 256 greedy tokens",
+    }
+    if with_cpu and rank == 0:
+        tps, desc = cpu_decode_sample(cfg)
+        d["cpu_baseline"] = {"value": round(tps, 5), "unit": "tok/s", "cores": 1, "kind": "port", "sample": desc}
+    m.free()
+    return d
+
+
+def decode_line(f, args):
+    """`--workload decode`: the config-5 decode as its own bench line (tok/s)."""
+    d = run_decode(f, args, 0, with_cpu=not args.no_cpu_baseline)
+    if args.profile_steps:
+        return d
+    gen = d["generations"]
+    line = {
+        "metric": METRIC, "value": d["tok_s"], "unit": "tok/s", "n_gpus": 1, "steps": 256 * gen,
+        "warmup": args.warmup, "ms_per_step": d["ms_per_token"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": d["config"], "bytes_per_step": d["bytes_per_step"], "parallelism": "1 GPU",
+                   "l2": "inputs larger than L2 (about 2 GB of weights and states per step)"},
+        "e2e": {"value": d["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": round(64 * 4 / 256, 3),
+                "d2h_bytes_per_step": 4, "note": "per generation: the 64-token prompt copied in (256 B), 256 ids "
+                "copied out (1 KiB), the resets and all 319 steps inside the timed region"},
+        "roofline": d["roofline"], "gpu_launches": d["gpu_launches_per_step"] * (64 + 256 - 1) * gen,
+        "clocks": d["clocks"], "decode": d,
+    }
+    if "cpu_baseline" in d:
+        line["cpu_baseline"] = d["cpu_baseline"]
+    return line
+
+
 def row_bytes_of(qtype, cols):
     from synth import TYPES
     _, qk, tb = TYPES[qtype]
@@ -299,8 +452,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--components", action="store_true",
                     help="per-component device times (sweep GEMVs alone, config-3 MoE layer, config-4 DeltaNet layer)")
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "lm_head"],
-                    help="lm_head: only the dominant kernel (the small case the ncu capture profiles)")
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "lm_head", "decode"],
+                    help="lm_head: only the dominant kernel (the small case the ncu capture profiles); decode: only "
+                         "the config-5 greedy decode (its own line, tok/s)")
+    ap.add_argument("--no-decode", action="store_true", help="leave the config-5 decode out of the sweep line")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="with --workload decode: run this many eager decode steps in an NVTX range and exit")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -328,6 +485,11 @@ def main():
 
     f = FN()
     f.set_device(local)
+    if args.workload == "decode":
+        if world > 1:
+            raise SystemExit("--workload decode runs on one GPU")
+        print(json.dumps(decode_line(f, args)), flush=True)
+        return
     work = workload() if args.workload == "sweep" else workload()[-1:]
     hs, xs, ys = [], [], []
     step_bytes = 0
@@ -477,11 +639,14 @@ def main():
         line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                                 "sample": f"every GEMV of the sweep cut to {frac:.3g} of its rows, one pass "
                                           f"({dt:.1f} s), gguf-py dequant + float64 numpy GEMV, 1 thread"}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     del g_small, g_head
     for h in hs:
         f.w_free(h)
+    if world == 1 and args.workload == "sweep" and not args.no_decode:
+        line["decode"] = run_decode(f, args, rank, with_cpu=not args.no_cpu_baseline)
+        line["gpu_launches"] += line["decode"]["gpu_launches_per_step"] * (64 + 256 - 1) * line["decode"]["generations"]
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -260,6 +260,10 @@ class FN:
         self.check(self.d.fn_moe_ep_run(h, C.c_void_p(logits_ptr), ls, C.c_void_p(x_ptr), C.c_void_p(y_ptr), nt, acc,
                                         C.c_void_p(stream)))
 
+    def gemv_override(self, warps=-1, ring_kb=0, stage_kb=0, ctas_per_sm=0):
+        """Plan settings for weights created from now on (engine/faie2fn.cu:2786-2791; warps 0 = by weight size)."""
+        self.d.fn_gemv_override(warps, ring_kb, stage_kb, ctas_per_sm)
+
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))
 

@@ -20,15 +20,32 @@ DS, HD = 128, 256
 
 
 class DecodeModel:
-    def __init__(self, fn, cfg: dict, W: dict, max_ctx: int = 512, logits: bool = False):
+    def __init__(self, fn, cfg: dict, W: dict, max_ctx: int = 512, logits: bool = False, warps: int = 16,
+                 stack: bool = True):
+        """warps: GEMV warps per CTA of the model's weights; stack: the projections that read the same input as one
+        GEMV each ([q k v z | alpha beta], [q gate | k | v]) rather than one GEMV per weight."""
         import torch
         self.fn, self.cfg, self.max_ctx = fn, cfg, max_ctx
+        self.stack = stack
         dev = torch.device("cuda", torch.cuda.current_device())
         f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)  # noqa: E731
-        d, nkh, nvh, nh, nkv = cfg["D"], cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
+        nkh, nvh, nh, nkv = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
         self.convch = 2 * nkh * DS + nvh * DS
-        ne, ffe, P = cfg["ne"], cfg["ffe"], cfg["proj"]
+        self.n_in = self.convch + nvh * DS + 2 * nvh  # q k v | z | alpha beta
+        self.n_qkv = nh * 2 * HD + 2 * nkv * HD  # q gate | k | v
         self.handles, self.moes, self.gdns = [], [], []
+        # a decode step is a chain of dependent GEMVs at batch 1: each is latency-bound, so its CTAs run 16 warps
+        # (more loads and decodes in flight per SM) rather than the few that let independent GEMVs share an SM
+        fn.gemv_override(warps=warps)
+        try:
+            self._build(fn, cfg, W, max_ctx, logits, dev, f32)
+        finally:
+            fn.gemv_override(warps=0)
+
+    def _build(self, fn, cfg, W, max_ctx, logits, dev, f32):
+        import torch
+        d, nkh, nvh, nh, nkv = cfg["D"], cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
+        ne, ffe, P = cfg["ne"], cfg["ffe"], cfg["proj"]
         self.E = torch.from_numpy(np.ascontiguousarray(W["embed"]).reshape(-1)).to(dev)
         self.head = self._w(cfg["head"], W["head"], cfg["vocab"], d)
         self.final_norm = f32(W["final_norm"])
@@ -37,16 +54,22 @@ class DecodeModel:
         for L in W["layers"]:
             o = dict(kind=L["kind"], norm1=f32(L["norm1"]), norm2=f32(L["norm2"]),
                      router=self._w(cfg["router"], L["router"], ne + 1, d))
-            if L["kind"] == "G":
-                o.update(w_in=self._w(P, L["w_in"], self.convch + nvh * DS, d), w_ab=self._w(P, L["w_ab"], 2 * nvh, d),
-                         w_out=self._w(P, L["w_out"], d, nvh * DS))
+            if L["kind"] == "G":  # [q k v z | alpha beta]: one GEMV over the stacked rows
+                if self.stack:
+                    o["w_in"] = self._w(P, np.concatenate([L["w_in"], L["w_ab"]]), self.n_in, d)
+                else:
+                    o["w_in"] = [(self._w(P, L["w_in"], self.convch + nvh * DS, d), self.convch + nvh * DS),
+                                 (self._w(P, L["w_ab"], 2 * nvh, d), 2 * nvh)]
+                o["w_out"] = self._w(P, L["w_out"], d, nvh * DS)
                 g = fn.gdn_create(nkh, nvh, L["conv_w"], L["dt_bias"], L["ssm_a"], L["gnorm"],
                                   np.zeros((nvh, DS, DS), np.float32), np.zeros((3, self.convch), np.float32))
                 self.gdns.append(g)
                 o["gdn"] = g
             else:
-                o.update(w_q=self._w(P, L["w_q"], nh * 2 * HD, d), w_k=self._w(P, L["w_k"], nkv * HD, d),
-                         w_v=self._w(P, L["w_v"], nkv * HD, d), w_o=self._w(P, L["w_o"], d, nh * HD),
+                o.update(w_qkv=self._w(P, np.concatenate([L["w_q"], L["w_k"], L["w_v"]]), self.n_qkv, d) if self.stack
+                         else [(self._w(P, L[n], r, d), r) for n, r in (("w_q", nh * 2 * HD), ("w_k", nkv * HD),
+                                                                           ("w_v", nkv * HD))],
+                         w_o=self._w(P, L["w_o"], d, nh * HD),
                          q_norm=f32(L["q_norm"]), k_norm=f32(L["k_norm"]),
                          Kc=torch.zeros(max_ctx, nkv, HD, device=dev), Vc=torch.zeros(max_ctx, nkv, HD, device=dev))
             m = fn.moe_create(cfg["gate_up"], cfg["down"], ne, cfg["k"], ffe, d, *L["moe"])
@@ -54,8 +77,8 @@ class DecodeModel:
             o["moe"] = m
             self.layers.append(o)
         z = lambda n: torch.zeros(n, device=dev)  # noqa: E731
-        self.h, self.x, self.qkvz, self.ab = z(d), z(d), z(self.convch + nvh * DS), z(2 * nvh)
-        self.core, self.qg, self.k, self.v = z(nvh * DS), z(nh * 2 * HD), z(nkv * HD), z(nkv * HD)
+        self.h, self.x, self.proj = z(d), z(d), z(max(self.n_in, self.n_qkv))
+        self.core = z(nvh * DS)
         self.Q, self.att, self.lr = z(nh * HD), z(nh * HD), z(ne + 1)
         self.logits = z(cfg["vocab"]) if logits else None
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -75,29 +98,47 @@ class DecodeModel:
         d, nvh, nh, nkv, eps = cfg["D"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["eps"]
         p = lambda t: t.data_ptr()  # noqa: E731
         fn.embed(cfg["embed"], p(self.E), d, p(self.tokens), p(self.pos), p(self.h), s)
+        h, x = p(self.h), p(self.x)
+
+        def gemv_normed(wh, norm, y):  # y = W rmsnorm(h); a list of (handle, rows): their outputs one after another
+            fn.rmsnorm(h, p(norm), x, d, eps, s)
+            off = 0
+            for w_, rows in (wh if isinstance(wh, list) else [(wh, 0)]):
+                fn.w_gemv(w_, x, d, y + 4 * off, 0, 1, 0, s)
+                off += rows
+
         for L in self.layers:
-            fn.rmsnorm(p(self.h), p(L["norm1"]), p(self.x), d, eps, s)
+            pr = p(self.proj)
             if L["kind"] == "G":
-                fn.w_gemv(L["w_in"], p(self.x), d, p(self.qkvz), 0, 1, 0, s)
-                fn.w_gemv(L["w_ab"], p(self.x), d, p(self.ab), 0, 1, 0, s)
+                gemv_normed(L["w_in"], L["norm1"], pr)
                 # the layer's previous core launch is a whole step back: its state is read before the wait
-                fn.gdn_run(L["gdn"], p(self.qkvz), self.convch, p(self.qkvz) + 4 * self.convch, nvh * DS, p(self.ab),
-                           2 * nvh, p(self.core), nvh * DS, 1, 1, s)
-                fn.w_gemv(L["w_out"], p(self.core), nvh * DS, p(self.h), 0, 1, 1, s)  # h += W_out core
+                qkv, z, ab = pr, pr + 4 * self.convch, pr + 4 * (self.convch + nvh * DS)
+                fn.gdn_run(L["gdn"], qkv, self.convch, z, nvh * DS, ab, 2 * nvh, p(self.core), nvh * DS, 1, 1, s)
+                fn.w_gemv(L["w_out"], p(self.core), nvh * DS, h, 0, 1, 1, s)  # h += W_out core
             else:
-                fn.w_gemv(L["w_q"], p(self.x), d, p(self.qg), 0, 1, 0, s)
-                fn.w_gemv(L["w_k"], p(self.x), d, p(self.k), 0, 1, 0, s)
-                fn.w_gemv(L["w_v"], p(self.x), d, p(self.v), 0, 1, 0, s)
-                fn.attn_decode(p(self.qg), p(self.k), p(self.v), p(L["q_norm"]), p(L["k_norm"]), p(self.inv_freq),
+                gemv_normed(L["w_qkv"], L["norm1"], pr)
+                qg, k, v = pr, pr + 4 * nh * 2 * HD, pr + 4 * (nh * 2 * HD + nkv * HD)
+                fn.attn_decode(qg, k, v, p(L["q_norm"]), p(L["k_norm"]), p(self.inv_freq),
                                p(self.Q), p(L["Kc"]), p(L["Vc"]), p(self.att), p(self.pos), nh, nkv, self.max_ctx, eps, s)
-                fn.w_gemv(L["w_o"], p(self.att), nh * HD, p(self.h), 0, 1, 1, s)  # h += W_o o
-            fn.rmsnorm(p(self.h), p(L["norm2"]), p(self.x), d, eps, s)
-            fn.w_gemv(L["router"], p(self.x), d, p(self.lr), 0, 1, 0, s)
-            fn.moe_run(L["moe"], p(self.lr), cfg["ne"] + 1, p(self.x), p(self.h), 1, 1, s)  # h += moe(x)
-        fn.rmsnorm(p(self.h), p(self.final_norm), p(self.x), d, eps, s)
-        fn.w_gemv_argmax(self.head, p(self.x), d, p(self.logits) if self.logits is not None else 0, 0, 1, 0, 0,
+                fn.w_gemv(L["w_o"], p(self.att), nh * HD, h, 0, 1, 1, s)  # h += W_o o
+            fn.rmsnorm(h, p(L["norm2"]), x, d, eps, s)
+            fn.w_gemv(L["router"], x, d, p(self.lr), 0, 1, 0, s)
+            fn.moe_run(L["moe"], p(self.lr), cfg["ne"] + 1, x, h, 1, 1, s)  # h += moe(x)
+        fn.rmsnorm(h, p(self.final_norm), x, d, eps, s)
+        fn.w_gemv_argmax(self.head, x, d, p(self.logits) if self.logits is not None else 0, 0, 1, 0, 0,
                          p(self.next), 0, s)
         fn.step_advance(p(self.pos), p(self.tokens), p(self.next), p(self.plen), self.max_ctx, s)
+
+    def launches_per_step(self) -> int:
+        """Kernel launches of one step: the embedding; per layer a norm, the input GEMV (stacked q k v z | alpha beta,
+        or q gate | k | v; one per weight unstacked), the DeltaNet core or the two attention kernels, the output GEMV,
+        a norm, the router GEMV and the MoE layer's three kernels (routing, gate/up, down + combine); the final norm,
+        the lm_head with its argmax and the step counter."""
+        n = 1 + 3
+        for L in self.layers:
+            w_in = L["w_in"] if L["kind"] == "G" else L["w_qkv"]
+            n += 1 + (len(w_in) if isinstance(w_in, list) else 1) + (1 if L["kind"] == "G" else 2) + 1 + 1 + 1 + 3
+        return n
 
     def start(self, prompt, stream=None):
         """A new sequence: the prompt loaded, the position at 0, the DeltaNet states and conv histories zeroed (the
@@ -127,17 +168,40 @@ class DecodeModel:
             self.launch_step(torch.cuda.current_stream().cuda_stream)
         self.graph = g
 
+    def generate_host(self, prompt, n_new, out, stream, marks=None):
+        """Greedy decode on host buffers, everything on `stream` (nothing synchronises): prompt (int32 host tensor,
+        pinned for an asynchronous copy) is copied in, the states reset, the step's graph replayed once per position,
+        and the ids of the n_new generated tokens copied out into out (int32 host tensor, pinned). marks: optional
+        CUDA events recorded after the reset, after the last prompt-only step and after the last step."""
+        import torch
+        n = len(prompt)
+        if not 1 <= n or n + n_new > self.max_ctx or n_new < 1:
+            raise ValueError("prompt + new tokens exceed the context")
+        with torch.cuda.stream(stream):  # copies, resets and replays all go to `stream`
+            self.tokens.zero_()
+            self.tokens[:n].copy_(prompt, non_blocking=True)
+            self.pos.zero_()
+            self.plen.fill_(n)
+            for g in self.gdns:
+                self.fn.gdn_reset(g, stream.cuda_stream)
+            if marks:
+                marks[0].record(stream)
+            for i in range(n + n_new - 1):
+                if marks and i == n - 1:
+                    marks[1].record(stream)
+                self.graph.replay()
+            if marks:
+                marks[2].record(stream)
+            out[:n_new].copy_(self.tokens[n:n + n_new], non_blocking=True)
+
     def generate(self, prompt, n_new, stream):
         """Greedy decode: the prompt, then n_new tokens; returns the token ids of all positions (device replays only)."""
         import torch
-        if len(prompt) + n_new > self.max_ctx:
-            raise ValueError("prompt + new tokens exceed the context")
-        self.start(prompt, stream)
-        with torch.cuda.stream(stream):  # replays go to the current stream
-            for _ in range(len(prompt) + n_new - 1):
-                self.graph.replay()
+        prompt = torch.from_numpy(np.asarray(prompt, np.int32)).pin_memory()
+        out = torch.zeros(n_new, dtype=torch.int32).pin_memory()
+        self.generate_host(prompt, n_new, out, stream)
         self.fn.sync(stream.cuda_stream)
-        return self.tokens[:len(prompt) + n_new].cpu().numpy()
+        return np.concatenate([prompt.numpy(), out.numpy()])
 
     def free(self):
         self.graph = None

@@ -92,39 +92,75 @@ def layer_kind(cfg: dict, l: int) -> str:
     return cfg["pattern"][l % len(cfg["pattern"])]
 
 
-def model_weights(cfg: dict, seed: int = 0) -> dict:
+class BlockPool:
+    """Zero-mean random blocks of one format (model_blocks), cut into tensors at random offsets (wrapping): the full
+    config-5 expert set (34 GB) then costs the host one pool per format and one copy per tensor, and every tensor no
+    larger than the pool still holds distinct blocks."""
+
+    def __init__(self, qtype: int, nblocks: int, rng: np.random.Generator, scale: float = 1e-3):
+        _, self.qk, self.tb = TYPES[qtype]
+        self.qtype, self.rng = qtype, rng
+        self.blocks = model_blocks(qtype, nblocks, self.qk, rng, scale).reshape(nblocks, self.tb)
+
+    def take(self, rows: int, cols: int) -> np.ndarray:
+        nb, n = rows * (cols // self.qk), len(self.blocks)
+        o = int(self.rng.integers(0, n))
+        parts = []
+        while nb > 0:
+            c = min(nb, n - o)
+            parts.append(self.blocks[o:o + c])
+            nb, o = nb - c, 0
+        return np.concatenate(parts).reshape(rows, row_bytes(self.qtype, cols))
+
+
+def model_weights(cfg: dict, seed: int = 0, pooled: bool = False) -> dict:
     """Seeded synthetic weights of the config-5 model as GGUF rows (uint8, zero-mean blocks: model_blocks) and fp32
     vectors. DeltaNet projections are stacked as in the reference's load_qw_cat: in = [q | k | v | z] (CONVCH + NVH*128
-    rows), ab = [alpha | beta]. The lm_head's scales are 1e-4 (logits of a few units, as a trained head gives)."""
+    rows), ab = [alpha | beta]. The lm_head's scales are 1e-4 (logits of a few units, as a trained head gives).
+
+    pooled: the routed experts' tensors are cut from one BlockPool per format and W["layers"] is a generator (each
+    layer made when it is consumed), so the full model never sits in host memory at once."""
     rng = np.random.default_rng(seed)
+    D = cfg["D"]
+    f32 = lambda a: np.asarray(a, np.float32)  # noqa: E731
+    W = dict(embed=model_blocks(cfg["embed"], cfg["vocab"], D, rng, scale=1e-2),
+             head=model_blocks(cfg["head"], cfg["vocab"], D, rng, scale=1e-4), final_norm=f32(1 + 0.1 * rng.standard_normal(D)))
+    pools = None
+    if pooled:
+        n = cfg["ne"] * cfg["ffe"] * max(D // TYPES[cfg["gate_up"]][1], 1)
+        pools = (BlockPool(cfg["gate_up"], n + n // 16, rng),
+                 BlockPool(cfg["down"], cfg["ne"] * D * max(cfg["ffe"] // TYPES[cfg["down"]][1], 1) * 17 // 16, rng))
+    gen = (_model_layer(cfg, l, rng, pools) for l in range(cfg["layers"]))
+    W["layers"] = gen if pooled else list(gen)
+    return W
+
+
+def _model_layer(cfg: dict, l: int, rng: np.random.Generator, pools) -> dict:
     D, DS, HD = cfg["D"], 128, 256
     nkh, nvh, nh, nkv = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
     convch = 2 * nkh * DS + nvh * DS
     ne, ffe = cfg["ne"], cfg["ffe"]
     P = cfg["proj"]
     f32 = lambda a: np.asarray(a, np.float32)  # noqa: E731
-    W = dict(embed=model_blocks(cfg["embed"], cfg["vocab"], D, rng, scale=1e-2),
-             head=model_blocks(cfg["head"], cfg["vocab"], D, rng, scale=1e-4), final_norm=f32(1 + 0.1 * rng.standard_normal(D)),
-             layers=[])
-    for l in range(cfg["layers"]):
-        L = dict(kind=layer_kind(cfg, l), norm1=f32(1 + 0.1 * rng.standard_normal(D)),
-                 norm2=f32(1 + 0.1 * rng.standard_normal(D)))
-        if L["kind"] == "G":
-            L.update(w_in=model_blocks(P, convch + nvh * DS, D, rng), w_ab=model_blocks(P, 2 * nvh, D, rng),
-                     w_out=model_blocks(P, D, nvh * DS, rng), conv_w=f32(rng.standard_normal((convch, 4)) * 0.5),
-                     dt_bias=f32(rng.standard_normal(nvh) * 0.5), ssm_a=f32(-np.exp(rng.standard_normal(nvh) * 0.5)),
-                     gnorm=f32(1 + 0.1 * rng.standard_normal(DS)))
-        else:
-            L.update(w_q=model_blocks(P, nh * 2 * HD, D, rng), w_k=model_blocks(P, nkv * HD, D, rng),
-                     w_v=model_blocks(P, nkv * HD, D, rng), w_o=model_blocks(P, D, nh * HD, rng),
-                     q_norm=f32(1 + 0.1 * rng.standard_normal(HD)), k_norm=f32(1 + 0.1 * rng.standard_normal(HD)))
-        gu, dn = cfg["gate_up"], cfg["down"]
-        L.update(router=model_blocks(cfg["router"], ne + 1, D, rng),
-                 moe=[model_blocks(gu, ne * ffe, D, rng), model_blocks(gu, ne * ffe, D, rng),
-                      model_blocks(dn, ne * D, ffe, rng), model_blocks(gu, ffe, D, rng), model_blocks(gu, ffe, D, rng),
-                      model_blocks(dn, D, ffe, rng)])
-        W["layers"].append(L)
-    return W
+    L = dict(kind=layer_kind(cfg, l), norm1=f32(1 + 0.1 * rng.standard_normal(D)),
+             norm2=f32(1 + 0.1 * rng.standard_normal(D)))
+    if L["kind"] == "G":
+        L.update(w_in=model_blocks(P, convch + nvh * DS, D, rng), w_ab=model_blocks(P, 2 * nvh, D, rng),
+                 w_out=model_blocks(P, D, nvh * DS, rng), conv_w=f32(rng.standard_normal((convch, 4)) * 0.5),
+                 dt_bias=f32(rng.standard_normal(nvh) * 0.5), ssm_a=f32(-np.exp(rng.standard_normal(nvh) * 0.5)),
+                 gnorm=f32(1 + 0.1 * rng.standard_normal(DS)))
+    else:
+        L.update(w_q=model_blocks(P, nh * 2 * HD, D, rng), w_k=model_blocks(P, nkv * HD, D, rng),
+                 w_v=model_blocks(P, nkv * HD, D, rng), w_o=model_blocks(P, D, nh * HD, rng),
+                 q_norm=f32(1 + 0.1 * rng.standard_normal(HD)), k_norm=f32(1 + 0.1 * rng.standard_normal(HD)))
+    gu, dn = cfg["gate_up"], cfg["down"]
+    L["router"] = model_blocks(cfg["router"], ne + 1, D, rng)
+    if pools is None:
+        routed = [model_blocks(gu, ne * ffe, D, rng), model_blocks(gu, ne * ffe, D, rng), model_blocks(dn, ne * D, ffe, rng)]
+    else:
+        routed = [pools[0].take(ne * ffe, D), pools[0].take(ne * ffe, D), pools[1].take(ne * D, ffe)]
+    L["moe"] = routed + [model_blocks(gu, ffe, D, rng), model_blocks(gu, ffe, D, rng), model_blocks(dn, D, ffe, rng)]
+    return L
 
 
 def rope_inv_freq(base: float, nrot: int = 64) -> np.ndarray:
