@@ -31,6 +31,7 @@ EXPORTS = [
     "fn_test_gemv_argmax", "fn_ipc_alloc", "fn_ipc_open", "fn_ipc_close", "fn_ipc_free", "fn_group_create",
     "fn_group_free", "fn_w_gemv_argmax_group", "fn_moe_ep_create", "fn_moe_ep_run", "fn_w_step_host",
     "fn_embed", "fn_rmsnorm", "fn_attn_decode", "fn_step_advance", "fn_gdn_reset",
+    "fn_tc_create", "fn_tc_free", "fn_tc_gemv", "fn_test_tc_gemv", "fn_bench_tc_gemv",
 ]
 
 
@@ -93,6 +94,11 @@ class FN:
         d.fn_attn_decode.argtypes = [vp] * 11 + [C.c_int, C.c_int, C.c_int, C.c_float, vp]
         d.fn_step_advance.argtypes = [vp, vp, vp, vp, C.c_int, vp]
         d.fn_gdn_reset.argtypes = [C.c_int, vp]
+        d.fn_tc_create.argtypes = [C.c_uint32, U8, C.c_int, C.c_int]
+        d.fn_tc_free.argtypes = [C.c_int]
+        d.fn_tc_gemv.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, vp]
+        d.fn_test_tc_gemv.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, F32]
+        d.fn_bench_tc_gemv.argtypes = [C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float)]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -259,6 +265,32 @@ class FN:
     def moe_ep_run(self, h, logits_ptr, ls, x_ptr, y_ptr, nt=1, acc=0, stream=0):
         self.check(self.d.fn_moe_ep_run(h, C.c_void_p(logits_ptr), ls, C.c_void_p(x_ptr), C.c_void_p(y_ptr), nt, acc,
                                         C.c_void_p(stream)))
+
+    # ---- batched decode on the tensor cores (tcgen05), 1..32 tokens ----
+    def tc_create(self, qtype, raw, rows, cols) -> int:
+        h = self.d.fn_tc_create(int(qtype), np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), rows, cols)
+        if h < 0:
+            raise RuntimeError(self.d.fn_error().decode())
+        return h
+
+    def tc_free(self, h):
+        self.check(self.d.fn_tc_free(h))
+
+    def tc_gemv(self, h, x_ptr, xs, y_ptr, ys, nt, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_tc_gemv(h, vp(x_ptr), xs, vp(y_ptr), ys, nt, vp(stream)))
+
+    def test_tc_gemv(self, qtype, raw, rows, cols, x):
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+        y = np.zeros((x.shape[0], rows), np.float32)
+        self.check(self.d.fn_test_tc_gemv(int(qtype), np.ascontiguousarray(raw, np.uint8).reshape(-1), rows, cols,
+                                          x.reshape(-1), x.shape[0], y.reshape(-1)))
+        return y
+
+    def bench_tc_gemv(self, qtype, rows, cols, nt, iters=200) -> float:
+        ms = C.c_float()
+        self.check(self.d.fn_bench_tc_gemv(int(qtype), rows, cols, nt, iters, C.byref(ms)))
+        return ms.value
 
     def gemv_override(self, warps=-1, ring_kb=0, stage_kb=0, ctas_per_sm=0):
         """Plan settings for weights created from now on (engine/faie2fn.cu:2786-2791; warps 0 = by weight size)."""

@@ -219,6 +219,22 @@ int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int k, int
                         const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
                         const float *logits, int ls, const float *x, float *y, int nt, void *stream);
 
+/* ---- batched decode on the tensor cores (tcgen05) ------------------------------------------------------------ */
+/* Resident weights for the tensor-core batched GEMV: GGUF rows Wh [rows][row_bytes] of any of the 19 formats (cols a
+ * multiple of 128). Handle >= 1 or -1. The batched form of gemv() (engine/faie2fn.cu:2250-2281; the reference's k_tgemv
+ * takes nt <= 8 on CUDA cores, :734-955). */
+int fn_tc_create(uint32_t type, const uint8_t *Wh, int rows, int cols);
+int fn_tc_free(int h);
+/* y[t][r] = W[r] . x[t] for t < nt <= 32 on a stream (device pointers; token strides xs, ys in floats; x 16-byte
+ * aligned): each weight tile dequantised once to bf16 hi/lo pairs and multiplied by all tokens with tcgen05.mma
+ * (hi*hi + hi*lo + lo*hi, fp32 accumulation in tensor memory); within 1e-4 of float64 relative to max |y|,
+ * deterministic. One call at a time per handle. */
+int fn_tc_gemv(int h, const float *x, int xs, float *y, int ys, int nt, void *stream);
+/* The same on host buffers (synchronous), as fn_test_gemv: x [nt][cols] -> y [nt][rows]. */
+int fn_test_tc_gemv(uint32_t type, const uint8_t *Wh, int rows, int cols, const float *x, int nt, float *y);
+/* Device ms per call of the tensor-core GEMV on random weights streamed from HBM (as fn_bench_gemv), nt tokens. */
+int fn_bench_tc_gemv(uint32_t type, int rows, int cols, int nt, int iters, float *ms);
+
 #ifdef __cplusplus
 }
 #endif
