@@ -25,6 +25,7 @@
 //     32w + l) with tcgen05.ld and stored to y (or to the split's partial).
 // Every wait is bounded: a wait that runs out records DEV_WAIT_TIMEOUT, the CTA still waits (bounded) for the MMAs it
 // issued, frees its tensor memory and returns.
+#include <cuda.h>
 #include <cuda_bf16.h>
 
 #include <mutex>
@@ -37,13 +38,14 @@ namespace fn {
 
 constexpr int TC_M = 128;       // rows per tile (one MMA's M)
 constexpr int TC_KC = 128;      // columns per chunk
-constexpr int TC_THREADS = 256;
+constexpr int TC_THREADS = 512;
 constexpr int TC_NMAX = 32;     // tokens per call
 constexpr int TC_TMEM_COLS = 32;
 
 static size_t tc_align(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct TcArgs {
+    CUtensorMap tmap;  // W as a 2-D byte array [rows][ldw]; box: 128 rows x raw_stride bytes
     const uint8_t *W;  // GGUF rows at stride ldw
     uint32_t ldw;
     int rows, cols;
@@ -54,6 +56,7 @@ struct TcArgs {
     int chunks_per_split, splits;
     float *part;        // [splits][32][rows] when splits > 1
     uint32_t *tickets;  // [tiles], zero between launches
+    uint32_t raw_stride;  // bytes per row of a raw chunk slot (16-byte multiple): the TMA box width
     uint32_t *err;
 };
 
@@ -61,7 +64,17 @@ struct TcArgs {
 constexpr uint32_t TC_A_BYTES = TC_M * TC_KC * 2;        // 32 KiB
 constexpr uint32_t TC_B_BYTES = TC_NMAX * TC_KC * 2;     // 8 KiB at N = 32
 constexpr uint32_t TC_BUF_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;
-constexpr uint32_t TC_SMEM = 2 * TC_BUF_BYTES + 128;     // two buffers + barriers
+constexpr uint32_t TC_BARS = 2 * TC_BUF_BYTES;           // 4 mbarriers: MMA done per buffer, raw chunk landed per slot
+constexpr uint32_t TC_RAW = TC_BARS + 128;              // two raw chunk slots of 128 rows x raw_stride
+constexpr size_t TC_SMEM_MAX = 227 * 1024 - 1024;       // less the static shared memory
+
+// bytes [start, end) of a row that chunk c (columns 128 c .. 128 c + 127) decodes from: whole blocks, widened to
+// 16-byte boundaries for the bulk copy (the row stride is a 16-byte multiple, so end <= the stride)
+__host__ __device__ inline void tc_chunk_bytes(int c, int qk, int tb, uint32_t &start, uint32_t &end) {
+    const uint32_t b0 = (uint32_t)(c * TC_KC / qk), b1 = (uint32_t)(((c + 1) * TC_KC + qk - 1) / qk);
+    start = (b0 * (uint32_t)tb) & ~15u;
+    end = (b1 * (uint32_t)tb + 15u) & ~15u;
+}
 
 // sm_100 shared-memory matrix descriptor: start address, leading / stride byte offsets (>> 4), version 1, no swizzle
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -111,22 +124,39 @@ __device__ __forceinline__ void split4(float a, float b, float c, float d, uint2
 }
 
 template <uint32_t TY>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const TcArgs a) {
+__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail, s_last;
-    uint64_t *bars = (uint64_t *)(sm + 2 * TC_BUF_BYTES);  // [2]: the MMAs reading buffer b are complete
+    uint64_t *mbars = (uint64_t *)(sm + TC_BARS);      // [2]: the MMAs reading buffer b are complete
+    uint64_t *rbars = mbars + 2;                       // [2]: raw chunk slot s has landed
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile = blockIdx.x, split = blockIdx.y, row0 = tile * TC_M;
     const int nchunks = a.cols / TC_KC;
     const int c0 = split * a.chunks_per_split, c1 = min(nchunks, c0 + a.chunks_per_split);
+    const int nrow = min(TC_M, a.rows - row0);
     const uint32_t n = (uint32_t)a.npad, bbytes = n * TC_KC * 2;  // B bytes per hi / lo
     const uint32_t idesc = umma_idesc_bf16(TC_M, a.npad);
     const uint32_t *grid = dev_grid<TY>();
+    constexpr int QK = Dec<TY>::qk, TB = Dec<TY>::bytes;
+
+    // the raw bytes of chunk c of the tile's rows into slot sl: one 2-D tensor copy of the box (128 rows x raw_stride
+    // bytes from byte column st, a 16-byte multiple; rows past the matrix and bytes past the stride read as zero)
+    auto issue_raw = [&](int c, int sl) {
+        if (tid != 0) return;
+        uint32_t st, en;
+        tc_chunk_bytes(c, QK, TB, st, en);
+        uint64_t *bar = &rbars[sl];
+        mbar_arrive_tx(bar, (uint32_t)TC_M * a.raw_stride);
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+            ::"r"(smem_u32(sm + TC_RAW + (size_t)sl * TC_M * a.raw_stride)), "l"(&a.tmap), "r"((int)st), "r"(row0),
+            "r"(smem_u32(bar))
+            : "memory");
+    };
 
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int q = 0; q < 4; ++q) mbar_init(&mbars[q], 1);
         mbar_fence_init();
         s_fail = 0;
     }
@@ -140,27 +170,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const TcArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    // the weights are read-only: the first two chunks' copies fly before the wait for the previous kernel
+    if (c0 < c1) issue_raw(c0, 0);
+    if (c0 + 1 < c1) issue_raw(c0 + 1, 1);
 
     pdl_wait();
     pdl_trigger();
     const float *x = after_wait(a.x);
+    // x: one (token, 8-column group) item per thread (n * 16 <= 512 items); the next chunk's values are loaded into
+    // registers while this chunk is decoded
+    const int xt = tid % (int)n, xkc = tid / (int)n;
+    const bool xitem = tid < (int)n * (TC_KC / 8), xlive = xitem && xt < a.nt;
+    auto load_x = [&](int c, float4 &p, float4 &q) {
+        if (xlive) {
+            const float4 *src = (const float4 *)(x + (size_t)xt * a.xs + c * TC_KC + xkc * 8);
+            p = src[0];
+            q = src[1];
+        }
+    };
+    float4 xp = make_float4(0.f, 0.f, 0.f, 0.f), xq = xp, np_ = xp, nq_ = xp;
+    if (c0 < c1) load_x(c0, xp, xq);
 
-    int issued = 0;  // chunks whose MMAs were issued (the commit of chunk i arrives on bars[i & 1])
+    int issued = 0;  // chunks whose MMAs were issued (the commit of chunk i arrives on mbars[i & 1])
     for (int c = c0; c < c1; ++c) {
         const int i = c - c0, b = i & 1;
         uint8_t *buf = sm + b * TC_BUF_BYTES;
         uint8_t *Ahi = buf, *Alo = buf + TC_A_BYTES, *Bhi = buf + 2 * TC_A_BYTES, *Blo = Bhi + bbytes;
-        if (i >= 2 && !mbar_wait(&bars[b], (uint32_t)((i - 2) >> 1) & 1u)) {  // chunk i - 2's MMAs read this buffer
-            if (tid == 0) s_fail = 1;
-        }
+        // the slot of chunk i + 1 held chunk i - 1, decoded before the barrier that ended that chunk's staging
+        if (i >= 1 && c + 1 < c1) issue_raw(c + 1, (i + 1) & 1);
+        bool ok = mbar_wait(&rbars[i & 1], (uint32_t)(i >> 1) & 1u);
+        if (i >= 2) ok = ok && mbar_wait(&mbars[b], (uint32_t)((i - 2) >> 1) & 1u);  // chunk i - 2 read this buffer
+        if (!ok) s_fail = 1;
         __syncthreads();
         if (s_fail) break;
-        // weights: item it = (row, group of 32 in the chunk); a warp takes 32 consecutive rows of one group
+        if (c + 1 < c1) load_x(c + 1, np_, nq_);
+        // weights: one (row, group of 32) per thread, a warp on 32 consecutive rows, decoded from the raw slot (the
+        // row pointer is shifted so that the decoder's block offsets of this chunk land in the slot)
+        uint32_t st, en;
+        tc_chunk_bytes(c, QK, TB, st, en);
+        const uint8_t *raw = sm + TC_RAW + (size_t)(i & 1) * TC_M * a.raw_stride;
         for (int it = tid; it < TC_M * (TC_KC / 32); it += TC_THREADS) {
-            const int r = it & (TC_M - 1), gl = it >> 7, row = row0 + r;
+            const int r = it & (TC_M - 1), gl = it >> 7;
             const uint32_t roff = (uint32_t)(r >> 3) * 128u + (uint32_t)(r & 7) * 16u;
-            if (row < a.rows) {
-                const uint8_t *rp = a.W + (size_t)row * a.ldw;
+            if (r < nrow) {
+                const uint8_t *rp = raw + (size_t)r * a.raw_stride - st;
                 Dec<TY>::group(rp, c * (TC_KC / 32) + gl, grid, [&](int j, float v0, float v1, float v2, float v3) {
                     const int k = gl * 32 + j;  // column within the chunk
                     const uint32_t off = (uint32_t)(k >> 3) * (TC_M * 16u) + roff + (uint32_t)(k & 7) * 2u;
@@ -178,23 +231,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const TcArgs a) {
                 }
             }
         }
-        // x: item it = (token, 8-column group); tokens >= nt are zero
-        for (int it = tid; it < (int)n * (TC_KC / 8); it += TC_THREADS) {
-            const int t = it % (int)n, kc = it / (int)n;
-            const uint32_t off = (uint32_t)kc * (n * 16u) + (uint32_t)(t >> 3) * 128u + (uint32_t)(t & 7) * 16u;
+        // x: this thread's (token, 8-column group); tokens >= nt are zero
+        if (xitem) {
+            const uint32_t off = (uint32_t)xkc * (n * 16u) + (uint32_t)(xt >> 3) * 128u + (uint32_t)(xt & 7) * 16u;
             uint2 h0, l0, h1, l1;
-            if (t < a.nt) {
-                const float4 *src = (const float4 *)(x + (size_t)t * a.xs + c * TC_KC + kc * 8);
-                const float4 p = src[0], q = src[1];
-                split4(p.x, p.y, p.z, p.w, h0, l0);
-                split4(q.x, q.y, q.z, q.w, h1, l1);
-            } else {
-                h0 = l0 = h1 = l1 = make_uint2(0, 0);
-            }
+            split4(xp.x, xp.y, xp.z, xp.w, h0, l0);
+            split4(xq.x, xq.y, xq.z, xq.w, h1, l1);
             *(uint4 *)(Bhi + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
             *(uint4 *)(Blo + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
         }
-        async_proxy_fence();  // the generic-proxy stores, visible to the tensor cores' reads
+        xp = np_;
+        xq = nq_;
+        async_proxy_fence();  // the generic-proxy stores (and reads of the raw slot) ordered before async-proxy use
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
@@ -208,14 +256,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const TcArgs a) {
                 umma_bf16(tmem, dah, dbl, idesc, 1u);
                 umma_bf16(tmem, dal, dbh, idesc, 1u);
             }
-            umma_commit(&bars[b]);
+            umma_commit(&mbars[b]);
         }
         ++issued;
     }
-    // the last commit covers every MMA this CTA issued
+    // the last commit covers every MMA this CTA issued; raw copies still in flight (a wait ran out) land first
     if (issued > 0) {
         const int i = issued - 1;
-        if (!mbar_wait(&bars[i & 1], (uint32_t)(i >> 1) & 1u) && tid == 0) s_fail = 1;
+        if (!mbar_wait(&mbars[i & 1], (uint32_t)(i >> 1) & 1u) && tid == 0) s_fail = 1;
+    }
+    if (s_fail && tid == 0) {
+        const int n_issued_raw = min(c1 - c0, issued + 2);
+        for (int q = issued; q < n_issued_raw; ++q) mbar_wait(&rbars[q & 1], (uint32_t)(q >> 1) & 1u, 1u << 16);
     }
     tc_fence_after();
     __syncthreads();
@@ -258,12 +310,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const TcArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int it = tid; it < a.nt * TC_M; it += TC_THREADS) {
-        const int t = it / TC_M, r = row0 + (it % TC_M);
-        if (r >= a.rows) continue;
-        float s = 0.0f;
-        for (int q = 0; q < a.splits; ++q) s += __ldcg(a.part + ((size_t)q * TC_NMAX + t) * a.rows + r);
-        a.y[(size_t)t * a.ys + r] = s;
+    // each thread's outputs (token t = it / 128, row it % 128; up to 8 of them): the splits added in order, one split's
+    // loads of all its outputs in flight at once
+    constexpr int PER = TC_NMAX * TC_M / TC_THREADS;
+    float sum[PER];
+#pragma unroll
+    for (int m = 0; m < PER; ++m) sum[m] = 0.0f;
+    for (int q = 0; q < a.splits; ++q) {
+        float v[PER];
+#pragma unroll
+        for (int m = 0; m < PER; ++m) {
+            const int it = tid + m * TC_THREADS, t = it / TC_M, r = row0 + (it % TC_M);
+            v[m] = t < a.nt && r < a.rows ? __ldcg(a.part + ((size_t)q * TC_NMAX + t) * a.rows + r) : 0.0f;
+        }
+#pragma unroll
+        for (int m = 0; m < PER; ++m) sum[m] += v[m];
+    }
+#pragma unroll
+    for (int m = 0; m < PER; ++m) {
+        const int it = tid + m * TC_THREADS, t = it / TC_M, r = row0 + (it % TC_M);
+        if (t < a.nt && r < a.rows) a.y[(size_t)t * a.ys + r] = sum[m];
     }
     if (tid == 0) a.tickets[tile] = 0u;
 }
@@ -271,8 +337,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const TcArgs a) {
 // ---- resident weights for the tensor-core path: GGUF rows at a 16-byte stride, plus the split-K scratch --------------
 
 struct TcH {
+    CUtensorMap tmap;
     uint32_t type = 0;
     int rows = 0, cols = 0, dev = 0, splits = 1, chunks_per_split = 1;
+    uint32_t raw_stride = 0;
+    size_t smem = 0;
     uint64_t rb = 0;
     uint32_t ldw = 0;
     DevBuf W, part, tickets;
@@ -287,7 +356,21 @@ static TcH *tc_get(int h) {
 
 static int tc_plan(TcH &w) {
     const int tiles = (w.rows + TC_M - 1) / TC_M, nchunks = w.cols / TC_KC;
-    const int target = std::max(1, num_sms() / tiles);  // one CTA per SM (its shared memory takes the SM)
+    int qk = 0, tb = 0;
+    type_info(w.type, qk, tb);
+    uint32_t mx = 0;
+    for (int c = 0; c < nchunks; ++c) {
+        uint32_t st, en;
+        tc_chunk_bytes(c, qk, tb, st, en);
+        mx = std::max(mx, en - st);
+    }
+    // the TMA box is one raw chunk of every row: an odd number of 16-byte units keeps a warp's 16-byte reads of its 32
+    // rows free of bank conflicts where that fits; a box row is at most 256 bytes
+    w.raw_stride = mx + ((mx / 16) % 2 == 0 && mx + 16 <= 256 && (size_t)TC_RAW + 2ull * TC_M * (mx + 16) <= TC_SMEM_MAX
+                             ? 16 : 0);
+    w.smem = (size_t)TC_RAW + 2ull * TC_M * w.raw_stride;
+    if (w.smem > TC_SMEM_MAX || w.raw_stride > 256) return fail("tc: rows too wide for the raw chunk slots");
+    const int target = std::max(1, std::min(8, num_sms() / tiles));  // one CTA per SM; at most 8 partials per row
     w.splits = std::max(1, std::min(nchunks, target));
     w.chunks_per_split = (nchunks + w.splits - 1) / w.splits;
     w.splits = (nchunks + w.chunks_per_split - 1) / w.chunks_per_split;  // no empty split
@@ -298,6 +381,7 @@ int launch_tc_gemv(const TcH &w, const float *x, int xs, float *y, int ys, int n
     if (nt < 1 || nt > TC_NMAX) return fail("tc gemv: nt out of range (1..32)");
     if (((uintptr_t)x & 15) || (xs & 3)) return fail("tc gemv: x must be 16-byte aligned, xs % 4 == 0");
     TcArgs a;
+    a.tmap = w.tmap;
     a.W = w.W.as<uint8_t>();
     a.ldw = w.ldw;
     a.rows = w.rows;
@@ -312,16 +396,34 @@ int launch_tc_gemv(const TcH &w, const float *x, int xs, float *y, int ys, int n
     a.splits = w.splits;
     a.part = w.part.as<float>();
     a.tickets = w.tickets.as<uint32_t>();
+    a.raw_stride = w.raw_stride;
     a.err = dev_error_ptr();
     const dim3 grid((w.rows + TC_M - 1) / TC_M, w.splits);
     cudaError_t e = cudaSuccess;
     const bool known = dispatch_type(w.type, [&]<uint32_t TY>() {
         e = allow_max_dynamic_smem(k_tc_gemv<TY>);
-        if (e == cudaSuccess) e = launch_k(k_tc_gemv<TY>, grid, dim3(TC_THREADS), (size_t)TC_SMEM, s, a);
+        if (e == cudaSuccess) e = launch_k(k_tc_gemv<TY>, grid, dim3(TC_THREADS), w.smem, s, a);
     });
     if (!known) return fail("tc gemv: unsupported type");
     if (e != cudaSuccess) return fail(std::string("tc gemv launch: ") + cudaGetErrorString(e));
     return 0;
+}
+
+// the driver's tensor-map encoder, looked up through the runtime (the library links no driver symbol, so it loads on a
+// machine without a GPU driver)
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiled encode_tiled() {
+    static EncodeTiled f = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (EncodeTiled) nullptr;
+        return (EncodeTiled)p;
+    }();
+    return f;
 }
 
 static TcH *tc_build(uint32_t type, const uint8_t *Wh, int rows, int cols) {
@@ -337,7 +439,10 @@ static TcH *tc_build(uint32_t type, const uint8_t *Wh, int rows, int cols) {
     w->rb = rb;
     w->ldw = (uint32_t)tc_align(rb, 16);
     cudaGetDevice(&w->dev);
-    tc_plan(*w);
+    if (tc_plan(*w)) {
+        delete w;
+        return nullptr;
+    }
     const int tiles = (rows + TC_M - 1) / TC_M;
     if (cudaMalloc(&w->W.p, (size_t)w->ldw * rows) != cudaSuccess ||
         cudaMemcpy2D(w->W.p, w->ldw, Wh, rb, rb, rows, cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -346,6 +451,19 @@ static TcH *tc_build(uint32_t type, const uint8_t *Wh, int rows, int cols) {
         cudaMemset(w->tickets.p, 0, (size_t)tiles * 4) != cudaSuccess) {
         delete w;
         fail("tc: device allocation / copy failed");
+        return nullptr;
+    }
+    // W as a 2-D byte tensor: dims {ldw, rows}, row stride ldw (a 16-byte multiple, base 256-byte aligned)
+    const cuuint64_t dims[2] = {w->ldw, (cuuint64_t)rows}, strides[1] = {w->ldw};
+    const cuuint32_t box[2] = {w->raw_stride, (cuuint32_t)TC_M}, es[2] = {1, 1};
+    const EncodeTiled enc = encode_tiled();
+    const CUresult cr = enc ? enc(&w->tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->W.p, dims, strides, box, es,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)
+                            : CUDA_ERROR_NOT_FOUND;
+    if (cr != CUDA_SUCCESS) {
+        delete w;
+        fail("tc: tensor map encoding failed (" + std::to_string((int)cr) + ")");
         return nullptr;
     }
     return w;
