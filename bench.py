@@ -19,8 +19,10 @@ bytes, fp16 scales |N(0,1)|*1e-3), x is N(0,1): the reference's real model tenso
 `--impl reference` times that CPU path with every host core instead (rank 0 only; other ranks exit 0).
 N > 1 (torchrun): every rank runs the sweep on its own GPU and weights (weak scaling; no data-path collective).
 `--components` (1 GPU) prints one JSON line per component instead of the bench line: every sweep GEMV alone with cold
-weights (fn_bench_gemv), the config-3 MoE layer and the config-4 DeltaNet layer step, each timed with CUDA events over
-a CUDA graph of back-to-back calls whose weights alternate between two copies (together larger than L2).
+weights (fn_bench_gemv), the tensor-core batched GEMV at 8 and 32 tokens against the CUDA-core batched GEMV, the
+config-3 MoE layer and the config-4 DeltaNet layer step, each timed with CUDA events over a CUDA graph of back-to-back
+calls whose weights alternate between copies (together larger than L2).
+`--workload decode` prints the config-5 decode line instead (tok/s; see run_decode).
 """
 
 from __future__ import annotations
@@ -162,6 +164,18 @@ def run_components():
         ms = f.bench_gemv(q, r, c, 1, 40 if r < 100000 else 10)
         emit({"component": "gemv", "format": name, "rows": r, "cols": c, "us": round(ms * 1e3, 2),
               "tb_per_s": round(alg_bytes(q, r, c) / (ms / 1e3) / 1e12, 3)})
+
+    # batched decode: the tensor-core GEMV (fn_bench_tc_gemv) against the CUDA-core batched GEMV (8 tokens per call)
+    for name, r, c in [("Q4_K", 4096, 2048), ("IQ3_XXS", 4096, 2048), ("Q8_0", 2048, 4096), LM_HEAD]:
+        q = BY_NAME[name]
+        it = 200 if r < 100000 else 20
+        cc8 = f.bench_gemv(q, r, c, 8, it)
+        for nt in (8, 32):
+            ms = f.bench_tc_gemv(q, r, c, nt, it)
+            emit({"component": "tc_gemv", "format": name, "rows": r, "cols": c, "tokens": nt, "us": round(ms * 1e3, 2),
+                  "cuda_core_us": round(cc8 * 1e3 * (nt // 8), 2), "speedup": round(cc8 * (nt // 8) / ms, 2),
+                  "tflop_per_s": round(2.0 * r * c * nt / (ms / 1e3) / 1e12, 2),
+                  "weight_tb_per_s": round(alg_bytes(q, r, c) / (ms / 1e3) / 1e12, 3)})
 
     st = torch.cuda.Stream()
     torch.cuda.set_stream(st)

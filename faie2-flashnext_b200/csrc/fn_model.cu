@@ -144,14 +144,31 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_decode(const AttnArgs a) {
     q[d] = after_wait(a.Q)[(size_t)h * ATT_HD + d];
     __syncthreads();
     const float *Kc = after_wait(a.Kc), *Vc = after_wait(a.Vc);
-    for (int t = warp; t < n; t += ATT_HD / 32) {  // one key per warp at a time, 8 dims per lane
-        const float *kr = Kc + ((size_t)t * a.nkv + kv) * ATT_HD;
-        float s = 0.0f;
+    // scores: keys t = warp, warp + 8, .. by one warp each, 8 dims per lane; a warp loads its next 4 keys at once (one
+    // memory round trip for four keys), each key's sum in the same order as one at a time
+    float qr[ATT_HD / 32];
 #pragma unroll
-        for (int i = 0; i < ATT_HD / 32; ++i) s = __fmaf_rn(q[lane + 32 * i], kr[lane + 32 * i], s);
+    for (int i = 0; i < ATT_HD / 32; ++i) qr[i] = q[lane + 32 * i];
+    constexpr int KB = 4, WS = ATT_HD / 32;
+    for (int t0 = warp; t0 < n; t0 += KB * WS) {
+        float kv_[KB][ATT_HD / 32];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sc[t] = s * 0.0625f;  // 1 / sqrt(256)
+        for (int u = 0; u < KB; ++u) {
+            const int t = t0 + u * WS;
+            const float *kr = Kc + ((size_t)min(t, n - 1) * a.nkv + kv) * ATT_HD;
+#pragma unroll
+            for (int i = 0; i < ATT_HD / 32; ++i) kv_[u][i] = kr[lane + 32 * i];
+        }
+#pragma unroll
+        for (int u = 0; u < KB; ++u) {
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < ATT_HD / 32; ++i) s = __fmaf_rn(qr[i], kv_[u][i], s);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            const int t = t0 + u * WS;
+            if (lane == 0 && t < n) sc[t] = s * 0.0625f;  // 1 / sqrt(256)
+        }
     }
     __syncthreads();
     float m = -INFINITY;
@@ -160,10 +177,13 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_decode(const AttnArgs a) {
     for (int t = d; t < n; t += ATT_HD) sc[t] = expf(sc[t] - m);
     __syncthreads();
     float l = 0.0f, o = 0.0f;
+    const float *vp = Vc + (size_t)kv * ATT_HD + d;
+    const size_t vs = (size_t)a.nkv * ATT_HD;
+#pragma unroll 8
     for (int t = 0; t < n; ++t) {  // every thread the same order: l is identical in all threads
         const float e = sc[t];
         l += e;
-        o = __fmaf_rn(e, Vc[((size_t)t * a.nkv + kv) * ATT_HD + d], o);
+        o = __fmaf_rn(e, vp[(size_t)t * vs], o);
     }
     const float gate = after_wait(a.qg)[(size_t)h * 2 * ATT_HD + ATT_HD + d];
     a.out[(size_t)h * ATT_HD + d] = (o / l) * sigm(gate);

@@ -14,7 +14,8 @@
 // Layout and schedule, per CTA (256 threads; one 128-row tile of W and a K range of its columns; CTAs split K when
 // there are fewer tiles than SMs, the last CTA of a tile adding the partials in split order, so y is deterministic):
 //   * K is walked in chunks of 128 columns, two chunk buffers in shared memory. For a chunk, warps decode the tile's
-//     128 x 128 values (one lane per row, so a warp's stores fall on consecutive 16-byte rows) into A_hi / A_lo and
+//     128 x 128 values (one lane per row and 32-value group, stored as whole 16-byte core-matrix rows, so the 8 lanes
+//     of a store phase fill one core matrix) into A_hi / A_lo and
 //     stage x's N x 128 values into B_hi / B_lo, all in the tensor cores' canonical K-major layout without swizzle:
 //     8-row x 16-byte core matrices, the 8-row groups 128 bytes apart (SBO), the 8-column groups a whole M (or N)
 //     extent apart (LBO).
@@ -214,14 +215,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
             const uint32_t roff = (uint32_t)(r >> 3) * 128u + (uint32_t)(r & 7) * 16u;
             if (r < nrow) {
                 const uint8_t *rp = raw + (size_t)r * a.raw_stride - st;
+                float v[32];  // the group's values, then four 16-byte core-matrix rows each of hi and lo: the 8 lanes of
+                              // a store phase write one core matrix's 128 contiguous bytes (no bank conflict)
                 Dec<TY>::group(rp, c * (TC_KC / 32) + gl, grid, [&](int j, float v0, float v1, float v2, float v3) {
-                    const int k = gl * 32 + j;  // column within the chunk
-                    const uint32_t off = (uint32_t)(k >> 3) * (TC_M * 16u) + roff + (uint32_t)(k & 7) * 2u;
-                    uint2 hi, lo;
-                    split4(v0, v1, v2, v3, hi, lo);
-                    *(uint2 *)(Ahi + off) = hi;
-                    *(uint2 *)(Alo + off) = lo;
+                    v[j] = v0;
+                    v[j + 1] = v1;
+                    v[j + 2] = v2;
+                    v[j + 3] = v3;
                 });
+#pragma unroll
+                for (int kc = 0; kc < 4; ++kc) {
+                    uint2 h0, l0, h1, l1;
+                    split4(v[8 * kc], v[8 * kc + 1], v[8 * kc + 2], v[8 * kc + 3], h0, l0);
+                    split4(v[8 * kc + 4], v[8 * kc + 5], v[8 * kc + 6], v[8 * kc + 7], h1, l1);
+                    const uint32_t off = (uint32_t)(gl * 4 + kc) * (TC_M * 16u) + roff;
+                    *(uint4 *)(Ahi + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+                    *(uint4 *)(Alo + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+                }
             } else {
 #pragma unroll
                 for (int kc = 0; kc < 4; ++kc) {
@@ -246,15 +256,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t ah = smem_u32(Ahi), al = smem_u32(Alo), bh = smem_u32(Bhi), bl = smem_u32(Blo);
+            // descriptors of step 0; a 16-deep step moves the start address by two core-matrix columns (the address
+            // field is address >> 4 in the low 14 bits, and shared addresses stay below 2^18, so adding cannot carry)
+            uint64_t dah = umma_desc(smem_u32(Ahi), TC_M * 16u, 128u), dal = umma_desc(smem_u32(Alo), TC_M * 16u, 128u);
+            uint64_t dbh = umma_desc(smem_u32(Bhi), n * 16u, 128u), dbl = umma_desc(smem_u32(Blo), n * 16u, 128u);
+            const uint64_t ainc = 2u * TC_M * 16u >> 4, binc = 2u * n * 16u >> 4;
 #pragma unroll
             for (int j = 0; j < TC_KC / 16; ++j) {  // 16-deep steps: two 8-column core matrices each
-                const uint32_t ao = (uint32_t)j * 2u * (TC_M * 16u), bo = (uint32_t)j * 2u * (n * 16u);
-                const uint64_t dah = umma_desc(ah + ao, TC_M * 16u, 128u), dal = umma_desc(al + ao, TC_M * 16u, 128u);
-                const uint64_t dbh = umma_desc(bh + bo, n * 16u, 128u), dbl = umma_desc(bl + bo, n * 16u, 128u);
                 umma_bf16(tmem, dah, dbh, idesc, (i > 0 || j > 0) ? 1u : 0u);
                 umma_bf16(tmem, dah, dbl, idesc, 1u);
                 umma_bf16(tmem, dal, dbh, idesc, 1u);
+                dah += ainc;
+                dal += ainc;
+                dbh += binc;
+                dbl += binc;
             }
             umma_commit(&mbars[b]);
         }
