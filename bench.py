@@ -393,8 +393,46 @@ def run_decode(f, args, rank, with_cpu=True):
     return d
 
 
+def run_decode_batch(f, args, batch):
+    """Config 5 at batch `batch` on the tensor-core path: `batch` seeded 64-token prompts, 256 greedy tokens each, one
+    step = one CUDA graph replay for all sequences. tok/s = batch x 256 / the CUDA-event time of the 256 steps."""
+    import torch
+    from model import BatchDecodeModel
+    from synth import model_config, model_weights
+    cfg = model_config()
+    n_prompt, n_new = 64, 256
+    t0 = time.perf_counter()
+    m = BatchDecodeModel(f, cfg, model_weights(cfg, seed=0, pooled=True), batch, max_ctx=n_prompt + n_new)
+    build_s = time.perf_counter() - t0
+    s = torch.cuda.Stream()
+    m.capture(s)
+    prompts = np.random.default_rng(0).integers(0, cfg["vocab"], (batch, n_prompt))
+    m.generate(prompts, 16, s)  # warm-up
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    ids = m.generate(prompts, n_new, s, marks=ev)
+    clk = clocks.stop()
+    gen_ms = ev[1].elapsed_time(ev[2])
+    ms_step = gen_ms / n_new
+    d = {"batch": batch, "tok_s": round(batch * n_new * 1e3 / gen_ms, 2), "ms_per_step": round(ms_step, 4),
+         "tok_s_per_sequence": round(1e3 / ms_step, 2), "gpu_launches_per_step": m.launches_per_step(),
+         "distinct_ids": int(len(np.unique(ids[:, n_prompt:]))), "build_s": round(build_s, 1), "clocks": clk,
+         "path": "projections, routers and lm_head on fn_tc_gemv (tcgen05.mma, bf16 hi/lo), MoE in groups of 8 tokens"}
+    m.free()
+    return d
+
+
 def decode_line(f, args):
     """`--workload decode`: the config-5 decode as its own bench line (tok/s)."""
+    if args.batch > 1:
+        d = run_decode_batch(f, args, args.batch)
+        return {"metric": METRIC, "value": d["tok_s"], "unit": "tok/s", "n_gpus": 1, "steps": 256, "warmup": 16,
+                "ms_per_step": d["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 (bf16 hi/lo tensor-core products)", "data": "synthetic",
+                "config": {"workload": f"config5 batched decode, batch {args.batch}: 64-token prompts, 256 greedy tokens "
+                                       "each", "parallelism": "1 GPU"},
+                "gpu_launches": d["gpu_launches_per_step"] * 256, "clocks": d["clocks"], "decode_batch": d}
     d = run_decode(f, args, 0, with_cpu=not args.no_cpu_baseline)
     if args.profile_steps:
         return d
@@ -470,6 +508,8 @@ def main():
                     help="lm_head: only the dominant kernel (the small case the ncu capture profiles); decode: only "
                          "the config-5 greedy decode (its own line, tok/s)")
     ap.add_argument("--no-decode", action="store_true", help="leave the config-5 decode out of the sweep line")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="with --workload decode: that many sequences at once on the tensor-core path (2..32)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="with --workload decode: run this many eager decode steps in an NVTX range and exit")
     args = ap.parse_args()

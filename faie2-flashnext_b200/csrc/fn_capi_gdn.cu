@@ -9,6 +9,7 @@
 namespace fn {
 
 struct GdnH {
+    int batch = 1;  // independent sequences, each with its own state and conv histories
     GdnParams p;
     DevBuf conv_w, dt_bias, ssm_a, norm_w, S, conv_v, conv_qk;
     GdnState st;
@@ -143,12 +144,54 @@ FN_API int fn_gdn_create(int nkh, int nvh, int ds, const float *conv_w, const fl
     return (int)g_gdn.size();
 }
 
+// A DeltaNet layer for `batch` independent sequences (batched decode): parameters as fn_gdn_create, every sequence's
+// state and conv histories zero. Returns a handle >= 1 or -1; run it with fn_gdn_run_batch.
+FN_API int fn_gdn_create_batch(int nkh, int nvh, int ds, const float *conv_w, const float *dt_bias, const float *ssm_a,
+                               const float *norm_w, int batch) {
+    if (batch < 1 || batch > 1024) return fail("fn_gdn_create_batch: batch out of range (1..1024)");
+    const size_t nS = (size_t)nvh * ds * ds, nconv = (size_t)3 * (2 * nkh * ds + nvh * ds);
+    std::vector<float> S0(nS, 0.f), c0(nconv, 0.f);
+    GdnH *g = gdn_build(nkh, nvh, ds, conv_w, dt_bias, ssm_a, norm_w, S0.data(), c0.data());
+    if (!g) return -1;
+    g->batch = batch;
+    if (batch > 1) {  // the per-sequence states, zero
+        const size_t bS = (size_t)batch * nS * 4, bv = (size_t)batch * 3 * nvh * ds * 4,
+                     bqk = (size_t)batch * nvh * 3 * 2 * ds * 4;
+        DevBuf S, v, qk;
+        if (cudaMalloc(&S.p, bS) != cudaSuccess || cudaMalloc(&v.p, bv) != cudaSuccess ||
+            cudaMalloc(&qk.p, bqk) != cudaSuccess || cudaMemset(S.p, 0, bS) != cudaSuccess ||
+            cudaMemset(v.p, 0, bv) != cudaSuccess || cudaMemset(qk.p, 0, bqk) != cudaSuccess) {
+            delete g;
+            return fail("fn_gdn_create_batch: device allocation failed");
+        }
+        std::swap(g->S.p, S.p);
+        std::swap(g->conv_v.p, v.p);
+        std::swap(g->conv_qk.p, qk.p);
+        g->st.S = g->S.as<float>();
+        g->st.conv_v = g->conv_v.as<float>();
+        g->st.conv_qk = g->conv_qk.as<float>();
+    }
+    std::lock_guard<std::mutex> l(g_gdn_mu);
+    g_gdn.push_back(g);
+    return (int)g_gdn.size();
+}
+
+// One decode step of every sequence of a batch handle: token row b of qkv / z / ab / out (strides qs, zs, abs_, os in
+// floats) is sequence b's. prefetch_state as fn_gdn_run.
+FN_API int fn_gdn_run_batch(int h, const float *qkv, int qs, const float *z, int zs, const float *ab, int abs_,
+                            float *out, int os, int prefetch_state, void *stream) {
+    GdnH *g = gdn_get(h);
+    if (!g) return fail("fn_gdn_run_batch: bad handle");
+    return launch_gdn(g->p, g->st, qkv, qs, z, zs, ab, abs_, out, os, 1, prefetch_state != 0, (cudaStream_t)stream,
+                      g->batch);
+}
+
 // Zero the handle's recurrent state and conv histories (the start of a new sequence), on `stream`.
 FN_API int fn_gdn_reset(int h, void *stream) {
     GdnH *g = gdn_get(h);
     if (!g) return fail("fn_gdn_reset: bad handle");
-    const size_t nS = (size_t)g->p.nvh * g->p.ds * g->p.ds, nv = (size_t)3 * g->p.nvh * g->p.ds,
-                 nqk = (size_t)g->p.nvh * 3 * 2 * g->p.ds;
+    const size_t nS = (size_t)g->batch * g->p.nvh * g->p.ds * g->p.ds, nv = (size_t)g->batch * 3 * g->p.nvh * g->p.ds,
+                 nqk = (size_t)g->batch * g->p.nvh * 3 * 2 * g->p.ds;
     cudaStream_t s = (cudaStream_t)stream;
     FN_CK(cudaMemsetAsync(g->st.S, 0, nS * 4, s));
     FN_CK(cudaMemsetAsync(g->st.conv_v, 0, nv * 4, s));
@@ -173,6 +216,7 @@ FN_API int fn_gdn_run(int h, const float *qkv, int qs, const float *z, int zs, c
                       int os, int nt, int prefetch_state, void *stream) {
     GdnH *g = gdn_get(h);
     if (!g) return fail("fn_gdn_run: bad handle");
+    if (g->batch > 1) return fail("fn_gdn_run: a batch handle runs with fn_gdn_run_batch");
     return launch_gdn(g->p, g->st, qkv, qs, z, zs, ab, abs_, out, os, nt, prefetch_state != 0, (cudaStream_t)stream);
 }
 

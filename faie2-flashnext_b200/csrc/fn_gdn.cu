@@ -54,6 +54,12 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int j = tid >> 2, c = tid & 3;
     const int kh = h % a.nkh, nvd = a.nvh * DS;
+    // a batch of independent sequences (gridDim.y > 1, one token each): sequence blockIdx.y's state, conv histories
+    // and token row
+    const int bq = blockIdx.y;
+    float *const stS = a.S + (size_t)bq * a.nvh * DS * DS;
+    float *const stQK = a.cst_qk + (size_t)bq * a.nvh * 3 * 2 * DS;
+    float *const stV = a.cst_v + (size_t)bq * 3 * nvd;
     // conv roles: threads 0..127 q channel d, 128..255 k channel d, 256..383 v channel d (of this value head)
     const int role = tid >> 7, d = tid & 127;
     int ch = -1;
@@ -61,21 +67,21 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     int sst = 0;  // state stride between the 3 history slots
     if (role == 0) {
         ch = kh * DS + d;
-        stp = a.cst_qk + (size_t)h * 3 * 2 * DS + d;
+        stp = stQK + (size_t)h * 3 * 2 * DS + d;
         sst = 2 * DS;
     } else if (role == 1) {
         ch = a.nkh * DS + kh * DS + d;
-        stp = a.cst_qk + (size_t)h * 3 * 2 * DS + DS + d;
+        stp = stQK + (size_t)h * 3 * 2 * DS + DS + d;
         sst = 2 * DS;
     } else if (role == 2) {
         ch = 2 * a.nkh * DS + h * DS + d;
-        stp = a.cst_v + (size_t)h * DS + d;
+        stp = stV + (size_t)h * DS + d;
         sst = nvd;
     }
     // ---- state, conv state, parameters: read before griddepcontrol.wait when the state was complete before the
     // previous kernel started (prefetch), else after it (the previous kernel may be this layer's previous step)
     float s[32];
-    float *Sh = a.S + (size_t)h * DS * DS;
+    float *Sh = stS + (size_t)h * DS * DS;
     float h0 = 0.f, h1 = 0.f, h2 = 0.f;
     float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
     auto load_state = [&]() {
@@ -97,9 +103,10 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
         if (stp) stp = after_wait(stp);
         load_state();
     }
-    const float *qkv = after_wait(a.qkv);
-    const float *zp = after_wait(a.z);
-    const float *abp = after_wait(a.ab);
+    const float *qkv = after_wait(a.qkv) + (size_t)bq * a.qs;
+    const float *zp = after_wait(a.z) + (size_t)bq * a.zs;
+    const float *abp = after_wait(a.ab) + (size_t)bq * a.abs_;
+    float *const outp = a.out + (size_t)bq * a.os;
 
     for (int t = 0; t < a.nt; ++t) {
         // conv + silu of this thread's channel; history shifts
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
             for (int i = 0; i < 16; ++i) ss += red_o[i];
             const float r = rsqrtf(ss / DS + 1e-6f);
             const size_t oi = (size_t)h * DS + j;
-            a.out[(size_t)t * a.os + oi] = o * r * nwj * sigm(zp[(size_t)t * a.zs + oi]);
+            outp[(size_t)t * a.os + oi] = o * r * nwj * sigm(zp[(size_t)t * a.zs + oi]);
         }
         __syncthreads();
     }
@@ -185,10 +192,11 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
 }
 
 int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs, const float *z, int zs, const float *ab,
-               int abs_, float *out, int os, int nt, bool prefetch_state, cudaStream_t s) {
+               int abs_, float *out, int os, int nt, bool prefetch_state, cudaStream_t s, int batch) {
     if (p.ds != GDN_DS) return fail("gdn: head dim must be 128");
     if (p.nkh < 1 || p.nvh < 1 || p.nvh % p.nkh) return fail("gdn: value heads must be a multiple of key heads");
     if (nt < 1) return fail("gdn: nt < 1");
+    if (batch < 1 || (batch > 1 && nt != 1)) return fail("gdn: a batch of sequences runs one token each");
     if (((uintptr_t)p.conv_w & 15)) return fail("gdn: conv weights must be 16-byte aligned");
     GdnArgs a;
     a.qkv = qkv;
@@ -210,7 +218,7 @@ int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs,
     a.nvh = p.nvh;
     a.nt = nt;
     a.prefetch = prefetch_state ? 1 : 0;
-    const cudaError_t e = launch_k(k_gdn, dim3(p.nvh), dim3(GDN_THREADS), 0, s, a);
+    const cudaError_t e = launch_k(k_gdn, dim3(p.nvh, batch), dim3(GDN_THREADS), 0, s, a);
     if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
     return 0;
 }

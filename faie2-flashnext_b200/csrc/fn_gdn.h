@@ -21,7 +21,9 @@ struct GdnState {  // device pointers
 // nt tokens of one layer: qkv [nt][qs], z [nt][zs], ab [nt][abs_] (alpha | beta) -> out [nt][os]; state advanced.
 // prefetch_state: the state was complete before the previous kernel in the stream started (true when the layer's
 // previous launch is two or more kernels back), so it may be read before the programmatic-launch wait.
+// batch > 1: that many independent sequences, one token each (nt == 1), sequence b's state at b times the state size
+// and its token row at b times the strides.
 int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs, const float *z, int zs, const float *ab,
-               int abs_, float *out, int os, int nt, bool prefetch_state, cudaStream_t s);
+               int abs_, float *out, int os, int nt, bool prefetch_state, cudaStream_t s, int batch = 1);
 
 }  // namespace fn

@@ -49,10 +49,12 @@ template <int NW> __device__ __forceinline__ float block_max_fixed(float v, floa
 // ---- embedding: h = dequant(E[tokens[*pos]]), one CTA
 template <uint32_t TY>
 __global__ void k_embed(const uint8_t *__restrict__ E, uint64_t rb, const int *__restrict__ tokens,
-                        const int *__restrict__ pos, float *__restrict__ h, int D) {
+                        const int *__restrict__ pos, float *__restrict__ h, int D, int tstride) {
     pdl_wait();
     pdl_trigger();
-    const int tok = after_wait(tokens)[*after_wait(pos)];
+    // CTA b: sequence b of a batch (its token ids at b * tstride, its row of h at b * D)
+    h += (size_t)blockIdx.x * D;
+    const int tok = after_wait(tokens)[(size_t)blockIdx.x * tstride + *after_wait(pos)];
     const uint8_t *row = E + (size_t)tok * rb;
     const uint32_t *grid = dev_grid<TY>();
     for (int g = threadIdx.x; g < D / 32; g += blockDim.x)
@@ -67,7 +69,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *__restrict__ x, co
     __shared__ float red[8];
     pdl_wait();
     pdl_trigger();
-    const float *xp = after_wait(x);
+    const float *xp = after_wait(x) + (size_t)blockIdx.x * D;  // CTA b: row b
+    out += (size_t)blockIdx.x * D;
     float ss = 0.0f;
     for (int i = threadIdx.x * 4; i < D; i += 1024) {
         const float4 v = *(const float4 *)(xp + i);
@@ -91,6 +94,7 @@ struct AttnQkvArgs {
     const int *pos;
     int nh, nkv, max_ctx;
     float eps;
+    int ss;  // a batch of sequences (gridDim.y): floats between sequence b's qg, k and v rows
 };
 
 __global__ void __launch_bounds__(ATT_HD) k_attn_qkv(const AttnQkvArgs a) {
@@ -98,15 +102,17 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_qkv(const AttnQkvArgs a) {
     __shared__ float buf[ATT_HD];
     pdl_wait();
     pdl_trigger();
-    const int j = blockIdx.x, d = threadIdx.x, p = *after_wait(a.pos);
+    const int j = blockIdx.x, d = threadIdx.x, p = *after_wait(a.pos), b = blockIdx.y;
     if (p >= a.max_ctx) return;  // past the cache: the host checks the length first
+    const size_t cache = (size_t)b * a.max_ctx * a.nkv * ATT_HD, row = (size_t)b * a.ss;
+    float *Kc = a.Kc + cache, *Vc = a.Vc + cache;
     if (j >= a.nh + a.nkv) {     // values
         const int kv = j - a.nh - a.nkv;
-        a.Vc[((size_t)p * a.nkv + kv) * ATT_HD + d] = after_wait(a.v)[kv * ATT_HD + d];
+        Vc[((size_t)p * a.nkv + kv) * ATT_HD + d] = after_wait(a.v)[row + kv * ATT_HD + d];
         return;
     }
     const bool isq = j < a.nh;
-    const float x = isq ? after_wait(a.qg)[(size_t)j * 2 * ATT_HD + d] : after_wait(a.k)[(j - a.nh) * ATT_HD + d];
+    const float x = isq ? after_wait(a.qg)[row + (size_t)j * 2 * ATT_HD + d] : after_wait(a.k)[row + (j - a.nh) * ATT_HD + d];
     const float ss = block_sum_fixed<ATT_HD / 32>(x * x, red);
     buf[d] = x * rsqrtf(ss / (float)ATT_HD + a.eps) * (isq ? a.wq[d] : a.wk[d]);
     __syncthreads();
@@ -121,16 +127,17 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_qkv(const AttnQkvArgs a) {
         const float x0 = buf[i], x1 = buf[i + ATT_NROT / 2];
         y = d < ATT_NROT / 2 ? x0 * cs - x1 * sn : x1 * cs + x0 * sn;
     }
-    if (isq) a.Q[(size_t)j * ATT_HD + d] = y;
-    else a.Kc[((size_t)p * a.nkv + (j - a.nh)) * ATT_HD + d] = y;
+    if (isq) a.Q[((size_t)b * a.nh + j) * ATT_HD + d] = y;
+    else Kc[((size_t)p * a.nkv + (j - a.nh)) * ATT_HD + d] = y;
 }
 
 // ---- attention, part 2: one CTA per q head over the positions 0..pos; out = softmax(q . k / 16) v * sigmoid(gate)
 struct AttnArgs {
     const float *Q, *Kc, *Vc, *qg;
-    float *out;  // [NH][HD]
+    float *out;  // [NH][HD] per sequence
     const int *pos;
     int nh, nkv, max_ctx;
+    int ss;  // a batch of sequences (gridDim.y): floats between sequence b's qg rows
 };
 
 __global__ void __launch_bounds__(ATT_HD) k_attn_decode(const AttnArgs a) {
@@ -139,11 +146,12 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_decode(const AttnArgs a) {
     __shared__ float red[ATT_HD / 32];
     pdl_wait();
     pdl_trigger();
-    const int h = blockIdx.x, d = threadIdx.x, warp = d >> 5, lane = d & 31;
+    const int h = blockIdx.x, d = threadIdx.x, warp = d >> 5, lane = d & 31, b = blockIdx.y;
     const int n = min(*after_wait(a.pos), a.max_ctx - 1) + 1, kv = h / (a.nh / a.nkv);
-    q[d] = after_wait(a.Q)[(size_t)h * ATT_HD + d];
+    q[d] = after_wait(a.Q)[((size_t)b * a.nh + h) * ATT_HD + d];
     __syncthreads();
-    const float *Kc = after_wait(a.Kc), *Vc = after_wait(a.Vc);
+    const size_t cache = (size_t)b * a.max_ctx * a.nkv * ATT_HD;
+    const float *Kc = after_wait(a.Kc) + cache, *Vc = after_wait(a.Vc) + cache;
     // scores: keys t = warp, warp + 8, .. by one warp each, 8 dims per lane; a warp loads its next 4 keys at once (one
     // memory round trip for four keys), each key's sum in the same order as one at a time
     float qr[ATT_HD / 32];
@@ -185,25 +193,28 @@ __global__ void __launch_bounds__(ATT_HD) k_attn_decode(const AttnArgs a) {
         l += e;
         o = __fmaf_rn(e, vp[(size_t)t * vs], o);
     }
-    const float gate = after_wait(a.qg)[(size_t)h * 2 * ATT_HD + ATT_HD + d];
-    a.out[(size_t)h * ATT_HD + d] = (o / l) * sigm(gate);
+    const float gate = after_wait(a.qg)[(size_t)b * a.ss + (size_t)h * 2 * ATT_HD + ATT_HD + d];
+    a.out[((size_t)b * a.nh + h) * ATT_HD + d] = (o / l) * sigm(gate);
 }
 
 // ---- the step counter: the token the step predicted becomes the next input once the prompt is consumed
-__global__ void k_step_advance(int *pos, int *tokens, const int *next, const int *prompt_len, int max_ctx) {
+// thread b: sequence b of a batch (its token ids at b * max_ctx); one position for all
+__global__ void k_step_advance(int *pos, int *tokens, const int *next, const int *prompt_len, int max_ctx, int batch) {
     pdl_wait();
     pdl_trigger();
-    const int p = *pos;
-    if (p + 1 < max_ctx && p + 1 >= *prompt_len) tokens[p + 1] = *next;
-    *pos = p + 1;
+    const int p = *pos, b = threadIdx.x;
+    if (b < batch && p + 1 < max_ctx && p + 1 >= *prompt_len) tokens[(size_t)b * max_ctx + p + 1] = next[b];
+    __syncthreads();
+    if (b == 0) *pos = p + 1;
 }
 
 int launch_embed(uint32_t type, const uint8_t *E, uint64_t rb, const int *tokens, const int *pos, float *h, int D,
-                 cudaStream_t s) {
+                 cudaStream_t s, int batch = 1, int tstride = 0) {
     if (D % 32 || row_bytes(type, D) != rb) return fail("embed: bad type/width");
+    if (batch < 1 || batch > 65535) return fail("embed: batch out of range");
     cudaError_t e = cudaSuccess;
     const bool known = dispatch_type(type, [&]<uint32_t TY>() {
-        e = launch_k(k_embed<TY>, dim3(1), dim3(256), 0, s, E, rb, tokens, pos, h, D);
+        e = launch_k(k_embed<TY>, dim3(batch), dim3(256), 0, s, E, rb, tokens, pos, h, D, tstride);
     });
     if (!known) return fail("embed: unsupported type");
     if (e != cudaSuccess) return fail(std::string("embed launch: ") + cudaGetErrorString(e));
@@ -224,6 +235,20 @@ FN_API int fn_embed(uint32_t type, const uint8_t *E, int D, const int *tokens, c
 
 // out = x * rsqrt(mean(x^2) + eps) * w over D values (D % 4 == 0, 16-byte aligned). Replaces k_groupnorm
 // (engine/faie2fn.cu:1222-1235) for one stream.
+// h[b][0..D) = dequant(E row tokens[b * tstride + *pos]) for b < batch (batched decode: one position for all).
+FN_API int fn_embed_batch(uint32_t type, const uint8_t *E, int D, const int *tokens, int tstride, const int *pos,
+                          float *h, int batch, void *stream) {
+    return launch_embed(type, E, row_bytes(type, D), tokens, pos, h, D, (cudaStream_t)stream, batch, tstride);
+}
+
+// fn_rmsnorm of `rows` rows of D values each (row b at b * D floats of x and out).
+FN_API int fn_rmsnorm_rows(const float *x, const float *w, float *out, int D, int rows, float eps, void *stream) {
+    if (D < 4 || D % 4 || rows < 1 || rows > 65535) return fail("rmsnorm: bad width / rows");
+    const cudaError_t e = launch_k(k_rmsnorm, dim3(rows), dim3(256), 0, (cudaStream_t)stream, x, w, out, D, eps);
+    if (e != cudaSuccess) return fail(std::string("rmsnorm launch: ") + cudaGetErrorString(e));
+    return 0;
+}
+
 FN_API int fn_rmsnorm(const float *x, const float *w, float *out, int D, float eps, void *stream) {
     if (D < 4 || D % 4) return fail("rmsnorm: D must be a positive multiple of 4");
     const cudaError_t e = launch_k(k_rmsnorm, dim3(1), dim3(256), 0, (cudaStream_t)stream, x, w, out, D, eps);
@@ -236,15 +261,15 @@ FN_API int fn_rmsnorm(const float *x, const float *w, float *out, int D, float e
 // the caches Kc, Vc [max_ctx][nkv][256] at *pos, then out [nh][256] = softmax(q . k / 16) v * sigmoid(gate) over the
 // positions 0..*pos. inv_freq [32] = rope_base^(-2i / 64). Replaces k_qk_norm_rope + k_attn_split + k_attn_combine
 // (engine/faie2fn.cu:1452-1478, 1598-1690) without the QSA indexer.
-FN_API int fn_attn_decode(const float *qg, const float *k, const float *v, const float *wq, const float *wk,
-                          const float *inv_freq, float *Q, float *Kc, float *Vc, float *out, const int *pos, int nh,
-                          int nkv, int max_ctx, float eps, void *stream) {
+static int attn_launch(const float *qg, const float *k, const float *v, int ss, const float *wq, const float *wk,
+                       const float *inv_freq, float *Q, float *Kc, float *Vc, float *out, const int *pos, int nh, int nkv,
+                       int max_ctx, int batch, float eps, cudaStream_t s) {
     if (nh < 1 || nkv < 1 || nh % nkv || max_ctx < 1 || max_ctx > 12288) return fail("attn: bad head counts / context");
-    cudaStream_t s = (cudaStream_t)stream;
-    AttnQkvArgs a{qg, k, v, wq, wk, inv_freq, Q, Kc, Vc, pos, nh, nkv, max_ctx, eps};
-    cudaError_t e = launch_k(k_attn_qkv, dim3(nh + 2 * nkv), dim3(ATT_HD), 0, s, a);
+    if (batch < 1 || batch > 65535) return fail("attn: batch out of range");
+    AttnQkvArgs a{qg, k, v, wq, wk, inv_freq, Q, Kc, Vc, pos, nh, nkv, max_ctx, eps, ss};
+    cudaError_t e = launch_k(k_attn_qkv, dim3(nh + 2 * nkv, batch), dim3(ATT_HD), 0, s, a);
     if (e != cudaSuccess) return fail(std::string("attn qkv launch: ") + cudaGetErrorString(e));
-    AttnArgs b{Q, Kc, Vc, qg, out, pos, nh, nkv, max_ctx};
+    AttnArgs b{Q, Kc, Vc, qg, out, pos, nh, nkv, max_ctx, ss};
     const size_t smem = (size_t)max_ctx * 4;
     static bool attr = false;
     if (!attr) {
@@ -252,9 +277,30 @@ FN_API int fn_attn_decode(const float *qg, const float *k, const float *v, const
         if (e != cudaSuccess) return fail(std::string("attn attribute: ") + cudaGetErrorString(e));
         attr = true;
     }
-    e = launch_k(k_attn_decode, dim3(nh), dim3(ATT_HD), smem, s, b);
+    e = launch_k(k_attn_decode, dim3(nh, batch), dim3(ATT_HD), smem, s, b);
     if (e != cudaSuccess) return fail(std::string("attn launch: ") + cudaGetErrorString(e));
     return 0;
+}
+
+// Gated attention for one token at position *pos (head dim 256, RoPE on the first 64 dims): qg [nh][512] (q then gate
+// per head), k, v [nkv][256] -> the q heads normed and rotated into Q [nh][256], k (normed, rotated) and v appended to
+// the caches Kc, Vc [max_ctx][nkv][256] at *pos, then out [nh][256] = softmax(q . k / 16) v * sigmoid(gate) over the
+// positions 0..*pos. inv_freq [32] = rope_base^(-2i / 64). Replaces k_qk_norm_rope + k_attn_split + k_attn_combine
+// (engine/faie2fn.cu:1452-1478, 1598-1690) without the QSA indexer.
+FN_API int fn_attn_decode(const float *qg, const float *k, const float *v, const float *wq, const float *wk,
+                          const float *inv_freq, float *Q, float *Kc, float *Vc, float *out, const int *pos, int nh,
+                          int nkv, int max_ctx, float eps, void *stream) {
+    return attn_launch(qg, k, v, 0, wq, wk, inv_freq, Q, Kc, Vc, out, pos, nh, nkv, max_ctx, 1, eps,
+                       (cudaStream_t)stream);
+}
+
+// fn_attn_decode for `batch` independent sequences at the same position: sequence b's qg, k and v rows at b * ss floats
+// after qg, k, v; its Q and out rows at b * nh * 256; its caches at b * max_ctx * nkv * 256 floats into Kc, Vc.
+FN_API int fn_attn_decode_batch(const float *qg, const float *k, const float *v, int ss, const float *wq,
+                                const float *wk, const float *inv_freq, float *Q, float *Kc, float *Vc, float *out,
+                                const int *pos, int nh, int nkv, int max_ctx, int batch, float eps, void *stream) {
+    return attn_launch(qg, k, v, ss, wq, wk, inv_freq, Q, Kc, Vc, out, pos, nh, nkv, max_ctx, batch, eps,
+                       (cudaStream_t)stream);
 }
 
 // After a step at position *pos: *pos += 1 and, once the prompt (tokens[0..*prompt_len)) is consumed, tokens[*pos] =
@@ -262,7 +308,18 @@ FN_API int fn_attn_decode(const float *qg, const float *k, const float *v, const
 // k_advance (engine/faie2fn.cu:1905) and the host's token feedback.
 FN_API int fn_step_advance(int *pos, int *tokens, const int *next, const int *prompt_len, int max_ctx, void *stream) {
     const cudaError_t e = launch_k(k_step_advance, dim3(1), dim3(1), 0, (cudaStream_t)stream, pos, tokens, next,
-                                   prompt_len, max_ctx);
+                                   prompt_len, max_ctx, 1);
+    if (e != cudaSuccess) return fail(std::string("step advance launch: ") + cudaGetErrorString(e));
+    return 0;
+}
+
+// fn_step_advance for `batch` sequences at one position: sequence b's token ids at tokens + b * max_ctx, its argmax at
+// next[b] (batch <= 1024).
+FN_API int fn_step_advance_batch(int *pos, int *tokens, const int *next, const int *prompt_len, int max_ctx, int batch,
+                                 void *stream) {
+    if (batch < 1 || batch > 1024) return fail("step advance: batch out of range (1..1024)");
+    const cudaError_t e = launch_k(k_step_advance, dim3(1), dim3(batch), 0, (cudaStream_t)stream, pos, tokens, next,
+                                   prompt_len, max_ctx, batch);
     if (e != cudaSuccess) return fail(std::string("step advance launch: ") + cudaGetErrorString(e));
     return 0;
 }

@@ -54,6 +54,7 @@ struct TcArgs {
     int xs;
     float *y;
     int ys, nt, npad;  // npad: the MMA's N (16 or 32)
+    int acc;           // 1: y += W x (the residual add of a projection)
     int chunks_per_split, splits;
     float *part;        // [splits][32][rows] when splits > 1
     uint32_t *tickets;  // [tiles], zero between launches
@@ -297,7 +298,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
                 for (int q = 0; q < 16; ++q) {
                     const int t = c + q;
                     if (t < a.nt) {
-                        if (a.splits == 1) a.y[(size_t)t * a.ys + r] = v[q];
+                        if (a.splits == 1) {
+                            float *o = a.y + (size_t)t * a.ys + r;
+                            *o = a.acc ? __fadd_rn(*o, v[q]) : v[q];
+                        }
                         else a.part[((size_t)split * TC_NMAX + t) * a.rows + r] = v[q];
                     }
                 }
@@ -344,7 +348,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
 #pragma unroll
     for (int m = 0; m < PER; ++m) {
         const int it = tid + m * TC_THREADS, t = it / TC_M, r = row0 + (it % TC_M);
-        if (t < a.nt && r < a.rows) a.y[(size_t)t * a.ys + r] = sum[m];
+        if (t < a.nt && r < a.rows) {
+            float *o = a.y + (size_t)t * a.ys + r;
+            *o = a.acc ? __fadd_rn(*o, sum[m]) : sum[m];
+        }
     }
     if (tid == 0) a.tickets[tile] = 0u;
 }
@@ -392,7 +399,7 @@ static int tc_plan(TcH &w) {
     return 0;
 }
 
-int launch_tc_gemv(const TcH &w, const float *x, int xs, float *y, int ys, int nt, cudaStream_t s) {
+int launch_tc_gemv(const TcH &w, const float *x, int xs, float *y, int ys, int nt, cudaStream_t s, bool acc = false) {
     if (nt < 1 || nt > TC_NMAX) return fail("tc gemv: nt out of range (1..32)");
     if (((uintptr_t)x & 15) || (xs & 3)) return fail("tc gemv: x must be 16-byte aligned, xs % 4 == 0");
     TcArgs a;
@@ -407,6 +414,7 @@ int launch_tc_gemv(const TcH &w, const float *x, int xs, float *y, int ys, int n
     a.ys = ys;
     a.nt = nt;
     a.npad = nt <= 16 ? 16 : 32;
+    a.acc = acc ? 1 : 0;
     a.chunks_per_split = w.chunks_per_split;
     a.splits = w.splits;
     a.part = w.part.as<float>();
@@ -510,13 +518,14 @@ FN_API int fn_tc_free(int h) {
     return 0;
 }
 
-// y[t][r] = W[r] . x[t] for t < nt <= 32 on a stream (device pointers; token strides xs, ys in floats; x 16-byte
-// aligned). One call at a time per handle (the split-K scratch belongs to the handle). The batched-decode form of
-// gemv() (engine/faie2fn.cu:2250-2281) on the tensor cores; within 1e-4 of float64 relative to max |y|.
-FN_API int fn_tc_gemv(int h, const float *x, int xs, float *y, int ys, int nt, void *stream) {
+// y[t][r] (+)= W[r] . x[t] for t < nt <= 32 on a stream (device pointers; token strides xs, ys in floats; x 16-byte
+// aligned; flags bit 0 adds into y). One call at a time per handle (the split-K scratch belongs to the handle). The
+// batched-decode form of gemv() (engine/faie2fn.cu:2250-2281) on the tensor cores; within 1e-4 of float64 relative to
+// max |y|.
+FN_API int fn_tc_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int flags, void *stream) {
     TcH *w = tc_get(h);
     if (!w) return fail("fn_tc_gemv: bad handle");
-    return launch_tc_gemv(*w, x, xs, y, ys, nt, (cudaStream_t)stream);
+    return launch_tc_gemv(*w, x, xs, y, ys, nt, (cudaStream_t)stream, (flags & 1) != 0);
 }
 
 // The same on host buffers (synchronous), the tensor-core counterpart of fn_test_gemv: W GGUF rows, x [nt][cols],

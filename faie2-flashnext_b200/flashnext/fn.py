@@ -32,6 +32,8 @@ EXPORTS = [
     "fn_group_free", "fn_w_gemv_argmax_group", "fn_moe_ep_create", "fn_moe_ep_run", "fn_w_step_host",
     "fn_embed", "fn_rmsnorm", "fn_attn_decode", "fn_step_advance", "fn_gdn_reset",
     "fn_tc_create", "fn_tc_free", "fn_tc_gemv", "fn_test_tc_gemv", "fn_bench_tc_gemv",
+    "fn_embed_batch", "fn_rmsnorm_rows", "fn_attn_decode_batch", "fn_step_advance_batch", "fn_gdn_create_batch",
+    "fn_gdn_run_batch",
 ]
 
 
@@ -96,7 +98,13 @@ class FN:
         d.fn_gdn_reset.argtypes = [C.c_int, vp]
         d.fn_tc_create.argtypes = [C.c_uint32, U8, C.c_int, C.c_int]
         d.fn_tc_free.argtypes = [C.c_int]
-        d.fn_tc_gemv.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, vp]
+        d.fn_tc_gemv.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp]
+        d.fn_embed_batch.argtypes = [C.c_uint32, vp, C.c_int, vp, C.c_int, vp, vp, C.c_int, vp]
+        d.fn_rmsnorm_rows.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_float, vp]
+        d.fn_attn_decode_batch.argtypes = [vp, vp, vp, C.c_int] + [vp] * 8 + [C.c_int] * 4 + [C.c_float, vp]
+        d.fn_step_advance_batch.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, vp]
+        d.fn_gdn_create_batch.argtypes = [C.c_int, C.c_int, C.c_int, F32, F32, F32, F32, C.c_int]
+        d.fn_gdn_run_batch.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, vp]
         d.fn_test_tc_gemv.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, F32]
         d.fn_bench_tc_gemv.argtypes = [C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float)]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
@@ -276,9 +284,43 @@ class FN:
     def tc_free(self, h):
         self.check(self.d.fn_tc_free(h))
 
-    def tc_gemv(self, h, x_ptr, xs, y_ptr, ys, nt, stream=0):
+    def tc_gemv(self, h, x_ptr, xs, y_ptr, ys, nt, flags=0, stream=0):
+        """flags: 1 = add into y."""
         vp = C.c_void_p
-        self.check(self.d.fn_tc_gemv(h, vp(x_ptr), xs, vp(y_ptr), ys, nt, vp(stream)))
+        self.check(self.d.fn_tc_gemv(h, vp(x_ptr), xs, vp(y_ptr), ys, nt, flags, vp(stream)))
+
+    # ---- batched decode: independent sequences at one position ----
+    def embed_batch(self, qtype, E_ptr, D, tokens_ptr, tstride, pos_ptr, h_ptr, batch, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_embed_batch(int(qtype), vp(E_ptr), D, vp(tokens_ptr), tstride, vp(pos_ptr), vp(h_ptr),
+                                         batch, vp(stream)))
+
+    def rmsnorm_rows(self, x_ptr, w_ptr, out_ptr, D, rows, eps=1e-6, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_rmsnorm_rows(vp(x_ptr), vp(w_ptr), vp(out_ptr), D, rows, eps, vp(stream)))
+
+    def attn_decode_batch(self, qg, k, v, ss, wq, wk, inv_freq, Q, Kc, Vc, out, pos, nh, nkv, max_ctx, batch,
+                          eps=1e-6, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_attn_decode_batch(vp(qg), vp(k), vp(v), ss, vp(wq), vp(wk), vp(inv_freq), vp(Q), vp(Kc),
+                                               vp(Vc), vp(out), vp(pos), nh, nkv, max_ctx, batch, eps, vp(stream)))
+
+    def step_advance_batch(self, pos, tokens, nxt, prompt_len_ptr, max_ctx, batch, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_step_advance_batch(vp(pos), vp(tokens), vp(nxt), vp(prompt_len_ptr), max_ctx, batch,
+                                                vp(stream)))
+
+    def gdn_create_batch(self, nkh, nvh, conv_w, dt_bias, ssm_a, norm_w, batch, ds=128) -> int:
+        f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+        h = self.d.fn_gdn_create_batch(nkh, nvh, ds, f(conv_w), f(dt_bias), f(ssm_a), f(norm_w), batch)
+        if h < 0:
+            raise RuntimeError(self.d.fn_error().decode())
+        return h
+
+    def gdn_run_batch(self, h, qkv_ptr, qs, z_ptr, zs, ab_ptr, abs_, out_ptr, os_, prefetch_state=0, stream=0):
+        vp = C.c_void_p
+        self.check(self.d.fn_gdn_run_batch(h, vp(qkv_ptr), qs, vp(z_ptr), zs, vp(ab_ptr), abs_, vp(out_ptr), os_,
+                                           prefetch_state, vp(stream)))
 
     def test_tc_gemv(self, qtype, raw, rows, cols, x):
         x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)

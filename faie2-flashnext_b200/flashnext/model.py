@@ -212,3 +212,158 @@ class DecodeModel:
         for g in self.gdns:
             self.fn.gdn_free(g)
         self.handles, self.moes, self.gdns = [], [], []
+
+
+class BatchDecodeModel:
+    """Batched decode of the same model: `batch` (1..32) independent sequences step together at one position, every
+    projection, router and lm_head on the tensor cores (fn_tc_gemv: each weight tile dequantised once for all the
+    batch's tokens), the MoE layer in groups of up to 8 tokens, one DeltaNet state and one attention cache per
+    sequence. The argmax of each sequence's logits feeds its next input, so a generation is again one CUDA graph
+    replayed per position. Results are those of DecodeModel within the tensor-core GEMV's tolerance (1e-4 of max |y|
+    per projection)."""
+
+    def __init__(self, fn, cfg: dict, W: dict, batch: int, max_ctx: int = 512):
+        import torch
+        if not 1 <= batch <= 32:
+            raise ValueError("batch out of range (1..32)")
+        self.fn, self.cfg, self.B, self.max_ctx = fn, cfg, batch, max_ctx
+        dev = torch.device("cuda", torch.cuda.current_device())
+        f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)  # noqa: E731
+        d, nkh, nvh, nh, nkv = cfg["D"], cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
+        ne, ffe, P = cfg["ne"], cfg["ffe"], cfg["proj"]
+        self.convch = 2 * nkh * DS + nvh * DS
+        self.n_in = self.convch + nvh * DS + 2 * nvh
+        self.n_qkv = nh * 2 * HD + 2 * nkv * HD
+        self.tcs, self.moes, self.gdns = [], [], []
+        tc = lambda q, raw, r, c: self._tc(q, raw, r, c)  # noqa: E731
+        self.E = torch.from_numpy(np.ascontiguousarray(W["embed"]).reshape(-1)).to(dev)
+        self.head = tc(cfg["head"], W["head"], cfg["vocab"], d)
+        self.final_norm = f32(W["final_norm"])
+        self.inv_freq = f32(rope_inv_freq(cfg["rope_base"]))
+        self.layers = []
+        B = batch
+        for L in W["layers"]:
+            o = dict(kind=L["kind"], norm1=f32(L["norm1"]), norm2=f32(L["norm2"]),
+                     router=tc(cfg["router"], L["router"], ne + 1, d))
+            if L["kind"] == "G":
+                o["w_in"] = tc(P, np.concatenate([L["w_in"], L["w_ab"]]), self.n_in, d)
+                o["w_out"] = tc(P, L["w_out"], d, nvh * DS)
+                g = fn.gdn_create_batch(nkh, nvh, L["conv_w"], L["dt_bias"], L["ssm_a"], L["gnorm"], B)
+                self.gdns.append(g)
+                o["gdn"] = g
+            else:
+                o.update(w_qkv=tc(P, np.concatenate([L["w_q"], L["w_k"], L["w_v"]]), self.n_qkv, d),
+                         w_o=tc(P, L["w_o"], d, nh * HD), q_norm=f32(L["q_norm"]), k_norm=f32(L["k_norm"]),
+                         Kc=torch.zeros(B, max_ctx, nkv, HD, device=dev), Vc=torch.zeros(B, max_ctx, nkv, HD, device=dev))
+            m = fn.moe_create(cfg["gate_up"], cfg["down"], ne, cfg["k"], ffe, d, *L["moe"])
+            self.moes.append(m)
+            o["moe"] = m
+            self.layers.append(o)
+        z = lambda *n: torch.zeros(*n, device=dev)  # noqa: E731
+        self.h, self.x, self.proj = z(B, d), z(B, d), z(B, max(self.n_in, self.n_qkv))
+        self.core, self.Q, self.att, self.lr = z(B, nvh * DS), z(B, nh * HD), z(B, nh * HD), z(B, ne + 1)
+        self.logits = z(B, cfg["vocab"])
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.next = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros(B, max_ctx, dtype=torch.int32, device=dev)
+        self.plen = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.graph = None
+
+    def _tc(self, qtype, raw, rows, cols):
+        h = self.fn.tc_create(qtype, raw, rows, cols)
+        self.tcs.append(h)
+        return h
+
+    def launches_per_step(self) -> int:
+        """The embedding; per layer two norms, the input GEMV, the DeltaNet core or the two attention kernels, the output
+        GEMV, the router GEMV and three MoE kernels per group of 8 tokens; the final norm, the lm_head, the argmax and
+        the step counter."""
+        moe = 3 * ((self.B + 7) // 8)
+        return 1 + sum(2 + 1 + (1 if L["kind"] == "G" else 2) + 1 + 1 + moe for L in self.layers) + 4
+
+    def launch_step(self, s: int):
+        """One decode step of every sequence on stream s (device pointers only; capturable)."""
+        fn, cfg, B = self.fn, self.cfg, self.B
+        d, nvh, nh, nkv, eps, ne1 = cfg["D"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["eps"], cfg["ne"] + 1
+        p = lambda t: t.data_ptr()  # noqa: E731
+        h, x, pr = p(self.h), p(self.x), p(self.proj)
+        ps = self.proj.shape[1]
+        fn.embed_batch(cfg["embed"], p(self.E), d, p(self.tokens), self.max_ctx, p(self.pos), h, B, s)
+        for L in self.layers:
+            fn.rmsnorm_rows(h, p(L["norm1"]), x, d, B, eps, s)
+            if L["kind"] == "G":
+                fn.tc_gemv(L["w_in"], x, d, pr, ps, B, 0, s)
+                fn.gdn_run_batch(L["gdn"], pr, ps, pr + 4 * self.convch, ps, pr + 4 * (self.convch + nvh * DS), ps,
+                                 p(self.core), nvh * DS, 1, s)
+                fn.tc_gemv(L["w_out"], p(self.core), nvh * DS, h, d, B, 1, s)  # h += W_out core
+            else:
+                fn.tc_gemv(L["w_qkv"], x, d, pr, ps, B, 0, s)
+                fn.attn_decode_batch(pr, pr + 4 * nh * 2 * HD, pr + 4 * (nh * 2 * HD + nkv * HD), ps, p(L["q_norm"]),
+                                     p(L["k_norm"]), p(self.inv_freq), p(self.Q), p(L["Kc"]), p(L["Vc"]), p(self.att),
+                                     p(self.pos), nh, nkv, self.max_ctx, B, eps, s)
+                fn.tc_gemv(L["w_o"], p(self.att), nh * HD, h, d, B, 1, s)  # h += W_o o
+            fn.rmsnorm_rows(h, p(L["norm2"]), x, d, B, eps, s)
+            fn.tc_gemv(L["router"], x, d, p(self.lr), ne1, B, 0, s)
+            for t0 in range(0, B, 8):  # the MoE layer takes up to 8 tokens per call; h += moe(x)
+                fn.moe_run(L["moe"], p(self.lr) + 4 * t0 * ne1, ne1, x + 4 * t0 * d, h + 4 * t0 * d, min(8, B - t0), 1,
+                           s)
+        fn.rmsnorm_rows(h, p(self.final_norm), x, d, B, eps, s)
+        vocab = cfg["vocab"]
+        fn.tc_gemv(self.head, x, d, p(self.logits), vocab, B, 0, s)
+        fn.argmax_dev(p(self.logits), vocab, vocab, B, p(self.next), s)
+        fn.step_advance_batch(p(self.pos), p(self.tokens), p(self.next), p(self.plen), self.max_ctx, B, s)
+
+    def start(self, prompts, stream):
+        """New sequences: prompts [B][P] (one length for all), the position at 0, every DeltaNet state zeroed."""
+        import torch
+        prompts = np.asarray(prompts, np.int32)
+        if prompts.shape[0] != self.B or not 1 <= prompts.shape[1] <= self.max_ctx:
+            raise ValueError("prompts must be [batch][1..max_ctx]")
+        with torch.cuda.stream(stream):
+            self.tokens.zero_()
+            self.tokens[:, :prompts.shape[1]] = torch.from_numpy(prompts).to(self.tokens.device)
+            self.pos.zero_()
+            self.plen.fill_(prompts.shape[1])
+        for g in self.gdns:
+            self.fn.gdn_reset(g, stream.cuda_stream)
+
+    def capture(self, stream):
+        """Capture one step as a CUDA graph (one eager step runs first, to set the kernels' attributes)."""
+        import torch
+        self.start(np.zeros((self.B, 1), np.int32), stream)
+        self.launch_step(stream.cuda_stream)
+        self.fn.sync(stream.cuda_stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+            self.launch_step(torch.cuda.current_stream().cuda_stream)
+        self.graph = g
+
+    def generate(self, prompts, n_new, stream, marks=None):
+        """Greedy decode of every sequence; returns ids [B][P + n_new]. marks: optional CUDA events recorded after the
+        reset, after the last prompt-only step and after the last step."""
+        import torch
+        P = np.asarray(prompts).shape[1]
+        if P + n_new > self.max_ctx:
+            raise ValueError("prompt + new tokens exceed the context")
+        self.start(prompts, stream)
+        with torch.cuda.stream(stream):
+            if marks:
+                marks[0].record(stream)
+            for i in range(P + n_new - 1):
+                if marks and i == P - 1:
+                    marks[1].record(stream)
+                self.graph.replay()
+            if marks:
+                marks[2].record(stream)
+        self.fn.sync(stream.cuda_stream)
+        return self.tokens[:, :P + n_new].cpu().numpy()
+
+    def free(self):
+        self.graph = None
+        for h in self.tcs:
+            self.fn.tc_free(h)
+        for m in self.moes:
+            self.fn.moe_free(m)
+        for g in self.gdns:
+            self.fn.gdn_free(g)
+        self.tcs, self.moes, self.gdns = [], [], []

@@ -228,12 +228,34 @@ int fn_tc_free(int h);
 /* y[t][r] = W[r] . x[t] for t < nt <= 32 on a stream (device pointers; token strides xs, ys in floats; x 16-byte
  * aligned): each weight tile dequantised once to bf16 hi/lo pairs and multiplied by all tokens with tcgen05.mma
  * (hi*hi + hi*lo + lo*hi, fp32 accumulation in tensor memory); within 1e-4 of float64 relative to max |y|,
- * deterministic. One call at a time per handle. */
-int fn_tc_gemv(int h, const float *x, int xs, float *y, int ys, int nt, void *stream);
+ * deterministic; flags bit 0 adds into y. One call at a time per handle. */
+int fn_tc_gemv(int h, const float *x, int xs, float *y, int ys, int nt, int flags, void *stream);
 /* The same on host buffers (synchronous), as fn_test_gemv: x [nt][cols] -> y [nt][rows]. */
 int fn_test_tc_gemv(uint32_t type, const uint8_t *Wh, int rows, int cols, const float *x, int nt, float *y);
 /* Device ms per call of the tensor-core GEMV on random weights streamed from HBM (as fn_bench_gemv), nt tokens. */
 int fn_bench_tc_gemv(uint32_t type, int rows, int cols, int nt, int iters, float *ms);
+
+/* ---- batched decode: a batch of independent sequences at one position ---------------------------------------- */
+/* h[b] = dequant(E row tokens[b * tstride + *pos]) for b < batch (k_embed per sequence). */
+int fn_embed_batch(uint32_t type, const uint8_t *E, int D, const int *tokens, int tstride, const int *pos, float *h,
+                   int batch, void *stream);
+/* fn_rmsnorm of `rows` rows of D values (row b at b * D). */
+int fn_rmsnorm_rows(const float *x, const float *w, float *out, int D, int rows, float eps, void *stream);
+/* fn_attn_decode for `batch` sequences: sequence b's qg, k, v rows at b * ss floats after qg, k, v; its Q and out rows
+ * at b * nh * 256; its caches at b * max_ctx * nkv * 256 floats into Kc, Vc. */
+int fn_attn_decode_batch(const float *qg, const float *k, const float *v, int ss, const float *wq, const float *wk,
+                         const float *inv_freq, float *Q, float *Kc, float *Vc, float *out, const int *pos, int nh,
+                         int nkv, int max_ctx, int batch, float eps, void *stream);
+/* fn_step_advance for `batch` sequences (token ids of sequence b at tokens + b * max_ctx, its argmax at next[b]). */
+int fn_step_advance_batch(int *pos, int *tokens, const int *next, const int *prompt_len, int max_ctx, int batch,
+                          void *stream);
+/* A gated-DeltaNet layer for `batch` independent sequences (zero states); fn_gdn_run_batch runs one token of each
+ * (token row b of qkv / z / ab / out is sequence b's). fn_gdn_reset zeroes every sequence. Batched form of k_gdn
+ * (engine/faie2fn.cu:1349-1431). */
+int fn_gdn_create_batch(int nkh, int nvh, int ds, const float *conv_w, const float *dt_bias, const float *ssm_a,
+                        const float *norm_w, int batch);
+int fn_gdn_run_batch(int h, const float *qkv, int qs, const float *z, int zs, const float *ab, int abs_, float *out,
+                     int os, int prefetch_state, void *stream);
 
 #ifdef __cplusplus
 }
