@@ -699,6 +699,12 @@ def main():
     if world == 1 and args.workload == "sweep" and not args.no_decode:
         line["decode"] = run_decode(f, args, rank, with_cpu=not args.no_cpu_baseline)
         line["gpu_launches"] += line["decode"]["gpu_launches_per_step"] * (64 + 256 - 1) * line["decode"]["generations"]
+        # batched decode on the tensor-core path (BASELINE config 5's batch 8 and 32)
+        line["decode"]["batched"] = []
+        for b in (8, 32):
+            db = run_decode_batch(f, args, b)
+            line["decode"]["batched"].append(db)
+            line["gpu_launches"] += db["gpu_launches_per_step"] * (64 + 16 - 1 + 64 + 256 - 1)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:
