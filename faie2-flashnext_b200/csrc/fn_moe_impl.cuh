@@ -172,8 +172,9 @@ struct MoeGuArgs {
 // block barrier after the staging). A lane takes groups lane, lane + 32, .. of both rows of a unit (gate and up) in
 // one loop with a single decode body (the kernel runs once per layer: short code keeps instruction fetch off the
 // critical path); the two rows meet in one transposed butterfly, lane 0 writes act = silu(g) * u.
-// XG > 0: one token whose row of G = 32 XG groups each warp holds in registers (read from global memory by each warp,
-// no staging barrier); XG == 0: x staged in shared memory for any token count and row length.
+// XG > 0: rows of G = 32 XG groups; each warp holds one token's x in registers (read from global memory by the warp,
+// no staging barrier), reloading it when its units move to the next token; XG == 0: x staged in shared memory for
+// any row length.
 template <uint32_t TY, bool SOA, int XG>
 __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -255,6 +256,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     };
     if (lane == 0)  // the weight copies fly while x is staged
         while (n_issued < min(nst, a.slots)) issue();
+    int x_tok = 0;  // XG > 0: the token whose x the warp holds in registers (token 0 first)
     if constexpr (XG > 0) {
         if (!a.x_early) xr.load_global(x, lane, ScaleX<TY, SOA>::v);
         __syncwarp();
@@ -278,6 +280,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
         const float *xt = xsm + (size_t)t * G * XPAD;
         double accg = 0.0, accu = 0.0;  // group sums of the gate and the up row, in group order
         if constexpr (XG > 0) {
+            // several tokens: a warp's units run in (token, slot, row) order, so it reloads x at most once per token
+            if (t != x_tok) {
+                xr.load_global(x + (size_t)t * a.d, lane, ScaleX<TY, SOA>::v);
+                x_tok = t;
+            }
 #pragma unroll
             for (int i = 0; i < XG; ++i) {
                 const int g = lane + 32 * i;
@@ -456,8 +463,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_down(const MoeDownArgs a
 template <uint32_t TY>
 cudaError_t moe_gu_launch_t(const MoeGuArgs &a, bool planes, int nt, int G, int ctas, size_t smem, cudaStream_t s) {
     void (*k)(const MoeGuArgs) = nullptr;
-    if (nt == 1 && G == 64) k = planes ? k_moe_gu<TY, true, 2> : k_moe_gu<TY, false, 2>;
-    else if (nt == 1 && G == 32) k = planes ? k_moe_gu<TY, true, 1> : k_moe_gu<TY, false, 1>;
+    (void)nt;  // any token count: the warps hold one token's x in registers at a time
+    if (G == 64) k = planes ? k_moe_gu<TY, true, 2> : k_moe_gu<TY, false, 2>;
+    else if (G == 32) k = planes ? k_moe_gu<TY, true, 1> : k_moe_gu<TY, false, 1>;
     else k = planes ? k_moe_gu<TY, true, 0> : k_moe_gu<TY, false, 0>;
     const cudaError_t e = allow_max_dynamic_smem(k);
     if (e != cudaSuccess) return e;
