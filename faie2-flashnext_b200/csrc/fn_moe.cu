@@ -231,16 +231,19 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         // (programmatic launch), and a gate/up CTA does not fit next to it
         const int ctas = (int)std::min<long long>(std::max(1, sm_count() - 1), (U + 7) / 8);
         const long long per_warp0 = (U + (long long)ctas * NW - 1) / ((long long)ctas * NW);
-        const size_t xb = (size_t)nt * (p.d / 32) * XPAD * 4, misc = 8 * 16 * 4, gw = (size_t)grid_words(p.gu_type) * 4;
+        // rows of 32 or 64 groups: the warps read x into registers themselves, nothing is staged in shared memory
+        const bool xreg = p.d == 1024 || p.d == 2048;
+        const size_t xb = xreg ? 0 : (size_t)nt * (p.d / 32) * XPAD * 4, misc = 8 * 16 * 4,
+                     gw = (size_t)grid_words(p.gu_type) * 4;
         const size_t fixed = 1024 + gw + 128 + misc + 128 + xb + 128;
-        // a warp's few units in one stage (one more stage where its run crosses an expert boundary); else one unit
-        // per stage; shorter runs where rows are wide
-        a.run = per_warp0 <= 4 ? (int)per_warp0 : 1;
+        // a warp's few units in one stage (one more stage where its run crosses an expert boundary); else two units
+        // per stage (several tokens: many units per warp); shorter runs where rows are wide
+        a.run = per_warp0 <= 4 ? (int)per_warp0 : 2;
         while (a.run > 1 && fixed + (size_t)NW * al((size_t)2 * a.run * p.ldw_gu, 128) > kMoeDynSmem / 2) --a.run;
         a.stage_bytes = (uint32_t)al((size_t)2 * a.run * p.ldw_gu, 128);
         if (fixed + (size_t)NW * a.stage_bytes > kMoeDynSmem) return fail("moe: gate/up rows too wide for shared memory");
         const long long per_warp = (per_warp0 + a.run - 1) / a.run + 1;  // stages per warp at most
-        const long long fit = (long long)(std::min<size_t>(128 * 1024, kMoeDynSmem - fixed) / ((size_t)NW * a.stage_bytes));
+        const long long fit = (long long)(std::min<size_t>(192 * 1024, kMoeDynSmem - fixed) / ((size_t)NW * a.stage_bytes));
         a.slots = (int)std::max<long long>(1, std::min<long long>(std::min<long long>(8, per_warp), fit));
         a.slots = std::min(a.slots, 1024 / (8 * NW));  // barriers: 1 KiB
         a.ring_off = 1024;
@@ -288,9 +291,11 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         const int max_rows = (int)((kMoeDynSmem - fixed) / ((size_t)ks * (p.ldw_down + 4)));
         int chunks = std::max(1, std::min((p.d + 7) / 8, sm_count() / nt));
         int rows = (p.d + chunks - 1) / chunks;
-        if (rows > max_rows) {
+        if (rows > max_rows) {  // more CTAs than SMs: as many chunks as fill whole waves of one CTA per SM
             rows = max_rows;
             chunks = (p.d + rows - 1) / rows;
+            const int waves = (chunks * nt + sm_count() - 1) / sm_count();
+            chunks = std::min(p.d, std::max(chunks, waves * sm_count() / nt));
         }
         rows = (p.d + chunks - 1) / chunks;  // the largest chunk of the even split
         a.rows = rows;
