@@ -125,6 +125,54 @@ __device__ __forceinline__ void split4(float a, float b, float c, float d, uint2
     lo = make_uint2(*(const uint32_t *)&l01, *(const uint32_t *)&l23);
 }
 
+// One 32-value group of a staged raw row, as Dec<TY>::group (the same values, bit for bit): for the formats whose
+// blocks sit 16-byte aligned in a row (Q4_K's 144 bytes, BF16) the block's header and quants are read with a few
+// 16-byte shared-memory loads and unpacked in registers; the other formats use Dec<TY> directly.
+template <uint32_t TY, class F>
+__device__ __forceinline__ void tc_group(const uint8_t *row, int g, const uint32_t *grid, F &&f) {
+    if constexpr (TY == T_Q4_K) {
+        const uint8_t *b = row + (g >> 3) * 144;
+        const int ib = g & 7;
+        const uint4 h = *(const uint4 *)b;  // d, dmin | the 12 packed 6-bit scales and mins
+        const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+        auto sb = [&](int i) {  // packed scale byte i (0..11)
+            const uint32_t w = i < 4 ? h.y : i < 8 ? h.z : h.w;
+            return (w >> (8 * (i & 3))) & 255u;
+        };
+        uint32_t sc, m;  // gguf-py Q4_K.get_scale_min, as kscale
+        if (ib < 4) {
+            sc = sb(ib) & 63u;
+            m = sb(ib + 4) & 63u;
+        } else {
+            sc = (sb(ib + 4) & 15u) | ((sb(ib - 4) >> 6) << 4);
+            m = (sb(ib + 4) >> 4) | ((sb(ib) >> 6) << 4);
+        }
+        const float dl = __fmul_rn(d, u2f(sc)), ml = __fmul_rn(dmin, u2f(m));
+        const uint4 q0 = *(const uint4 *)(b + 16 + 32 * (ib >> 1)), q1 = *(const uint4 *)(b + 32 + 32 * (ib >> 1));
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const int sh = 4 * (ib & 1);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const uint32_t w = qw[j >> 2] >> sh;
+            auto v = [&](int k) { return __fsub_rn(__fmul_rn(dl, u2f((w >> (8 * k)) & 15u)), ml); };
+            f(j, v(0), v(1), v(2), v(3));
+        }
+    } else if constexpr (TY == T_BF16) {
+        const uint4 *p = (const uint4 *)(row + g * 64);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 u = p[i];
+            f(8 * i, __uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+              __uint_as_float(u.y & 0xffff0000u));
+            f(8 * i + 4, __uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u), __uint_as_float(u.w << 16),
+              __uint_as_float(u.w & 0xffff0000u));
+        }
+    } else {
+        Dec<TY>::group(row, g, grid, f);
+    }
+}
+
 template <uint32_t TY>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -218,7 +266,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
                 const uint8_t *rp = raw + (size_t)r * a.raw_stride - st;
                 float v[32];  // the group's values, then four 16-byte core-matrix rows each of hi and lo: the 8 lanes of
                               // a store phase write one core matrix's 128 contiguous bytes (no bank conflict)
-                Dec<TY>::group(rp, c * (TC_KC / 32) + gl, grid, [&](int j, float v0, float v1, float v2, float v3) {
+                tc_group<TY>(rp, c * (TC_KC / 32) + gl, grid, [&](int j, float v0, float v1, float v2, float v3) {
                     v[j] = v0;
                     v[j + 1] = v1;
                     v[j + 2] = v2;
