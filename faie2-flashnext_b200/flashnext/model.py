@@ -174,6 +174,8 @@ class DecodeModel:
         and the ids of the n_new generated tokens copied out into out (int32 host tensor, pinned). marks: optional
         CUDA events recorded after the reset, after the last prompt-only step and after the last step."""
         import torch
+        if self.graph is None:
+            raise RuntimeError("capture() the step first")
         n = len(prompt)
         if not 1 <= n or n + n_new > self.max_ctx or n_new < 1:
             raise ValueError("prompt + new tokens exceed the context")
@@ -342,8 +344,10 @@ class BatchDecodeModel:
         """Greedy decode of every sequence; returns ids [B][P + n_new]. marks: optional CUDA events recorded after the
         reset, after the last prompt-only step and after the last step."""
         import torch
+        if self.graph is None:
+            raise RuntimeError("capture() the step first")
         P = np.asarray(prompts).shape[1]
-        if P + n_new > self.max_ctx:
+        if P + n_new > self.max_ctx or n_new < 1:
             raise ValueError("prompt + new tokens exceed the context")
         self.start(prompts, stream)
         with torch.cuda.stream(stream):
