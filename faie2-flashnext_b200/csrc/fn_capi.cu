@@ -394,6 +394,28 @@ FN_API int fn_w_gemv(int h, const float *x, int xs, float *y, int ys, int nt, in
                        (cudaStream_t)stream);
 }
 
+// Device address and size of a resident weight (its rows at the handle's 16-byte stride), e.g. for a prefetch hint.
+FN_API int fn_w_weights(int h, const void **ptr, uint64_t *bytes) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_weights: bad handle");
+    *ptr = w->d;
+    *bytes = plan_weight_bytes(w->plan1);
+    return 0;
+}
+
+// L2 prefetch hint: from now on every launch of GEMV handle h also brings [ptr, ptr + bytes) of device memory into L2,
+// spread over its CTAs, before its wait for the previous kernel (read-only data that a later kernel of the chain
+// reads, typically the next weight of a decode step). ptr must be 16-byte aligned; bytes is rounded down to 16;
+// ptr = NULL clears the hint. No counterpart in the reference (its decode reads every weight cold).
+FN_API int fn_w_prefetch_after(int h, const void *ptr, uint64_t bytes) {
+    WeightH *w = wget(h);
+    if (!w) return fail("fn_w_prefetch_after: bad handle");
+    if ((uintptr_t)ptr & 15) return fail("fn_w_prefetch_after: ptr must be 16-byte aligned");
+    w->plan1.pf = w->plan8.pf = (const uint8_t *)ptr;
+    w->plan1.pf_bytes = w->plan8.pf_bytes = ptr ? (bytes & ~15ull) : 0;
+    return 0;
+}
+
 // The lm_head GEMV with the fused argmax (k_argmax, engine/faie2fn.cu:1910-1935, folded into the GEMV's last CTA):
 // y (nullable: logits not written) as fn_w_gemv; index[t] (nullable) = the lowest global row index of the largest
 // value for token t, global index = row0 + local row; keys[t] (nullable, may be a peer GPU's memory) = the 64-bit

@@ -129,6 +129,17 @@ FN_API int fn_moe_free(int h) {
     return 0;
 }
 
+// L2 prefetch hint of a MoE layer: from now on its down kernel (the layer's last) also brings [ptr, ptr + bytes) into
+// L2 before its wait (as fn_w_prefetch_after; typically the next layer's input projection).
+FN_API int fn_moe_prefetch_after(int h, const void *ptr, uint64_t bytes) {
+    MoeH *m = moe_get(h);
+    if (!m) return fail("fn_moe_prefetch_after: bad handle");
+    if ((uintptr_t)ptr & 15) return fail("fn_moe_prefetch_after: ptr must be 16-byte aligned");
+    m->p.pf = (const uint8_t *)ptr;
+    m->p.pf_bytes = ptr ? (bytes & ~15ull) : 0;
+    return 0;
+}
+
 // Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d]. flags: bit 0 adds
 // into y; bit 1 = x early: x was complete before the kernel before this call started (so the layer reads it without
 // waiting for that kernel, as an early GEMV does; engine/faie2fn.cu:2247-2249).

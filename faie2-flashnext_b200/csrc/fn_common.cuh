@@ -89,6 +89,21 @@ __device__ __forceinline__ void dev_fail(uint32_t *errw, uint32_t code) {
     if (errw) atomicCAS(errw, 0u, code);
 }
 
+// L2 prefetch of [p, p + bytes): this CTA's even share of the grid's, by thread 0, in pieces of at most 64 KiB (p and
+// bytes 16-byte multiples). A hint for data a later kernel reads: nothing waits for it.
+__device__ __forceinline__ void l2_prefetch_share(const uint8_t *p, uint64_t bytes) {
+    if (!p || !bytes || threadIdx.x != 0) return;
+    const uint64_t nb = (uint64_t)gridDim.x * gridDim.y * gridDim.z;
+    const uint64_t b = ((uint64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    const uint64_t per = ((bytes + nb - 1) / nb + 15) & ~15ull;
+    uint64_t lo = b * per;
+    const uint64_t hi = lo + per < bytes ? lo + per : bytes;
+    for (; lo < hi; lo += 65536) {
+        const uint32_t n = (uint32_t)(hi - lo < 65536 ? hi - lo : 65536) & ~15u;
+        if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p + lo), "r"(n) : "memory");
+    }
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {

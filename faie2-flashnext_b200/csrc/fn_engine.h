@@ -27,6 +27,8 @@ struct GemvPlan {
     uint32_t stage_bytes = 0;
     uint32_t x_off = 0, ring_off = 0, grid_off = 0;
     size_t smem = 0;
+    const uint8_t *pf = nullptr;  // L2 prefetch hint: every launch also brings [pf, pf + pf_bytes) into L2 (the next
+    uint64_t pf_bytes = 0;        // weights of a decode chain), spread over its CTAs
 };
 
 bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap);

@@ -199,6 +199,8 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.grid_off = p.grid_off;
     a.acc = acc ? 1 : 0;
     a.early = early && settings().early && settings().pdl ? 1 : 0;
+    a.pf = p.pf;
+    a.pf_bytes = p.pf_bytes;
     a.err = dev_error_ptr();
     a.amx = 0;
     a.row0 = 0;

@@ -21,6 +21,8 @@ struct GemvArgs {
     int rps, slots;
     uint32_t stage_bytes, x_off, ring_off, grid_off;
     int acc, early;
+    const uint8_t *pf;  // L2 prefetch hint (GemvPlan::pf), null: none
+    uint64_t pf_bytes;
     uint32_t *err;
     // fused argmax (GemvArgmax); amx == 0: none
     int amx, row0;
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
         for (int st = 0; st < min(nst, a.slots); ++st) issue(st, st);
     }
     __syncwarp();
+    l2_prefetch_share(a.pf, a.pf_bytes);  // the next weights of a chain: read-only, so before any wait
     // The next kernel may launch (its CTAs stage their own weights beside this one where they fit; its
     // griddepcontrol.wait still waits for this whole grid; a dependent grid starts about 2 us after the trigger):
     // an early GEMV triggers at once, as the reference's does (engine/faie2fn.cu:920-922); any other kernel only after

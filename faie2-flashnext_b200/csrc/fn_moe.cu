@@ -283,6 +283,8 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.acc = acc ? 1 : 0;
         a.rsel = rsel;
         a.rw = rw;
+        a.pf = p.pf;
+        a.pf_bytes = p.pf_bytes;
         // CTA (chunk, t): rows [r0, r1) of token t, every computed slot's rows in shared memory at once
         const size_t xb = (size_t)ks * (p.ffe / 32) * XPAD * 4, misc = 0,
                      gw = (size_t)grid_words(p.down_type) * 4;

@@ -11,6 +11,8 @@ struct MoePlan {
     uint64_t rb_gu = 0, rb_down = 0;       // GGUF row bytes
     uint32_t ldw_gu = 0, ldw_down = 0;     // device row strides (16-byte multiples)
     int lpr_down = 32;
+    const uint8_t *pf = nullptr;  // L2 prefetch hint of the down kernel (GemvPlan::pf)
+    uint64_t pf_bytes = 0;
 };
 
 // device weights, rows at the plan's strides: gate/up ne * ffe rows of d columns (expert e at rows e * ffe ..),

@@ -351,6 +351,8 @@ struct MoeDownArgs {
     uint32_t w_off, x_off, grid_off, res_off, misc_off;
     uint32_t *err;
     MoeEp ep;
+    const uint8_t *pf;  // L2 prefetch hint (MoePlan::pf), null: none
+    uint64_t pf_bytes;
 };
 
 // CTA (chunk, t) owns output rows [r0, r1) of token t. Before griddepcontrol.wait it routes token t and issues one
@@ -399,6 +401,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_down(const MoeDownArgs a
             bulk_g2s(wbuf + j * wslot, src, (uint32_t)(n * a.ldw), &bars[j]);
         }
     stage_grid<TY>(grid);
+    l2_prefetch_share(a.pf, a.pf_bytes);  // the next weights of a chain: read-only, so before the wait
     pdl_wait();
     pdl_trigger();
     const float *act = after_wait(a.act);

@@ -33,7 +33,7 @@ EXPORTS = [
     "fn_embed", "fn_rmsnorm", "fn_attn_decode", "fn_step_advance", "fn_gdn_reset",
     "fn_tc_create", "fn_tc_free", "fn_tc_gemv", "fn_test_tc_gemv", "fn_bench_tc_gemv",
     "fn_embed_batch", "fn_rmsnorm_rows", "fn_attn_decode_batch", "fn_step_advance_batch", "fn_gdn_create_batch",
-    "fn_gdn_run_batch",
+    "fn_gdn_run_batch", "fn_w_weights", "fn_w_prefetch_after", "fn_moe_prefetch_after",
 ]
 
 
@@ -96,6 +96,9 @@ class FN:
         d.fn_attn_decode.argtypes = [vp] * 11 + [C.c_int, C.c_int, C.c_int, C.c_float, vp]
         d.fn_step_advance.argtypes = [vp, vp, vp, vp, C.c_int, vp]
         d.fn_gdn_reset.argtypes = [C.c_int, vp]
+        d.fn_w_weights.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]
+        d.fn_w_prefetch_after.argtypes = [C.c_int, vp, C.c_uint64]
+        d.fn_moe_prefetch_after.argtypes = [C.c_int, vp, C.c_uint64]
         d.fn_tc_create.argtypes = [C.c_uint32, U8, C.c_int, C.c_int]
         d.fn_tc_free.argtypes = [C.c_int]
         d.fn_tc_gemv.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp]
@@ -333,6 +336,19 @@ class FN:
         ms = C.c_float()
         self.check(self.d.fn_bench_tc_gemv(int(qtype), rows, cols, nt, iters, C.byref(ms)))
         return ms.value
+
+    # ---- L2 prefetch hints of a decode chain ----
+    def w_weights(self, h):
+        """(device address, bytes) of a resident weight."""
+        p, n = C.c_void_p(), C.c_uint64()
+        self.check(self.d.fn_w_weights(h, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def w_prefetch_after(self, h, ptr, nbytes):
+        self.check(self.d.fn_w_prefetch_after(h, C.c_void_p(ptr or None), nbytes))
+
+    def moe_prefetch_after(self, h, ptr, nbytes):
+        self.check(self.d.fn_moe_prefetch_after(h, C.c_void_p(ptr or None), nbytes))
 
     def gemv_override(self, warps=-1, ring_kb=0, stage_kb=0, ctas_per_sm=0):
         """Plan settings for weights created from now on (engine/faie2fn.cu:2786-2791; warps 0 = by weight size)."""

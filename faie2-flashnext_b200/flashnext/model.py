@@ -21,9 +21,11 @@ DS, HD = 128, 256
 
 class DecodeModel:
     def __init__(self, fn, cfg: dict, W: dict, max_ctx: int = 512, logits: bool = False, warps: int = 16,
-                 stack: bool = True):
+                 stack: bool = True, prefetch: bool = True):
         """warps: GEMV warps per CTA of the model's weights; stack: the projections that read the same input as one
-        GEMV each ([q k v z | alpha beta], [q gate | k | v]) rather than one GEMV per weight."""
+        GEMV each ([q k v z | alpha beta], [q gate | k | v]) rather than one GEMV per weight; prefetch: each
+        projection brings the step's next dense weight into L2 while it runs (input -> output projection -> router,
+        the MoE layer -> the next layer's input projection)."""
         import torch
         self.fn, self.cfg, self.max_ctx = fn, cfg, max_ctx
         self.stack = stack
@@ -41,6 +43,20 @@ class DecodeModel:
             self._build(fn, cfg, W, max_ctx, logits, dev, f32)
         finally:
             fn.gemv_override(warps=0)
+        if prefetch:
+            self._prefetch_hints()
+
+    def _prefetch_hints(self):
+        fn = self.fn
+        first = lambda w: w[0][0] if isinstance(w, list) else w  # noqa: E731
+        last = lambda w: w[-1][0] if isinstance(w, list) else w  # noqa: E731
+        for i, L in enumerate(self.layers):
+            inp, out = (L["w_in"], L["w_out"]) if L["kind"] == "G" else (L["w_qkv"], L["w_o"])
+            fn.w_prefetch_after(last(inp), *fn.w_weights(out))
+            fn.w_prefetch_after(out, *fn.w_weights(L["router"]))
+            if i + 1 < len(self.layers):
+                nxt = self.layers[i + 1]
+                fn.moe_prefetch_after(L["moe"], *fn.w_weights(first(nxt["w_in"] if nxt["kind"] == "G" else nxt["w_qkv"])))
 
     def _build(self, fn, cfg, W, max_ctx, logits, dev, f32):
         import torch

@@ -257,6 +257,16 @@ int fn_gdn_create_batch(int nkh, int nvh, int ds, const float *conv_w, const flo
 int fn_gdn_run_batch(int h, const float *qkv, int qs, const float *z, int zs, const float *ab, int abs_, float *out,
                      int os, int prefetch_state, void *stream);
 
+/* ---- L2 prefetch hints for a decode chain (no counterpart in the reference, whose decode reads every weight cold) -- */
+/* Device address and byte size of a resident weight (rows at the handle's 16-byte stride). */
+int fn_w_weights(int h, const void **ptr, uint64_t *bytes);
+/* From now on every launch of GEMV handle h, or the down kernel of MoE handle h, also prefetches [ptr, ptr + bytes) of
+ * device memory into L2, spread over its CTAs, before its wait for the previous kernel: read-only data that a later
+ * kernel of the chain reads (the next weight of a decode step). ptr 16-byte aligned (NULL clears); bytes rounded
+ * down to 16. */
+int fn_w_prefetch_after(int h, const void *ptr, uint64_t bytes);
+int fn_moe_prefetch_after(int h, const void *ptr, uint64_t bytes);
+
 #ifdef __cplusplus
 }
 #endif
