@@ -54,8 +54,8 @@ static MoeH *moe_build(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
         upload_rows(m->sg, gu_type, Wsg, p.rb_gu, p.ldw_gu, ffe, d, s) ||
         upload_rows(m->su, gu_type, Wsu, p.rb_gu, p.ldw_gu, ffe, d, s) ||
         upload_rows(m->sd, down_type, Wsd, p.rb_down, p.ldw_down, d, ffe, s) ||
-        cudaMalloc(&m->act.p, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess ||
-        cudaMemset(m->act.p, 0, (size_t)8 * (k + 1) * ffe * 4) != cudaSuccess ||
+        cudaMalloc(&m->act.p, (size_t)MOE_MAXT * (k + 1) * ffe * 4) != cudaSuccess ||
+        cudaMemset(m->act.p, 0, (size_t)MOE_MAXT * (k + 1) * ffe * 4) != cudaSuccess ||
         cudaMalloc(&m->route.p, MOE_ROUTE_WORDS * 4) != cudaSuccess) {
         delete m;
         if (err().empty()) fail("moe: device allocation failed");
@@ -76,7 +76,7 @@ using namespace fn;
 FN_API int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, int nt, const uint8_t *Wg,
                        const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
                        const float *logits, const float *x, float *y, int *sel, float *wsel) {
-    if (nt < 1 || nt > 8) return fail("fn_test_moe: nt out of range (1..8)");
+    if (nt < 1 || nt > MOE_MAXT) return fail("fn_test_moe: nt out of range (1..32)");
     FN_CK(cudaSetDevice(hook_device()));
     cudaStream_t s = hook_stream();
     MoeH *m = moe_build(gu_type, down_type, ne, k, ffe, d, Wg, Wu, Wd, Wsg, Wsu, Wsd, s);

@@ -178,10 +178,10 @@ constexpr size_t kMoeDynSmem = 227 * 1024 - 4 * 1024;
 int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act,
                uint32_t *route, float *y, int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s,
                const MoeEp *ep, bool x_early) {
-    if (nt < 1 || nt > 8) return fail("moe: nt out of range (1..8)");
+    if (nt < 1 || nt > (ep ? MOE_EP_MAXT : MOE_MAXT)) return fail("moe: nt out of range (1..32, 1..8 expert parallel)");
     if (!route) return fail("moe: no routing scratch");
     int *rsel = (int *)route;
-    float *rw = (float *)(route + 8 * 16);
+    float *rw = (float *)(route + MOE_MAXT * 16);
     const MoeEp none{};
     const MoeEp &E = ep ? *ep : none;
     if (ep) {
@@ -233,7 +233,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         const long long per_warp0 = (U + (long long)ctas * NW - 1) / ((long long)ctas * NW);
         // rows of 32 or 64 groups: the warps read x into registers themselves, nothing is staged in shared memory
         const bool xreg = p.d == 1024 || p.d == 2048;
-        const size_t xb = xreg ? 0 : (size_t)nt * (p.d / 32) * XPAD * 4, misc = 8 * 16 * 4,
+        const size_t xb = xreg ? 0 : (size_t)nt * (p.d / 32) * XPAD * 4, misc = (size_t)nt * 16 * 4,
                      gw = (size_t)grid_words(p.gu_type) * 4;
         const size_t fixed = 1024 + gw + 128 + misc + 128 + xb + 128;
         // a warp's few units in one stage (one more stage where its run crosses an expert boundary); else two units

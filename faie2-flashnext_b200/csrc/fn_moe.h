@@ -31,7 +31,8 @@ bool plan_moe(MoePlan &p, uint32_t gu_type, uint32_t down_type, int ne, int k, i
 // stores each computed slot's output rows into every rank's slot-output area (peer memory over NVLink) and counts
 // the CTA's arrival at every rank; the combine kernel then adds the k + 1 slot outputs in slot order on every rank,
 // exactly as the one-GPU down kernel does.
-constexpr int MOE_EP_MAXT = 8;
+constexpr int MOE_EP_MAXT = 8;   // tokens per call of an expert-parallel layer
+constexpr int MOE_MAXT = 32;     // tokens per call of a one-GPU layer (batched decode)
 struct MoeEp {
     int n = 0, rank = 0, e0 = 0;
     float *dpart[MAX_RANKS] = {};        // each rank's slot-output area [2][MOE_EP_MAXT][k + 1][d]
@@ -39,13 +40,13 @@ struct MoeEp {
     uint32_t *calls = nullptr;           // this rank's [call count, expected arrivals per source rank, ticket]
 };
 
-// y[t] (+)= sum_{s<k} w[t][s] down_{sel[t][s]} . act[t][s] + sigmoid(logits[t][ne]) shared(x[t]) for t < nt <= 8, with
+// y[t] (+)= sum_{s<k} w[t][s] down_{sel[t][s]} . act[t][s] + sigmoid(logits[t][ne]) shared(x[t]) for t < nt <= 32 (8 expert parallel), with
 // act[t][s] = silu(gate_e . x[t]) * (up_e . x[t]) and (sel, w) the top-k routing of logits[t][0..ne). logits: token
 // stride ls >= ne + 1. act: scratch of nt * (k + 1) * ffe floats; route: scratch of MOE_ROUTE_WORDS 32-bit words.
 // sel_out / w_out (nullable): [nt][k]. planes: the weights are in the engine's plane layout (launch_plane_repack),
 // else GGUF rows at the plan's strides. x_early: x was complete before the kernel before this layer started (the
 // router GEMV's predecessor wrote it), so the gate/up kernel reads it beside the routing kernel.
-constexpr int MOE_ROUTE_WORDS = 2 * 8 * 16;  // sel [8][16] ints, then w [8][16] floats
+constexpr int MOE_ROUTE_WORDS = 2 * MOE_MAXT * 16;  // sel [MOE_MAXT][16] ints, then w [MOE_MAXT][16] floats
 int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act,
                uint32_t *route, float *y, int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s,
                const MoeEp *ep = nullptr, bool x_early = false);

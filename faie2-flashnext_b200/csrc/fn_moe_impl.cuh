@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     float *xsm = (float *)(sm + a.x_off);
     uint32_t *grid = (uint32_t *)(sm + a.grid_off);
     int *sel = (int *)(sm + a.misc_off);  // [nt][16]
-    __shared__ int s_pair[MOE_EP_MAXT * 17];  // the (token, slot) pairs this rank computes, t << 5 | s, in order
+    __shared__ int s_pair[MOE_MAXT * 17];  // the (token, slot) pairs this rank computes, t << 5 | s, in order
     __shared__ int s_np;
     const int G = a.d / 32, ks = a.k + 1;
 

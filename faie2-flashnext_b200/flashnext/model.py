@@ -235,7 +235,7 @@ class DecodeModel:
 class BatchDecodeModel:
     """Batched decode of the same model: `batch` (1..32) independent sequences step together at one position, every
     projection, router and lm_head on the tensor cores (fn_tc_gemv: each weight tile dequantised once for all the
-    batch's tokens), the MoE layer in groups of up to 8 tokens, one DeltaNet state and one attention cache per
+    batch's tokens), the MoE layer for all the batch's tokens in one call, one DeltaNet state and one attention cache per
     sequence. The argmax of each sequence's logits feeds its next input, so a generation is again one CUDA graph
     replayed per position. Results are those of DecodeModel within the tensor-core GEMV's tolerance (1e-4 of max |y|
     per projection)."""
@@ -294,9 +294,9 @@ class BatchDecodeModel:
 
     def launches_per_step(self) -> int:
         """The embedding; per layer two norms, the input GEMV, the DeltaNet core or the two attention kernels, the output
-        GEMV, the router GEMV and three MoE kernels per group of 8 tokens; the final norm, the lm_head, the argmax and
-        the step counter."""
-        moe = 3 * ((self.B + 7) // 8)
+        GEMV, the router GEMV and the MoE layer's three kernels; the final norm, the lm_head, the argmax and the step
+        counter."""
+        moe = 3
         return 1 + sum(2 + 1 + (1 if L["kind"] == "G" else 2) + 1 + 1 + moe for L in self.layers) + 4
 
     def launch_step(self, s: int):
@@ -322,9 +322,7 @@ class BatchDecodeModel:
                 fn.tc_gemv(L["w_o"], p(self.att), nh * HD, h, d, B, 1, s)  # h += W_o o
             fn.rmsnorm_rows(h, p(L["norm2"]), x, d, B, eps, s)
             fn.tc_gemv(L["router"], x, d, p(self.lr), ne1, B, 0, s)
-            for t0 in range(0, B, 8):  # the MoE layer takes up to 8 tokens per call; h += moe(x)
-                fn.moe_run(L["moe"], p(self.lr) + 4 * t0 * ne1, ne1, x + 4 * t0 * d, h + 4 * t0 * d, min(8, B - t0), 1,
-                           s)
+            fn.moe_run(L["moe"], p(self.lr), ne1, x, h, B, 1, s)  # every sequence's token in one call; h += moe(x)
         fn.rmsnorm_rows(h, p(self.final_norm), x, d, B, eps, s)
         vocab = cfg["vocab"]
         fn.tc_gemv(self.head, x, d, p(self.logits), vocab, B, 0, s)

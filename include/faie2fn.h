@@ -161,7 +161,7 @@ int fn_test_gemv_argmax(uint32_t type, const uint8_t *W, int rows, int cols, con
  * (sel, w) the top-k routing of logits[t][0..ne) (probability descending, ties to the lower index, renormalised),
  * plus sigmoid(logits[t][ne]) times the shared expert. Routed weights are expert-stacked GGUF rows (gate/up:
  * ne * ffe rows of d columns; down: ne * d rows of ffe columns); shared: ffe (gate/up) and d (down) rows in the same
- * formats. nt <= 8. sel / wsel ([nt][k] int32 / fp32) may be NULL. New hook with the conventions of fn_test_gemv;
+ * formats. nt <= 32. sel / wsel ([nt][k] int32 / fp32) may be NULL. New hook with the conventions of fn_test_gemv;
  * replaces the per-layer MoE of layer_forward (engine/faie2fn.cu:2406-2420: k_route, moe_gu, moe_down, k_hc_add). */
 int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, int nt, const uint8_t *Wg,
                 const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
@@ -171,7 +171,7 @@ int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, in
 int fn_moe_create(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
                   const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd);
 int fn_moe_free(int h);
-/* Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d] (three kernels:
+/* Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d], nt <= 32 (three kernels:
  * routing, gate/up, down + combine). acc flags: bit 0 adds into y; bit 1 = x early: x was complete before the kernel
  * before this call started (e.g. the router GEMV's predecessor wrote it), so the gate/up kernel reads it beside the
  * routing kernel, as an early GEMV does (engine/faie2fn.cu:2247-2249). */

@@ -1,6 +1,6 @@
 """GPU parity of batched decode on the tensor-core path (flashnext/model.py BatchDecodeModel): independent sequences
 stepping together, every projection / router / lm_head on fn_tc_gemv, per-sequence DeltaNet states and attention
-caches, the MoE in groups of up to 8 tokens.
+caches, the MoE layer for the whole batch in one call.
 
 Stated tolerance of the tensor-core path at model level (BASELINE: "the tensor-core batched path must stay within a
 stated logit tolerance"): every sequence's log-probabilities within 1e-3 of the float64 oracle (oracle/model.py,
@@ -35,7 +35,7 @@ def small_w():
 @pytest.mark.parametrize("B", [4, 11])
 def test_batch_steps_match_oracle(fn, small_w, B):
     """Eager steps: each sequence's logits against its own float64 oracle, fed the same tokens (prompt, then the
-    batched model's greedy continuation). B = 11 runs the MoE in two groups (8 + 3)."""
+    batched model's greedy continuation)."""
     import torch
     from model import BatchDecodeModel
     cfg, W = small_w

@@ -62,6 +62,12 @@ def test_moe_small(fn, gu, dn, nt):
     check(fn, BY_NAME[gu], BY_NAME[dn], 24, 4, 256, 512, nt, seed=nt * 7 + len(gu))
 
 
+@pytest.mark.parametrize("nt", [9, 17, 32])
+def test_moe_batched_tokens(fn, nt):
+    """More than 8 tokens per call (batched decode, up to 32): the gate/up warps move through several tokens' units."""
+    check(fn, BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 64, 10, 512, 2048, nt, seed=nt)
+
+
 @pytest.mark.parametrize("ne,k,nt", [(700, 8, 1), (1024, 16, 2), (513, 10, 1)])
 def test_moe_many_experts(fn, ne, k, nt):
     """More than 512 experts (two logits per routing lane), the largest k, and an expert count that is not a multiple
