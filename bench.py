@@ -508,6 +508,7 @@ def main():
                     help="lm_head: only the dominant kernel (the small case the ncu capture profiles); decode: only "
                          "the config-5 greedy decode (its own line, tok/s)")
     ap.add_argument("--no-decode", action="store_true", help="leave the config-5 decode out of the sweep line")
+    ap.add_argument("--branches", type=int, default=8, help="concurrent graph chains of the sweep's independent GEMVs")
     ap.add_argument("--batch", type=int, default=1,
                     help="with --workload decode: that many sequences at once on the tensor-core path (2..32)")
     ap.add_argument("--profile-steps", type=int, default=0,
@@ -579,7 +580,7 @@ def main():
 
     # the 39 sweep GEMVs are independent (own weights, inputs and outputs): they run as BRANCHES concurrent chains of
     # the graph (a fork and a join on the capture stream), so several are resident on an SM at once
-    BRANCHES = 8
+    BRANCHES = args.branches
     side = [torch.cuda.Stream() for _ in range(BRANCHES)]
     g_small, g_head = (torch.cuda.CUDAGraph() if len(work) > 1 else None), torch.cuda.CUDAGraph()
     if g_small is not None:
