@@ -418,7 +418,7 @@ def run_decode_batch(f, args, batch):
     d = {"batch": batch, "tok_s": round(batch * n_new * 1e3 / gen_ms, 2), "ms_per_step": round(ms_step, 4),
          "tok_s_per_sequence": round(1e3 / ms_step, 2), "gpu_launches_per_step": m.launches_per_step(),
          "distinct_ids": int(len(np.unique(ids[:, n_prompt:]))), "build_s": round(build_s, 1), "clocks": clk,
-         "path": "projections, routers and lm_head on fn_tc_gemv (tcgen05.mma, bf16 hi/lo), MoE in groups of 8 tokens"}
+         "path": "projections, routers and lm_head on fn_tc_gemv (tcgen05.mma, bf16 hi/lo), the MoE layer for the whole batch in one call"}
     m.free()
     return d
 
