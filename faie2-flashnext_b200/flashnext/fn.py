@@ -120,6 +120,59 @@ class FN:
     def set_device(self, dev: int):
         self.check(self.d.fn_set_device(int(dev)))
 
+    # ---- the reference's model API (flashnext/fn.py:40-54; engine/faie2fn.cu fn_load .. fn_debug_layers) ----
+    # A GGUF model (runner.py: the qwen3next tensor names) loaded into the decode runner on the current GPU.
+    def load(self, shard1, shard2=None, max_ctx=32768, split=0):
+        """fn_load: shard2 is an optional second GGUF shard (None: one file); split is accepted for the reference's
+        signature (every layer stays on the current GPU)."""
+        from runner import Engine
+        self.free()
+        self.eng = Engine(self, str(shard1), str(shard2) if shard2 else None, int(max_ctx), int(split))
+
+    def _engine(self):
+        if getattr(self, "eng", None) is None:
+            raise RuntimeError("not loaded")
+        return self.eng
+
+    def reset(self):
+        self._engine().reset()
+
+    def forward(self, tokens, logits=False):
+        """argmax ids int32 [nt] (and logits float32 [nt, vocab] when logits=True), nt = len(tokens) in 1..8."""
+        e = self._engine()
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        am = np.zeros(len(t), np.int32)
+        lg = np.zeros((len(t), e.cfg["vocab"]), np.float32) if logits else None
+        e.forward(t, lg, am)
+        return (am, lg) if logits else am
+
+    def debug_layers(self, buf):
+        self._engine().debug_layers(buf)
+
+    def use_graphs(self, on):
+        self._engine().use_graphs = bool(on)
+
+    def n_past(self) -> int:
+        return self.eng.n_past if getattr(self, "eng", None) else -1
+
+    def last_ms(self) -> float:
+        return self.eng.last_ms if getattr(self, "eng", None) else -1.0
+
+    def split(self) -> int:
+        return self.eng.split if getattr(self, "eng", None) else -1
+
+    def dev_gb(self, dv=0) -> float:
+        """Weight bytes of the loaded model on device dv, in GB (-1 when nothing is loaded)."""
+        if getattr(self, "eng", None) is None:
+            return -1.0
+        return self.eng.bytes / 1e9 if dv == 0 else 0.0
+
+    def free(self):
+        """fn_free: release the loaded model (nothing loaded: no-op)."""
+        e, self.eng = getattr(self, "eng", None), None
+        if e is not None:
+            e.free()
+
     # ---- the reference's unit-test hooks (flashnext/fn.py:56-66) ----
     def dequant(self, qtype, raw, rows, cols):
         out = np.zeros((rows, cols), np.float32)

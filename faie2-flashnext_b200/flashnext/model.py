@@ -68,27 +68,32 @@ class DecodeModel:
         self.inv_freq = f32(rope_inv_freq(cfg["rope_base"]))
         self.layers = []
         for L in W["layers"]:
+            # per-weight formats (a GGUF file's own tensor types, flashnext/runner.py); default: the config's
+            T = L.get("qt", {})
+            ty = lambda n, T=T: T.get(n, P)  # noqa: E731
             o = dict(kind=L["kind"], norm1=f32(L["norm1"]), norm2=f32(L["norm2"]),
-                     router=self._w(cfg["router"], L["router"], ne + 1, d))
-            if L["kind"] == "G":  # [q k v z | alpha beta]: one GEMV over the stacked rows
-                if self.stack:
-                    o["w_in"] = self._w(P, np.concatenate([L["w_in"], L["w_ab"]]), self.n_in, d)
+                     router=self._w(T.get("router", cfg["router"]), L["router"], ne + 1, d))
+            if L["kind"] == "G":  # [q k v z | alpha beta]: one GEMV over the stacked rows (when one format)
+                if self.stack and ty("w_in") == ty("w_ab"):
+                    o["w_in"] = self._w(ty("w_in"), np.concatenate([L["w_in"], L["w_ab"]]), self.n_in, d)
                 else:
-                    o["w_in"] = [(self._w(P, L["w_in"], self.convch + nvh * DS, d), self.convch + nvh * DS),
-                                 (self._w(P, L["w_ab"], 2 * nvh, d), 2 * nvh)]
-                o["w_out"] = self._w(P, L["w_out"], d, nvh * DS)
+                    o["w_in"] = [(self._w(ty("w_in"), L["w_in"], self.convch + nvh * DS, d), self.convch + nvh * DS),
+                                 (self._w(ty("w_ab"), L["w_ab"], 2 * nvh, d), 2 * nvh)]
+                o["w_out"] = self._w(ty("w_out"), L["w_out"], d, nvh * DS)
                 g = fn.gdn_create(nkh, nvh, L["conv_w"], L["dt_bias"], L["ssm_a"], L["gnorm"],
                                   np.zeros((nvh, DS, DS), np.float32), np.zeros((3, self.convch), np.float32))
                 self.gdns.append(g)
                 o["gdn"] = g
             else:
-                o.update(w_qkv=self._w(P, np.concatenate([L["w_q"], L["w_k"], L["w_v"]]), self.n_qkv, d) if self.stack
-                         else [(self._w(P, L[n], r, d), r) for n, r in (("w_q", nh * 2 * HD), ("w_k", nkv * HD),
-                                                                           ("w_v", nkv * HD))],
-                         w_o=self._w(P, L["w_o"], d, nh * HD),
+                one = ty("w_q") == ty("w_k") == ty("w_v")
+                o.update(w_qkv=self._w(ty("w_q"), np.concatenate([L["w_q"], L["w_k"], L["w_v"]]), self.n_qkv, d)
+                         if self.stack and one
+                         else [(self._w(ty(n), L[n], r, d), r) for n, r in (("w_q", nh * 2 * HD), ("w_k", nkv * HD),
+                                                                               ("w_v", nkv * HD))],
+                         w_o=self._w(ty("w_o"), L["w_o"], d, nh * HD),
                          q_norm=f32(L["q_norm"]), k_norm=f32(L["k_norm"]),
                          Kc=torch.zeros(max_ctx, nkv, HD, device=dev), Vc=torch.zeros(max_ctx, nkv, HD, device=dev))
-            m = fn.moe_create(cfg["gate_up"], cfg["down"], ne, cfg["k"], ffe, d, *L["moe"])
+            m = fn.moe_create(T.get("gate_up", cfg["gate_up"]), T.get("down", cfg["down"]), ne, cfg["k"], ffe, d, *L["moe"])
             self.moes.append(m)
             o["moe"] = m
             self.layers.append(o)
@@ -108,8 +113,9 @@ class DecodeModel:
         self.handles.append(h)
         return h
 
-    def launch_step(self, s: int):
-        """Launch one decode step on stream s (device pointers only; capturable)."""
+    def launch_step(self, s: int, after_layer=None):
+        """Launch one decode step on stream s (device pointers only; capturable). after_layer(l), eager steps only:
+        called once layer l's launches are enqueued (the residual h then holds that layer's output)."""
         fn, cfg = self.fn, self.cfg
         d, nvh, nh, nkv, eps = cfg["D"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["eps"]
         p = lambda t: t.data_ptr()  # noqa: E731
@@ -123,7 +129,7 @@ class DecodeModel:
                 fn.w_gemv(w_, x, d, y + 4 * off, 0, 1, 0, s)
                 off += rows
 
-        for L in self.layers:
+        for li, L in enumerate(self.layers):
             pr = p(self.proj)
             if L["kind"] == "G":
                 gemv_normed(L["w_in"], L["norm1"], pr)
@@ -140,6 +146,8 @@ class DecodeModel:
             fn.rmsnorm(h, p(L["norm2"]), x, d, eps, s)
             fn.w_gemv(L["router"], x, d, p(self.lr), 0, 1, 0, s)
             fn.moe_run(L["moe"], p(self.lr), cfg["ne"] + 1, x, h, 1, 1, s)  # h += moe(x)
+            if after_layer is not None:
+                after_layer(li)
         fn.rmsnorm(h, p(self.final_norm), x, d, eps, s)
         fn.w_gemv_argmax(self.head, x, d, p(self.logits) if self.logits is not None else 0, 0, 1, 0, 0,
                          p(self.next), 0, s)

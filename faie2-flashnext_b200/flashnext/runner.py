@@ -1,0 +1,317 @@
+"""The model-level API of the reference (fn_load / fn_reset / fn_forward / fn_n_past / fn_last_ms / fn_dev_gb /
+fn_split / fn_use_graphs / fn_debug_layers / fn_free, engine/faie2fn.cu:2466-2492 and :2680-2740, wrapped by
+flashnext/fn.py FN.load / reset / forward): a GGUF model file loaded into the config-5 decode runner (model.py
+DecodeModel) and stepped from host token ids.
+
+Files: GGUF v3 (gguf_file.py) with the qwen3next tensor names the reference's loader reads (engine/faie2fn.cu:2617-2657):
+token_embd / output / output_norm; per layer blk.N.attn_norm and post_attention_norm; the gated DeltaNet's attn_qkv,
+attn_gate, ssm_alpha, ssm_beta, ssm_out, ssm_conv1d, ssm_dt.bias, ssm_a, ssm_norm; the gated attention's attn_q (query
+and gate rows interleaved per head), attn_k, attn_v, attn_output, attn_q_norm, attn_k_norm; the MoE's ffn_gate_inp
+with ffn_gate_inp_shexp (the shared-expert gate row, stacked under the router as the reference's load_qw_cat does,
+:2651), ffn_gate_exps / ffn_up_exps / ffn_down_exps and the shared expert's ffn_gate_shexp / ffn_up_shexp /
+ffn_down_shexp. The layer kind comes from which tensors a layer has; the sizes from the tensor shapes; the routed
+experts per token from the metadata key <arch>.expert_used_count; eps and the RoPE base from
+<arch>.attention.layer_norm_rms_epsilon and <arch>.rope.freq_base. The reference's own model adds tensors this runner
+has no kernels for (hyper-connections, the PLE n-gram table, the attention indexer); such files are refused by name.
+
+forward(tokens) follows the reference's contract (:2466-2490): 1..8 tokens per call (MAXT, :67), appended at n_past
+(an error once n_past + nt would pass max_ctx), each token's greedy next id returned (and its logits when asked), the
+host wall time of the call kept as last_ms. Tokens are stepped one position at a time through the step's CUDA graph.
+"""
+
+from __future__ import annotations
+
+import re
+import time
+
+import numpy as np
+
+import gguf_file as gguf
+from model import DS, HD, DecodeModel
+from synth import TYPES
+
+ARCH = "qwen3next"
+MAXT = 8  # tokens per forward call (engine/faie2fn.cu:67)
+_UNSUPPORTED = ("hc_", "ple_", "indexer.", "per_layer_token_embd", "output_hc_")
+
+
+def save_model(path: str, cfg: dict, W: dict) -> None:
+    """Write a model of the config-5 structure (synth.model_weights layout) as one GGUF v3 file."""
+    D, V = cfg["D"], cfg["vocab"]
+    nkh, nvh, nh, nkv, ne, ffe = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["ne"], cfg["ffe"]
+    convch = 2 * nkh * DS + nvh * DS
+    P, F = cfg["proj"], gguf.GGML_F32
+    layers = list(W["layers"])
+    meta = {"general.architecture": ARCH, "general.alignment": gguf.ALIGN, f"{ARCH}.block_count": len(layers),
+            f"{ARCH}.embedding_length": D, f"{ARCH}.attention.head_count": nh, f"{ARCH}.attention.head_count_kv": nkv,
+            f"{ARCH}.attention.key_length": HD, f"{ARCH}.attention.value_length": HD,
+            f"{ARCH}.attention.layer_norm_rms_epsilon": float(cfg["eps"]), f"{ARCH}.rope.freq_base": float(cfg["rope_base"]),
+            f"{ARCH}.rope.dimension_count": 64, f"{ARCH}.expert_count": ne, f"{ARCH}.expert_used_count": cfg["k"],
+            f"{ARCH}.expert_feed_forward_length": ffe, f"{ARCH}.expert_shared_feed_forward_length": ffe,
+            f"{ARCH}.ssm.conv_kernel": 4, f"{ARCH}.ssm.state_size": DS, f"{ARCH}.ssm.group_count": nkh,
+            f"{ARCH}.ssm.time_step_rank": nvh, f"{ARCH}.ssm.inner_size": nvh * DS,
+            f"{ARCH}.full_attention_interval": len(cfg["pattern"])}
+
+    def tensors():
+        yield "token_embd.weight", cfg["embed"], [D, V], W["embed"]
+        yield "output.weight", cfg["head"], [D, V], W["head"]
+        yield "output_norm.weight", F, [D], np.asarray(W["final_norm"], np.float32)
+        for l, L in enumerate(layers):
+            p = f"blk.{l}."
+            T = L.get("qt", {})
+            ty = lambda n, T=T: T.get(n, P)  # noqa: E731
+            yield p + "attn_norm.weight", F, [D], np.asarray(L["norm1"], np.float32)
+            yield p + "post_attention_norm.weight", F, [D], np.asarray(L["norm2"], np.float32)
+            if L["kind"] == "G":
+                yield p + "attn_qkv.weight", ty("w_in"), [D, convch], L["w_in"][:convch]
+                yield p + "attn_gate.weight", ty("w_in"), [D, nvh * DS], L["w_in"][convch:]
+                yield p + "ssm_alpha.weight", ty("w_ab"), [D, nvh], L["w_ab"][:nvh]
+                yield p + "ssm_beta.weight", ty("w_ab"), [D, nvh], L["w_ab"][nvh:]
+                yield p + "ssm_out.weight", ty("w_out"), [nvh * DS, D], L["w_out"]
+                yield p + "ssm_conv1d.weight", F, [4, convch], np.asarray(L["conv_w"], np.float32)
+                yield p + "ssm_dt.bias", F, [nvh], np.asarray(L["dt_bias"], np.float32)
+                yield p + "ssm_a", F, [nvh], np.asarray(L["ssm_a"], np.float32)
+                yield p + "ssm_norm.weight", F, [DS], np.asarray(L["gnorm"], np.float32)
+            else:
+                yield p + "attn_q.weight", ty("w_q"), [D, nh * 2 * HD], L["w_q"]
+                yield p + "attn_k.weight", ty("w_k"), [D, nkv * HD], L["w_k"]
+                yield p + "attn_v.weight", ty("w_v"), [D, nkv * HD], L["w_v"]
+                yield p + "attn_output.weight", ty("w_o"), [nh * HD, D], L["w_o"]
+                yield p + "attn_q_norm.weight", F, [HD], np.asarray(L["q_norm"], np.float32)
+                yield p + "attn_k_norm.weight", F, [HD], np.asarray(L["k_norm"], np.float32)
+            rt, gu, dn = T.get("router", cfg["router"]), T.get("gate_up", cfg["gate_up"]), T.get("down", cfg["down"])
+            yield p + "ffn_gate_inp.weight", rt, [D, ne], L["router"][:ne]
+            yield p + "ffn_gate_inp_shexp.weight", rt, [D], L["router"][ne:]
+            m = L["moe"]
+            yield p + "ffn_gate_exps.weight", gu, [D, ffe, ne], m[0]
+            yield p + "ffn_up_exps.weight", gu, [D, ffe, ne], m[1]
+            yield p + "ffn_down_exps.weight", dn, [ffe, D, ne], m[2]
+            yield p + "ffn_gate_shexp.weight", gu, [D, ffe], m[3]
+            yield p + "ffn_up_shexp.weight", gu, [D, ffe], m[4]
+            yield p + "ffn_down_shexp.weight", dn, [ffe, D], m[5]
+
+    gguf.write(path, meta, tensors())
+
+
+class _Tensors:
+    """The tensors of one or two GGUF shards by name, with shape checks that name the tensor."""
+
+    def __init__(self, paths):
+        self.meta, self.t = {}, {}
+        for path in paths:
+            meta, t = gguf.read(path)
+            for k, v in meta.items():
+                self.meta.setdefault(k, v)
+            for k, v in t.items():
+                if k in self.t:
+                    raise gguf.GGUFError(f"tensor {k} in more than one shard")
+                self.t[k] = v
+        self.used = set()
+
+    def has(self, name):
+        return name in self.t
+
+    def get(self, name, cols=None, rows=None, quant=True):
+        if name not in self.t:
+            raise gguf.GGUFError(f"missing tensor {name}")
+        t = self.t[name]
+        self.used.add(name)
+        if cols is not None and t.cols != cols or rows is not None and t.rows != rows:
+            raise gguf.GGUFError(f"{name}: shape {list(t.dims)}, expected {cols} columns x {rows} rows")
+        if quant and t.qtype not in TYPES:
+            raise gguf.GGUFError(f"{name}: ggml type {t.qtype} has no GEMV kernel")
+        return t
+
+    def vec(self, name, n, rows=None):
+        t = self.get(name, cols=n, rows=rows, quant=False)
+        return np.array(t.f32(), np.float32)  # a writable copy (device tensors are made from it)
+
+
+def load_model(shard1: str, shard2: str | None = None):
+    """-> (cfg, W, weight bytes): a GGUF model (one file, or two shards) in the layout model.DecodeModel builds from
+    (synth.model_weights' dictionary, plus per-weight formats in W["layers"][l]["qt"])."""
+    T = _Tensors([shard1] + ([shard2] if shard2 else []))
+    bad = sorted(n for n in T.t if any(n.startswith(u) or ("." + u) in n for u in _UNSUPPORTED))
+    if bad:
+        raise gguf.GGUFError(f"tensors this runner has no kernels for: {', '.join(bad[:4])}{' ...' if len(bad) > 4 else ''}")
+    arch = T.meta.get("general.architecture", ARCH)
+    emb = T.get("token_embd.weight")
+    D, V = emb.cols, emb.rows
+    head = T.get("output.weight", cols=D, rows=V)
+    idx = sorted({int(m.group(1)) for n in T.t for m in [re.match(r"blk\.(\d+)\.", n)] if m})
+    if not idx or idx != list(range(len(idx))):
+        raise gguf.GGUFError("layers blk.0 .. blk.N-1 expected")
+    if f"{arch}.expert_used_count" not in T.meta:
+        raise gguf.GGUFError(f"missing metadata {arch}.expert_used_count")
+    k = int(T.meta[f"{arch}.expert_used_count"])
+    W = dict(embed=np.array(emb.rows_u8()), head=head.rows_u8(), final_norm=T.vec("output_norm.weight", D))
+    kinds, cfg_t = [], {}
+    nkh = nvh = nh = nkv = None
+    layers = []
+    for l in idx:
+        p = f"blk.{l}."
+        L = dict(norm1=T.vec(p + "attn_norm.weight", D), norm2=T.vec(p + "post_attention_norm.weight", D), qt={})
+        if T.has(p + "attn_q.weight"):
+            L["kind"] = "A"
+            q = T.get(p + "attn_q.weight", cols=D)
+            kv = T.get(p + "attn_k.weight", cols=D)
+            if q.rows % (2 * HD) or kv.rows % HD:
+                raise gguf.GGUFError(f"{p}attn_q / attn_k: head size {HD} expected")
+            nh, nkv = q.rows // (2 * HD), kv.rows // HD
+            v = T.get(p + "attn_v.weight", cols=D, rows=nkv * HD)
+            o = T.get(p + "attn_output.weight", cols=nh * HD, rows=D)
+            L.update(w_q=q.rows_u8(), w_k=kv.rows_u8(), w_v=v.rows_u8(), w_o=o.rows_u8(),
+                     q_norm=T.vec(p + "attn_q_norm.weight", HD), k_norm=T.vec(p + "attn_k_norm.weight", HD))
+            L["qt"].update(w_q=q.qtype, w_k=kv.qtype, w_v=v.qtype, w_o=o.qtype)
+        else:
+            L["kind"] = "G"
+            a = T.get(p + "ssm_a", quant=False)
+            nvh = a.cols
+            qkv = T.get(p + "attn_qkv.weight", cols=D)
+            if (qkv.rows - nvh * DS) % (2 * DS) or qkv.rows <= nvh * DS:
+                raise gguf.GGUFError(f"{p}attn_qkv: {qkv.rows} rows do not fit {nvh} value heads of {DS}")
+            nkh = (qkv.rows - nvh * DS) // (2 * DS)
+            convch = qkv.rows
+            z = T.get(p + "attn_gate.weight", cols=D, rows=nvh * DS)
+            al = T.get(p + "ssm_alpha.weight", cols=D, rows=nvh)
+            be = T.get(p + "ssm_beta.weight", cols=D, rows=nvh)
+            out = T.get(p + "ssm_out.weight", cols=nvh * DS, rows=D)
+            if qkv.qtype != z.qtype or al.qtype != be.qtype:
+                raise gguf.GGUFError(f"{p}attn_qkv / attn_gate (or ssm_alpha / ssm_beta) in different formats")
+            L.update(w_in=np.concatenate([qkv.rows_u8(), z.rows_u8()]), w_ab=np.concatenate([al.rows_u8(), be.rows_u8()]),
+                     w_out=out.rows_u8(), conv_w=T.vec(p + "ssm_conv1d.weight", 4, rows=convch),
+                     dt_bias=T.vec(p + "ssm_dt.bias", nvh), ssm_a=np.array(a.f32(), np.float32).reshape(nvh),
+                     gnorm=T.vec(p + "ssm_norm.weight", DS))
+            L["qt"].update(w_in=qkv.qtype, w_ab=al.qtype, w_out=out.qtype)
+        r = T.get(p + "ffn_gate_inp.weight", cols=D)
+        ne = r.rows
+        rs = T.get(p + "ffn_gate_inp_shexp.weight", cols=D, rows=1)
+        ge = T.get(p + "ffn_gate_exps.weight", cols=D)
+        if ge.rows % ne:
+            raise gguf.GGUFError(f"{p}ffn_gate_exps: {ge.rows} rows for {ne} experts")
+        ffe = ge.rows // ne
+        ue = T.get(p + "ffn_up_exps.weight", cols=D, rows=ne * ffe)
+        de = T.get(p + "ffn_down_exps.weight", cols=ffe, rows=ne * D)
+        gs = T.get(p + "ffn_gate_shexp.weight", cols=D, rows=ffe)
+        us = T.get(p + "ffn_up_shexp.weight", cols=D, rows=ffe)
+        ds = T.get(p + "ffn_down_shexp.weight", cols=ffe, rows=D)
+        if r.qtype != rs.qtype:
+            raise gguf.GGUFError(f"{p}ffn_gate_inp / ffn_gate_inp_shexp in different formats")
+        if len({ge.qtype, ue.qtype, gs.qtype, us.qtype}) > 1 or de.qtype != ds.qtype:
+            raise gguf.GGUFError(f"{p}expert gate / up (or down) tensors in different formats")
+        L["router"] = np.concatenate([r.rows_u8(), rs.rows_u8()])
+        L["moe"] = [ge.rows_u8(), ue.rows_u8(), de.rows_u8(), gs.rows_u8(), us.rows_u8(), ds.rows_u8()]
+        L["qt"].update(router=r.qtype, gate_up=ge.qtype, down=de.qtype)
+        if cfg_t.setdefault("moe", (ne, ffe)) != (ne, ffe):
+            raise gguf.GGUFError(f"{p}: expert count or size differs between layers")
+        kinds.append(L["kind"])
+        layers.append(L)
+    if nkh is None or nh is None:
+        raise gguf.GGUFError("a model with both gated-DeltaNet and attention layers expected")
+    unused = sorted(set(T.t) - T.used)
+    if unused:
+        raise gguf.GGUFError(f"tensors this runner does not use: {', '.join(unused[:4])}")
+    ne, ffe = cfg_t["moe"]
+    if not 1 <= k <= min(ne, 16):
+        raise gguf.GGUFError(f"{arch}.expert_used_count {k} out of range")
+    first = layers[0]["qt"]
+    cfg = dict(D=D, layers=len(layers), pattern="".join(kinds), vocab=V,
+               eps=float(T.meta.get(f"{arch}.attention.layer_norm_rms_epsilon", 1e-6)), nkh=nkh, nvh=nvh, nh=nh,
+               nkv=nkv, rope_base=float(T.meta.get(f"{arch}.rope.freq_base", 1e7)), ne=ne, k=k, ffe=ffe,
+               proj=first.get("w_in", first.get("w_q")), gate_up=first["gate_up"], down=first["down"],
+               embed=emb.qtype, head=head.qtype, router=first["router"])
+    W["layers"] = layers
+    nbytes = sum(t.data.nbytes for t in T.t.values())
+    return cfg, W, nbytes
+
+
+class Engine:
+    """A loaded model: fn_load's engine (engine/faie2fn.cu:2524-2680) on one GPU. Every call raises RuntimeError with
+    the reference's message on a misuse (nt out of range, context full)."""
+
+    def __init__(self, fn, shard1: str, shard2: str | None = None, max_ctx: int = 32768, split: int = 0):
+        import torch
+        if max_ctx < 1:
+            raise RuntimeError("max_ctx out of range")
+        try:
+            cfg, W, self.bytes = load_model(shard1, shard2)
+        except (OSError, gguf.GGUFError) as e:
+            raise RuntimeError(str(e)) from e
+        self.cfg, self.fn = cfg, fn
+        # the reference splits the layers over two GPUs at `split` (<= 0: by free memory); this runner keeps every
+        # layer on the current GPU, so split reads back as the layer count
+        self.split = cfg["layers"]
+        self.model = DecodeModel(fn, cfg, W, max_ctx=max_ctx, logits=True)
+        self.max_ctx, self.n_past, self.last_ms = max_ctx, 0, -1.0
+        self.use_graphs, self.dbg = True, None
+        self.stream = torch.cuda.Stream()
+        self.model.capture(self.stream)
+        self.am = torch.zeros(MAXT, dtype=torch.int32).pin_memory()
+        self.lg = torch.zeros(MAXT, cfg["vocab"], dtype=torch.float32).pin_memory()
+        self.reset()
+
+    def reset(self):
+        """fn_reset (:2703-2716): DeltaNet states and conv histories zeroed, position 0, n_past 0."""
+        import torch
+        m = self.model
+        with torch.cuda.stream(self.stream):
+            m.tokens.zero_()
+            m.pos.zero_()
+            m.plen.zero_()
+        for g in m.gdns:
+            self.fn.gdn_reset(g, self.stream.cuda_stream)
+        self.fn.sync(self.stream.cuda_stream)
+        self.n_past = 0
+
+    def forward(self, tokens, logits=None, argmax=None):
+        """fn_forward (:2466-2490): tokens (1..8 int32 ids) at positions n_past.. ; argmax[i] = the greedy next id
+        after token i; logits[i] = its logits (float32 [nt, vocab], when given)."""
+        import torch
+        t = np.ascontiguousarray(tokens, np.int32).reshape(-1)
+        nt = len(t)
+        if nt < 1 or nt > MAXT:
+            raise RuntimeError("nt out of range")
+        if self.n_past + nt > self.max_ctx:
+            raise RuntimeError("context full")
+        if t.min() < 0 or t.max() >= self.cfg["vocab"]:
+            raise RuntimeError("token id out of range")
+        t0 = time.perf_counter()
+        m, s = self.model, self.stream
+        graphs = self.use_graphs and self.dbg is None
+        with torch.cuda.stream(s):
+            m.tokens[self.n_past:self.n_past + nt].copy_(torch.from_numpy(t), non_blocking=False)
+            m.plen.fill_(self.n_past + nt)  # the step keeps these ids: it writes its argmax only past the prompt
+            for i in range(nt):
+                if graphs:
+                    m.graph.replay()
+                else:
+                    hook = None
+                    if self.dbg is not None:
+                        hook = lambda l, i=i: self.dbg[l, i].copy_(m.h.cpu())  # noqa: E731
+                    m.launch_step(s.cuda_stream, after_layer=hook)
+                self.am[i].copy_(m.next[0], non_blocking=True)
+                if logits is not None:
+                    self.lg[i].copy_(m.logits, non_blocking=True)
+        self.fn.sync(s.cuda_stream)
+        if argmax is not None:
+            argmax[:nt] = self.am[:nt].numpy()
+        if logits is not None:
+            logits[:nt] = self.lg[:nt].numpy()
+        self.n_past += nt
+        self.last_ms = (time.perf_counter() - t0) * 1e3
+        return 0
+
+    def debug_layers(self, buf):
+        """fn_debug_layers (:2737-2742): buf float32 [layers][nt][D] (host) receives h after every layer of the next
+        forwards (their steps then run eagerly); None turns it off."""
+        import torch
+        if buf is None:
+            self.dbg = None
+            return
+        a = np.asarray(buf)
+        if a.dtype != np.float32 or a.ndim != 3 or a.shape[0] != self.cfg["layers"] or a.shape[2] != self.cfg["D"]:
+            raise RuntimeError("debug buffer: float32 [layers][nt][D] expected")
+        self.dbg = torch.from_numpy(a)
+
+    def free(self):
+        self.model.free()

@@ -89,17 +89,19 @@ class OracleModel:
         self.L = []
         for L in W["layers"]:
             o = dict(kind=L["kind"], norm1=L["norm1"], norm2=L["norm2"])
+            T = L.get("qt", {})  # per-weight formats (a GGUF file's tensor types); default: the config's
+            ty = lambda n, T=T: T.get(n, P)  # noqa: E731
             if L["kind"] == "G":
-                o.update(w_in=deq(L["w_in"], P, convch + nvh * DS, d), w_ab=deq(L["w_ab"], P, 2 * nvh, d),
-                         w_out=deq(L["w_out"], P, d, nvh * DS), conv_w=L["conv_w"], dt_bias=L["dt_bias"],
+                o.update(w_in=deq(L["w_in"], ty("w_in"), convch + nvh * DS, d), w_ab=deq(L["w_ab"], ty("w_ab"), 2 * nvh, d),
+                         w_out=deq(L["w_out"], ty("w_out"), d, nvh * DS), conv_w=L["conv_w"], dt_bias=L["dt_bias"],
                          ssm_a=L["ssm_a"], gnorm=L["gnorm"])
             else:
-                o.update(w_q=deq(L["w_q"], P, nh * 2 * HD, d), w_k=deq(L["w_k"], P, nkv * HD, d),
-                         w_v=deq(L["w_v"], P, nkv * HD, d), w_o=deq(L["w_o"], P, d, nh * HD),
+                o.update(w_q=deq(L["w_q"], ty("w_q"), nh * 2 * HD, d), w_k=deq(L["w_k"], ty("w_k"), nkv * HD, d),
+                         w_v=deq(L["w_v"], ty("w_v"), nkv * HD, d), w_o=deq(L["w_o"], ty("w_o"), d, nh * HD),
                          q_norm=L["q_norm"], k_norm=L["k_norm"])
-            gu, dn = cfg["gate_up"], cfg["down"]
+            gu, dn = T.get("gate_up", cfg["gate_up"]), T.get("down", cfg["down"])
             Wg, Wu, Wd, Wsg, Wsu, Wsd = L["moe"]
-            o.update(router=deq(L["router"], cfg["router"], ne + 1, d),
+            o.update(router=deq(L["router"], T.get("router", cfg["router"]), ne + 1, d),
                      experts=(M.GGUFExperts(Wg, gu, ffe, d), M.GGUFExperts(Wu, gu, ffe, d), M.GGUFExperts(Wd, dn, d, ffe),
                               deq(Wsg, gu, ffe, d), deq(Wsu, gu, ffe, d), deq(Wsd, dn, d, ffe)))
             self.L.append(o)

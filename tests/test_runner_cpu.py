@@ -1,0 +1,163 @@
+"""Host side of the model API (flashnext/gguf_file.py, flashnext/runner.py): GGUF v3 files written and read back byte for
+byte, a synthetic config-5-structure model saved under the qwen3next tensor names the reference's loader reads
+(engine/faie2fn.cu:2617-2657) and loaded back into the runner's layout, one file or two shards, and the loader's
+refusals (not GGUF, truncated, a missing or unexpected tensor, tensors the runner has no kernels for, mixed formats
+inside a stacked weight). No GPU."""
+
+import os
+
+import numpy as np
+import pytest
+
+import gguf_file as gguf
+from runner import load_model, save_model
+from synth import BY_NAME, model_blocks, model_config, model_weights
+
+
+def test_gguf_round_trip(tmp_path):
+    rng = np.random.default_rng(0)
+    q4 = model_blocks(BY_NAME["Q4_K"], 6, 512, rng)
+    ex = model_blocks(BY_NAME["IQ3_XXS"], 3 * 4, 256, rng)
+    v = rng.standard_normal(96).astype(np.float32)
+    h = rng.standard_normal((3, 64)).astype(np.float16)
+    meta = {"general.architecture": "test", "a.u32": 7, "a.neg": -5, "a.big": 2**40, "a.f": 0.5, "a.b": True,
+            "a.s": "hello", "a.ints": [1, 2, 3], "a.strs": ["x", "yz"], "a.empty": []}
+    p = str(tmp_path / "t.gguf")
+    gguf.write(p, meta, [("v", gguf.GGML_F32, [96], v), ("w", BY_NAME["Q4_K"], [512, 6], q4),
+                         ("e", BY_NAME["IQ3_XXS"], [256, 4, 3], ex), ("h", gguf.GGML_F16, [64, 3], h)])
+    m, t = gguf.read(p)
+    assert m == meta
+    assert np.array_equal(t["v"].f32(), v)
+    assert np.array_equal(t["w"].rows_u8(), q4) and t["w"].dims == (512, 6) and t["w"].rows == 6
+    assert np.array_equal(t["e"].rows_u8(), ex) and t["e"].rows == 12 and t["e"].cols == 256
+    assert np.array_equal(t["h"].f32(), h.astype(np.float32))
+    for x in t.values():  # every tensor starts on the alignment
+        assert (x.data.ctypes.data - t["v"].data.ctypes.data) % gguf.ALIGN == 0
+
+
+def test_gguf_refusals(tmp_path):
+    p = tmp_path / "bad.gguf"
+    p.write_bytes(b"GGUX" + b"\0" * 64)
+    with pytest.raises(gguf.GGUFError, match="not a GGUF"):
+        gguf.read(str(p))
+    good = str(tmp_path / "g.gguf")
+    gguf.write(good, {"k": 1}, [("v", gguf.GGML_F32, [32], np.zeros(32, np.float32))])
+    raw = open(good, "rb").read()
+    (tmp_path / "cut.gguf").write_bytes(raw[:-8])
+    with pytest.raises(gguf.GGUFError, match="out of range"):
+        gguf.read(str(tmp_path / "cut.gguf"))
+    (tmp_path / "cut2.gguf").write_bytes(raw[:30])
+    with pytest.raises(gguf.GGUFError, match="truncated"):
+        gguf.read(str(tmp_path / "cut2.gguf"))
+    with pytest.raises(gguf.GGUFError):  # bytes that do not match the dims
+        gguf.write(str(tmp_path / "x.gguf"), {}, [("v", gguf.GGML_F32, [32], np.zeros(31, np.float32))])
+
+
+@pytest.fixture(scope="module")
+def small():
+    cfg = model_config(small=True)
+    return cfg, model_weights(cfg, 3)
+
+
+def _same_model(cfg, W, cfg2, W2):
+    for k in ("D", "layers", "vocab", "nkh", "nvh", "nh", "nkv", "ne", "k", "ffe", "proj", "gate_up", "down", "embed",
+              "head", "router"):
+        assert cfg2[k] == cfg[k], k
+    assert cfg2["pattern"] == cfg["pattern"] * (cfg["layers"] // len(cfg["pattern"]))
+    assert np.float32(cfg2["eps"]) == np.float32(cfg["eps"]) and cfg2["rope_base"] == cfg["rope_base"]
+    for k in ("embed", "head", "final_norm"):
+        assert np.array_equal(W2[k], W[k]), k
+    for L, L2 in zip(W["layers"], W2["layers"]):
+        assert L2["kind"] == L["kind"]
+        for k, v in L.items():
+            if k == "moe":
+                assert all(np.array_equal(a, b) for a, b in zip(v, L2["moe"]))
+            elif k not in ("kind", "qt"):
+                assert np.array_equal(np.asarray(L2[k]).reshape(np.shape(v)), v), k
+
+
+def test_save_load_model(small, tmp_path):
+    cfg, W = small
+    p = str(tmp_path / "m.gguf")
+    save_model(p, cfg, W)
+    cfg2, W2, nbytes = load_model(p)
+    _same_model(cfg, W, cfg2, W2)
+    assert nbytes > W["embed"].nbytes + W["head"].nbytes
+    assert all(L["qt"]["w_in" if L["kind"] == "G" else "w_q"] == cfg["proj"] for L in W2["layers"])
+
+
+def test_two_shards(small, tmp_path):
+    """The tensors split over two files (the reference's shard1 / shard2) load as one model."""
+    cfg, W = small
+    one = str(tmp_path / "m.gguf")
+    save_model(one, cfg, W)
+    meta, t = gguf.read(one)
+    names = list(t)
+    half = len(names) // 2
+    rows = lambda n: (n, t[n].qtype, list(t[n].dims), t[n].data)  # noqa: E731
+    gguf.write(str(tmp_path / "s1.gguf"), meta, [rows(n) for n in names[:half]])
+    gguf.write(str(tmp_path / "s2.gguf"), {}, [rows(n) for n in names[half:]])
+    cfg2, W2, _ = load_model(str(tmp_path / "s1.gguf"), str(tmp_path / "s2.gguf"))
+    _same_model(cfg, W, cfg2, W2)
+    with pytest.raises(gguf.GGUFError, match="more than one shard"):
+        load_model(one, str(tmp_path / "s2.gguf"))
+    with pytest.raises(gguf.GGUFError, match="missing tensor"):
+        load_model(str(tmp_path / "s1.gguf"))
+
+
+def test_mixed_formats_per_weight(small, tmp_path):
+    """Per-weight formats survive the file: a Q6_K output projection and Q8_0 attention values in one layer each."""
+    cfg, W = small
+    rng = np.random.default_rng(1)
+    layers = [dict(L) for L in W["layers"]]
+    g = next(i for i, L in enumerate(layers) if L["kind"] == "G")
+    a = next(i for i, L in enumerate(layers) if L["kind"] == "A")
+    layers[g]["w_out"] = model_blocks(BY_NAME["Q6_K"], cfg["D"], cfg["nvh"] * 128, rng)
+    layers[g]["qt"] = {"w_out": BY_NAME["Q6_K"]}
+    layers[a]["w_v"] = model_blocks(BY_NAME["Q8_0"], cfg["nkv"] * 256, cfg["D"], rng)
+    layers[a]["qt"] = {"w_v": BY_NAME["Q8_0"]}
+    W2 = dict(W, layers=layers)
+    p = str(tmp_path / "m.gguf")
+    save_model(p, cfg, W2)
+    _, W3, _ = load_model(p)
+    assert W3["layers"][g]["qt"]["w_out"] == BY_NAME["Q6_K"]
+    assert W3["layers"][a]["qt"]["w_v"] == BY_NAME["Q8_0"] and W3["layers"][a]["qt"]["w_q"] == cfg["proj"]
+    assert np.array_equal(W3["layers"][g]["w_out"], layers[g]["w_out"])
+
+
+def test_loader_refusals(small, tmp_path):
+    cfg, W = small
+    p = str(tmp_path / "m.gguf")
+    save_model(p, cfg, W)
+    meta, t = gguf.read(p)
+    rows = lambda n: (n, t[n].qtype, list(t[n].dims), t[n].data)  # noqa: E731
+
+    def variant(name, tensors, meta_=meta):
+        q = str(tmp_path / name)
+        gguf.write(q, meta_, tensors)
+        return q
+
+    with pytest.raises(gguf.GGUFError, match="missing tensor blk.1.ssm_a"):
+        load_model(variant("a.gguf", [rows(n) for n in t if n != "blk.1.ssm_a"]))
+    extra = [rows(n) for n in t] + [("blk.0.hc_attn_norm.weight", gguf.GGML_F32, [32], np.zeros(32, np.float32))]
+    with pytest.raises(gguf.GGUFError, match="no kernels for"):
+        load_model(variant("b.gguf", extra))
+    extra = [rows(n) for n in t] + [("blk.0.something.weight", gguf.GGML_F32, [32], np.zeros(32, np.float32))]
+    with pytest.raises(gguf.GGUFError, match="does not use"):
+        load_model(variant("c.gguf", extra))
+    with pytest.raises(gguf.GGUFError, match="expert_used_count"):
+        load_model(variant("d.gguf", [rows(n) for n in t], {k: v for k, v in meta.items() if "expert_used" not in k}))
+    rng = np.random.default_rng(2)
+    mixed = [rows(n) for n in t if n != "blk.0.attn_gate.weight"]
+    mixed.append(("blk.0.attn_gate.weight", BY_NAME["Q8_0"], [cfg["D"], cfg["nvh"] * 128],
+                  model_blocks(BY_NAME["Q8_0"], cfg["nvh"] * 128, cfg["D"], rng)))
+    with pytest.raises(gguf.GGUFError, match="different formats"):
+        load_model(variant("e.gguf", mixed))
+    short = [rows(n) for n in t if n != "blk.3.attn_v.weight"]
+    short.append(("blk.3.attn_v.weight", t["blk.3.attn_v.weight"].qtype, [cfg["D"], 128],
+                  t["blk.3.attn_v.weight"].data[:t["blk.3.attn_v.weight"].data.nbytes // 2]))
+    with pytest.raises(gguf.GGUFError, match="blk.3.attn_v.weight: shape"):
+        load_model(variant("f.gguf", short))
+    assert not os.path.exists(str(tmp_path / "never.gguf"))
+    with pytest.raises(OSError):
+        load_model(str(tmp_path / "never.gguf"))
