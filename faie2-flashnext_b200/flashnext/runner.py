@@ -302,7 +302,7 @@ class Engine:
         return 0
 
     def debug_layers(self, buf):
-        """fn_debug_layers (:2737-2742): buf float32 [layers][nt][D] (host) receives h after every layer of the next
+        """fn_debug_layers (:2739-2743): buf float32 [layers][nt][D] (host) receives h after every layer of the next
         forwards (their steps then run eagerly); None turns it off."""
         import torch
         if buf is None:

@@ -1,5 +1,5 @@
 """GPU parity of the model API (FN.load / reset / forward / debug_layers; the reference's fn_load / fn_forward,
-engine/faie2fn.cu:2466-2490, 2524, 2703-2742): a small model of the config-5 structure saved as a GGUF file, loaded
+engine/faie2fn.cu:2466-2490, 2524, 2703-2743): a small model of the config-5 structure saved as a GGUF file, loaded
 and stepped from host token ids.
 
 Bars: the log-probabilities of every forwarded token within 1e-4 of the float64 oracle (oracle/model.py) fed the same
