@@ -122,12 +122,13 @@ class FN:
 
     # ---- the reference's model API (flashnext/fn.py:40-54; engine/faie2fn.cu fn_load .. fn_debug_layers) ----
     # A GGUF model (runner.py: the qwen3next tensor names) loaded into the decode runner on the current GPU.
-    def load(self, shard1, shard2=None, max_ctx=32768, split=0):
+    def load(self, shard1, shard2=None, max_ctx=32768, split=0, batch=0):
         """fn_load: shard2 is an optional second GGUF shard (None: one file); split is accepted for the reference's
-        signature (every layer stays on the current GPU)."""
+        signature (every layer stays on the current GPU); batch > 0 (<= 32) also prepares forward_batch for that many
+        independent sequences."""
         from runner import Engine
         self.free()
-        self.eng = Engine(self, str(shard1), str(shard2) if shard2 else None, int(max_ctx), int(split))
+        self.eng = Engine(self, str(shard1), str(shard2) if shard2 else None, int(max_ctx), int(split), int(batch))
 
     def _engine(self):
         if getattr(self, "eng", None) is None:
@@ -145,6 +146,19 @@ class FN:
         lg = np.zeros((len(t), e.cfg["vocab"]), np.float32) if logits else None
         e.forward(t, lg, am)
         return (am, lg) if logits else am
+
+    def forward_batch(self, tokens, logits=False):
+        """The batched entry for independent sequences: tokens [batch][nt] (nt 1..8) -> argmax ids int32 [batch][nt]
+        (and logits float32 [batch][nt][vocab]); the sequences advance together from n_past_batch()."""
+        e = self._engine()
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        am = np.zeros(t.shape, np.int32) if t.ndim == 2 else None
+        lg = np.zeros(t.shape + (e.cfg["vocab"],), np.float32) if logits and t.ndim == 2 else None
+        e.forward_batch(t, lg if logits else None, am)
+        return (am, lg) if logits else am
+
+    def n_past_batch(self) -> int:
+        return self.eng.n_past_batch if getattr(self, "eng", None) else -1
 
     def debug_layers(self, buf):
         self._engine().debug_layers(buf)

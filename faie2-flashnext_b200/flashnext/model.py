@@ -261,6 +261,11 @@ class BatchDecodeModel:
         self.n_in = self.convch + nvh * DS + 2 * nvh
         self.n_qkv = nh * 2 * HD + 2 * nkv * HD
         self.tcs, self.moes, self.gdns = [], [], []
+        for L in W["layers"]:  # before any allocation: a weight stacked into one projection needs one format
+            T = L.get("qt", {})
+            f = [T.get(n, P) for n in (("w_in", "w_ab") if L["kind"] == "G" else ("w_q", "w_k", "w_v"))]
+            if len(set(f)) > 1:
+                raise ValueError("batched decode: the weights stacked into one projection need one format")
         tc = lambda q, raw, r, c: self._tc(q, raw, r, c)  # noqa: E731
         self.E = torch.from_numpy(np.ascontiguousarray(W["embed"]).reshape(-1)).to(dev)
         self.head = tc(cfg["head"], W["head"], cfg["vocab"], d)
@@ -269,19 +274,21 @@ class BatchDecodeModel:
         self.layers = []
         B = batch
         for L in W["layers"]:
+            T = L.get("qt", {})  # per-weight formats, as DecodeModel (checked above: one per stacked weight)
+            ty = lambda n, T=T: T.get(n, P)  # noqa: E731
             o = dict(kind=L["kind"], norm1=f32(L["norm1"]), norm2=f32(L["norm2"]),
-                     router=tc(cfg["router"], L["router"], ne + 1, d))
+                     router=tc(T.get("router", cfg["router"]), L["router"], ne + 1, d))
             if L["kind"] == "G":
-                o["w_in"] = tc(P, np.concatenate([L["w_in"], L["w_ab"]]), self.n_in, d)
-                o["w_out"] = tc(P, L["w_out"], d, nvh * DS)
+                o["w_in"] = tc(ty("w_in"), np.concatenate([L["w_in"], L["w_ab"]]), self.n_in, d)
+                o["w_out"] = tc(ty("w_out"), L["w_out"], d, nvh * DS)
                 g = fn.gdn_create_batch(nkh, nvh, L["conv_w"], L["dt_bias"], L["ssm_a"], L["gnorm"], B)
                 self.gdns.append(g)
                 o["gdn"] = g
             else:
-                o.update(w_qkv=tc(P, np.concatenate([L["w_q"], L["w_k"], L["w_v"]]), self.n_qkv, d),
-                         w_o=tc(P, L["w_o"], d, nh * HD), q_norm=f32(L["q_norm"]), k_norm=f32(L["k_norm"]),
+                o.update(w_qkv=tc(ty("w_q"), np.concatenate([L["w_q"], L["w_k"], L["w_v"]]), self.n_qkv, d),
+                         w_o=tc(ty("w_o"), L["w_o"], d, nh * HD), q_norm=f32(L["q_norm"]), k_norm=f32(L["k_norm"]),
                          Kc=torch.zeros(B, max_ctx, nkv, HD, device=dev), Vc=torch.zeros(B, max_ctx, nkv, HD, device=dev))
-            m = fn.moe_create(cfg["gate_up"], cfg["down"], ne, cfg["k"], ffe, d, *L["moe"])
+            m = fn.moe_create(T.get("gate_up", cfg["gate_up"]), T.get("down", cfg["down"]), ne, cfg["k"], ffe, d, *L["moe"])
             self.moes.append(m)
             o["moe"] = m
             self.layers.append(o)

@@ -27,7 +27,7 @@ import time
 import numpy as np
 
 import gguf_file as gguf
-from model import DS, HD, DecodeModel
+from model import DS, HD, BatchDecodeModel, DecodeModel
 from synth import TYPES
 
 ARCH = "qwen3next"
@@ -229,10 +229,13 @@ class Engine:
     """A loaded model: fn_load's engine (engine/faie2fn.cu:2524-2680) on one GPU. Every call raises RuntimeError with
     the reference's message on a misuse (nt out of range, context full)."""
 
-    def __init__(self, fn, shard1: str, shard2: str | None = None, max_ctx: int = 32768, split: int = 0):
+    def __init__(self, fn, shard1: str, shard2: str | None = None, max_ctx: int = 32768, split: int = 0,
+                 batch: int = 0):
         import torch
         if max_ctx < 1:
             raise RuntimeError("max_ctx out of range")
+        if not 0 <= batch <= 32:
+            raise RuntimeError("batch out of range (0..32)")
         try:
             cfg, W, self.bytes = load_model(shard1, shard2)
         except (OSError, gguf.GGUFError) as e:
@@ -248,10 +251,21 @@ class Engine:
         self.model.capture(self.stream)
         self.am = torch.zeros(MAXT, dtype=torch.int32).pin_memory()
         self.lg = torch.zeros(MAXT, cfg["vocab"], dtype=torch.float32).pin_memory()
+        # batch > 0: `batch` independent sequences stepping together on the tensor-core path (forward_batch)
+        self.bmodel, self.n_past_batch, self.blg = None, 0, None
+        if batch:
+            try:
+                self.bmodel = BatchDecodeModel(fn, cfg, W, batch, max_ctx=max_ctx)
+            except ValueError as e:
+                self.model.free()
+                raise RuntimeError(str(e)) from e
+            self.bmodel.capture(self.stream)
+            self.bam = torch.zeros(MAXT, batch, dtype=torch.int32).pin_memory()
         self.reset()
 
     def reset(self):
-        """fn_reset (:2703-2716): DeltaNet states and conv histories zeroed, position 0, n_past 0."""
+        """fn_reset (:2703-2716): DeltaNet states and conv histories zeroed, position 0, n_past 0 (the batched
+        sequences too)."""
         import torch
         m = self.model
         with torch.cuda.stream(self.stream):
@@ -260,8 +274,16 @@ class Engine:
             m.plen.zero_()
         for g in m.gdns:
             self.fn.gdn_reset(g, self.stream.cuda_stream)
+        if self.bmodel is not None:
+            b = self.bmodel
+            with torch.cuda.stream(self.stream):
+                b.tokens.zero_()
+                b.pos.zero_()
+                b.plen.zero_()
+            for g in b.gdns:
+                self.fn.gdn_reset(g, self.stream.cuda_stream)
         self.fn.sync(self.stream.cuda_stream)
-        self.n_past = 0
+        self.n_past = self.n_past_batch = 0
 
     def forward(self, tokens, logits=None, argmax=None):
         """fn_forward (:2466-2490): tokens (1..8 int32 ids) at positions n_past.. ; argmax[i] = the greedy next id
@@ -301,6 +323,49 @@ class Engine:
         self.last_ms = (time.perf_counter() - t0) * 1e3
         return 0
 
+    def forward_batch(self, tokens, logits=None, argmax=None):
+        """The batched entry: tokens int32 [batch][nt] (nt 1..8), one row per sequence, all sequences at position
+        n_past_batch (their own states and caches, apart from forward's sequence); argmax[b][i] = sequence b's greedy
+        next id after its token i, logits[b][i] its logits (tensor-core GEMVs: within 1e-4 of max |y| per projection
+        of the CUDA-core path). Same errors as forward, plus "batch not loaded" and a shape check."""
+        import torch
+        b = self.bmodel
+        if b is None:
+            raise RuntimeError("batch not loaded (load with batch > 0)")
+        t = np.ascontiguousarray(tokens, np.int32)
+        if t.ndim != 2 or t.shape[0] != b.B:
+            raise RuntimeError(f"tokens must be [{b.B}][nt]")
+        nt = t.shape[1]
+        if nt < 1 or nt > MAXT:
+            raise RuntimeError("nt out of range")
+        if self.n_past_batch + nt > self.max_ctx:
+            raise RuntimeError("context full")
+        if t.min() < 0 or t.max() >= self.cfg["vocab"]:
+            raise RuntimeError("token id out of range")
+        if logits is not None and self.blg is None:
+            self.blg = torch.zeros(MAXT, b.B, self.cfg["vocab"], dtype=torch.float32).pin_memory()
+        t0 = time.perf_counter()
+        s, n = self.stream, self.n_past_batch
+        with torch.cuda.stream(s):
+            b.tokens[:, n:n + nt].copy_(torch.from_numpy(t))
+            b.plen.fill_(n + nt)
+            for i in range(nt):
+                if self.use_graphs:
+                    b.graph.replay()
+                else:
+                    b.launch_step(s.cuda_stream)
+                self.bam[i].copy_(b.next, non_blocking=True)
+                if logits is not None:
+                    self.blg[i].copy_(b.logits, non_blocking=True)
+        self.fn.sync(s.cuda_stream)
+        if argmax is not None:
+            argmax[:, :nt] = self.bam[:nt].numpy().T
+        if logits is not None:
+            logits[:, :nt] = self.blg[:nt].numpy().transpose(1, 0, 2)
+        self.n_past_batch += nt
+        self.last_ms = (time.perf_counter() - t0) * 1e3
+        return 0
+
     def debug_layers(self, buf):
         """fn_debug_layers (:2739-2743): buf float32 [layers][nt][D] (host) receives h after every layer of the next
         forwards (their steps then run eagerly); None turns it off."""
@@ -315,3 +380,5 @@ class Engine:
 
     def free(self):
         self.model.free()
+        if self.bmodel is not None:
+            self.bmodel.free()

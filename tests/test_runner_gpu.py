@@ -157,6 +157,74 @@ def test_mixed_formats_file(fn, loaded, tmp_path):
         top = np.sort(ref)[::-1]
         if top[0] - top[1] > TIE:
             assert int(am[i]) == int(np.argmax(ref))
+    with pytest.raises(RuntimeError, match="one format"):  # the batched path stacks q / k / v into one weight
+        fn.load(p, max_ctx=16, batch=2)
+
+
+BATCH_LOGPROB_TOL = 1e-3  # the tensor-core path's stated model-level tolerance (tests/test_batch_gpu.py)
+BATCH_TIE = 1e-2
+
+
+def test_forward_batch(fn, loaded, tmp_path):
+    """forward_batch: three sequences against three float64 oracles (tensor-core tolerance); forward's own sequence
+    alongside, untouched by the batch; reset and eager steps replay the batch bit for bit; the batched errors."""
+    from runner import save_model
+    cfg, W = loaded
+    p = str(tmp_path / "small.gguf")
+    save_model(p, cfg, W)
+    fn.load(p, max_ctx=24, batch=3)
+    rng = np.random.default_rng(29)
+    prompts = rng.integers(0, cfg["vocab"], (3, 5))
+    oracles = [OracleModel(cfg, W, rope_inv_freq(cfg["rope_base"])) for _ in range(3)]
+    worst = 0.0
+
+    def check(tokens, am, lg):
+        nonlocal worst
+        for b in range(3):
+            for i, tok in enumerate(tokens[b]):
+                ref = oracles[b].step(int(tok))
+                diff = np.abs(logprobs(lg[b, i]) - logprobs(ref)).max()
+                worst = max(worst, diff)
+                assert diff <= BATCH_LOGPROB_TOL, (b, i, diff)
+                top = np.sort(ref)[::-1]
+                if top[0] - top[1] > BATCH_TIE:
+                    assert int(am[b, i]) == int(np.argmax(ref)), (b, i)
+
+    am0, lg0 = fn.forward_batch(prompts, logits=True)
+    assert am0.shape == (3, 5) and lg0.shape == (3, 5, cfg["vocab"])
+    check(prompts, am0, lg0)
+    toks = am0[:, -1:]
+    for _ in range(4):
+        a, lg = fn.forward_batch(toks, logits=True)
+        check(toks, a, lg)
+        toks = a
+    assert fn.n_past_batch() == 9
+    one = OracleModel(cfg, W, rope_inv_freq(cfg["rope_base"]))  # forward's sequence: its own states
+    a1, l1 = fn.forward(prompts[1], logits=True)
+    for i, tok in enumerate(prompts[1]):
+        assert np.abs(logprobs(l1[i]) - logprobs(one.step(int(tok)))).max() <= LOGPROB_TOL
+    assert fn.n_past() == 5 and fn.n_past_batch() == 9
+    with pytest.raises(RuntimeError, match=r"tokens must be \[3\]\[nt\]"):
+        fn.forward_batch(np.zeros((2, 1), np.int32))
+    with pytest.raises(RuntimeError, match="nt out of range"):
+        fn.forward_batch(np.zeros((3, 9), np.int32))
+    fn.reset()
+    assert fn.n_past_batch() == 0 and fn.n_past() == 0
+    am2, lg2 = fn.forward_batch(prompts, logits=True)
+    fn.reset()
+    fn.use_graphs(0)
+    try:
+        am3, lg3 = fn.forward_batch(prompts, logits=True)
+    finally:
+        fn.use_graphs(1)
+    for a, lg in ((am2, lg2), (am3, lg3)):
+        assert np.array_equal(a, am0) and np.array_equal(lg.view(np.uint32), lg0.view(np.uint32))
+    for _ in range(24 // 8 - 1):
+        fn.forward_batch(np.zeros((3, 8), np.int32))
+    fn.forward_batch(np.zeros((3, 3), np.int32))
+    with pytest.raises(RuntimeError, match="context full"):
+        fn.forward_batch(np.zeros((3, 1), np.int32))
+    print(f"batch max log-prob diff {worst:.3g}")
 
 
 def test_not_loaded(fn, loaded, tmp_path):
@@ -166,6 +234,8 @@ def test_not_loaded(fn, loaded, tmp_path):
         fn.forward([1])
     with pytest.raises(RuntimeError, match="not loaded"):
         fn.reset()
+    with pytest.raises(RuntimeError, match="not loaded"):
+        fn.forward_batch(np.zeros((1, 1), np.int32))
     with pytest.raises(RuntimeError):
         fn.load(str(tmp_path / "missing.gguf"))
     with pytest.raises(RuntimeError, match="not loaded"):
