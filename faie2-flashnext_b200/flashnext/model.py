@@ -261,11 +261,6 @@ class BatchDecodeModel:
         self.n_in = self.convch + nvh * DS + 2 * nvh
         self.n_qkv = nh * 2 * HD + 2 * nkv * HD
         self.tcs, self.moes, self.gdns = [], [], []
-        for L in W["layers"]:  # before any allocation: a weight stacked into one projection needs one format
-            T = L.get("qt", {})
-            f = [T.get(n, P) for n in (("w_in", "w_ab") if L["kind"] == "G" else ("w_q", "w_k", "w_v"))]
-            if len(set(f)) > 1:
-                raise ValueError("batched decode: the weights stacked into one projection need one format")
         tc = lambda q, raw, r, c: self._tc(q, raw, r, c)  # noqa: E731
         self.E = torch.from_numpy(np.ascontiguousarray(W["embed"]).reshape(-1)).to(dev)
         self.head = tc(cfg["head"], W["head"], cfg["vocab"], d)
@@ -274,8 +269,11 @@ class BatchDecodeModel:
         self.layers = []
         B = batch
         for L in W["layers"]:
-            T = L.get("qt", {})  # per-weight formats, as DecodeModel (checked above: one per stacked weight)
+            T = L.get("qt", {})  # per-weight formats, as DecodeModel; a weight stacked into one projection needs one
             ty = lambda n, T=T: T.get(n, P)  # noqa: E731
+            if len({ty(n) for n in (("w_in", "w_ab") if L["kind"] == "G" else ("w_q", "w_k", "w_v"))}) > 1:
+                self.free()  # (W["layers"] may be a generator: checked layer by layer, what was built is released)
+                raise ValueError("batched decode: the weights stacked into one projection need one format")
             o = dict(kind=L["kind"], norm1=f32(L["norm1"]), norm2=f32(L["norm2"]),
                      router=tc(T.get("router", cfg["router"]), L["router"], ne + 1, d))
             if L["kind"] == "G":

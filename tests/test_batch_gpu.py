@@ -184,3 +184,21 @@ def test_batch_building_blocks_bit_identical(fn):
         fn.gdn_free(gb)
         for g in gs:
             fn.gdn_free(g)
+
+
+def test_models_take_layer_generators(fn):
+    """The bench builds the config-5 models from pooled weights whose layers come from a generator (each layer made
+    as it is consumed): both models must build every layer from it."""
+    import torch
+    from model import BatchDecodeModel, DecodeModel
+    cfg = model_config(small=True)
+    s = torch.cuda.Stream()
+    for make in (lambda W: DecodeModel(fn, cfg, W, max_ctx=8), lambda W: BatchDecodeModel(fn, cfg, W, 2, max_ctx=8)):
+        W = model_weights(cfg, 1, pooled=True)
+        assert not isinstance(W["layers"], list)
+        m = make(W)
+        try:
+            assert len(m.layers) == cfg["layers"]
+            m.capture(s)
+        finally:
+            m.free()
