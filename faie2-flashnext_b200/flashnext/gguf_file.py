@@ -11,6 +11,7 @@ general.alignment key at :239, the data start at :254); ggml type ids are the en
 
 from __future__ import annotations
 
+import os
 import struct
 
 import numpy as np
@@ -49,7 +50,10 @@ class _Cursor:
 
     def string(self):
         n = self.scalar(U64)
-        return bytes(self.take(n)).decode("utf-8")
+        try:
+            return bytes(self.take(n)).decode("utf-8")
+        except UnicodeDecodeError as e:
+            raise GGUFError(f"{self.path}: a string that is not UTF-8 at byte {self.o - n}") from e
 
     def value(self, t):
         if t == STR:
@@ -105,6 +109,8 @@ def _nbytes(qtype: int, dims) -> int:
 
 def read(path: str):
     """-> (metadata dict, {name: GGUFTensor}); tensor bytes are views of a read-only memory map of the file."""
+    if os.path.getsize(path) < 24:  # magic, version and the two counts (and numpy maps no empty file)
+        raise GGUFError(f"{path}: truncated at byte 0")
     buf = np.memmap(path, dtype=np.uint8, mode="r")
     c = _Cursor(buf, path)
     if bytes(c.take(4)) != MAGIC:

@@ -41,6 +41,9 @@ class DecodeModel:
         fn.gemv_override(warps=warps)
         try:
             self._build(fn, cfg, W, max_ctx, logits, dev, f32)
+        except BaseException:
+            self.free()  # a weight the engine refused: release what was uploaded before it
+            raise
         finally:
             fn.gemv_override(warps=0)
         if prefetch:

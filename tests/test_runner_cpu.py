@@ -49,6 +49,14 @@ def test_gguf_refusals(tmp_path):
     (tmp_path / "cut2.gguf").write_bytes(raw[:30])
     with pytest.raises(gguf.GGUFError, match="truncated"):
         gguf.read(str(tmp_path / "cut2.gguf"))
+    (tmp_path / "empty.gguf").write_bytes(b"")
+    with pytest.raises(gguf.GGUFError, match="truncated"):
+        gguf.read(str(tmp_path / "empty.gguf"))
+    key = b"\xff\xfe"  # a metadata key that is not UTF-8
+    (tmp_path / "utf.gguf").write_bytes(b"GGUF" + (3).to_bytes(4, "little") + (0).to_bytes(8, "little")
+                                        + (1).to_bytes(8, "little") + (2).to_bytes(8, "little") + key + b"\0" * 16)
+    with pytest.raises(gguf.GGUFError, match="not UTF-8"):
+        gguf.read(str(tmp_path / "utf.gguf"))
     with pytest.raises(gguf.GGUFError):  # bytes that do not match the dims
         gguf.write(str(tmp_path / "x.gguf"), {}, [("v", gguf.GGML_F32, [32], np.zeros(31, np.float32))])
 
