@@ -8,6 +8,11 @@
  *
  * Type ids are ggml's: Q4_0=2 Q4_1=3 Q5_0=6 Q5_1=7 Q8_0=8 Q2_K=10 Q3_K=11 Q4_K=12 Q5_K=13 Q6_K=14 IQ2_XXS=16
  * IQ2_XS=17 IQ3_XXS=18 IQ4_NL=20 IQ3_S=21 IQ2_S=22 IQ4_XS=23 BF16=30 Q2_0=42.
+ *
+ * The reference's model hooks (fn_load, fn_reset, fn_forward, fn_debug_layers, fn_use_graphs, fn_n_past,
+ * fn_last_ms, fn_dev_gb, fn_split, fn_free; engine/faie2fn.cu:2466-2743) are not symbols of this library: the decode
+ * runner they drive is built in the host layer from the entry points below, so they are the methods of the same
+ * names on flashnext/fn.py's FN (flashnext/runner.py: GGUF files, same argument meaning and error messages).
  */
 #ifndef FAIE2FN_H
 #define FAIE2FN_H
