@@ -169,3 +169,26 @@ def test_loader_refusals(small, tmp_path):
     assert not os.path.exists(str(tmp_path / "never.gguf"))
     with pytest.raises(OSError):
         load_model(str(tmp_path / "never.gguf"))
+
+
+def test_fn_model_api_without_a_model(libpath, tmp_path):
+    """FN's model methods before a model is loaded, and loads that fail in the file reader (before any device work):
+    the reference's return values (-1) and RuntimeError messages."""
+    from fn import FN
+    f = FN(libpath)
+    assert f.n_past() == -1 and f.n_past_batch() == -1 and f.last_ms() == -1.0 and f.dev_gb(0) == -1.0
+    assert f.split() == -1
+    for call in (lambda: f.forward([1]), f.reset, lambda: f.forward_batch([[1]]), lambda: f.debug_layers(None),
+                 lambda: f.use_graphs(1)):
+        with pytest.raises(RuntimeError, match="not loaded"):
+            call()
+    f.free()  # nothing loaded: no-op
+    with pytest.raises(RuntimeError):
+        f.load(str(tmp_path / "missing.gguf"))
+    (tmp_path / "bad.gguf").write_bytes(b"GGML" + b"\0" * 60)
+    with pytest.raises(RuntimeError, match="not a GGUF"):
+        f.load(str(tmp_path / "bad.gguf"))
+    with pytest.raises(RuntimeError, match="batch out of range"):
+        f.load(str(tmp_path / "bad.gguf"), batch=33)
+    with pytest.raises(RuntimeError, match="not loaded"):
+        f.forward([1])
