@@ -173,30 +173,40 @@ def _put_value(out, t, v):
         out += struct.pack(_SCALAR[t], v)
 
 
-def write(path: str, meta: dict, tensors) -> None:
-    """Write a GGUF v3 file. tensors: iterable of (name, ggml type, dims innermost first, bytes-like data)."""
+def write(path: str, meta: dict, tensors, data=None) -> None:
+    """Write a GGUF v3 file. tensors: iterable of (name, ggml type, dims innermost first, bytes-like data); or, with
+    `data` given, of (name, ggml type, dims) and `data` an iterable of the tensors' bytes in the same order, consumed
+    once while the file is written (the header needs only the names, types and dims, so a model larger than host
+    memory can be written tensor by tensor)."""
     tensors = list(tensors)
+    if data is None:
+        data = (t[3] for t in tensors)
     head = bytearray(MAGIC + struct.pack("<IQQ", 3, len(tensors), len(meta)))
     for k, v in meta.items():
         t = _meta_type(v)
         _put_value(head, STR, k)
         head += struct.pack("<I", t)
         _put_value(head, t, v)
-    off, datas = 0, []
-    for name, qt, dims, data in tensors:
-        data = memoryview(np.ascontiguousarray(data)).cast("B")
-        if len(data) != _nbytes(qt, dims):
-            raise GGUFError(f"{name}: {len(data)} bytes for dims {dims} of ggml type {qt}")
+    off, offs = 0, []
+    for name, qt, dims, *_ in tensors:
         _put_value(head, STR, name)
         head += struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
         head += struct.pack("<IQ", qt, off)
-        datas.append((off, data))
-        off = (off + len(data) + ALIGN - 1) // ALIGN * ALIGN
+        offs.append(off)
+        off = (off + _nbytes(qt, dims) + ALIGN - 1) // ALIGN * ALIGN
     with open(path, "wb") as f:
         f.write(head)
         f.write(b"\0" * ((-len(head)) % ALIGN))
-        pos = 0
-        for o, data in datas:
+        pos, it = 0, iter(data)
+        for (name, qt, dims, *_), o in zip(tensors, offs):
+            try:
+                d = memoryview(np.ascontiguousarray(next(it))).cast("B")
+            except StopIteration:
+                raise GGUFError(f"{name}: no data") from None
+            if len(d) != _nbytes(qt, dims):
+                raise GGUFError(f"{name}: {len(d)} bytes for dims {dims} of ggml type {qt}")
             f.write(b"\0" * (o - pos))
-            f.write(data)
-            pos = o + len(data)
+            f.write(d)
+            pos = o + len(d)
+        if next(it, None) is not None:
+            raise GGUFError("more data than tensors")

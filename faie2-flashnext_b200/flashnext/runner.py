@@ -28,21 +28,58 @@ import numpy as np
 
 import gguf_file as gguf
 from model import DS, HD, BatchDecodeModel, DecodeModel
-from synth import TYPES
+from synth import TYPES, layer_kind
 
 ARCH = "qwen3next"
 MAXT = 8  # tokens per forward call (engine/faie2fn.cu:67)
 _UNSUPPORTED = ("hc_", "ple_", "indexer.", "per_layer_token_embd", "output_hc_")
 
 
-def save_model(path: str, cfg: dict, W: dict) -> None:
-    """Write a model of the config-5 structure (synth.model_weights layout) as one GGUF v3 file."""
-    D, V = cfg["D"], cfg["vocab"]
-    nkh, nvh, nh, nkv, ne, ffe = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["ne"], cfg["ffe"]
+def _layer_specs(cfg: dict, kind: str, T: dict, p: str):
+    """(name, ggml type, dims, the tensor's data from the layer dict) of one layer, in file order."""
+    D, nkh, nvh, nh, nkv, ne, ffe = cfg["D"], cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["ne"], cfg["ffe"]
     convch = 2 * nkh * DS + nvh * DS
     P, F = cfg["proj"], gguf.GGML_F32
-    layers = list(W["layers"])
-    meta = {"general.architecture": ARCH, "general.alignment": gguf.ALIGN, f"{ARCH}.block_count": len(layers),
+    ty = lambda n: T.get(n, P)  # noqa: E731
+    f32 = lambda k: lambda L: np.asarray(L[k], np.float32)  # noqa: E731
+    sp = [("attn_norm.weight", F, [D], f32("norm1")), ("post_attention_norm.weight", F, [D], f32("norm2"))]
+    if kind == "G":
+        sp += [("attn_qkv.weight", ty("w_in"), [D, convch], lambda L: L["w_in"][:convch]),
+               ("attn_gate.weight", ty("w_in"), [D, nvh * DS], lambda L: L["w_in"][convch:]),
+               ("ssm_alpha.weight", ty("w_ab"), [D, nvh], lambda L: L["w_ab"][:nvh]),
+               ("ssm_beta.weight", ty("w_ab"), [D, nvh], lambda L: L["w_ab"][nvh:]),
+               ("ssm_out.weight", ty("w_out"), [nvh * DS, D], lambda L: L["w_out"]),
+               ("ssm_conv1d.weight", F, [4, convch], f32("conv_w")), ("ssm_dt.bias", F, [nvh], f32("dt_bias")),
+               ("ssm_a", F, [nvh], f32("ssm_a")), ("ssm_norm.weight", F, [DS], f32("gnorm"))]
+    else:
+        sp += [("attn_q.weight", ty("w_q"), [D, nh * 2 * HD], lambda L: L["w_q"]),
+               ("attn_k.weight", ty("w_k"), [D, nkv * HD], lambda L: L["w_k"]),
+               ("attn_v.weight", ty("w_v"), [D, nkv * HD], lambda L: L["w_v"]),
+               ("attn_output.weight", ty("w_o"), [nh * HD, D], lambda L: L["w_o"]),
+               ("attn_q_norm.weight", F, [HD], f32("q_norm")), ("attn_k_norm.weight", F, [HD], f32("k_norm"))]
+    rt, gu, dn = T.get("router", cfg["router"]), T.get("gate_up", cfg["gate_up"]), T.get("down", cfg["down"])
+    sp += [("ffn_gate_inp.weight", rt, [D, ne], lambda L: L["router"][:ne]),
+           ("ffn_gate_inp_shexp.weight", rt, [D], lambda L: L["router"][ne:]),
+           ("ffn_gate_exps.weight", gu, [D, ffe, ne], lambda L: L["moe"][0]),
+           ("ffn_up_exps.weight", gu, [D, ffe, ne], lambda L: L["moe"][1]),
+           ("ffn_down_exps.weight", dn, [ffe, D, ne], lambda L: L["moe"][2]),
+           ("ffn_gate_shexp.weight", gu, [D, ffe], lambda L: L["moe"][3]),
+           ("ffn_up_shexp.weight", gu, [D, ffe], lambda L: L["moe"][4]),
+           ("ffn_down_shexp.weight", dn, [ffe, D], lambda L: L["moe"][5])]
+    return [(p + n, q, d, g) for n, q, d, g in sp]
+
+
+def save_model(path: str, cfg: dict, W: dict) -> None:
+    """Write a model of the config-5 structure (synth.model_weights layout) as one GGUF v3 file. W["layers"] may be a
+    generator (synth.model_weights(pooled=True)): the layers are then written as they are made, in the config's
+    formats, so the whole model never sits in host memory."""
+    D, V, nh, nkv, nkh, nvh = cfg["D"], cfg["vocab"], cfg["nh"], cfg["nkv"], cfg["nkh"], cfg["nvh"]
+    ne, ffe = cfg["ne"], cfg["ffe"]
+    layers = W["layers"]
+    listed = isinstance(layers, list)
+    kinds = [L["kind"] for L in layers] if listed else [layer_kind(cfg, l) for l in range(cfg["layers"])]
+    Ts = [L.get("qt", {}) for L in layers] if listed else [{} for _ in kinds]
+    meta = {"general.architecture": ARCH, "general.alignment": gguf.ALIGN, f"{ARCH}.block_count": len(kinds),
             f"{ARCH}.embedding_length": D, f"{ARCH}.attention.head_count": nh, f"{ARCH}.attention.head_count_kv": nkv,
             f"{ARCH}.attention.key_length": HD, f"{ARCH}.attention.value_length": HD,
             f"{ARCH}.attention.layer_norm_rms_epsilon": float(cfg["eps"]), f"{ARCH}.rope.freq_base": float(cfg["rope_base"]),
@@ -51,46 +88,22 @@ def save_model(path: str, cfg: dict, W: dict) -> None:
             f"{ARCH}.ssm.conv_kernel": 4, f"{ARCH}.ssm.state_size": DS, f"{ARCH}.ssm.group_count": nkh,
             f"{ARCH}.ssm.time_step_rank": nvh, f"{ARCH}.ssm.inner_size": nvh * DS,
             f"{ARCH}.full_attention_interval": len(cfg["pattern"])}
+    top = [("token_embd.weight", cfg["embed"], [D, V], lambda: W["embed"]),
+           ("output.weight", cfg["head"], [D, V], lambda: W["head"]),
+           ("output_norm.weight", gguf.GGML_F32, [D], lambda: np.asarray(W["final_norm"], np.float32))]
+    per = [_layer_specs(cfg, k, T, f"blk.{l}.") for l, (k, T) in enumerate(zip(kinds, Ts))]
 
-    def tensors():
-        yield "token_embd.weight", cfg["embed"], [D, V], W["embed"]
-        yield "output.weight", cfg["head"], [D, V], W["head"]
-        yield "output_norm.weight", F, [D], np.asarray(W["final_norm"], np.float32)
-        for l, L in enumerate(layers):
-            p = f"blk.{l}."
-            T = L.get("qt", {})
-            ty = lambda n, T=T: T.get(n, P)  # noqa: E731
-            yield p + "attn_norm.weight", F, [D], np.asarray(L["norm1"], np.float32)
-            yield p + "post_attention_norm.weight", F, [D], np.asarray(L["norm2"], np.float32)
-            if L["kind"] == "G":
-                yield p + "attn_qkv.weight", ty("w_in"), [D, convch], L["w_in"][:convch]
-                yield p + "attn_gate.weight", ty("w_in"), [D, nvh * DS], L["w_in"][convch:]
-                yield p + "ssm_alpha.weight", ty("w_ab"), [D, nvh], L["w_ab"][:nvh]
-                yield p + "ssm_beta.weight", ty("w_ab"), [D, nvh], L["w_ab"][nvh:]
-                yield p + "ssm_out.weight", ty("w_out"), [nvh * DS, D], L["w_out"]
-                yield p + "ssm_conv1d.weight", F, [4, convch], np.asarray(L["conv_w"], np.float32)
-                yield p + "ssm_dt.bias", F, [nvh], np.asarray(L["dt_bias"], np.float32)
-                yield p + "ssm_a", F, [nvh], np.asarray(L["ssm_a"], np.float32)
-                yield p + "ssm_norm.weight", F, [DS], np.asarray(L["gnorm"], np.float32)
-            else:
-                yield p + "attn_q.weight", ty("w_q"), [D, nh * 2 * HD], L["w_q"]
-                yield p + "attn_k.weight", ty("w_k"), [D, nkv * HD], L["w_k"]
-                yield p + "attn_v.weight", ty("w_v"), [D, nkv * HD], L["w_v"]
-                yield p + "attn_output.weight", ty("w_o"), [nh * HD, D], L["w_o"]
-                yield p + "attn_q_norm.weight", F, [HD], np.asarray(L["q_norm"], np.float32)
-                yield p + "attn_k_norm.weight", F, [HD], np.asarray(L["k_norm"], np.float32)
-            rt, gu, dn = T.get("router", cfg["router"]), T.get("gate_up", cfg["gate_up"]), T.get("down", cfg["down"])
-            yield p + "ffn_gate_inp.weight", rt, [D, ne], L["router"][:ne]
-            yield p + "ffn_gate_inp_shexp.weight", rt, [D], L["router"][ne:]
-            m = L["moe"]
-            yield p + "ffn_gate_exps.weight", gu, [D, ffe, ne], m[0]
-            yield p + "ffn_up_exps.weight", gu, [D, ffe, ne], m[1]
-            yield p + "ffn_down_exps.weight", dn, [ffe, D, ne], m[2]
-            yield p + "ffn_gate_shexp.weight", gu, [D, ffe], m[3]
-            yield p + "ffn_up_shexp.weight", gu, [D, ffe], m[4]
-            yield p + "ffn_down_shexp.weight", dn, [ffe, D], m[5]
+    def data():
+        for *_, get in top:
+            yield get()
+        for l, L in enumerate(layers):  # a generator is consumed here, once
+            if l >= len(per) or L["kind"] != kinds[l] or L.get("qt", {}) != Ts[l]:
+                raise gguf.GGUFError(f"layer {l} does not match the config (kind or formats)")
+            for *_, get in per[l]:
+                yield get(L)
 
-    gguf.write(path, meta, tensors())
+    infos = [(n, q, d) for n, q, d, _ in top] + [(n, q, d) for sp in per for n, q, d, _ in sp]
+    gguf.write(path, meta, infos, data())
 
 
 class _Tensors:

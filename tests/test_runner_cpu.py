@@ -192,3 +192,24 @@ def test_fn_model_api_without_a_model(libpath, tmp_path):
         f.load(str(tmp_path / "bad.gguf"), batch=33)
     with pytest.raises(RuntimeError, match="not loaded"):
         f.forward([1])
+
+
+def test_save_streams_generator_layers(tmp_path):
+    """Pooled weights (layers from a generator, consumed once) write the same file, byte for byte, as the same seed's
+    layers held in a list; the writer refuses data that does not match its tensor list."""
+    cfg = model_config(small=True)
+    a, b = str(tmp_path / "gen.gguf"), str(tmp_path / "list.gguf")
+    Wg = model_weights(cfg, 4, pooled=True)
+    assert not isinstance(Wg["layers"], list)
+    save_model(a, cfg, Wg)
+    Wl = model_weights(cfg, 4, pooled=True)
+    Wl["layers"] = list(Wl["layers"])
+    save_model(b, cfg, Wl)
+    assert open(a, "rb").read() == open(b, "rb").read()
+    cfg2, W2, _ = load_model(a)
+    _same_model(cfg, Wl, cfg2, W2)
+    v = np.zeros(32, np.float32)
+    with pytest.raises(gguf.GGUFError, match="no data"):
+        gguf.write(str(tmp_path / "x.gguf"), {}, [("a", gguf.GGML_F32, [32]), ("b", gguf.GGML_F32, [32])], [v])
+    with pytest.raises(gguf.GGUFError, match="more data"):
+        gguf.write(str(tmp_path / "y.gguf"), {}, [("a", gguf.GGML_F32, [32])], [v, v])
