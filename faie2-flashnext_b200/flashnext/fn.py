@@ -15,6 +15,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 DLL = os.environ.get("FN_DLL") or os.path.join(os.path.dirname(HERE), "lib", "libfaie2fn.so")
+# the model shards FN.load reads when called without paths, as the reference's SH1 / SH2 (flashnext/fn.py:9-10)
+SH1 = os.environ.get("FN_SHARD1")
+SH2 = os.environ.get("FN_SHARD2")
 
 P = np.ctypeslib.ndpointer
 F32 = P(np.float32, flags="C_CONTIGUOUS")
@@ -122,11 +125,16 @@ class FN:
 
     # ---- the reference's model API (flashnext/fn.py:40-54; engine/faie2fn.cu fn_load .. fn_debug_layers) ----
     # A GGUF model (runner.py: the qwen3next tensor names) loaded into the decode runner on the current GPU.
-    def load(self, shard1, shard2=None, max_ctx=32768, split=0, batch=0):
-        """fn_load: shard2 is an optional second GGUF shard (None: one file); split is accepted for the reference's
-        signature (every layer stays on the current GPU); batch > 0 (<= 32) also prepares forward_batch for that many
-        independent sequences."""
+    def load(self, shard1=None, shard2=None, max_ctx=32768, split=0, batch=0):
+        """fn_load: shard1 / shard2 default to SH1 / SH2 (env FN_SHARD1 / FN_SHARD2), so the reference's calls
+        (fn.load(max_ctx=8192, split=...)) run unchanged; shard2 is an optional second GGUF shard (None: one file);
+        split is accepted for the reference's signature (every layer stays on the current GPU); batch > 0 (<= 32) also
+        prepares forward_batch for that many independent sequences."""
         from runner import Engine
+        if shard1 is None:
+            shard1, shard2 = SH1, shard2 or SH2
+        if not shard1:
+            raise RuntimeError("no model file: pass shard1 or set FN_SHARD1")
         self.free()
         self.eng = Engine(self, str(shard1), str(shard2) if shard2 else None, int(max_ctx), int(split), int(batch))
 

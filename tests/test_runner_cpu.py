@@ -192,6 +192,17 @@ def test_fn_model_api_without_a_model(libpath, tmp_path):
         f.load(str(tmp_path / "bad.gguf"), batch=33)
     with pytest.raises(RuntimeError, match="not loaded"):
         f.forward([1])
+    import fn as fnmod  # the reference's call form: paths from SH1 / SH2 (env FN_SHARD1 / FN_SHARD2)
+    old = fnmod.SH1, fnmod.SH2
+    try:
+        fnmod.SH1, fnmod.SH2 = None, None
+        with pytest.raises(RuntimeError, match="no model file"):
+            f.load(max_ctx=4096)
+        fnmod.SH1 = str(tmp_path / "bad.gguf")
+        with pytest.raises(RuntimeError, match="not a GGUF"):
+            f.load(max_ctx=8192, split=0)
+    finally:
+        fnmod.SH1, fnmod.SH2 = old
 
 
 def test_save_streams_generator_layers(tmp_path):
