@@ -166,6 +166,10 @@ def test_loader_refusals(small, tmp_path):
                   t["blk.3.attn_v.weight"].data[:t["blk.3.attn_v.weight"].data.nbytes // 2]))
     with pytest.raises(gguf.GGUFError, match="blk.3.attn_v.weight: shape"):
         load_model(variant("f.gguf", short))
+    attn_only = [rows(n) for n in t if not n.startswith(("blk.0.", "blk.1.", "blk.2."))]  # blk.3 is the attention layer
+    attn_only = [(n.replace("blk.3.", "blk.0."), q, d, x) for n, q, d, x in attn_only]
+    with pytest.raises(gguf.GGUFError, match="both gated-DeltaNet and attention"):
+        load_model(variant("g.gguf", attn_only, dict(meta, **{"qwen3next.block_count": 1})))
     assert not os.path.exists(str(tmp_path / "never.gguf"))
     with pytest.raises(OSError):
         load_model(str(tmp_path / "never.gguf"))
