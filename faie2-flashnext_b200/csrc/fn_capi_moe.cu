@@ -197,7 +197,8 @@ FN_API int fn_moe_ep_run(int h, const float *logits, int ls, const float *x, flo
 
 // Routing on router outputs given as split-K partials part[ks][8][528] (the reference's router + shared-gate GEMV
 // output layout: 512 router rows, row stride 528): sel / wsel [nt][10] of nt <= 8 tokens and the time per call
-// (iters calls replayed as one CUDA graph). variant: 0 or 1, both the engine's routing. Replaces fn_bench_route
+// (iters calls replayed as one CUDA graph). variant 0: the reference's order counted out expert by expert (the
+// role of k_route_ref, :1697-1740), 1: the engine's routing (k_route's role), bit-identical. Replaces fn_bench_route
 // (engine/faie2fn.cu:2873-2912).
 FN_API int fn_bench_route(int variant, int nt, int ks, const float *parth, int iters, int *selh, float *wselh, float *ms) {
     constexpr int NE = 512, NEU = 10, MAXT = 8, RSG = 528;
@@ -216,7 +217,7 @@ FN_API int fn_bench_route(int variant, int nt, int ks, const float *parth, int i
     FN_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     int rc = 0;
     for (int i = 0; i < iters && !rc; ++i)
-        rc = launch_route(part.as<float>(), ks, (size_t)MAXT * RSG, RSG, NE, NEU, nt, sel.as<int>(), w.as<float>(), st);
+        rc = launch_route(variant, part.as<float>(), ks, (size_t)MAXT * RSG, RSG, NE, NEU, nt, sel.as<int>(), w.as<float>(), st);
     cudaError_t ce = cudaStreamEndCapture(st, &g);
     if (rc) return rc;
     FN_CK(ce);

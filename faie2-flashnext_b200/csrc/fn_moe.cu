@@ -16,10 +16,8 @@
 //              happens in the CTA (no per-slot partial buffer, no combine kernel). It routes from the logits (complete
 //              two kernels back) and issues all of its down-weight stages BEFORE griddepcontrol.wait, so under
 //              programmatic dependent launch its weight stream overlaps k_moe_gu; then it waits for act.
-// Ranking: by logit descending, ties to the lower index. exp is monotone, so this is the probability order of the
-// reference; it differs from ranking the rounded fp32 exp values only where two different logits round to the same
-// probability (the reference then prefers the lower index). The weights are the reference's arithmetic on the chosen
-// logits: v_i = expf(l_i - l_max), s = sum_i v_i in rank order, w_i = v_i / s.
+// Ranking (route_token): the reference's order, fp32 v = expf(l - max l) descending with equal v to the lower index,
+// and its weights: s = sum of the k v's in rank order, w = v / s.
 #include "fn_moe_impl.cuh"
 
 namespace fn {
@@ -58,6 +56,14 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_moe_route(const float *logits
 // ---------------------------------------------------------------------------------------------------------------
 // routing alone (fn_bench_route): logits = sum over ks split-K partials part[k][t][rsg] in split order, then route
 
+__device__ __forceinline__ float sum_splits(const float *part, int ks, int kst, int ts, int t, int i) {
+    const float *q = part + (size_t)t * ts + i;
+    float s = q[0];
+    for (int j = 1; j < ks; ++j) s += q[(size_t)j * kst];
+    return s;
+}
+
+// variant 1: the engine's routing (route_token)
 __global__ void __launch_bounds__(ROUTE_THREADS) k_route(const float *part, int ks, int kst, int ts, int ne, int k,
                                                          int *sel_out, float *w_out) {
     __shared__ float lg[1024];
@@ -67,18 +73,59 @@ __global__ void __launch_bounds__(ROUTE_THREADS) k_route(const float *part, int 
     __shared__ float vals[16];
     const int t = blockIdx.x;
     pdl_wait();
-    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
-        const float *q = part + (size_t)t * ts + i;
-        float s = q[0];
-        for (int j = 1; j < ks; ++j) s += q[(size_t)j * kst];
-        lg[i] = s;
-    }
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) lg[i] = sum_splits(part, ks, kst, ts, t, i);
     __syncthreads();
     pdl_trigger();
     route_token(lg, ne, k, sel, w, keys, vals);
     if (threadIdx.x < k) {
         sel_out[t * k + threadIdx.x] = sel[threadIdx.x];
         w_out[t * k + threadIdx.x] = w[threadIdx.x];
+    }
+}
+
+// variant 0: the reference's order counted out directly, the check for route_token. Expert i's rank is the number of
+// experts ahead of it: larger v, or equal v and a lower index (v = expf(l - max l) in fp32); rank r < k is slot r,
+// s = the k v's summed in rank order by one thread, w = v / s. ne comparisons per expert: a checker, not the
+// engine's path.
+__global__ void __launch_bounds__(ROUTE_THREADS) k_route_count(const float *part, int ks, int kst, int ts, int ne,
+                                                               int k, int *sel_out, float *w_out) {
+    __shared__ float lg[1024];
+    __shared__ float pv[1024];
+    __shared__ float wmax[ROUTE_THREADS / 32];
+    __shared__ int sel[16];
+    __shared__ float val[16];
+    const int t = blockIdx.x, lane = threadIdx.x & 31;
+    pdl_wait();
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
+        lg[i] = sum_splits(part, ks, kst, ts, t, i);
+        m = fmaxf(m, lg[i]);
+    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = wmax[0];
+    for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) m = fmaxf(m, wmax[w2]);
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) pv[i] = expf(lg[i] - m);
+    __syncthreads();
+    pdl_trigger();
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
+        const float v = pv[i];
+        int r = 0;
+        for (int j = 0; j < ne; ++j) r += pv[j] > v || (pv[j] == v && j < i);
+        if (r < k) {
+            sel[r] = i;
+            val[r] = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int r = 0; r < k; ++r) s += val[r];
+        for (int r = 0; r < k; ++r) {
+            sel_out[t * k + r] = sel[r];
+            w_out[t * k + r] = val[r] / s;
+        }
     }
 }
 
@@ -326,10 +373,12 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
     return 0;
 }
 
-int launch_route(const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,
+int launch_route(int variant, const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,
                  cudaStream_t s) {
     if (ne < 1 || ne > 1024 || k < 1 || k > 16 || k > ne || nt < 1) return fail("route: unsupported ne/k/nt");
-    cudaError_t e = launch_k(k_route, dim3(nt), dim3(ROUTE_THREADS), 0, s, part, ks, (int)kst, ts, ne, k, sel, w);
+    if (variant != 0 && variant != 1) return fail("route: variant must be 0 or 1");
+    cudaError_t e = launch_k(variant == 0 ? k_route_count : k_route, dim3(nt), dim3(ROUTE_THREADS), 0, s, part, ks,
+                             (int)kst, ts, ne, k, sel, w);
     if (e != cudaSuccess) return fail(std::string("route launch: ") + cudaGetErrorString(e));
     return 0;
 }

@@ -52,7 +52,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
                const MoeEp *ep = nullptr, bool x_early = false);
 
 // routing alone on split-K partials: logits[t][i] = sum_{j<ks} part[j * kst + t * ts + i] (split order)
-int launch_route(const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,
+int launch_route(int variant, const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,
                  cudaStream_t s);
 
 }  // namespace fn

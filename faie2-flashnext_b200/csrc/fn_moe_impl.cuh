@@ -13,17 +13,18 @@ namespace fn {
 // ---------------------------------------------------------------------------------------------------------------
 // top-k routing
 //
-// Order: larger logit first, ties to the lower expert index (-0 and +0 tie), as a 64-bit key (order-preserving logit
-// bits above the complemented index), so every key is distinct. 16 warps each sort their 32 E keys (a bitonic network
-// in registers), the merged rank of a warp's candidate is its place in its own list plus, for every other warp, how
-// many of that warp's k best are larger (a binary search in the sorted list), and rank r < k is slot r.
+// Order (the reference's k_route, engine/faie2fn.cu:1742-1800): m = the largest logit, v_i = expf(l_i - m) in fp32,
+// larger v first, equal v to the lower expert index. Distinct logits can share one v (l - m rounds to the same float,
+// or expf saturates at 0 or 1); the lower index then wins, as in the reference. The order is a 64-bit key: v's bits
+// (v >= +0, so they order as unsigned integers) above the complemented index, so every key is distinct. 16 warps each
+// sort their 32 E keys (a bitonic network in registers); a candidate's merged rank is the number of larger keys in
+// the 16 sorted lists, and rank r < k is slot r.
 
-__device__ __forceinline__ unsigned long long route_key(float l, int idx) {
-    uint32_t u = __float_as_uint(l == 0.0f ? 0.0f : l);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)idx);
+__device__ __forceinline__ unsigned long long prob_key(float v, int idx) {
+    return ((unsigned long long)__float_as_uint(v) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)idx);
 }
 __device__ __forceinline__ int key_index(unsigned long long k) { return (int)(0xFFFFFFFFu - (uint32_t)k); }
+__device__ __forceinline__ float key_prob(unsigned long long k) { return __uint_as_float((uint32_t)(k >> 32)); }
 
 // Descending bitonic sort of 32 * E keys held by one warp, element i = lane * E + e.
 template <int E> __device__ __forceinline__ void warp_sort_desc(unsigned long long (&v)[E], int lane) {
@@ -59,33 +60,50 @@ template <int E> __device__ __forceinline__ void warp_sort_desc(unsigned long lo
 
 constexpr int ROUTE_THREADS = 512;  // 16 warps
 
-// Route one token: the k best of logits[0, ne) into sel[k], w[k] (shared memory). Weights as the reference:
-// v_r = expf(l_r - l_0), s = sum_r v_r in rank order, w_r = v_r / s. Every thread of a 512-thread block calls it;
-// ne <= 1024, k <= 16. keys: 16 * 16 entries, vals: 16 floats of shared memory.
+// Each warp's k best keys of logits[0, ne) (warp w holds experts [32 E w, 32 E (w + 1))), zero-padded to 16, into
+// keys[w * 16 ..]. red: 16 floats for the block maximum.
+template <int E>
+__device__ __forceinline__ void route_warp_best(const float *logits, int ne, int k, unsigned long long *keys,
+                                                float *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float l[E];
+    float m = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = warp * 32 * E + lane * E + e;
+        l[e] = i < ne ? logits[i] : -INFINITY;
+        m = fmaxf(m, l[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int w2 = 1; w2 < 16; ++w2) m = fmaxf(m, red[w2]);
+    unsigned long long v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = warp * 32 * E + lane * E + e;
+        v[e] = i < ne ? prob_key(expf(l[e] - m), i) : 0ull;
+    }
+    warp_sort_desc<E>(v, lane);
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+        if (lane * E + e < 16) keys[warp * 16 + lane * E + e] = lane * E + e < k ? v[e] : 0ull;
+}
+
+// Route one token: the k best of logits[0, ne) into sel[k], w[k] (shared memory), with the reference's weights
+// w_r = v_r / s, s = sum_r v_r in rank order (fp32, from 0). Every thread of a 512-thread block calls it; ne <= 1024,
+// k <= 16. keys: 16 * 16 entries, vals: 16 floats of shared memory.
 static __device__ __noinline__ void route_token(const float *logits, int ne, int k, int *sel, float *w,
                                                 unsigned long long *keys, float *vals) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (ne <= 512) {
-        unsigned long long v[1];
-        const int i = warp * 32 + lane;
-        v[0] = i < ne ? route_key(logits[i], i) : 0ull;
-        warp_sort_desc<1>(v, lane);
-        if (lane < 16) keys[warp * 16 + lane] = lane < k ? v[0] : 0ull;  // each warp's k best, zero-padded to 16
-    } else {
-        unsigned long long v[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int i = warp * 64 + lane * 2 + e;
-            v[e] = i < ne ? route_key(logits[i], i) : 0ull;
-        }
-        warp_sort_desc<2>(v, lane);
-#pragma unroll
-        for (int e = 0; e < 2; ++e)
-            if (lane * 2 + e < 16) keys[warp * 16 + lane * 2 + e] = lane * 2 + e < k ? v[e] : 0ull;
-    }
+    if (ne <= 512) route_warp_best<1>(logits, ne, k, keys, vals);
+    else route_warp_best<2>(logits, ne, k, keys, vals);
     __syncthreads();
     // candidate c = warp c / k's rank c % k: its merged rank = the number of larger keys in all 16 lists (the keys are
-    // distinct); the k best go to sel in rank order, with their logits
+    // distinct); the k best go to sel in rank order, with their v
     const int c = threadIdx.x, wc = c / k;
     if (wc < 16) {
         const unsigned long long key = keys[wc * 16 + (c - wc * k)];
@@ -100,14 +118,13 @@ static __device__ __noinline__ void route_token(const float *logits, int ne, int
             }
         }
         if (rank < k && key != 0ull) {
-            const int e = key_index(key);
-            sel[rank] = e;
-            vals[rank] = logits[e];
+            sel[rank] = key_index(key);
+            vals[rank] = key_prob(key);
         }
     }
     __syncthreads();
     if (warp == 0) {
-        const float ev = lane < k ? expf(vals[lane] - vals[0]) : 0.0f;
+        const float ev = lane < k ? vals[lane] : 0.0f;
         float s = 0.0f;
         for (int r = 0; r < k; ++r) s += __shfl_sync(0xffffffffu, ev, r);
         if (lane < k) w[lane] = ev / s;

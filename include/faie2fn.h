@@ -182,7 +182,9 @@ int fn_moe_free(int h);
  * routing kernel, as an early GEMV does (engine/faie2fn.cu:2247-2249). */
 int fn_moe_run(int h, const float *logits, int ls, const float *x, float *y, int nt, int acc, void *stream);
 /* Routing of router outputs given as split-K partials part[ks][8][528] (512 experts, top 10): sel / wsel [nt][10],
- * ms per call over iters graph-replayed calls. Replaces fn_bench_route (engine/faie2fn.cu:2873-2912). */
+ * ms per call over iters graph-replayed calls. variant 0 counts the reference's order out expert by expert (as
+ * k_route_ref), 1 runs the engine's routing (as k_route); both rank by fp32 expf(l - max) with ties to the lower
+ * index. Replaces fn_bench_route (engine/faie2fn.cu:2873-2912). */
 int fn_bench_route(int variant, int nt, int ks, const float *part, int iters, int *sel, float *wsel, float *ms);
 
 /* ---- gated-DeltaNet core ------------------------------------------------------------- */

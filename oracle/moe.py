@@ -1,8 +1,8 @@
 """CPU oracle for the MoE layer (routing, routed SwiGLU experts, gated shared expert).  TEST INFRASTRUCTURE ONLY.
 
 Float64 restatement of the reference's MoE arithmetic for one decode token:
-  routing   engine/faie2fn.cu:1742-1800 (k_route): softmax over the ne router logits, the k experts of highest
-            probability (ties to the lower expert index), their weights renormalised to sum to 1
+  routing   engine/faie2fn.cu:1742-1800 (k_route): v = expf(l - max l) in float32 over the ne router logits, the k
+            experts of largest v (equal v to the lower expert index), weights v / (sum of the k v's)
   experts   engine/faie2fn.cu:1082-1184 (k_tmoe_gu8, k_tmoe_down): act = silu(gate_e . x) * (up_e . x),
             d_e = down_e . act
   shared    engine/faie2fn.cu:2411-2416 and the swiglu of k_route (:1758-1759): sh = down_s . (silu(gate_s . x) * (up_s . x))
@@ -21,13 +21,24 @@ from . import dequant as D
 
 
 def route(logits: np.ndarray, k: int):
-    """Top-k of one token's router logits (ne,): indices by probability descending (= logit descending), ties to the
-    lower index; float64 weights exp(l - l_max) / sum over the k."""
-    l = np.asarray(logits, np.float64)
-    order = np.lexsort((np.arange(l.size), -l))
+    """Top-k of one token's router logits (ne,), following k_route (engine/faie2fn.cu:1747-1800) step by step in
+    float32: m = max l; v_i = exp(l_i - m), the difference rounded to float32 and the exponential to the nearest
+    float32 (computed in float64, then rounded); the k largest v, equal v to the lower index; s = the k v's summed in
+    rank order in float32; w = v / s in float32. Returns sel (int64 [k]) and w (float32 [k]).
+
+    The engine calls CUDA's expf, whose result may differ from the nearest float32 by an ulp; this oracle does not
+    model that library. Distinct logits tie exactly where their v's are equal whatever the exponential's rounding:
+    equal differences l - m, and results that saturate at 0 (underflow) or 1 (l - m above -2**-25)."""
+    l = np.asarray(logits, np.float32)
+    m = np.float32(l.max())
+    d = (l - m).astype(np.float32)
+    v = np.exp(d.astype(np.float64)).astype(np.float32)
+    order = np.lexsort((np.arange(l.size), -v.astype(np.float64)))
     sel = order[:k]
-    v = np.exp(l[sel] - l[sel[0]])
-    return sel.astype(np.int64), v / v.sum()
+    s = np.float32(0.0)
+    for i in sel:
+        s = np.float32(s + v[i])
+    return sel.astype(np.int64), (v[sel] / s).astype(np.float32)
 
 
 def silu(v):

@@ -1,8 +1,10 @@
 """GPU parity of routing and the MoE layer through the C ABI.
 
 Routing: the reference's KAT (flashnext/route_fn.py:29-47: 200 random router outputs with forced ties, ks split-K
-partials summed in split order) against the CPU oracle: the selected experts are identical, the weights within
-1e-6 relative (the CPU takes exp in float64, the GPU uses expf). MoE layer (and small shapes):
+partials summed in split order): the engine's routing (variant 1) is bit-identical to the reference's order counted
+out expert by expert (variant 0, k_route_ref's role), its selection equals the CPU oracle's and its weights are
+within 1e-6 relative (the CPU rounds exp from float64, the GPU calls expf); and router outputs where distinct logits
+share one float32 probability select the hand-derived experts (equal v to the lower index, not the larger logit). MoE layer (and small shapes):
 max |y - y64| / max |y64| <= 1e-5 against the float64 oracle on the exactly dequantised weights (the reference's own
 GEMV gate bar, flashnext/test_fn_quants.py:37), routing identical; one token's output is bit-identical alone and
 inside a batch.
@@ -121,7 +123,9 @@ def test_route_kat_200_cases(fn):
                 part[0, t, dst] = part[0, t, src]
         if trial % 7 == 0:  # many exact ties
             part[:, :, :512] = np.round(part[:, :, :512])
+        sel0, w0, _ = fn.bench_route(0, part, nt, ks)
         sel, w, _ = fn.bench_route(1, part, nt, ks)
+        assert np.array_equal(sel0, sel) and np.array_equal(w0.view(np.uint32), w.view(np.uint32)), f"trial {trial}"
         sel, w = sel.reshape(nt, NEU), w.reshape(nt, NEU)
         for t in range(nt):
             lg = part[0, t, :512].copy()
@@ -130,3 +134,29 @@ def test_route_kat_200_cases(fn):
             s64, w64 = M.route(lg, NEU)
             assert np.array_equal(sel[t], s64), f"trial {trial} token {t}"
             assert np.allclose(w[t], w64, rtol=1e-6, atol=0), f"trial {trial} token {t}"
+
+
+def test_route_probability_collisions(fn):
+    from route_cases import collision_cases
+    cases = collision_cases()
+    part = np.zeros((1, MAXT, RSG), np.float32)
+    for t, (l, _) in enumerate(cases):
+        part[0, t, :512] = l
+    nt = len(cases)
+    for variant in (0, 1):
+        sel, w, _ = fn.bench_route(variant, part, nt, 1)
+        sel, w = sel.reshape(nt, NEU), w.reshape(nt, NEU)
+        for t, (l, want) in enumerate(cases):
+            assert sel[t].tolist() == want, f"variant {variant} case {t}"
+            _, w64 = M.route(l, NEU)
+            assert np.allclose(w[t], w64, rtol=1e-6, atol=0), f"variant {variant} case {t}"
+
+
+def test_route_small_logit_collisions_variants_agree(fn):
+    # logits within 1e-3 of the max: many v's land on neighbouring floats just below 1, where expf's own rounding
+    # decides ties; both variants call the same expf, so they must agree bit for bit
+    rng = np.random.default_rng(3)
+    part = (-rng.uniform(0, 1e-3, (1, MAXT, RSG))).astype(np.float32)
+    s0, w0, _ = fn.bench_route(0, part, MAXT, 1)
+    s1, w1, _ = fn.bench_route(1, part, MAXT, 1)
+    assert np.array_equal(s0, s1) and np.array_equal(w0.view(np.uint32), w1.view(np.uint32))

@@ -1,10 +1,13 @@
 """CPU: the MoE oracle's semantics are pinned against transformers' Qwen3NextSparseMoeBlock (float64), and its
-routing against the reference's KAT cases (ties forced by copying and rounding logits, flashnext/route_fn.py:29-40)."""
+routing against the reference's KAT cases (ties forced by copying and rounding logits, flashnext/route_fn.py:29-40)
+and against hand-derived selections where distinct logits share one float32 probability (k_route's order,
+engine/faie2fn.cu:1757-1785: equal v to the lower index)."""
 
 import numpy as np
 import pytest
 
 from oracle import moe as M
+from route_cases import collision_cases
 
 torch = pytest.importorskip("torch")
 
@@ -26,7 +29,28 @@ def test_route_matches_softmax_topk_renorm():
         p /= p.sum()
         top = np.argsort(-p, kind="stable")[:10]
         assert sel.tolist() == top.tolist()
-        assert np.allclose(w, p[top] / p[top].sum(), rtol=1e-12)
+        assert w.dtype == np.float32
+        assert np.allclose(w, p[top] / p[top].sum(), rtol=1e-6)
+
+
+def test_route_probability_ties_go_to_lower_index():
+    for l, want in collision_cases():
+        sel, w = M.route(l, 10)
+        assert sel.tolist() == want
+        by_logit = np.lexsort((np.arange(l.size), -l.astype(np.float64)))[:10].tolist()
+        assert by_logit != want  # each case separates the two orders
+
+
+def test_route_weights_follow_the_reference_arithmetic():
+    # v = expf(l - m) in float32, s summed in rank order from 0 in float32, w = v / s
+    l = np.array([0.0, -1.0, -0.5, -3.0], np.float32)
+    sel, w = M.route(l, 3)
+    assert sel.tolist() == [0, 2, 1]
+    v = [np.float32(np.exp(np.float64(np.float32(l[i] - np.float32(0.0))))) for i in sel]
+    s = np.float32(0.0)
+    for x in v:
+        s = np.float32(s + x)
+    assert np.array_equal(w, np.array([x / s for x in v], np.float32))
 
 
 def test_moe_layer_matches_transformers_qwen3next():

@@ -21,8 +21,8 @@ def ref(qt, W, rows, cols, x):
     return x.astype(np.float64) @ D.dequant_rows(W, qt, rows, cols).astype(np.float64).T
 
 
-@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "IQ3_XXS", "Q8_0", "BF16", "Q5_K", "IQ2_XXS", "Q4_0", "IQ4_XS",
-                                  "Q2_K", "Q3_K"])
+@pytest.mark.parametrize("name", ["Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K",
+                                  "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_NL", "IQ4_XS", "BF16", "Q2_0"])
 @pytest.mark.parametrize("rows,cols,nt", [(4096, 2048, 32), (2048, 4096, 8), (300, 1024, 17)])
 def test_tc_gemv_parity(fn, name, rows, cols, nt):
     rng = np.random.default_rng(rows + cols + nt + len(name))
