@@ -123,9 +123,6 @@ template <int NT> __device__ __forceinline__ void zero2(float2 (&a)[NT][2]) {
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *(const uint4 *)p; }
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *(const uint2 *)p; }
 
-// 4 sign bits n -> per-byte masks 0xFF (bit set) / 0x00: bit k moves to bit 0 of byte k (n * 0x00204081 puts the
-// copies of each bit at distinct positions, so nothing carries), then * 0xFF widens each 0/1 byte
-__device__ __forceinline__ uint32_t sign_mask4(uint32_t n) { return ((n * 0x00204081u) & 0x01010101u) * 0xFFu; }
 // grid bytes g (< 128) with signs m (per byte 0xFF: negative) -> bytes 128 + (+-g)
 __device__ __forceinline__ uint32_t signed_bias128(uint32_t g, uint32_t m) {
     return (g ^ (m & 0x7F7F7F7Fu)) + (0x80808080u ^ (m & 0x81818181u));
@@ -142,10 +139,6 @@ __device__ __forceinline__ void iq4_lut(uint32_t w, uint32_t &lo, uint32_t &hi) 
     const uint32_t t0 = __byte_perm(a0, b0, sel), t1 = __byte_perm(a1, b1, sel >> 16);  // v0 v16 v1 v17 | v2 v18 v3 v19
     lo = __byte_perm(t0, t1, 0x6420);
     hi = __byte_perm(t0, t1, 0x7531);
-}
-
-__device__ __forceinline__ float h16(uint32_t w, int hi) {
-    return __half2float(__ushort_as_half((unsigned short)(hi ? (w >> 16) : (w & 0xFFFFu))));
 }
 
 constexpr float MAG = 8388608.0f;
@@ -168,7 +161,7 @@ template <> struct Fast<T_Q4_0> {
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
         const uint4 w = lds128(row + 16 * g);
-        const float d = ldh(row + plane_off<T_Q4_0, 1>(nb) + 2 * g);
+        const float d = f16_at(row + plane_off<T_Q4_0, 1>(nb) + 2 * g);
         const float2 mo = f2(-(MAG + 8.0f));
         float2 a[NT][2], b[NT][2];
         zero2<NT>(a);
@@ -190,7 +183,7 @@ template <> struct Fast<T_IQ4_NL> {
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
         const uint4 w = lds128(row + 16 * g);
-        const float d = ldh(row + plane_off<T_IQ4_NL, 1>(nb) + 2 * g);
+        const float d = f16_at(row + plane_off<T_IQ4_NL, 1>(nb) + 2 * g);
         const float2 mo = f2(-(MAG + 128.0f));
         float2 a[NT][2], b[NT][2];
         zero2<NT>(a);
@@ -214,8 +207,8 @@ template <> struct Fast<T_Q4_1> {
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
         const uint4 w = lds128(row + 16 * g);
-        const uint32_t dm = ld32a(row + plane_off<T_Q4_1, 1>(nb) + 4 * g);
-        const float d = h16(dm, 0), m = h16(dm, 1);
+        const uint32_t dm = u32_at(row + plane_off<T_Q4_1, 1>(nb) + 4 * g);
+        const float d = f16_of(dm, 0), m = f16_of(dm, 1);
         const float2 mo = f2(-MAG);
         float2 a[NT][2], b[NT][2];
         zero2<NT>(a);
@@ -244,8 +237,8 @@ template <> struct Fast<T_Q5_0> {
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
         const uint4 w = lds128(row + 16 * g);
-        const uint32_t qh = ld32a(row + plane_off<T_Q5_0, 1>(nb) + 4 * g);
-        const float d = ldh(row + plane_off<T_Q5_0, 2>(nb) + 2 * g);
+        const uint32_t qh = u32_at(row + plane_off<T_Q5_0, 1>(nb) + 4 * g);
+        const float d = f16_at(row + plane_off<T_Q5_0, 2>(nb) + 2 * g);
         const float2 mo = f2(-(MAG + 16.0f));
         float2 a[NT][2], b[NT][2];
         zero2<NT>(a);
@@ -267,9 +260,9 @@ template <> struct Fast<T_Q5_1> {
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
         const uint4 w = lds128(row + 16 * g);
-        const uint32_t qh = ld32a(row + plane_off<T_Q5_1, 1>(nb) + 4 * g);
-        const uint32_t dm = ld32a(row + plane_off<T_Q5_1, 2>(nb) + 4 * g);
-        const float d = h16(dm, 0), m = h16(dm, 1);
+        const uint32_t qh = u32_at(row + plane_off<T_Q5_1, 1>(nb) + 4 * g);
+        const uint32_t dm = u32_at(row + plane_off<T_Q5_1, 2>(nb) + 4 * g);
+        const float d = f16_of(dm, 0), m = f16_of(dm, 1);
         const float2 mo = f2(-MAG);
         float2 a[NT][2], b[NT][2];
         zero2<NT>(a);
@@ -295,7 +288,7 @@ template <> struct Fast<T_Q8_0> {
     __device__ __forceinline__ static void group(const uint8_t *row, int nb, int g, const uint32_t *, const XA &xa, int nt,
                                                  float (&r)[NT]) {
         const uint4 w0 = lds128(row + 32 * g), w1 = lds128(row + 32 * g + 16);
-        const float d = ldh(row + plane_off<T_Q8_0, 1>(nb) + 2 * g);
+        const float d = f16_at(row + plane_off<T_Q8_0, 1>(nb) + 2 * g);
         const float2 mo = f2(-(MAG + 128.0f));
         float2 a[NT][2], b[NT][2];
         zero2<NT>(a);
@@ -320,11 +313,11 @@ template <> struct Fast<T_Q2_K> {
         const int b = g >> 3, ib = g & 7, h = ib >> 2, s = 2 * (ib & 3);
         const uint8_t *q = row + 64 * b + 32 * h;
         const uint4 w0 = lds128(q), w1 = lds128(q + 16);
-        const uint32_t sc = ld16(row + plane_off<T_Q2_K, 1>(nb) + 16 * b + 2 * ib);
-        const uint32_t dm = ld32a(row + plane_off<T_Q2_K, 2>(nb) + 4 * b);
-        const float d = h16(dm, 0), dmin = h16(dm, 1);
-        const float dl0 = __fmul_rn(d, u2f(sc & 15u)), ml0 = __fmul_rn(dmin, u2f((sc >> 4) & 15u));
-        const float dl1 = __fmul_rn(d, u2f((sc >> 8) & 15u)), ml1 = __fmul_rn(dmin, u2f((sc >> 12) & 15u));
+        const uint32_t sc = u16_at(row + plane_off<T_Q2_K, 1>(nb) + 16 * b + 2 * ib);
+        const uint32_t dm = u32_at(row + plane_off<T_Q2_K, 2>(nb) + 4 * b);
+        const float d = f16_of(dm, 0), dmin = f16_of(dm, 1);
+        const float dl0 = __fmul_rn(d, __uint2float_rn(sc & 15u)), ml0 = __fmul_rn(dmin, __uint2float_rn((sc >> 4) & 15u));
+        const float dl1 = __fmul_rn(d, __uint2float_rn((sc >> 8) & 15u)), ml1 = __fmul_rn(dmin, __uint2float_rn((sc >> 12) & 15u));
         const float2 mo = f2(-MAG);
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
@@ -354,13 +347,13 @@ template <> struct Fast<T_Q3_K> {
         const uint8_t *q = row + 64 * b + 32 * h, *hm = row + plane_off<T_Q3_K, 1>(nb) + 32 * b;
         const uint4 w0 = lds128(q), w1 = lds128(q + 16), m0 = lds128(hm), m1 = lds128(hm + 16);
         const uint8_t *scp = row + plane_off<T_Q3_K, 2>(nb) + 12 * b;
-        const float d = ldh(row + plane_off<T_Q3_K, 3>(nb) + 2 * b);
+        const float d = f16_at(row + plane_off<T_Q3_K, 3>(nb) + 2 * b);
         float dl[2];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             const int k = 2 * ib + half;
             const uint32_t lo = (scp[k & 7] >> (4 * (k >> 3))) & 15u, hi = (scp[8 + (k & 3)] >> (2 * (k >> 2))) & 3u;
-            dl[half] = __fmul_rn(d, u2f_off(lo | (hi << 4), 32.0f));
+            dl[half] = __fmul_rn(d, __int2float_rn((int)(lo | (hi << 4)) - 32));
         }
         const float2 mo = f2(-(MAG + 4.0f));  // q = low 2 bits + 4 * hmask bit, minus 4
         float2 a[NT][2], c[NT][2];
@@ -388,9 +381,9 @@ template <> struct Fast<T_Q4_K> {
         const int b = g >> 3, ib = g & 7;
         const uint4 w = lds128(row + 16 * g);
         uint32_t sc, m;
-        kscale(ib, row + plane_off<T_Q4_K, 1>(nb) + 12 * b, sc, m);
-        const uint32_t dm = ld32a(row + plane_off<T_Q4_K, 2>(nb) + 4 * b);
-        const float dl = __fmul_rn(h16(dm, 0), u2f(sc)), ml = __fmul_rn(h16(dm, 1), u2f(m));
+        kq_scale_min(ib, row + plane_off<T_Q4_K, 1>(nb) + 12 * b, sc, m);
+        const uint32_t dm = u32_at(row + plane_off<T_Q4_K, 2>(nb) + 4 * b);
+        const float dl = __fmul_rn(f16_of(dm, 0), __uint2float_rn(sc)), ml = __fmul_rn(f16_of(dm, 1), __uint2float_rn(m));
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
@@ -418,11 +411,11 @@ template <> struct Fast<T_Q5_K> {
                                                  float (&r)[NT]) {
         const int b = g >> 3, ib = g & 7;
         const uint4 w = lds128(row + 16 * g);
-        const uint32_t H = ld32a(row + plane_off<T_Q5_K, 1>(nb) + 4 * g);
+        const uint32_t H = u32_at(row + plane_off<T_Q5_K, 1>(nb) + 4 * g);
         uint32_t sc, m;
-        kscale(ib, row + plane_off<T_Q5_K, 2>(nb) + 12 * b, sc, m);
-        const uint32_t dm = ld32a(row + plane_off<T_Q5_K, 3>(nb) + 4 * b);
-        const float dl = __fmul_rn(h16(dm, 0), u2f(sc)), ml = __fmul_rn(h16(dm, 1), u2f(m));
+        kq_scale_min(ib, row + plane_off<T_Q5_K, 2>(nb) + 12 * b, sc, m);
+        const uint32_t dm = u32_at(row + plane_off<T_Q5_K, 3>(nb) + 4 * b);
+        const float dl = __fmul_rn(f16_of(dm, 0), __uint2float_rn(sc)), ml = __fmul_rn(f16_of(dm, 1), __uint2float_rn(m));
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
@@ -452,8 +445,8 @@ template <> struct Fast<T_Q6_K> {
         const int b = g >> 3, j8 = g & 7;
         const uint4 w = lds128(row + 16 * g);
         const uint2 hb = lds64(row + plane_off<T_Q6_K, 1>(nb) + 8 * g);
-        const uint32_t sc = ld16(row + plane_off<T_Q6_K, 2>(nb) + 16 * b + 2 * j8);
-        const float d = ldh(row + plane_off<T_Q6_K, 3>(nb) + 2 * b);
+        const uint32_t sc = u16_at(row + plane_off<T_Q6_K, 2>(nb) + 16 * b + 2 * j8);
+        const float d = f16_at(row + plane_off<T_Q6_K, 3>(nb) + 2 * b);
         const float ds0 = __fmul_rn(d, (float)(int8_t)(sc & 255u)), ds1 = __fmul_rn(d, (float)(int8_t)(sc >> 8));
         const float2 mo = f2(-(MAG + 32.0f));
         float2 a[NT][2], c[NT][2];
@@ -482,10 +475,10 @@ template <> struct Fast<T_IQ4_XS> {
                                                  float (&r)[NT]) {
         const int b = g >> 3, ib = g & 7;
         const uint4 w = lds128(row + 128 * b + 16 * ib);
-        const uint32_t sl = ld32a(row + plane_off<T_IQ4_XS, 1>(nb) + 4 * b);
-        const uint32_t dsh = ld32a(row + plane_off<T_IQ4_XS, 2>(nb) + 4 * b);  // d | scales_h << 16
+        const uint32_t sl = u32_at(row + plane_off<T_IQ4_XS, 1>(nb) + 4 * b);
+        const uint32_t dsh = u32_at(row + plane_off<T_IQ4_XS, 2>(nb) + 4 * b);  // d | scales_h << 16
         const uint32_t ls = ((sl >> (4 * ib)) & 15u) | (((dsh >> (16 + 2 * ib)) & 3u) << 4);
-        const float dl = __fmul_rn(h16(dsh, 0), u2f_off(ls, 32.0f));
+        const float dl = __fmul_rn(f16_of(dsh, 0), __int2float_rn((int)ls - 32));
         const float2 mo = f2(-(MAG + 128.0f));
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
@@ -510,8 +503,8 @@ template <> struct Fast<T_IQ2_XXS> {
                                                  int nt, float (&r)[NT]) {
         const int b = g >> 3, ib = g & 7;
         const uint2 w = lds64(row + 64 * b + 8 * ib);
-        const float d = ldh(row + plane_off<T_IQ2_XXS, 1>(nb) + 2 * b);
-        const float db = db_half(d, w.y >> 28, 0.25f);
+        const float d = f16_at(row + plane_off<T_IQ2_XXS, 1>(nb) + 2 * b);
+        const float db = iq_scale(d, w.y >> 28, 0.25f);
         const float2 mo = f2(-(MAG + 128.0f));
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
@@ -519,7 +512,7 @@ template <> struct Fast<T_IQ2_XXS> {
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
             const uint2 gw = *(const uint2 *)(grid + 2 * ((w.x >> (8 * l)) & 255u));
-            const uint32_t s8 = ksign((w.y >> (7 * l)) & 127u);
+            const uint32_t s8 = even_signs((w.y >> (7 * l)) & 127u);
             if (l < 2) {
                 acc_word<NT>(signed_bias128(gw.x, sign_mask4(s8 & 15u)), mo, xa, 8 * l, nt, a);
                 acc_word<NT>(signed_bias128(gw.y, sign_mask4(s8 >> 4)), mo, xa, 8 * l + 4, nt, a);
@@ -557,9 +550,9 @@ template <> struct Fast<T_IQ3_XXS> {
         const uint2 *tab = (const uint2 *)(grid + 256);
         const int b = g >> 3, ib = g & 7;
         const uint2 q = lds64(row + 64 * b + 8 * ib);
-        const uint32_t aux = ld32a(row + plane_off<T_IQ3_XXS, 1>(nb) + 32 * b + 4 * ib);
-        const float d = ldh(row + plane_off<T_IQ3_XXS, 2>(nb) + 2 * b);
-        const float db = db_half(d, aux >> 28, 0.5f);
+        const uint32_t aux = u32_at(row + plane_off<T_IQ3_XXS, 1>(nb) + 32 * b + 4 * ib);
+        const float d = f16_at(row + plane_off<T_IQ3_XXS, 2>(nb) + 2 * b);
+        const float db = iq_scale(d, aux >> 28, 0.5f);
         float2 a[NT][2], c[NT][2];
         zero2<NT>(a);
         zero2<NT>(c);
@@ -567,7 +560,7 @@ template <> struct Fast<T_IQ3_XXS> {
         for (int l = 0; l < 4; ++l) {
             const uint32_t qq = l < 2 ? q.x : q.y, s = 16 * (l & 1);
             const uint32_t code = (aux >> (7 * l)) & 127u;
-            const uint32_t shi = (code >> 4) | ((__popc(code) & 1u) << 3);  // signs 4..7: 3 bits and the parity
+            const uint32_t shi = even_signs(code) >> 4;  // signs 4..7: 3 bits and the parity
             const uint2 t0 = tab[(((qq >> s) & 255u) << 4) | (code & 15u)];
             const uint2 t1 = tab[(((qq >> (s + 8)) & 255u) << 4) | shi];
             if (l < 2) {

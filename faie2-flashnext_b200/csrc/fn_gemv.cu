@@ -10,7 +10,7 @@
 // launch the weight stream of this GEMV overlaps the tail of the kernel before it. x is staged once per CTA into a
 // bank-conflict-free padded layout ([t][group][36] floats); for one token each lane then keeps its K-slice of x in
 // registers. Lane l of a row (lpr lanes per row) owns groups l, l + lpr, ... of 32 values: it decodes each group in
-// registers (Dec<TY>, bit-exact vs gguf-py) into four FMA chains, adds the chains (fp32), accumulates the group sums
+// registers (load_group, bit-exact vs gguf-py) into four FMA chains, adds the chains (fp32), accumulates the group sums
 // in double in group order, and the row's lanes meet in a double butterfly; the row result is rounded to fp32 once.
 // A row never spans warps or CTAs, so there is no split-K scratch and no reduce kernel; the sum order is a function
 // of (format, cols) alone.
@@ -89,9 +89,9 @@ __global__ void k_dequant(const uint8_t *__restrict__ W, uint64_t rb, int rows, 
     const int r = (int)(i / G), g = (int)(i % G);
     const uint32_t *grid = dev_grid<TY>();
     float *o = out + ((size_t)r * G + g) * 32;
-    Dec<TY>::group(W + (size_t)r * rb, g, grid, [&](int j, float v0, float v1, float v2, float v3) {
-        *(float4 *)(o + j) = make_float4(v0, v1, v2, v3);
-    });
+    const auto v = load_group<TY>(W + (size_t)r * rb, g, grid);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) *(float4 *)(o + j) = v.quad(j);
 }
 
 int launch_dequant(uint32_t type, const uint8_t *W, uint64_t rb, int rows, int cols, float *out, cudaStream_t s) {

@@ -57,10 +57,11 @@ __global__ void k_embed(const uint8_t *__restrict__ E, uint64_t rb, const int *_
     const int tok = after_wait(tokens)[(size_t)blockIdx.x * tstride + *after_wait(pos)];
     const uint8_t *row = E + (size_t)tok * rb;
     const uint32_t *grid = dev_grid<TY>();
-    for (int g = threadIdx.x; g < D / 32; g += blockDim.x)
-        Dec<TY>::group(row, g, grid, [&](int j, float v0, float v1, float v2, float v3) {
-            *(float4 *)(h + g * 32 + j) = make_float4(v0, v1, v2, v3);
-        });
+    for (int g = threadIdx.x; g < D / 32; g += blockDim.x) {
+        const auto v = load_group<TY>(row, g, grid);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) *(float4 *)(h + g * 32 + j) = v.quad(j);
+    }
 }
 
 // ---- RMSNorm: out = x * rsqrt(mean x^2 + eps) * w, one CTA of 256 threads, D % 1024 == 0 ... any D % 4 == 0

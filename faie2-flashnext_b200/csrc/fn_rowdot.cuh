@@ -3,7 +3,7 @@
 //
 // Sum order (a function of the weight's format and row length only, never of the tokens or the launch shape):
 // lane l of a row (lpr lanes per row) owns the 32-value groups l, l + lpr, l + 2 lpr, ...; each group's dot product
-// is one fp32 value (Fast<TY> on the plane layout, or the bit-exact generic decoder Dec<TY> reduced by four FMA
+// is one fp32 value (Fast<TY> on the plane layout, or the bit-exact generic decoder load_group reduced by four FMA
 // chains on GGUF rows); the group values are accumulated in double in group order, and the row's lanes meet in a
 // double butterfly (xor lpr/2, ..., 1; when a warp works on two rows the first step exchanges halves, which adds the
 // same pairs). The row result is rounded to fp32 once by the caller.
@@ -29,11 +29,11 @@ template <uint32_t TY> __device__ __forceinline__ const uint32_t *dev_grid() {
 // codebook word i with the signs of the 4 bits of s (bit j set: value j negative) as bf16, exact for |v| <= 62, two
 // per word: tab[2 (16 i + s) + h] = bf16(v[2h]) | bf16(v[2h + 1]) << 16)
 template <uint32_t TY> __device__ __forceinline__ void stage_grid(uint32_t *grid) {
-    if constexpr (Dec<TY>::gridw > 0) {
+    if constexpr (Gguf<TY>::gridw > 0) {
         const uint32_t *g = dev_grid<TY>();
-        for (int i = threadIdx.x; i < Dec<TY>::gridw; i += blockDim.x) grid[i] = g[i];
+        for (int i = threadIdx.x; i < Gguf<TY>::gridw; i += blockDim.x) grid[i] = g[i];
         if constexpr (TY == T_IQ3_XXS) {  // (generated with the codebook by gen_grids.py)
-            uint4 *tab = (uint4 *)(grid + Dec<TY>::gridw);
+            uint4 *tab = (uint4 *)(grid + Gguf<TY>::gridw);
             const uint4 *src = (const uint4 *)kIq3xxsSigned;
             for (int i = threadIdx.x; i < 8192 / 4; i += blockDim.x) tab[i] = src[i];
         }
@@ -167,17 +167,20 @@ __device__ __forceinline__ void group_dot(const uint8_t *rowp, int nb, int g, co
         float c[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; ++t) c[t][0] = c[t][1] = c[t][2] = c[t][3] = 0.0f;
-        Dec<TY>::group(rowp, g, grid, [&](int j, float v0, float v1, float v2, float v3) {
+        const auto w = load_group<TY>(rowp, g, grid);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 v = w.quad(j);
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (NT > 1 && t >= nt) break;
                 const float2 x01 = xa.x2(t, j), x23 = xa.x2(t, j + 2);
-                c[t][0] = __fmaf_rn(v0, x01.x, c[t][0]);
-                c[t][1] = __fmaf_rn(v1, x01.y, c[t][1]);
-                c[t][2] = __fmaf_rn(v2, x23.x, c[t][2]);
-                c[t][3] = __fmaf_rn(v3, x23.y, c[t][3]);
+                c[t][0] = __fmaf_rn(v.x, x01.x, c[t][0]);
+                c[t][1] = __fmaf_rn(v.y, x01.y, c[t][1]);
+                c[t][2] = __fmaf_rn(v.z, x23.x, c[t][2]);
+                c[t][3] = __fmaf_rn(v.w, x23.y, c[t][3]);
             }
-        });
+        }
 #pragma unroll
         for (int t = 0; t < NT; ++t)
             if (NT == 1 || t < nt) r[t] = __fadd_rn(__fadd_rn(c[t][0], c[t][1]), __fadd_rn(c[t][2], c[t][3]));

@@ -6,7 +6,7 @@
 // reference has no batched path (its k_tgemv takes nt <= 8 on CUDA cores, engine/faie2fn.cu:734-955); the operator
 // contract is the same as fn_w_gemv's.
 //
-// Precision: the tensor cores take bf16 operands, so every weight value v (the exact GGUF dequantisation, Dec<TY>) and
+// Precision: the tensor cores take bf16 operands, so every weight value v (the exact GGUF dequantisation, load_group) and
 // every x value is split into v_hi = bf16(v) and v_lo = bf16(v - v_hi), and each 16-deep step runs three MMAs,
 // hi*hi + hi*lo + lo*hi, accumulated in fp32 in tensor memory: each product keeps about 16 mantissa bits (the lo*lo
 // term is below 2^-16 of it), so y is within about 3e-5 of float64, relative to max |y| (the stated tolerance is 1e-4).
@@ -125,51 +125,27 @@ __device__ __forceinline__ void split4(float a, float b, float c, float d, uint2
     lo = make_uint2(*(const uint32_t *)&l01, *(const uint32_t *)&l23);
 }
 
-// One 32-value group of a staged raw row, as Dec<TY>::group (the same values, bit for bit): for the formats whose
-// blocks sit 16-byte aligned in a row (Q4_K's 144 bytes, BF16) the block's header and quants are read with a few
-// 16-byte shared-memory loads and unpacked in registers; the other formats use Dec<TY> directly.
-template <uint32_t TY, class F>
-__device__ __forceinline__ void tc_group(const uint8_t *row, int g, const uint32_t *grid, F &&f) {
+// One 32-value group of a staged raw row, as load_group (the same values, bit for bit). Q4_K blocks sit 16-byte
+// aligned in a row, so their header and quants are read with four 16-byte shared-memory loads; the other formats go
+// through load_group.
+template <uint32_t TY> __device__ __forceinline__ auto tc_load(const uint8_t *row, int g, const uint32_t *grid) {
     if constexpr (TY == T_Q4_K) {
-        const uint8_t *b = row + (g >> 3) * 144;
-        const int ib = g & 7;
-        const uint4 h = *(const uint4 *)b;  // d, dmin | the 12 packed 6-bit scales and mins
-        const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-        auto sb = [&](int i) {  // packed scale byte i (0..11)
-            const uint32_t w = i < 4 ? h.y : i < 8 ? h.z : h.w;
-            return (w >> (8 * (i & 3))) & 255u;
-        };
-        uint32_t sc, m;  // gguf-py Q4_K.get_scale_min, as kscale
-        if (ib < 4) {
-            sc = sb(ib) & 63u;
-            m = sb(ib + 4) & 63u;
-        } else {
-            sc = (sb(ib + 4) & 15u) | ((sb(ib - 4) >> 6) << 4);
-            m = (sb(ib + 4) >> 4) | ((sb(ib) >> 6) << 4);
-        }
-        const float dl = __fmul_rn(d, u2f(sc)), ml = __fmul_rn(dmin, u2f(m));
-        const uint4 q0 = *(const uint4 *)(b + 16 + 32 * (ib >> 1)), q1 = *(const uint4 *)(b + 32 + 32 * (ib >> 1));
+        const uint8_t *blk = row + (g >> 3) * 144;
+        const int s = g & 7;
+        const uint4 h = *(const uint4 *)blk;  // d, dmin | the 12 packed scale and min bytes
+        uint32_t sc, mn;
+        kq_scale_min(s, h.y, h.z, h.w, sc, mn);
+        Codes32 c;
+        c.a[0] = c.a[1] = __fmul_rn(f16_of(h.x, 0), __uint2float_rn(sc));
+        c.b[0] = c.b[1] = -__fmul_rn(f16_of(h.x, 1), __uint2float_rn(mn));
+        const uint4 q0 = *(const uint4 *)(blk + 16 + 32 * (s >> 1)), q1 = *(const uint4 *)(blk + 32 + 32 * (s >> 1));
         const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const int sh = 4 * (ib & 1);
+        const int sh = 4 * (s & 1);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-            const uint32_t w = qw[j >> 2] >> sh;
-            auto v = [&](int k) { return __fsub_rn(__fmul_rn(dl, u2f((w >> (8 * k)) & 15u)), ml); };
-            f(j, v(0), v(1), v(2), v(3));
-        }
-    } else if constexpr (TY == T_BF16) {
-        const uint4 *p = (const uint4 *)(row + g * 64);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 u = p[i];
-            f(8 * i, __uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
-              __uint_as_float(u.y & 0xffff0000u));
-            f(8 * i + 4, __uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u), __uint_as_float(u.w << 16),
-              __uint_as_float(u.w & 0xffff0000u));
-        }
+        for (int i = 0; i < 8; ++i) c.q[i] = (qw[i] >> sh) & LOW4;
+        return c;
     } else {
-        Dec<TY>::group(row, g, grid, f);
+        return load_group<TY>(row, g, grid);
     }
 }
 
@@ -188,7 +164,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
     const uint32_t n = (uint32_t)a.npad, bbytes = n * TC_KC * 2;  // B bytes per hi / lo
     const uint32_t idesc = umma_idesc_bf16(TC_M, a.npad);
     const uint32_t *grid = dev_grid<TY>();
-    constexpr int QK = Dec<TY>::qk, TB = Dec<TY>::bytes;
+    constexpr int QK = Gguf<TY>::qk, TB = Gguf<TY>::bytes;
 
     // the raw bytes of chunk c of the tile's rows into slot sl: one 2-D tensor copy of the box (128 rows x raw_stride
     // bytes from byte column st, a 16-byte multiple; rows past the matrix and bytes past the stride read as zero)
@@ -264,19 +240,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
             const uint32_t roff = (uint32_t)(r >> 3) * 128u + (uint32_t)(r & 7) * 16u;
             if (r < nrow) {
                 const uint8_t *rp = raw + (size_t)r * a.raw_stride - st;
-                float v[32];  // the group's values, then four 16-byte core-matrix rows each of hi and lo: the 8 lanes of
-                              // a store phase write one core matrix's 128 contiguous bytes (no bank conflict)
-                tc_group<TY>(rp, c * (TC_KC / 32) + gl, grid, [&](int j, float v0, float v1, float v2, float v3) {
-                    v[j] = v0;
-                    v[j + 1] = v1;
-                    v[j + 2] = v2;
-                    v[j + 3] = v3;
-                });
+                // the group's values as four 16-byte core-matrix rows each of hi and lo: the 8 lanes of a store
+                // phase write one core matrix's 128 contiguous bytes (no bank conflict)
+                const auto G = tc_load<TY>(rp, c * (TC_KC / 32) + gl, grid);
 #pragma unroll
                 for (int kc = 0; kc < 4; ++kc) {
                     uint2 h0, l0, h1, l1;
-                    split4(v[8 * kc], v[8 * kc + 1], v[8 * kc + 2], v[8 * kc + 3], h0, l0);
-                    split4(v[8 * kc + 4], v[8 * kc + 5], v[8 * kc + 6], v[8 * kc + 7], h1, l1);
+                    const float4 p = G.quad(8 * kc), q = G.quad(8 * kc + 4);
+                    split4(p.x, p.y, p.z, p.w, h0, l0);
+                    split4(q.x, q.y, q.z, q.w, h1, l1);
                     const uint32_t off = (uint32_t)(gl * 4 + kc) * (TC_M * 16u) + roff;
                     *(uint4 *)(Ahi + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
                     *(uint4 *)(Alo + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
