@@ -18,6 +18,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")  # the C ABI header (include/faie2fn.h)
 OBJ = os.path.join(HERE, "_build")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libfaie2fn.so")
@@ -38,7 +39,8 @@ def sources():
 
 
 def headers():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")))
+    return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) +
+                  glob.glob(os.path.join(INCLUDE, "*.h")))
 
 
 def stale(target, deps) -> bool:
@@ -52,7 +54,7 @@ def compile_one(src, extra):
     obj = os.path.join(OBJ, os.path.basename(src) + ".o")
     if not stale(obj, [src, *headers(), __file__]) and not extra.get("force"):
         return obj, None
-    cmd = [nvcc(), *ARCH, *FLAGS, *extra.get("flags", []), "-I", CSRC, "-c", src, "-o", obj]
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra.get("flags", []), "-I", CSRC, "-I", INCLUDE, "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         return None, f"$ {' '.join(cmd)}\n{r.stdout}\n{r.stderr}"

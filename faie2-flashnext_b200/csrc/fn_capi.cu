@@ -2,6 +2,7 @@
 // the reference (engine/faie2fn.cu:2492-2935) and resident-weight handles for device-pointer callers.
 // Conventions of the reference are kept: int return 0 = ok, -1 = error with the message in fn_error(); the caller
 // owns every host buffer; every fn_test_* / fn_bench_* call is synchronous.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -197,13 +198,38 @@ FN_API int fn_set_device(int dev) {
 FN_API void fn_pdl(int on) { settings().pdl = on != 0; }
 FN_API void fn_early(int on) { settings().early = on != 0; }
 FN_API void fn_bench_hot(int on) { settings().bench_hot = on; }
-// GEMV plan overrides for sweeps: warps per CTA, ring KiB, stage KiB, CTAs per SM (0 = keep)
-FN_API void fn_gemv_override(int warps, int ring_kb, int stage_kb, int ctas_per_sm) {
+// GEMV plan settings for weights planned from now on: warps per CTA (0: automatic, < 0 keeps), ring KiB, stage KiB,
+// CTAs per SM (0 = keep)
+FN_API void fn_gemv_tune(int warps, int ring_kb, int stage_kb, int ctas_per_sm) {
     Settings &s = settings();
     if (warps >= 0) s.warps_per_cta = warps;  // 0: automatic
     if (ring_kb > 0) s.ring_kb = ring_kb;
     if (stage_kb > 0) s.stage_kb = stage_kb;
     if (ctas_per_sm > 0) s.ctas_per_sm = ctas_per_sm;
+}
+// The reference's plan override (engine/faie2fn.cu:2786-2791) with its argument meaning: tb = threads per CTA of the
+// GEMVs planned from now on (0: automatic), warps_per_sm = the target warps per SM (the reference's default 16: one
+// CTA of 16 warps per SM). wpt (weights per thread of a tile) and ks (split-K) have no counterpart in this plan, where
+// a row never spans warps; they are accepted and ignored.
+FN_API void fn_gemv_override(int wpt, int ks, int tb, int warps_per_sm) {
+    (void)wpt;
+    (void)ks;
+    Settings &s = settings();
+    const int warps = tb > 0 ? std::max(1, std::min(16, tb / 32)) : 0;
+    s.warps_per_cta = warps;
+    s.ctas_per_sm = warps > 0 && warps_per_sm > 0 ? std::max(1, warps_per_sm / warps) : 1;
+}
+// MoE layer variant (the reference's A/B switch, engine/faie2fn.cu:2799): 0 = a routing kernel before gate/up
+// (default: measured faster on the config-5 decode step, 2.99 against 3.18 ms per token), 1 = one token on one GPU
+// routed inside the gate/up and down kernels
+FN_API void fn_moe_var(int v) { settings().moe_var = v; }
+// The reference's routed-expert launch shapes (engine/faie2fn.cu:2801-2806). The B200 MoE kernels size their grids
+// and rings from the layer's shape and the SM count, so there is nothing to override: accepted and ignored.
+FN_API void fn_moe_override(int gu_wpt, int gu_tb, int dn_wpt, int dn_tb) {
+    (void)gu_wpt;
+    (void)gu_tb;
+    (void)dn_wpt;
+    (void)dn_tb;
 }
 FN_API void fn_gemv_waves(int ctas_per_sm) { settings().ctas_per_sm = ctas_per_sm > 0 ? ctas_per_sm : 1; }
 
@@ -413,6 +439,19 @@ FN_API int fn_w_prefetch_after(int h, const void *ptr, uint64_t bytes) {
     if ((uintptr_t)ptr & 15) return fail("fn_w_prefetch_after: ptr must be 16-byte aligned");
     w->plan1.pf = w->plan8.pf = (const uint8_t *)ptr;
     w->plan1.pf_bytes = w->plan8.pf_bytes = ptr ? (bytes & ~15ull) : 0;
+    return 0;
+}
+
+// RMSNorm folded into GEMV handle h: from now on every launch computes y[t] = rsqrt(mean x[t]^2 + eps) (W . (x[t] * w))
+// from the raw x (the reference's k_groupnorm before the GEMV, engine/faie2fn.cu:1222-1235, without its launch): the
+// sum of squares is taken while x is staged and the scale is applied to each row's result. w: cols floats of device
+// memory, 16-byte aligned, kept by reference; w = NULL turns it off.
+FN_API int fn_w_norm(int h, const float *w, float eps) {
+    WeightH *wh = wget(h);
+    if (!wh) return fail("fn_w_norm: bad handle");
+    if ((uintptr_t)w & 15) return fail("fn_w_norm: w must be 16-byte aligned");
+    wh->plan1.nw = wh->plan8.nw = w;
+    wh->plan1.eps = wh->plan8.eps = eps;
     return 0;
 }
 

@@ -140,6 +140,18 @@ FN_API int fn_moe_prefetch_after(int h, const void *ptr, uint64_t bytes) {
     return 0;
 }
 
+// RMSNorm folded into MoE layer h: from now on the layer's input is rmsnorm(x) * w (rsqrt(mean x^2 + eps)), computed
+// by the gate/up kernel from the raw x it reads (no separate norm launch). w: d floats of device memory, 16-byte
+// aligned, kept by reference; NULL turns it off.
+FN_API int fn_moe_norm(int h, const float *w, float eps) {
+    MoeH *m = moe_get(h);
+    if (!m) return fail("fn_moe_norm: bad handle");
+    if ((uintptr_t)w & 15) return fail("fn_moe_norm: w must be 16-byte aligned");
+    m->p.nw = w;
+    m->p.eps = eps;
+    return 0;
+}
+
 // Launch one MoE layer on device pointers: logits [nt][ls] (ls >= ne + 1), x [nt][d] -> y [nt][d]. flags: bit 0 adds
 // into y; bit 1 = x early: x was complete before the kernel before this call started (so the layer reads it without
 // waiting for that kernel, as an early GEMV does; engine/faie2fn.cu:2247-2249).

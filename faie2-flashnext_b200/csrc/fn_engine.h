@@ -29,6 +29,8 @@ struct GemvPlan {
     size_t smem = 0;
     const uint8_t *pf = nullptr;  // L2 prefetch hint: every launch also brings [pf, pf + pf_bytes) into L2 (the next
     uint64_t pf_bytes = 0;        // weights of a decode chain), spread over its CTAs
+    const float *nw = nullptr;    // RMSNorm folded in: y[t] = rsqrt(mean x[t]^2 + eps) (W . (x[t] * nw)) (cols floats,
+    float eps = 0.0f;             // device memory, 16-byte aligned); null: y = W . x
 };
 
 bool plan_gemv(GemvPlan &p, uint32_t type, int rows, int cols, int ntcap);
@@ -95,6 +97,8 @@ struct Settings {
     int ctas_per_sm = 1;     // GEMV CTAs per SM
     int ov_rps = 0;          // overrides (0 = automatic)
     int bench_hot = 0;
+    int moe_var = 0;         // MoE layer variant (fn_moe_var): 0 = a routing kernel before gate/up; 1 = one token
+                             // on one GPU routed inside the gate/up and down kernels
 };
 Settings &settings();
 int num_sms();

@@ -201,6 +201,9 @@ int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, flo
     a.early = early && settings().early && settings().pdl ? 1 : 0;
     a.pf = p.pf;
     a.pf_bytes = p.pf_bytes;
+    a.nw = p.nw;
+    a.eps = p.eps;
+    if (p.nw && ((uintptr_t)p.nw & 15)) return fail("gemv: the norm weight must be 16-byte aligned");
     a.err = dev_error_ptr();
     a.amx = 0;
     a.row0 = 0;

@@ -23,6 +23,8 @@ struct GemvArgs {
     int acc, early;
     const uint8_t *pf;  // L2 prefetch hint (GemvPlan::pf), null: none
     uint64_t pf_bytes;
+    const float *nw;  // RMSNorm folded in (GemvPlan::nw), null: none
+    float eps;
     uint32_t *err;
     // fused argmax (GemvArgmax); amx == 0: none
     int amx, row0;
@@ -133,7 +135,11 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
     }
     const float *x = after_wait(a.x);
     const int nt = a.nt;
-    stage_x(xsm, x, a.xs, nt, a.G, ScaleX<TY, true>::v);
+    stage_x(xsm, x, a.xs, nt, a.G, ScaleX<TY, true>::v, a.nw);
+    // RMSNorm folded in: y = s_t (W . (x_t * nw)), s_t applied to the row result
+    float ns[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) ns[t] = a.nw && (NT == 1 || t < nt) ? norm_scale(xsm, a.G, t, 32 * a.G, a.eps) : 1.0f;
 
     const int lr = lane % LPR, sub = lane / LPR;
     XReg<LPR, (GPL > 0 ? GPL : 1)> xr;
@@ -169,7 +175,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv(const GemvArgs a) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (NT > 1 && t >= nt) break;
-                const float v = __double2float_rn(acc[0][t]);
+                float v = __double2float_rn(acc[0][t]);
+                if (a.nw) v = __fmul_rn(v, ns[t]);
                 if (a.y) {
                     float *o = a.y + (size_t)t * a.ys + r;
                     *o = a.acc ? __fadd_rn(*o, v) : v;

@@ -7,9 +7,9 @@
 // (:2411-2416, swiglu in k_route :1758-1759) and the combine inside k_hc_add (:1299-1318:
 // y = sum_k wsel[k] dpart[k] in slot order + sigmoid(shared-gate logit) * shared).
 //
-// B200 design: two kernels.
-//  k_moe_gu    every CTA routes all tokens itself (a 64-bit-key bitonic top-k in shared memory, a few hundred cycles,
-//              cheaper than a kernel boundary), then streams its share of the (token, slot, row) pairs of the k routed
+// B200 design: two kernels (one token on one GPU), or a routing kernel (k_moe_route, one CTA per token) and two.
+//  k_moe_gu    routes the tokens itself for one token (a 64-bit-key bitonic top-k in shared memory, a few hundred
+//              cycles, cheaper than a kernel boundary), then streams its share of the (token, slot, row) pairs of the k routed
 //              experts plus the shared expert (slot k) through the TMA-bulk ring: a stage holds R gate rows and the R
 //              matching up rows; act[t][slot][r] = silu(g) * u goes to a small scratch buffer.
 //  k_moe_down  CTA (chunk, t) owns output rows [r0, r1) of token t for all k + 1 slots, so the slot-order combine
@@ -241,8 +241,11 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
     if (ls < p.ne + 1) return fail("moe: logits stride must hold ne + 1 columns (router + shared gate)");
     if (((uintptr_t)x & 15) || ((uintptr_t)act & 15) || (p.d & 3) || (p.ffe & 3)) return fail("moe: x/act alignment");
     const int ks = p.k + 1;
-    // ---- routing, once per layer
-    {
+    if (p.nw && ((uintptr_t)p.nw & 15)) return fail("moe: the norm weight must be 16-byte aligned");
+    // ---- routing: one token on one GPU is routed inside the gate/up and down kernels (one launch fewer per layer);
+    // otherwise once per layer by its own kernel (one CTA per token)
+    const bool route_self = nt == 1 && !ep && settings().moe_var == 1;
+    if (!route_self) {
         const cudaError_t e = launch_k(k_moe_route, dim3(nt), dim3(ROUTE_THREADS), 0, s, logits, ls, p.ne, p.k, rsel, rw,
                                        sel_out, w_out);
         if (e != cudaSuccess) return fail(std::string("moe route launch: ") + cudaGetErrorString(e));
@@ -270,13 +273,16 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.x = x;
         a.act = act;
         a.rsel = rsel;
+        a.route_self = route_self ? 1 : 0;
         a.x_early = x_early && settings().pdl ? 1 : 0;
+        a.nw = p.nw;
+        a.eps = p.eps;
         // one unit (a gate row and its up row) per ring stage; each warp has its own ring of `slots` stages
         constexpr int NW = MOE_THREADS / 32;
         const long long U = (long long)nt * ks * p.ffe;  // upper bound (every slot computed here)
-        // one SM fewer than the GPU has: the routing kernel's CTA keeps an SM while the gate/up CTAs start beside it
-        // (programmatic launch), and a gate/up CTA does not fit next to it
-        const int ctas = (int)std::min<long long>(std::max(1, sm_count() - 1), (U + 7) / 8);
+        // with a routing kernel, one SM fewer than the GPU has: its CTA keeps an SM while the gate/up CTAs start beside
+        // it (programmatic launch), and a gate/up CTA does not fit next to it
+        const int ctas = (int)std::min<long long>(std::max(1, sm_count() - (route_self ? 0 : 1)), (U + 7) / 8);
         const long long per_warp0 = (U + (long long)ctas * NW - 1) / ((long long)ctas * NW);
         // rows of 32 or 64 groups: the warps read x into registers themselves, nothing is staged in shared memory
         const bool xreg = p.d == 1024 || p.d == 2048;
@@ -299,6 +305,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.x_off = (uint32_t)al(a.misc_off + misc, 128);
         const size_t smem = al(a.x_off + xb, 128);
         if (smem > kMoeDynSmem) return fail("moe: gate/up shared memory too large");
+        if (route_self && (size_t)NW * a.slots * a.stage_bytes < 2304) return fail("moe: ring too small for the routing scratch");
         a.err = dev_error_ptr();
         a.ep = E;
         const int G = p.d / 32;
@@ -330,6 +337,9 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.acc = acc ? 1 : 0;
         a.rsel = rsel;
         a.rw = rw;
+        a.route_self = route_self ? 1 : 0;
+        a.sel_out = sel_out;
+        a.w_out = w_out;
         a.pf = p.pf;
         a.pf_bytes = p.pf_bytes;
         // CTA (chunk, t): rows [r0, r1) of token t, every computed slot's rows in shared memory at once
@@ -355,6 +365,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         a.x_off = (uint32_t)al(a.misc_off + misc, 128);
         const size_t smem = al(a.x_off + xb, 128);
         if (smem > kMoeDynSmem) return fail("moe: down shared memory too large");
+        if (route_self && xb < 2304) return fail("moe: activation staging too small for the routing scratch");
         a.err = dev_error_ptr();
         a.ep = E;
         cudaError_t e = cudaSuccess;

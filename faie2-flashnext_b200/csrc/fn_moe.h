@@ -13,6 +13,8 @@ struct MoePlan {
     int lpr_down = 32;
     const uint8_t *pf = nullptr;  // L2 prefetch hint of the down kernel (GemvPlan::pf)
     uint64_t pf_bytes = 0;
+    const float *nw = nullptr;    // RMSNorm folded in (GemvPlan::nw): the layer's input is rmsnorm(x) * nw
+    float eps = 0.0f;
 };
 
 // device weights, rows at the plan's strides: gate/up ne * ffe rows of d columns (expert e at rows e * ffe ..),

@@ -175,8 +175,11 @@ struct MoeGuArgs {
     int ls;  // logits token stride (>= ne + 1: column ne is the shared-gate logit)
     const float *x;  // [nt][d]
     float *act;      // [nt][k + 1][ffe]
-    const int *rsel;  // routing [nt][16] (k_moe_route, the kernel before this one)
-    int x_early;      // x was complete before the routing kernel started: read it before the wait
+    const int *rsel;  // routing [nt][16] (k_moe_route, the kernel before this one), unless route_self
+    int route_self;   // every CTA routes the tokens itself from the logits (no routing kernel before this one)
+    int x_early;      // x was complete before the kernel before this one started: read it before the wait
+    const float *nw;  // RMSNorm folded in (MoePlan::nw), null: none
+    float eps;
     int slots;  // ring stages per warp
     int run;    // units per stage at most: `run` consecutive gate rows of one expert, then the matching up rows
     uint32_t stage_bytes, ring_off, x_off, grid_off, misc_off;
@@ -211,14 +214,30 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     }
     stage_grid<TY>(grid);
     XReg<32, (XG > 0 ? XG : 1)> xr;
+    float xscale = 1.0f;  // RMSNorm scale of the token whose x the warp holds (1 without a folded norm)
     if constexpr (XG > 0)
-        if (a.x_early) xr.load_global(a.x, lane, ScaleX<TY, SOA>::v);  // beside the routing kernel
+        if (a.x_early) xscale = xr.load_global(a.x, lane, ScaleX<TY, SOA>::v, a.nw, a.eps);  // beside the kernel before
     pdl_wait();
-    pdl_trigger();  // after the wait: the down kernel may rely on the routing being complete before it starts
+    pdl_trigger();  // after the wait: the down kernel may rely on the router's logits being complete when it starts
     const float *x = after_wait(a.x);
-    const int *rsel = after_wait(a.rsel);
+    if (a.route_self) {
+        // every CTA routes the tokens itself (no routing kernel, one launch fewer per layer); the scratch is the start
+        // of the ring, which no copy has reached yet (the copies need the routing)
+        unsigned long long *keys = (unsigned long long *)(sm + a.ring_off);
+        float *vals = (float *)(keys + 256), *rw = vals + 16;
+        int *rs = (int *)(rw + 16);
+        const float *lg = after_wait(a.logits);
+        for (int t = 0; t < a.nt; ++t) {
+            route_token(lg + (size_t)t * a.ls, a.ne, a.k, rs, rw, keys, vals);
+            if (tid < 16) sel[t * 16 + tid] = tid < a.k ? rs[tid] : 0;
+        }
+        __syncthreads();
+    }
     if (warp == 0) {  // the routing and this rank's (token, slot) pairs, then one block barrier
-        for (int i = lane; i < a.nt * 16; i += 32) sel[i] = rsel[i];
+        if (!a.route_self) {
+            const int *rsel = after_wait(a.rsel);
+            for (int i = lane; i < a.nt * 16; i += 32) sel[i] = rsel[i];
+        }
         __syncwarp();
         if (lane == 0) {
             int np = 0;
@@ -273,12 +292,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
     };
     if (lane == 0)  // the weight copies fly while x is staged
         while (n_issued < min(nst, a.slots)) issue();
-    int x_tok = 0;  // XG > 0: the token whose x the warp holds in registers (token 0 first)
+    int x_tok = 0;  // the token whose x the warp holds in registers (XG > 0) or whose norm scale it holds (token 0)
     if constexpr (XG > 0) {
-        if (!a.x_early) xr.load_global(x, lane, ScaleX<TY, SOA>::v);
+        if (!a.x_early) xscale = xr.load_global(x, lane, ScaleX<TY, SOA>::v, a.nw, a.eps);
         __syncwarp();
     } else {
-        stage_x(xsm, x, a.d, a.nt, G, ScaleX<TY, SOA>::v);  // ends with a __syncthreads
+        stage_x(xsm, x, a.d, a.nt, G, ScaleX<TY, SOA>::v, a.nw);  // ends with a __syncthreads
+        if (a.nw) xscale = norm_scale(xsm, G, 0, a.d, a.eps);
     }
 
     const int ni = (G + 31) / 32;
@@ -299,7 +319,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
         if constexpr (XG > 0) {
             // several tokens: a warp's units run in (token, slot, row) order, so it reloads x at most once per token
             if (t != x_tok) {
-                xr.load_global(x + (size_t)t * a.d, lane, ScaleX<TY, SOA>::v);
+                xscale = xr.load_global(x + (size_t)t * a.d, lane, ScaleX<TY, SOA>::v, a.nw, a.eps);
                 x_tok = t;
             }
 #pragma unroll
@@ -313,6 +333,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
                 accu += (double)ru[0];
             }
         } else {
+            if (a.nw && t != x_tok) {
+                xscale = norm_scale(xsm, G, t, a.d, a.eps);
+                x_tok = t;
+            }
 #pragma unroll 1
             for (int i = 0; i < ni; ++i) {
                 const int g = lane + 32 * i;
@@ -333,7 +357,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_gu(const MoeGuArgs a) {
         keep += __shfl_xor_sync(0xffffffffu, uh ? accg : accu, 16);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
-        const float v = __double2float_rn(keep);  // lanes 0-15: the gate row, 16-31: the up row
+        float v = __double2float_rn(keep);  // lanes 0-15: the gate row, 16-31: the up row
+        if (a.nw) v = __fmul_rn(v, xscale);  // the folded RMSNorm's scale, on both rows
         const float up = __shfl_sync(0xffffffffu, v, 16);
         if (lane == 0) a.act[((size_t)t * ks + q) * a.ffe + r] = silu(v) * up;
         }
@@ -362,8 +387,11 @@ struct MoeDownArgs {
     const float *act;  // [nt][k + 1][ffe]
     float *y;          // [nt][d]
     int acc;
-    const int *rsel;   // routing [nt][16] and its weights (k_moe_route, two kernels back)
+    const int *rsel;   // routing [nt][16] and its weights (k_moe_route, two kernels back), unless route_self
     const float *rw;
+    int route_self;    // each CTA routes its token itself from the logits (before its wait)
+    int *sel_out;      // route_self: the routing [nt][k] (nullable), written by the token's first CTA
+    float *w_out;
     int rows;  // rows per CTA at most (gridDim.x chunks of d)
     uint32_t w_off, x_off, grid_off, res_off, misc_off;
     uint32_t *err;
@@ -392,13 +420,21 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) k_moe_down(const MoeDownArgs a
     const int t = blockIdx.y, G = a.ffe / 32, ks = a.k + 1;
     const int r0 = (int)((long long)blockIdx.x * a.d / gridDim.x), r1 = (int)((long long)(blockIdx.x + 1) * a.d / gridDim.x);
     const int n = r1 - r0;
-    // the routing was written by k_moe_route before the previous kernel (k_moe_gu) passed its own wait, so it is
-    // complete here without waiting; the expert rows to stream follow from it
-    if (tid < a.k) {
-        sel[tid] = a.rsel[t * 16 + tid];
-        wsel[tid] = a.rw[t * 16 + tid];
+    // the routing (k_moe_route's output, or the logits of the router GEMV) was complete before the previous kernel
+    // (k_moe_gu) passed its own wait, so it is complete here without waiting; the expert rows to stream follow from it
+    if (a.route_self) {  // route the token here (the same function and logits as the gate/up kernel: the same result)
+        route_token(a.logits + (size_t)t * a.ls, a.ne, a.k, sel, wsel, (unsigned long long *)xsm, xsm + 512);
+        if (blockIdx.x == 0 && a.sel_out && tid < a.k) {
+            a.sel_out[t * a.k + tid] = sel[tid];
+            a.w_out[t * a.k + tid] = wsel[tid];
+        }
+    } else {
+        if (tid < a.k) {
+            sel[tid] = a.rsel[t * 16 + tid];
+            wsel[tid] = a.rw[t * 16 + tid];
+        }
+        __syncthreads();
     }
-    __syncthreads();
     const uint32_t own = owned_slots(sel, a.k, a.ne, a.ep);
     const int m = __popc(own);
     auto slot_at = [&](int j) {  // the j-th (from 0) set bit of own

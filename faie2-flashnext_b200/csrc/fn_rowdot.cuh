@@ -56,7 +56,10 @@ constexpr int XPAD = 36;  // floats per staged x group: 32 values, the two 16-va
 // denormals (denorm) the values scaled by 2^K_t with K_t = 124 - exponent(max_c |x[t][c]|) clamped to [22, 127]
 // (an exact power-of-two scaling; the products q * 2^-149 * x * 2^K_t then stay in the normal range) and
 // 2^(149 - K_t) at + 34. nt <= 32. Every thread calls this; it ends with a __syncthreads.
-__device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int nt, int G, bool denorm) {
+// nw (an RMSNorm weight, nullable): the values staged are x[t][c] * nw[c], and + 35 of group g holds the sum of the
+// squares of the raw x over the group's 32 values (fixed order) for norm_scale.
+__device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int nt, int G, bool denorm,
+                                        const float *nw = nullptr) {
     __shared__ int s_xmax[32];
     if (denorm) {
         if ((int)threadIdx.x < nt) s_xmax[threadIdx.x] = 0;
@@ -68,9 +71,30 @@ __device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int 
         float *dst = xsm + ((size_t)t * G + g) * XPAD;
         float4 v[4];
         float mx = 0.0f;
+        if (nw) {
+            // the group's sum of squares, by the h == 0 item over both halves (16 products each, in order)
+            if (h == 0) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 f = src[q];
+                    ss = __fmaf_rn(f.x, f.x, ss);
+                    ss = __fmaf_rn(f.y, f.y, ss);
+                    ss = __fmaf_rn(f.z, f.z, ss);
+                    ss = __fmaf_rn(f.w, f.w, ss);
+                }
+                dst[35] = ss;
+            }
+            const float4 *wv = (const float4 *)(nw + g * 32 + 16 * h);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 f = src[q], w = wv[q];
+                v[q] = make_float4(__fmul_rn(f.x, w.x), __fmul_rn(f.y, w.y), __fmul_rn(f.z, w.z), __fmul_rn(f.w, w.w));
+            }
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            v[q] = src[q];
+            if (!nw) v[q] = src[q];
             *(float4 *)(dst + 16 * h + 4 * q) = v[q];
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w))));
         }
@@ -95,6 +119,18 @@ __device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int 
     __syncthreads();
 }
 
+// RMSNorm scale of token t from stage_x's per-group sums of squares (stage_x with nw): rsqrt(sum / n + eps) with the
+// sum over groups in a fixed order (lane l: groups l, l + 32, ..; then a butterfly), so every warp of every CTA gets
+// the same value. Called by whole warps after stage_x.
+__device__ __forceinline__ float norm_scale(const float *xsm, int G, int t, int n, float eps) {
+    const int lane = threadIdx.x & 31;
+    float ss = 0.0f;
+    for (int g = lane; g < G; g += 32) ss = __fadd_rn(ss, xsm[((size_t)t * G + g) * XPAD + 35]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    return rsqrtf(ss / (float)n + eps);
+}
+
 // a lane's x slice in registers (one token): groups lr + LPR * i, i < GPL
 template <int LPR, int GPL> struct XReg {
     float2 v[GPL][16];
@@ -103,14 +139,29 @@ template <int LPR, int GPL> struct XReg {
     // Straight from x in global memory (16-byte aligned), by one warp whose lanes together hold every group of the
     // row (LPR == 32 and GPL == G / 32): the same values, half sums and power-of-two scaling (denorm) as stage_x,
     // with the row maximum taken over the warp instead of the block, so no block barrier is needed.
-    __device__ __forceinline__ void load_global(const float *x, int lr, bool denorm) {
-        float mx = 0.0f;
+    // nw (an RMSNorm weight, nullable): the values held are x * nw, and the return value is the RMSNorm scale
+    // rsqrt(sum x^2 / (32 G) + eps) (the sum in group order per lane, then a butterfly: the same in every warp); else 1.
+    __device__ __forceinline__ float load_global(const float *x, int lr, bool denorm, const float *nw = nullptr,
+                                                 float eps = 0.0f) {
+        float mx = 0.0f, ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < GPL; ++i) {
             const float4 *src = (const float4 *)(x + (size_t)(lr + LPR * i) * 32);
             float4 q[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) q[j] = src[j];
+            if (nw) {
+                const float4 *wv = (const float4 *)(nw + (size_t)(lr + LPR * i) * 32);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 f = q[j], w = wv[j];
+                    ss = __fmaf_rn(f.x, f.x, ss);
+                    ss = __fmaf_rn(f.y, f.y, ss);
+                    ss = __fmaf_rn(f.z, f.z, ss);
+                    ss = __fmaf_rn(f.w, f.w, ss);
+                    q[j] = make_float4(__fmul_rn(f.x, w.x), __fmul_rn(f.y, w.y), __fmul_rn(f.z, w.z), __fmul_rn(f.w, w.w));
+                }
+            }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float p[4];
@@ -128,7 +179,13 @@ template <int LPR, int GPL> struct XReg {
                 v[i][2 * j + 1] = make_float2(q[j].z, q[j].w);
             }
         }
-        if (!denorm) return;
+        float scale = 1.0f;
+        if (nw) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+            scale = rsqrtf(ss / (float)(32 * LPR * GPL) + eps);
+        }
+        if (!denorm) return scale;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         const int e = ((__float_as_int(mx) >> 23) & 255) - 127;
@@ -139,6 +196,7 @@ template <int LPR, int GPL> struct XReg {
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[i][j] = make_float2(__fmul_rn(v[i][j].x, sc), __fmul_rn(v[i][j].y, sc));
         iv = __int_as_float((149 - K + 127) << 23);
+        return scale;
     }
     __device__ __forceinline__ void load(const float *xsm, int lr) {
         iv = xsm[34];

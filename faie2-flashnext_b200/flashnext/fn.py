@@ -36,8 +36,28 @@ EXPORTS = [
     "fn_embed", "fn_rmsnorm", "fn_attn_decode", "fn_step_advance", "fn_gdn_reset",
     "fn_tc_create", "fn_tc_free", "fn_tc_gemv", "fn_test_tc_gemv", "fn_bench_tc_gemv",
     "fn_embed_batch", "fn_rmsnorm_rows", "fn_attn_decode_batch", "fn_step_advance_batch", "fn_gdn_create_batch",
-    "fn_gdn_run_batch", "fn_w_weights", "fn_w_prefetch_after", "fn_moe_prefetch_after",
+    "fn_gdn_run_batch", "fn_w_weights", "fn_w_prefetch_after", "fn_moe_prefetch_after", "fn_w_norm", "fn_moe_norm",
+    "fn_gemv_tune", "fn_moe_var", "fn_moe_override",
+    "fn_decoder_create", "fn_decoder_free", "fn_decoder_step", "fn_decoder_launches",
+    "fn_load", "fn_forward", "fn_reset", "fn_free", "fn_debug_layers", "fn_use_graphs", "fn_n_past", "fn_last_ms",
+    "fn_dev_gb", "fn_split", "fn_model_dims",
 ]
+
+
+class FnLayer(C.Structure):
+    """fn_layer_t (include/faie2fn.h): one layer of the decode step."""
+    _fields_ = [("kind", C.c_int), ("w_in", C.c_int * 3), ("w_in_rows", C.c_int * 3), ("w_out", C.c_int),
+                ("gdn", C.c_int), ("router", C.c_int), ("moe", C.c_int), ("norm1", C.c_void_p), ("norm2", C.c_void_p),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("Kc", C.c_void_p), ("Vc", C.c_void_p)]
+
+
+class FnModel(C.Structure):
+    """fn_model_t (include/faie2fn.h): the decode step's sizes, shared weights and device buffers."""
+    _fields_ = [(n, C.c_int) for n in ("D", "nkh", "nvh", "nh", "nkv", "ne", "vocab", "max_ctx")] + [
+        ("eps", C.c_float), ("embed_type", C.c_uint32), ("embed", C.c_void_p), ("head", C.c_int),
+        ("final_norm", C.c_void_p), ("inv_freq", C.c_void_p), ("fuse_norm", C.c_int), ("prefetch", C.c_int)] + [
+        (n, C.c_void_p) for n in ("hidden", "xnorm", "proj", "core", "Q", "att", "router_out", "logits", "tokens", "pos",
+                                  "next", "prompt_len")]
 
 
 class FN:
@@ -52,6 +72,9 @@ class FN:
         d.fn_early.argtypes = [C.c_int]
         d.fn_bench_hot.argtypes = [C.c_int]
         d.fn_gemv_override.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
+        d.fn_gemv_tune.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
+        d.fn_moe_var.argtypes = [C.c_int]
+        d.fn_moe_override.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
         d.fn_gemv_waves.argtypes = [C.c_int]
         d.fn_gemv_plan.argtypes = [C.c_uint32, C.c_int, C.c_int, I32]
         d.fn_test_dequant.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32]
@@ -102,6 +125,8 @@ class FN:
         d.fn_w_weights.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_uint64)]
         d.fn_w_prefetch_after.argtypes = [C.c_int, vp, C.c_uint64]
         d.fn_moe_prefetch_after.argtypes = [C.c_int, vp, C.c_uint64]
+        d.fn_w_norm.argtypes = [C.c_int, vp, C.c_float]
+        d.fn_moe_norm.argtypes = [C.c_int, vp, C.c_float]
         d.fn_tc_create.argtypes = [C.c_uint32, U8, C.c_int, C.c_int]
         d.fn_tc_free.argtypes = [C.c_int]
         d.fn_tc_gemv.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp]
@@ -113,6 +138,20 @@ class FN:
         d.fn_gdn_run_batch.argtypes = [C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, vp]
         d.fn_test_tc_gemv.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, F32]
         d.fn_bench_tc_gemv.argtypes = [C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float)]
+        # the reference's model hooks, bound as its fn.py binds them (flashnext/fn.py:27-33), and the rest
+        d.fn_load.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.c_int]
+        d.fn_forward.argtypes = [I32, C.c_int, C.c_void_p, C.c_void_p]
+        d.fn_debug_layers.argtypes = [C.c_void_p]
+        d.fn_dev_gb.restype = C.c_double
+        d.fn_dev_gb.argtypes = [C.c_int]
+        d.fn_last_ms.restype = C.c_double
+        d.fn_use_graphs.argtypes = [C.c_int]
+        d.fn_model_dims.argtypes = [I32]
+        d.fn_free.restype = None
+        d.fn_decoder_create.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        d.fn_decoder_free.argtypes = [C.c_int]
+        d.fn_decoder_step.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int64]
+        d.fn_decoder_launches.argtypes = [C.c_int]
         d.fn_moe_layer_static.argtypes = [C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp, vp,
                                           vp, vp, C.c_int, vp, vp, C.c_int, vp]
 
@@ -124,76 +163,104 @@ class FN:
         self.check(self.d.fn_set_device(int(dev)))
 
     # ---- the reference's model API (flashnext/fn.py:40-54; engine/faie2fn.cu fn_load .. fn_debug_layers) ----
-    # A GGUF model (runner.py: the qwen3next tensor names) loaded into the decode runner on the current GPU.
-    def load(self, shard1=None, shard2=None, max_ctx=32768, split=0, batch=0):
-        """fn_load: shard1 / shard2 default to SH1 / SH2 (env FN_SHARD1 / FN_SHARD2), so the reference's calls
-        (fn.load(max_ctx=8192, split=...)) run unchanged; shard2 is an optional second GGUF shard (None: one file);
-        split is accepted for the reference's signature (every layer stays on the current GPU); batch > 0 (<= 32) also
-        prepares forward_batch for that many independent sequences."""
-        from runner import Engine
+    # The C symbols fn_load .. fn_free (csrc/fn_runner.cu): a GGUF model with the qwen3next tensor names on the current
+    # GPU; the batched entry (forward_batch) is this layer's (runner.py BatchEngine).
+    def load(self, max_ctx=32768, split=0, *, shard1=None, shard2=None, batch=0):
+        """fn_load: the reference's call form load(max_ctx, split) reads SH1 / SH2 (env FN_SHARD1 / FN_SHARD2);
+        shard1 / shard2 (keywords) name the GGUF file (shard2 None: one file) or its two shards; split is accepted for
+        the reference's signature (every layer stays on the current GPU); batch > 0 (<= 32) also prepares
+        forward_batch for that many independent sequences."""
         if shard1 is None:
             shard1, shard2 = SH1, shard2 or SH2
         if not shard1:
             raise RuntimeError("no model file: pass shard1 or set FN_SHARD1")
+        if not 0 <= int(batch) <= 32:
+            raise RuntimeError("batch out of range (0..32)")
         self.free()
-        self.eng = Engine(self, str(shard1), str(shard2) if shard2 else None, int(max_ctx), int(split), int(batch))
+        self.check(self.d.fn_load(str(shard1).encode(), str(shard2).encode() if shard2 else None, int(max_ctx),
+                                  int(split)))
+        if batch:
+            from runner import BatchEngine
+            try:
+                self.beng = BatchEngine(self, str(shard1), str(shard2) if shard2 else None, int(max_ctx), int(batch))
+            except BaseException:
+                self.free()
+                raise
 
-    def _engine(self):
-        if getattr(self, "eng", None) is None:
-            raise RuntimeError("not loaded")
-        return self.eng
+    def dims(self):
+        """{vocab, D, layers, max_ctx} of the loaded model."""
+        out = np.zeros(4, np.int32)
+        self.check(self.d.fn_model_dims(out))
+        return dict(zip(["vocab", "D", "layers", "max_ctx"], out.tolist()))
 
     def reset(self):
-        self._engine().reset()
+        self.check(self.d.fn_reset())
+        if getattr(self, "beng", None) is not None:
+            self.beng.reset()
 
     def forward(self, tokens, logits=False):
         """argmax ids int32 [nt] (and logits float32 [nt, vocab] when logits=True), nt = len(tokens) in 1..8."""
-        e = self._engine()
         t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
-        am = np.zeros(len(t), np.int32)
-        lg = np.zeros((len(t), e.cfg["vocab"]), np.float32) if logits else None
-        e.forward(t, lg, am)
-        return (am, lg) if logits else am
+        am = np.zeros(max(1, len(t)), np.int32)
+        lg = np.zeros((len(t), self.dims()["vocab"]), np.float32) if logits and self.d.fn_n_past() >= 0 else None
+        self.check(self.d.fn_forward(t, len(t), lg.ctypes.data if lg is not None else None, am.ctypes.data))
+        self._last_batch = False
+        return (am[:len(t)], lg) if logits else am[:len(t)]
 
     def forward_batch(self, tokens, logits=False):
         """The batched entry for independent sequences: tokens [batch][nt] (nt 1..8) -> argmax ids int32 [batch][nt]
         (and logits float32 [batch][nt][vocab]); the sequences advance together from n_past_batch()."""
-        e = self._engine()
+        e = getattr(self, "beng", None)
+        if e is None:
+            raise RuntimeError("not loaded" if self.d.fn_n_past() < 0 else "batch not loaded (load with batch > 0)")
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         am = np.zeros(t.shape, np.int32) if t.ndim == 2 else None
         lg = np.zeros(t.shape + (e.cfg["vocab"],), np.float32) if logits and t.ndim == 2 else None
         e.forward_batch(t, lg if logits else None, am)
+        self._last_batch = True
         return (am, lg) if logits else am
 
     def n_past_batch(self) -> int:
-        return self.eng.n_past_batch if getattr(self, "eng", None) else -1
+        e = getattr(self, "beng", None)
+        return e.n_past_batch if e is not None else -1
 
     def debug_layers(self, buf):
-        self._engine().debug_layers(buf)
+        """fn_debug_layers: buf float32 [layers][nt][D] (host) receives the residual after every layer of the next
+        forwards (they then step eagerly); None turns it off. The buffer is kept alive here while set."""
+        if buf is not None:
+            a = buf
+            if (not isinstance(a, np.ndarray) or a.dtype != np.float32 or a.ndim != 3 or not a.flags.c_contiguous or
+                    (self.d.fn_n_past() >= 0 and (a.shape[0] != self.dims()["layers"] or a.shape[2] != self.dims()["D"]))):
+                raise RuntimeError("debug buffer: float32 [layers][nt][D] expected")
+        self.check(self.d.fn_debug_layers(buf.ctypes.data if buf is not None else None))
+        self._dbg = buf
 
     def use_graphs(self, on):
-        self._engine().use_graphs = bool(on)
+        self.check(self.d.fn_use_graphs(int(bool(on))))
+        if getattr(self, "beng", None) is not None:
+            self.beng.use_graphs = bool(on)
 
     def n_past(self) -> int:
-        return self.eng.n_past if getattr(self, "eng", None) else -1
+        return self.d.fn_n_past()
 
     def last_ms(self) -> float:
-        return self.eng.last_ms if getattr(self, "eng", None) else -1.0
+        e = getattr(self, "beng", None)
+        return e.last_ms if e is not None and getattr(self, "_last_batch", False) else self.d.fn_last_ms()
 
     def split(self) -> int:
-        return self.eng.split if getattr(self, "eng", None) else -1
+        return self.d.fn_split()
 
     def dev_gb(self, dv=0) -> float:
         """Weight bytes of the loaded model on device dv, in GB (-1 when nothing is loaded)."""
-        if getattr(self, "eng", None) is None:
-            return -1.0
-        return self.eng.bytes / 1e9 if dv == 0 else 0.0
+        return self.d.fn_dev_gb(int(dv))
 
     def free(self):
         """fn_free: release the loaded model (nothing loaded: no-op)."""
-        e, self.eng = getattr(self, "eng", None), None
+        e, self.beng = getattr(self, "beng", None), None
         if e is not None:
             e.free()
+        self.d.fn_free()
+        self._dbg = None
 
     # ---- the reference's unit-test hooks (flashnext/fn.py:56-66) ----
     def dequant(self, qtype, raw, rows, cols):
@@ -425,9 +492,26 @@ class FN:
     def moe_prefetch_after(self, h, ptr, nbytes):
         self.check(self.d.fn_moe_prefetch_after(h, C.c_void_p(ptr or None), nbytes))
 
-    def gemv_override(self, warps=-1, ring_kb=0, stage_kb=0, ctas_per_sm=0):
-        """Plan settings for weights created from now on (engine/faie2fn.cu:2786-2791; warps 0 = by weight size)."""
-        self.d.fn_gemv_override(warps, ring_kb, stage_kb, ctas_per_sm)
+    def w_norm(self, h, w_ptr, eps=1e-6):
+        """RMSNorm folded into GEMV handle h (w_ptr: device norm weight; 0 turns it off)."""
+        self.check(self.d.fn_w_norm(h, C.c_void_p(w_ptr or None), eps))
+
+    def moe_norm(self, h, w_ptr, eps=1e-6):
+        """RMSNorm folded into MoE layer h (w_ptr: device norm weight; 0 turns it off)."""
+        self.check(self.d.fn_moe_norm(h, C.c_void_p(w_ptr or None), eps))
+
+    def gemv_override(self, wpt=0, ks=0, tb=0, warps_per_sm=16):
+        """The reference's plan override (engine/faie2fn.cu:2786-2791): tb threads per CTA (0: automatic) and the
+        target warps per SM for weights created from now on; wpt and ks have no counterpart here."""
+        self.d.fn_gemv_override(wpt, ks, tb, warps_per_sm)
+
+    def gemv_tune(self, warps=-1, ring_kb=0, stage_kb=0, ctas_per_sm=0):
+        """This plan's own settings for weights created from now on (warps 0 = by weight size, < 0 keeps)."""
+        self.d.fn_gemv_tune(warps, ring_kb, stage_kb, ctas_per_sm)
+
+    def moe_var(self, v):
+        """MoE variant (engine/faie2fn.cu:2799): 0 = a routing kernel, 1 = routed inside the expert kernels."""
+        self.d.fn_moe_var(v)
 
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))

@@ -21,14 +21,15 @@ DS, HD = 128, 256
 
 class DecodeModel:
     def __init__(self, fn, cfg: dict, W: dict, max_ctx: int = 512, logits: bool = False, warps: int = 16,
-                 stack: bool = True, prefetch: bool = True):
+                 stack: bool = True, prefetch: bool = True, fuse_norm: bool = True):
         """warps: GEMV warps per CTA of the model's weights; stack: the projections that read the same input as one
         GEMV each ([q k v z | alpha beta], [q gate | k | v]) rather than one GEMV per weight; prefetch: each
         projection brings the step's next dense weight into L2 while it runs (input -> output projection -> router,
-        the MoE layer -> the next layer's input projection)."""
+        the MoE layer -> the next layer's input projection); fuse_norm: every RMSNorm folded into the GEMVs and MoE
+        layer that read its output (fn_w_norm / fn_moe_norm: no norm launches) rather than run as its own kernel."""
         import torch
         self.fn, self.cfg, self.max_ctx = fn, cfg, max_ctx
-        self.stack = stack
+        self.stack, self.fuse_norm = stack, fuse_norm
         dev = torch.device("cuda", torch.cuda.current_device())
         f32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)  # noqa: E731
         nkh, nvh, nh, nkv = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
@@ -38,28 +39,51 @@ class DecodeModel:
         self.handles, self.moes, self.gdns = [], [], []
         # a decode step is a chain of dependent GEMVs at batch 1: each is latency-bound, so its CTAs run 16 warps
         # (more loads and decodes in flight per SM) rather than the few that let independent GEMVs share an SM
-        fn.gemv_override(warps=warps)
+        fn.gemv_tune(warps=warps)
         try:
             self._build(fn, cfg, W, max_ctx, logits, dev, f32)
         except BaseException:
             self.free()  # a weight the engine refused: release what was uploaded before it
             raise
         finally:
-            fn.gemv_override(warps=0)
-        if prefetch:
-            self._prefetch_hints()
+            fn.gemv_tune(warps=0)
+        try:
+            self._create_decoder(prefetch, fuse_norm)
+        except BaseException:
+            self.free()
+            raise
 
-    def _prefetch_hints(self):
-        fn = self.fn
-        first = lambda w: w[0][0] if isinstance(w, list) else w  # noqa: E731
-        last = lambda w: w[-1][0] if isinstance(w, list) else w  # noqa: E731
-        for i, L in enumerate(self.layers):
-            inp, out = (L["w_in"], L["w_out"]) if L["kind"] == "G" else (L["w_qkv"], L["w_o"])
-            fn.w_prefetch_after(last(inp), *fn.w_weights(out))
-            fn.w_prefetch_after(out, *fn.w_weights(L["router"]))
-            if i + 1 < len(self.layers):
-                nxt = self.layers[i + 1]
-                fn.moe_prefetch_after(L["moe"], *fn.w_weights(first(nxt["w_in"] if nxt["kind"] == "G" else nxt["w_qkv"])))
+    def _create_decoder(self, prefetch, fuse_norm):
+        """The step itself is the library's (fn_decoder_create / fn_decoder_step, csrc/fn_decoder.cu): the handles and
+        buffers built here, described as fn_model_t / fn_layer_t."""
+        import ctypes as C
+        from fn import FnLayer, FnModel
+        fn, cfg = self.fn, self.cfg
+        p = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        Ls = (FnLayer * len(self.layers))()
+        for o, L in zip(Ls, self.layers):
+            w_in = L["w_in"] if L["kind"] == "G" else L["w_qkv"]
+            ins = w_in if isinstance(w_in, list) else [(w_in, self.n_in if L["kind"] == "G" else self.n_qkv)]
+            o.kind = 0 if L["kind"] == "G" else 1
+            for i, (h, rows) in enumerate(ins):
+                o.w_in[i], o.w_in_rows[i] = h, rows
+            o.w_out = L["w_out"] if L["kind"] == "G" else L["w_o"]
+            o.gdn = L.get("gdn", 0)
+            o.router, o.moe = L["router"], L["moe"]
+            o.norm1, o.norm2 = p(L["norm1"]), p(L["norm2"])
+            if L["kind"] == "A":
+                o.q_norm, o.k_norm, o.Kc, o.Vc = p(L["q_norm"]), p(L["k_norm"]), p(L["Kc"]), p(L["Vc"])
+        m = FnModel(D=cfg["D"], nkh=cfg["nkh"], nvh=cfg["nvh"], nh=cfg["nh"], nkv=cfg["nkv"], ne=cfg["ne"],
+                    vocab=cfg["vocab"], max_ctx=self.max_ctx, eps=cfg["eps"], embed_type=cfg["embed"], embed=p(self.E),
+                    head=self.head, final_norm=p(self.final_norm), inv_freq=p(self.inv_freq),
+                    fuse_norm=int(fuse_norm), prefetch=int(prefetch), hidden=p(self.h), xnorm=p(self.x),
+                    proj=p(self.proj), core=p(self.core), Q=p(self.Q), att=p(self.att), router_out=p(self.lr),
+                    logits=p(self.logits), tokens=p(self.tokens), pos=p(self.pos), next=p(self.next),
+                    prompt_len=p(self.plen))
+        h = fn.d.fn_decoder_create(C.byref(m), Ls, len(self.layers))
+        if h < 0:
+            raise RuntimeError(fn.d.fn_error().decode())
+        self.dec = h
 
     def _build(self, fn, cfg, W, max_ctx, logits, dev, f32):
         import torch
@@ -116,55 +140,21 @@ class DecodeModel:
         self.handles.append(h)
         return h
 
-    def launch_step(self, s: int, after_layer=None):
-        """Launch one decode step on stream s (device pointers only; capturable). after_layer(l), eager steps only:
-        called once layer l's launches are enqueued (the residual h then holds that layer's output)."""
-        fn, cfg = self.fn, self.cfg
-        d, nvh, nh, nkv, eps = cfg["D"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["eps"]
-        p = lambda t: t.data_ptr()  # noqa: E731
-        fn.embed(cfg["embed"], p(self.E), d, p(self.tokens), p(self.pos), p(self.h), s)
-        h, x = p(self.h), p(self.x)
-
-        def gemv_normed(wh, norm, y):  # y = W rmsnorm(h); a list of (handle, rows): their outputs one after another
-            fn.rmsnorm(h, p(norm), x, d, eps, s)
-            off = 0
-            for w_, rows in (wh if isinstance(wh, list) else [(wh, 0)]):
-                fn.w_gemv(w_, x, d, y + 4 * off, 0, 1, 0, s)
-                off += rows
-
-        for li, L in enumerate(self.layers):
-            pr = p(self.proj)
-            if L["kind"] == "G":
-                gemv_normed(L["w_in"], L["norm1"], pr)
-                # the layer's previous core launch is a whole step back: its state is read before the wait
-                qkv, z, ab = pr, pr + 4 * self.convch, pr + 4 * (self.convch + nvh * DS)
-                fn.gdn_run(L["gdn"], qkv, self.convch, z, nvh * DS, ab, 2 * nvh, p(self.core), nvh * DS, 1, 1, s)
-                fn.w_gemv(L["w_out"], p(self.core), nvh * DS, h, 0, 1, 1, s)  # h += W_out core
-            else:
-                gemv_normed(L["w_qkv"], L["norm1"], pr)
-                qg, k, v = pr, pr + 4 * nh * 2 * HD, pr + 4 * (nh * 2 * HD + nkv * HD)
-                fn.attn_decode(qg, k, v, p(L["q_norm"]), p(L["k_norm"]), p(self.inv_freq),
-                               p(self.Q), p(L["Kc"]), p(L["Vc"]), p(self.att), p(self.pos), nh, nkv, self.max_ctx, eps, s)
-                fn.w_gemv(L["w_o"], p(self.att), nh * HD, h, 0, 1, 1, s)  # h += W_o o
-            fn.rmsnorm(h, p(L["norm2"]), x, d, eps, s)
-            fn.w_gemv(L["router"], x, d, p(self.lr), 0, 1, 0, s)
-            fn.moe_run(L["moe"], p(self.lr), cfg["ne"] + 1, x, h, 1, 1, s)  # h += moe(x)
-            if after_layer is not None:
-                after_layer(li)
-        fn.rmsnorm(h, p(self.final_norm), x, d, eps, s)
-        fn.w_gemv_argmax(self.head, x, d, p(self.logits) if self.logits is not None else 0, 0, 1, 0, 0,
-                         p(self.next), 0, s)
-        fn.step_advance(p(self.pos), p(self.tokens), p(self.next), p(self.plen), self.max_ctx, s)
+    def launch_step(self, s: int, dbg=None):
+        """Launch one decode step on stream s (device pointers only; capturable). dbg (host float32 [layers][D],
+        eager steps only): the residual after every layer."""
+        import ctypes as C
+        self.fn.check(self.fn.d.fn_decoder_step(self.dec, C.c_void_p(s), dbg.ctypes.data if dbg is not None else None,
+                                                self.cfg["D"]))
 
     def launches_per_step(self) -> int:
-        """Kernel launches of one step: the embedding; per layer a norm, the input GEMV (stacked q k v z | alpha beta,
-        or q gate | k | v; one per weight unstacked), the DeltaNet core or the two attention kernels, the output GEMV,
-        a norm, the router GEMV and the MoE layer's three kernels (routing, gate/up, down + combine); the final norm,
-        the lm_head with its argmax and the step counter."""
-        n = 1 + 3
-        for L in self.layers:
-            w_in = L["w_in"] if L["kind"] == "G" else L["w_qkv"]
-            n += 1 + (len(w_in) if isinstance(w_in, list) else 1) + (1 if L["kind"] == "G" else 2) + 1 + 1 + 1 + 3
+        """Kernel launches of one step: the embedding; per layer the input GEMV(s), the DeltaNet core or the two
+        attention kernels, the output GEMV, the router GEMV and the MoE layer's two kernels (three with a routing
+        kernel, fn_moe_var(0)), plus two norms unless they are folded; the lm_head with its argmax and the step
+        counter (and the final norm unless folded)."""
+        n = self.fn.d.fn_decoder_launches(self.dec)
+        if n < 0:
+            raise RuntimeError(self.fn.d.fn_error().decode())
         return n
 
     def start(self, prompt, stream=None):
@@ -234,6 +224,9 @@ class DecodeModel:
 
     def free(self):
         self.graph = None
+        if getattr(self, "dec", 0):
+            self.fn.d.fn_decoder_free(self.dec)
+            self.dec = 0
         for h in self.handles:
             self.fn.w_free(h)
         for m in self.moes:

@@ -1,7 +1,9 @@
-"""The model-level API of the reference (fn_load / fn_reset / fn_forward / fn_n_past / fn_last_ms / fn_dev_gb /
-fn_split / fn_use_graphs / fn_debug_layers / fn_free, engine/faie2fn.cu:2466-2492 and :2680-2740, wrapped by
-flashnext/fn.py FN.load / reset / forward): a GGUF model file loaded into the config-5 decode runner (model.py
-DecodeModel) and stepped from host token ids.
+"""GGUF model files for the model-level API: save_model writes a model of the config-5 structure (synth.model_weights)
+as a GGUF v3 file; load_model reads one back into that layout (the CPU-side twin of the library's fn_load,
+csrc/fn_runner.cu, with the same checks and messages); BatchEngine is forward_batch's runner (the batched entry for
+independent sequences on the tensor-core path). The batch-1 model API itself (fn_load / fn_reset / fn_forward /
+fn_n_past / fn_last_ms / fn_dev_gb / fn_split / fn_use_graphs / fn_debug_layers / fn_free, engine/faie2fn.cu:2466-2492
+and :2680-2740) is the library's.
 
 Files: GGUF v3 (gguf_file.py) with the qwen3next tensor names the reference's loader reads (engine/faie2fn.cu:2617-2657):
 token_embd / output / output_norm; per layer blk.N.attn_norm and post_attention_norm; the gated DeltaNet's attn_qkv,
@@ -14,9 +16,8 @@ experts per token from the metadata key <arch>.expert_used_count; eps and the Ro
 <arch>.attention.layer_norm_rms_epsilon and <arch>.rope.freq_base. The reference's own model adds tensors this runner
 has no kernels for (hyper-connections, the PLE n-gram table, the attention indexer); such files are refused by name.
 
-forward(tokens) follows the reference's contract (:2466-2490): 1..8 tokens per call (MAXT, :67), appended at n_past
-(an error once n_past + nt would pass max_ctx), each token's greedy next id returned (and its logits when asked), the
-host wall time of the call kept as last_ms. Tokens are stepped one position at a time through the step's CUDA graph.
+forward_batch follows forward's contract (:2466-2490) per sequence: 1..8 tokens per call (MAXT, :67), appended at
+n_past_batch (an error once it would pass max_ctx), each token's greedy next id returned (and its logits when asked).
 """
 
 from __future__ import annotations
@@ -27,7 +28,7 @@ import time
 import numpy as np
 
 import gguf_file as gguf
-from model import DS, HD, BatchDecodeModel, DecodeModel
+from model import DS, HD, BatchDecodeModel
 from synth import TYPES, layer_kind
 
 ARCH = "qwen3next"
@@ -238,113 +239,52 @@ def load_model(shard1: str, shard2: str | None = None):
     return cfg, W, nbytes
 
 
-class Engine:
-    """A loaded model: fn_load's engine (engine/faie2fn.cu:2524-2680) on one GPU. Every call raises RuntimeError with
-    the reference's message on a misuse (nt out of range, context full)."""
+class BatchEngine:
+    """forward_batch's runner (the batched entry for independent sequences, which the reference lacks): the GGUF model
+    loaded again into the tensor-core BatchDecodeModel on the current GPU, `batch` sequences stepping together from
+    position n_past_batch. The batch-1 model API is the library's (fn_load .. fn_free, csrc/fn_runner.cu)."""
 
-    def __init__(self, fn, shard1: str, shard2: str | None = None, max_ctx: int = 32768, split: int = 0,
-                 batch: int = 0):
+    def __init__(self, fn, shard1: str, shard2: str | None = None, max_ctx: int = 32768, batch: int = 8):
         import torch
         if max_ctx < 1:
             raise RuntimeError("max_ctx out of range")
-        if not 0 <= batch <= 32:
-            raise RuntimeError("batch out of range (0..32)")
+        if not 1 <= batch <= 32:
+            raise RuntimeError("batch out of range (1..32)")
         try:
-            cfg, W, self.bytes = load_model(shard1, shard2)
+            cfg, W, _ = load_model(shard1, shard2)
         except (OSError, gguf.GGUFError) as e:
             raise RuntimeError(str(e)) from e
-        self.cfg, self.fn = cfg, fn
-        # the reference splits the layers over two GPUs at `split` (<= 0: by free memory); this runner keeps every
-        # layer on the current GPU, so split reads back as the layer count
-        self.split = cfg["layers"]
-        self.model = DecodeModel(fn, cfg, W, max_ctx=max_ctx, logits=True)
-        self.max_ctx, self.n_past, self.last_ms = max_ctx, 0, -1.0
-        self.use_graphs, self.dbg = True, None
+        self.cfg, self.fn, self.max_ctx = cfg, fn, max_ctx
+        self.n_past_batch, self.last_ms, self.use_graphs, self.blg = 0, -1.0, True, None
         self.stream = torch.cuda.Stream()
-        self.model.capture(self.stream)
-        self.am = torch.zeros(MAXT, dtype=torch.int32).pin_memory()
-        self.lg = torch.zeros(MAXT, cfg["vocab"], dtype=torch.float32).pin_memory()
-        # batch > 0: `batch` independent sequences stepping together on the tensor-core path (forward_batch)
-        self.bmodel, self.n_past_batch, self.blg = None, 0, None
-        if batch:
-            try:
-                self.bmodel = BatchDecodeModel(fn, cfg, W, batch, max_ctx=max_ctx)
-            except ValueError as e:
-                self.model.free()
-                raise RuntimeError(str(e)) from e
-            self.bmodel.capture(self.stream)
-            self.bam = torch.zeros(MAXT, batch, dtype=torch.int32).pin_memory()
+        try:
+            self.bmodel = BatchDecodeModel(fn, cfg, W, batch, max_ctx=max_ctx)
+        except ValueError as e:
+            raise RuntimeError(str(e)) from e
+        self.bmodel.capture(self.stream)
+        self.bam = torch.zeros(MAXT, batch, dtype=torch.int32).pin_memory()
         self.reset()
 
     def reset(self):
-        """fn_reset (:2703-2716): DeltaNet states and conv histories zeroed, position 0, n_past 0 (the batched
-        sequences too)."""
-        import torch
-        m = self.model
-        with torch.cuda.stream(self.stream):
-            m.tokens.zero_()
-            m.pos.zero_()
-            m.plen.zero_()
-        for g in m.gdns:
-            self.fn.gdn_reset(g, self.stream.cuda_stream)
-        if self.bmodel is not None:
-            b = self.bmodel
-            with torch.cuda.stream(self.stream):
-                b.tokens.zero_()
-                b.pos.zero_()
-                b.plen.zero_()
-            for g in b.gdns:
-                self.fn.gdn_reset(g, self.stream.cuda_stream)
-        self.fn.sync(self.stream.cuda_stream)
-        self.n_past = self.n_past_batch = 0
-
-    def forward(self, tokens, logits=None, argmax=None):
-        """fn_forward (:2466-2490): tokens (1..8 int32 ids) at positions n_past.. ; argmax[i] = the greedy next id
-        after token i; logits[i] = its logits (float32 [nt, vocab], when given)."""
-        import torch
-        t = np.ascontiguousarray(tokens, np.int32).reshape(-1)
-        nt = len(t)
-        if nt < 1 or nt > MAXT:
-            raise RuntimeError("nt out of range")
-        if self.n_past + nt > self.max_ctx:
-            raise RuntimeError("context full")
-        if t.min() < 0 or t.max() >= self.cfg["vocab"]:
-            raise RuntimeError("token id out of range")
-        t0 = time.perf_counter()
-        m, s = self.model, self.stream
-        graphs = self.use_graphs and self.dbg is None
-        with torch.cuda.stream(s):
-            m.tokens[self.n_past:self.n_past + nt].copy_(torch.from_numpy(t), non_blocking=False)
-            m.plen.fill_(self.n_past + nt)  # the step keeps these ids: it writes its argmax only past the prompt
-            for i in range(nt):
-                if graphs:
-                    m.graph.replay()
-                else:
-                    hook = None
-                    if self.dbg is not None:
-                        hook = lambda l, i=i: self.dbg[l, i].copy_(m.h.cpu())  # noqa: E731
-                    m.launch_step(s.cuda_stream, after_layer=hook)
-                self.am[i].copy_(m.next[0], non_blocking=True)
-                if logits is not None:
-                    self.lg[i].copy_(m.logits, non_blocking=True)
-        self.fn.sync(s.cuda_stream)
-        if argmax is not None:
-            argmax[:nt] = self.am[:nt].numpy()
-        if logits is not None:
-            logits[:nt] = self.lg[:nt].numpy()
-        self.n_past += nt
-        self.last_ms = (time.perf_counter() - t0) * 1e3
-        return 0
-
-    def forward_batch(self, tokens, logits=None, argmax=None):
-        """The batched entry: tokens int32 [batch][nt] (nt 1..8), one row per sequence, all sequences at position
-        n_past_batch (their own states and caches, apart from forward's sequence); argmax[b][i] = sequence b's greedy
-        next id after its token i, logits[b][i] its logits (tensor-core GEMVs: within 1e-4 of max |y| per projection
-        of the CUDA-core path). Same errors as forward, plus "batch not loaded" and a shape check."""
+        """fn_reset for the batched sequences: their DeltaNet states and conv histories zeroed, position 0."""
         import torch
         b = self.bmodel
-        if b is None:
-            raise RuntimeError("batch not loaded (load with batch > 0)")
+        with torch.cuda.stream(self.stream):
+            b.tokens.zero_()
+            b.pos.zero_()
+            b.plen.zero_()
+        for g in b.gdns:
+            self.fn.gdn_reset(g, self.stream.cuda_stream)
+        self.fn.sync(self.stream.cuda_stream)
+        self.n_past_batch = 0
+
+    def forward_batch(self, tokens, logits=None, argmax=None):
+        """tokens int32 [batch][nt] (nt 1..8), one row per sequence, all sequences at position n_past_batch (their own
+        states and caches); argmax[b][i] = sequence b's greedy next id after its token i, logits[b][i] its logits
+        (tensor-core GEMVs: within 1e-4 of max |y| per projection of the CUDA-core path). forward's errors, plus a
+        shape check."""
+        import torch
+        b = self.bmodel
         t = np.ascontiguousarray(tokens, np.int32)
         if t.ndim != 2 or t.shape[0] != b.B:
             raise RuntimeError(f"tokens must be [{b.B}][nt]")
@@ -379,19 +319,5 @@ class Engine:
         self.last_ms = (time.perf_counter() - t0) * 1e3
         return 0
 
-    def debug_layers(self, buf):
-        """fn_debug_layers (:2739-2743): buf float32 [layers][nt][D] (host) receives h after every layer of the next
-        forwards (their steps then run eagerly); None turns it off."""
-        import torch
-        if buf is None:
-            self.dbg = None
-            return
-        a = np.asarray(buf)
-        if a.dtype != np.float32 or a.ndim != 3 or a.shape[0] != self.cfg["layers"] or a.shape[2] != self.cfg["D"]:
-            raise RuntimeError("debug buffer: float32 [layers][nt][D] expected")
-        self.dbg = torch.from_numpy(a)
-
     def free(self):
-        self.model.free()
-        if self.bmodel is not None:
-            self.bmodel.free()
+        self.bmodel.free()

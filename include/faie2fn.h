@@ -10,9 +10,8 @@
  * IQ2_XS=17 IQ3_XXS=18 IQ4_NL=20 IQ3_S=21 IQ2_S=22 IQ4_XS=23 BF16=30 Q2_0=42.
  *
  * The reference's model hooks (fn_load, fn_reset, fn_forward, fn_debug_layers, fn_use_graphs, fn_n_past,
- * fn_last_ms, fn_dev_gb, fn_split, fn_free; engine/faie2fn.cu:2466-2743) are not symbols of this library: the decode
- * runner they drive is built in the host layer from the entry points below, so they are the methods of the same
- * names on flashnext/fn.py's FN (flashnext/runner.py: GGUF files, same argument meaning and error messages).
+ * fn_last_ms, fn_dev_gb, fn_split, fn_free; engine/faie2fn.cu:2466-2743) are symbols here too, with the same
+ * signatures: a GGUF file (qwen3next tensor names) loaded into the decode step below on the current GPU.
  */
 #ifndef FAIE2FN_H
 #define FAIE2FN_H
@@ -38,11 +37,19 @@ void fn_pdl(int on);
 void fn_early(int on);
 /* 1: fn_bench_gemv replays one hot copy without an L2 flush. Replaces fn_bench_hot (engine/faie2fn.cu:2822). */
 void fn_bench_hot(int on);
-/* GEMV plan overrides for sweeps: warps per CTA (0: automatic by weight size, < 0 keeps), shared-memory ring KiB
- * (all warps' rings), stage KiB (unused by the per-warp rings; kept for the signature), CTAs per SM (> 0 sets).
- * Replaces fn_gemv_override(wpt, ks, tb, warps_per_sm) (engine/faie2fn.cu:2786-2791); the B200 plan has no split-K,
- * so its knobs differ. */
-void fn_gemv_override(int warps, int ring_kb, int stage_kb, int ctas_per_sm);
+/* The reference's GEMV plan override for weights planned from now on (engine/faie2fn.cu:2786-2791), same arguments:
+ * tb = threads per CTA (0: automatic), warps_per_sm = target warps per SM (default 16). wpt and ks (weights per
+ * thread, split-K) have no counterpart in this plan (a row never spans warps): accepted and ignored. */
+void fn_gemv_override(int wpt, int ks, int tb, int warps_per_sm);
+/* This plan's own knobs for sweeps: warps per CTA (0: automatic by weight size, < 0 keeps), shared-memory ring KiB
+ * (all warps' rings), stage KiB (unused by the per-warp rings), CTAs per SM (> 0 sets). No reference counterpart. */
+void fn_gemv_tune(int warps, int ring_kb, int stage_kb, int ctas_per_sm);
+/* MoE layer variant, the reference's A/B switch (engine/faie2fn.cu:2799): 0 (default) = a routing kernel before
+ * gate/up, 1 = one token on one GPU routed inside the gate/up and down kernels. */
+void fn_moe_var(int v);
+/* The reference's routed-expert launch shapes (engine/faie2fn.cu:2801-2806); the B200 MoE kernels size themselves
+ * from the layer's shape and the SM count: accepted and ignored. */
+void fn_moe_override(int gu_wpt, int gu_tb, int dn_wpt, int dn_tb);
 /* CTAs per SM of the GEMV grid. Replaces fn_gemv_waves (engine/faie2fn.cu:2793). */
 void fn_gemv_waves(int ctas_per_sm);
 /* Plan of a rows x cols weight: out[7] = {lanes per row, groups per lane, rows per stage, ring slots, CTAs,
@@ -273,6 +280,78 @@ int fn_w_weights(int h, const void **ptr, uint64_t *bytes);
  * down to 16. */
 int fn_w_prefetch_after(int h, const void *ptr, uint64_t bytes);
 int fn_moe_prefetch_after(int h, const void *ptr, uint64_t bytes);
+/* RMSNorm folded into the consumer (the reference launches k_groupnorm before each normed GEMV / MoE layer,
+ * engine/faie2fn.cu:1222-1235 and its callers :2380-2447): from now on GEMV handle h computes
+ * y[t] = rsqrt(mean x[t]^2 + eps) (W . (x[t] * w)) from the raw x, and MoE layer h takes rmsnorm(x) * w as its input.
+ * w: the norm weight (cols / d floats of device memory, 16-byte aligned, kept by reference); NULL turns it off. */
+int fn_w_norm(int h, const float *w, float eps);
+int fn_moe_norm(int h, const float *w, float eps);
+
+/* ---- the decode step (the reference's layer_forward + forward, engine/faie2fn.cu:2370-2490) --------------------
+ * One step of the hybrid MoE decoder over resident handles (fn_w_create, fn_gdn_create, fn_moe_create) and device
+ * buffers the caller owns: the embedding row of tokens[*pos], per layer the input projection, the gated-DeltaNet core
+ * or the gated attention, the output projection adding into the residual, the router and the MoE layer adding into the
+ * residual; the lm_head with its fused argmax into *next; *pos += 1 and, past the prompt, tokens[*pos] = *next. */
+typedef struct fn_layer_t {
+    int kind;                      /* 0: gated DeltaNet layer, 1: gated attention layer */
+    int w_in[3];                   /* input projection GEMV handle(s), outputs one after another (unused: 0):
+                                    * DeltaNet [q k v z | alpha beta], attention [q gate | k | v] */
+    int w_in_rows[3];              /* rows of each */
+    int w_out;                     /* output projection (its result is added into the residual) */
+    int gdn;                       /* DeltaNet core (kind 0) */
+    int router;                    /* router GEMV: ne expert rows, then the shared-expert gate row */
+    int moe;                       /* MoE layer */
+    const float *norm1, *norm2;    /* RMSNorm weights before the mixer and before the MoE layer [D] */
+    const float *q_norm, *k_norm;  /* attention q / k head norms [256] (kind 1) */
+    float *Kc, *Vc;                /* attention caches [max_ctx][nkv][256] (kind 1) */
+} fn_layer_t;
+typedef struct fn_model_t {
+    int D, nkh, nvh, nh, nkv, ne, vocab, max_ctx;
+    float eps;
+    uint32_t embed_type;
+    const uint8_t *embed;          /* token embedding, GGUF rows [vocab] */
+    int head;                      /* lm_head GEMV handle */
+    const float *final_norm;       /* [D] */
+    const float *inv_freq;         /* RoPE inverse frequencies [32] (attention layers) */
+    int fuse_norm;                 /* 1: every RMSNorm folded into its consumers (fn_w_norm / fn_moe_norm); 0: launched */
+    int prefetch;                  /* 1: L2 prefetch hints along the chain (fn_w_prefetch_after) */
+    float *hidden, *xnorm;         /* residual [D]; normed input [D] (fuse_norm 0 only) */
+    float *proj, *core, *Q, *att;  /* input projection output, DeltaNet output [nvh 128], attention q / output [nh 256] */
+    float *router_out;             /* [ne + 1] */
+    float *logits;                 /* [vocab], nullable (not written) */
+    int *tokens, *pos, *next, *prompt_len;  /* [max_ctx], position, argmax, prompt length */
+} fn_model_t;
+/* Create a step (validates, and sets the norm folding and prefetch hints on the handles, which must belong to this
+ * step alone); a handle >= 1 or -1. No reference counterpart as a symbol (the reference's step is inside fn_forward). */
+int fn_decoder_create(const fn_model_t *m, const fn_layer_t *layers, int n_layers);
+int fn_decoder_free(int h);
+/* One step on a stream (capturable). dbg (host, nullable): the residual after layer l copied to dbg + l * dbg_stride. */
+int fn_decoder_step(int h, void *stream, float *dbg, int64_t dbg_stride);
+/* Kernel launches of one step. */
+int fn_decoder_launches(int h);
+
+/* ---- the reference's model hooks (engine/faie2fn.cu:2497-2743) ------------------------------------------------
+ * fn_load reads a GGUF v3 model (shard2 nullable: one file; otherwise the tensors of both) with the qwen3next tensor
+ * names onto the current GPU (split is accepted and every layer stays on this GPU; fn_split reads back the layer count)
+ * and builds the decode step with its CUDA graph. fn_forward runs nt (1..8) tokens at n_past: argmax[i] = the greedy
+ * next id after token i, logits (nullable) [nt][vocab]; errors "not loaded", "nt out of range", "context full". */
+int fn_load(const char *shard1, const char *shard2, int max_ctx, int split);
+int fn_forward(const int *tokens, int nt, float *logits, int *argmax);
+int fn_reset(void);
+void fn_free(void);
+/* The residual after every layer of the following forwards into out [layers][nt][D] (host; kept until reset with
+ * NULL); those forwards then step eagerly. */
+int fn_debug_layers(float *out);
+/* CUDA graph replay on / off (the graph is recaptured at the next forward either way). */
+int fn_use_graphs(int on);
+int fn_n_past(void);
+double fn_last_ms(void);
+/* Weight GB on device dv (this GPU: all of them; -1 when not loaded). */
+double fn_dev_gb(int dv);
+int fn_split(void);
+/* Sizes of the loaded model: out[4] = {vocab, hidden size, layers, max_ctx} (the reference's fn.py keeps these as
+ * module constants, flashnext/fn.py:11-13; no counterpart symbol). */
+int fn_model_dims(int *out);
 
 #ifdef __cplusplus
 }

@@ -73,15 +73,39 @@ def gated_attention(qg, k, v, q_norm, k_norm, inv_freq, pos, cache, nh, nkv, eps
     return o.reshape(-1), qr
 
 
+class _LazyRows:
+    """GGUF rows dequantised (to float64) one at a time when indexed, for an embedding table of any vocabulary."""
+
+    def __init__(self, raw, qtype, cols):
+        self.raw, self.qtype, self.cols = raw, qtype, cols
+
+    def __getitem__(self, i):
+        return D.dequant_rows(self.raw[int(i):int(i) + 1], self.qtype, 1, self.cols)[0].astype(np.float64)
+
+
 class OracleModel:
     """The float64 model of a config dict and its weights (flashnext/synth.py model_config / model_weights)."""
+
+    @classmethod
+    def from_dense(cls, cfg: dict, dense: dict, inv_freq: np.ndarray):
+        """The same model over float weights given directly (no GGUF rows): dense has E [vocab][D], Hd [vocab][D],
+        final_norm, and layers, each a dict of the keys step() reads (norm1, norm2; w_in, w_ab, w_out, conv_w,
+        dt_bias, ssm_a, gnorm or w_q, w_k, w_v, w_o, q_norm, k_norm; router [ne + 1][D]; experts = (gate, up, down
+        [ne][..], shared gate, up, down))."""
+        o = cls.__new__(cls)
+        o.cfg, o.W = cfg, dict(final_norm=dense["final_norm"], layers=dense["layers"])
+        o.inv_freq = np.asarray(inv_freq, np.float64)
+        o.E, o.Hd = np.asarray(dense["E"], np.float64), np.asarray(dense["Hd"], np.float64)
+        o.L = [dict(L) for L in dense["layers"]]
+        o.reset()
+        return o
 
     def __init__(self, cfg: dict, W: dict, inv_freq: np.ndarray):
         self.cfg, self.W = cfg, W
         d = cfg["D"]
         self.inv_freq = np.asarray(inv_freq, np.float32).astype(np.float64)
         deq = lambda raw, t, r, c: D.dequant_rows(raw, t, r, c).astype(np.float64)  # noqa: E731
-        self.E = deq(W["embed"], cfg["embed"], cfg["vocab"], d)
+        self.E = _LazyRows(W["embed"], cfg["embed"], d)  # only the rows of the tokens stepped are dequantised
         self.Hd = deq(W["head"], cfg["head"], cfg["vocab"], d)
         nkh, nvh, nh, nkv = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
         convch = 2 * nkh * DS + nvh * DS
@@ -113,7 +137,7 @@ class OracleModel:
         convch = 2 * nkh * DS + nvh * DS
         self.pos = 0
         self.state = []
-        for L, Wl in zip(self.L, self.W["layers"]):
+        for L in self.L:
             if L["kind"] == "G":
                 self.state.append(dict(S=np.zeros((nvh, DS, DS)), cs=np.zeros((3, convch))))
             else:

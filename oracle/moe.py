@@ -50,16 +50,21 @@ def sigmoid(v):
 
 
 class GGUFExperts:
-    """Expert-stacked GGUF rows (ne * rows_per_expert rows) with lazy per-expert dequantisation."""
+    """Expert-stacked GGUF rows (ne * rows_per_expert rows) with lazy per-expert dequantisation; the most recently
+    used `keep` experts stay dequantised (float64)."""
 
-    def __init__(self, raw: np.ndarray, qtype: int, rows_per_expert: int, cols: int):
-        self.raw, self.qtype, self.rpe, self.cols = raw, qtype, rows_per_expert, cols
+    def __init__(self, raw: np.ndarray, qtype: int, rows_per_expert: int, cols: int, keep: int = 64):
+        self.raw, self.qtype, self.rpe, self.cols, self.keep = raw, qtype, rows_per_expert, cols, keep
         self.cache = {}
 
     def __getitem__(self, e: int) -> np.ndarray:
-        if e not in self.cache:
+        if e in self.cache:
+            self.cache[e] = self.cache.pop(e)  # most recent last
+        else:
             rows = self.raw[e * self.rpe:(e + 1) * self.rpe]
             self.cache[e] = D.dequant_rows(rows, self.qtype, self.rpe, self.cols).astype(np.float64)
+            while len(self.cache) > self.keep:
+                self.cache.pop(next(iter(self.cache)))
         return self.cache[e]
 
 

@@ -153,3 +153,43 @@ def test_gemv_activation_scale_extremes(fn, qtype, scale):
         assert O.gemv_rel_err(y[t:t + 1], y64) <= GEMV_TOL, f"token {t}"
         y1 = fn.gemv(qtype, raw, rows, cols, x[t:t + 1])
         assert np.array_equal(bits(y1), bits(y[t:t + 1]))
+
+
+# ---- RMSNorm folded into the GEMV (fn_w_norm) ------------------------------------------------------------------
+# y = rsqrt(mean x^2 + eps) (W . (x * w)): the float64 reference normalises first. The folded form rounds x * w, the
+# row sum and the scale's product separately and takes rsqrtf (2 ulp), so its bar is 4e-7 of max |y| (2e-7 for the
+# GEMV plus the scale's error).
+NORM_TOL = 4e-7
+
+
+@pytest.mark.parametrize("name,rows,cols,nt", [("Q4_K", 1024, 2048, 1), ("Q6_K", 512, 2048, 1), ("BF16", 513, 2048, 1),
+                                               ("Q5_K", 700, 4096, 1), ("IQ3_XXS", 256, 2048, 3),
+                                               ("Q8_0", 300, 1024, 8)])
+def test_gemv_folded_rmsnorm(fn, name, rows, cols, nt):
+    import torch
+    rng = np.random.default_rng(rows + cols)
+    qt = BY_NAME[name]
+    raw = random_blocks(qt, rows, cols, rng)
+    x = (random_x(nt, cols, rng) * rng.uniform(0.1, 30.0, (nt, 1))).astype(np.float32)
+    w = (1.0 + 0.2 * rng.standard_normal(cols)).astype(np.float32)
+    eps = 1e-6
+    h = fn.w_create(qt, raw, rows, cols)
+    try:
+        dev = torch.device("cuda", 0)
+        xd, wd = torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev)
+        yd = torch.zeros(nt, rows, device=dev)
+        fn.w_norm(h, wd.data_ptr(), eps)
+        fn.w_gemv(h, xd.data_ptr(), cols, yd.data_ptr(), rows, nt, 0, 0)
+        y = yd.cpu().numpy()
+        fn.w_norm(h, 0)  # off again: the plain GEMV
+        fn.w_gemv(h, xd.data_ptr(), cols, yd.data_ptr(), rows, nt, 0, 0)
+        y_plain = yd.cpu().numpy()
+    finally:
+        fn.w_free(h)
+    W64 = O.dequant_rows(raw, qt, rows, cols).astype(np.float64)
+    x64 = x.astype(np.float64)
+    xn = x64 / np.sqrt((x64 ** 2).mean(axis=1, keepdims=True) + eps) * w.astype(np.float64)
+    y64 = xn @ W64.T
+    err = float(np.abs(y - y64).max() / np.abs(y64).max())
+    assert err <= NORM_TOL, f"{name} {rows}x{cols} nt={nt}: rel err {err:.3e}"
+    assert O.gemv_rel_err(y_plain, O.gemv64(W64.astype(np.float32), x)) <= GEMV_TOL

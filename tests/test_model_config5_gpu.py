@@ -1,0 +1,59 @@
+"""GPU parity of the decode step at BASELINE config 5's widths against the float64 oracle (oracle/model.py, itself
+pinned to transformers' Qwen3NextForCausalLM by tests/test_model_oracle.py).
+
+The model: hidden 2048; gated DeltaNet 16 key / 32 value heads of 128; gated attention 16 q / 2 kv heads of 256 with
+RoPE theta 1e7 on 64 dims; MoE of 512 experts of width 512, top-10, plus the sigmoid-gated shared expert; the full
+151936-row Q6_K lm_head; the config's formats (Q4_K projections and down, IQ3_XXS gate/up, BF16 router, Q4_K
+embedding). Four full-width layers (GGGA: every kind of layer) stand in for the 48, so the float64 oracle runs in
+seconds. Teacher-forced: 10 seeded prompt tokens, one step each through the library's decode step. Bars (the north
+star's): every step's log-probabilities within 1e-4 of the oracle's, and the greedy id equal to the oracle's wherever
+its top two logits are more than 1e-3 apart.
+"""
+
+import numpy as np
+import pytest
+
+from oracle.model import OracleModel
+from synth import model_config, model_weights, rope_inv_freq
+
+pytestmark = pytest.mark.gpu
+LOGPROB_TOL = 1e-4
+TIE = 1e-3
+
+
+def logprobs(lg):
+    lg = np.asarray(lg, np.float64)
+    m = lg.max()
+    return lg - m - np.log(np.exp(lg - m).sum())
+
+
+def test_config5_widths_match_oracle(fn):
+    import torch
+    from model import DecodeModel
+    cfg = dict(model_config(), layers=4)
+    assert (cfg["D"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["ne"], cfg["k"], cfg["vocab"]) == (2048, 32, 16, 2, 512, 10,
+                                                                                               151936)
+    W = model_weights(cfg, seed=17)
+    m = DecodeModel(fn, cfg, W, max_ctx=16, logits=True)
+    try:
+        o = OracleModel(cfg, W, rope_inv_freq(cfg["rope_base"]))
+        prompt = np.random.default_rng(29).integers(0, cfg["vocab"], 10)
+        s = torch.cuda.Stream()
+        m.start(prompt, s)
+        worst, checked = 0.0, 0
+        for i, tok in enumerate(prompt):
+            m.launch_step(s.cuda_stream)
+            fn.sync(s.cuda_stream)
+            lg = m.logits.cpu().numpy()
+            ref = o.step(int(tok))
+            diff = float(np.abs(logprobs(lg) - logprobs(ref)).max())
+            worst = max(worst, diff)
+            assert diff <= LOGPROB_TOL, (i, diff)
+            top = np.sort(ref)[::-1]
+            if top[0] - top[1] > TIE:
+                assert int(m.next.item()) == int(np.argmax(ref)), i
+                checked += 1
+        assert checked >= len(prompt) // 2
+        print(f"config-5 widths: max log-prob diff {worst:.3g} over {len(prompt)} steps, {checked} greedy ids checked")
+    finally:
+        m.free()

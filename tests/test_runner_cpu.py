@@ -188,12 +188,12 @@ def test_fn_model_api_without_a_model(libpath, tmp_path):
             call()
     f.free()  # nothing loaded: no-op
     with pytest.raises(RuntimeError):
-        f.load(str(tmp_path / "missing.gguf"))
+        f.load(shard1=str(tmp_path / "missing.gguf"))
     (tmp_path / "bad.gguf").write_bytes(b"GGML" + b"\0" * 60)
     with pytest.raises(RuntimeError, match="not a GGUF"):
-        f.load(str(tmp_path / "bad.gguf"))
+        f.load(shard1=str(tmp_path / "bad.gguf"))
     with pytest.raises(RuntimeError, match="batch out of range"):
-        f.load(str(tmp_path / "bad.gguf"), batch=33)
+        f.load(shard1=str(tmp_path / "bad.gguf"), batch=33)
     with pytest.raises(RuntimeError, match="not loaded"):
         f.forward([1])
     import fn as fnmod  # the reference's call form: paths from SH1 / SH2 (env FN_SHARD1 / FN_SHARD2)
@@ -228,3 +228,90 @@ def test_save_streams_generator_layers(tmp_path):
         gguf.write(str(tmp_path / "x.gguf"), {}, [("a", gguf.GGML_F32, [32]), ("b", gguf.GGML_F32, [32])], [v])
     with pytest.raises(gguf.GGUFError, match="more data"):
         gguf.write(str(tmp_path / "y.gguf"), {}, [("a", gguf.GGML_F32, [32])], [v, v])
+
+
+def test_library_loader_refusals(libpath, small, tmp_path):
+    """The library's fn_load (csrc/fn_runner.cu) reads the same files with its own C++ reader and refuses the same
+    ones with the same messages; every check here fires before any device work, so it runs without a GPU."""
+    from fn import FN
+    f = FN(libpath)
+    cfg, W = small
+    p = str(tmp_path / "m.gguf")
+    save_model(p, cfg, W)
+    meta, t = gguf.read(p)
+    rows = lambda n: (n, t[n].qtype, list(t[n].dims), t[n].data)  # noqa: E731
+
+    def variant(name, tensors, meta_=meta):
+        q = str(tmp_path / name)
+        gguf.write(q, meta_, tensors)
+        return q
+
+    def refuses(match, s1, s2=None):
+        with pytest.raises(RuntimeError, match=match):
+            f.load(max_ctx=64, shard1=s1, shard2=s2)
+        assert f.n_past() == -1  # nothing loaded
+
+    (tmp_path / "x.gguf").write_bytes(b"GGUX" + b"\0" * 64)
+    refuses("not a GGUF", str(tmp_path / "x.gguf"))
+    raw = open(p, "rb").read()
+    (tmp_path / "cut.gguf").write_bytes(raw[:-8])
+    refuses("out of range", str(tmp_path / "cut.gguf"))
+    (tmp_path / "cut2.gguf").write_bytes(raw[:30])
+    refuses("truncated", str(tmp_path / "cut2.gguf"))
+    (tmp_path / "empty.gguf").write_bytes(b"")
+    refuses("truncated", str(tmp_path / "empty.gguf"))
+    (tmp_path / "utf.gguf").write_bytes(b"GGUF" + (3).to_bytes(4, "little") + (0).to_bytes(8, "little")
+                                        + (1).to_bytes(8, "little") + (2).to_bytes(8, "little") + b"\xff\xfe" + b"\0" * 16)
+    refuses("not UTF-8", str(tmp_path / "utf.gguf"))
+    refuses("No such file", str(tmp_path / "never.gguf"))
+    refuses("missing tensor blk.1.ssm_a", variant("a.gguf", [rows(n) for n in t if n != "blk.1.ssm_a"]))
+    extra = [rows(n) for n in t] + [("blk.0.hc_attn_norm.weight", gguf.GGML_F32, [32], np.zeros(32, np.float32))]
+    refuses("no kernels for", variant("b.gguf", extra))
+    extra = [rows(n) for n in t] + [("blk.0.something.weight", gguf.GGML_F32, [32], np.zeros(32, np.float32))]
+    refuses("does not use", variant("c.gguf", extra))
+    refuses("expert_used_count", variant("d.gguf", [rows(n) for n in t], {k: v for k, v in meta.items()
+                                                                          if "expert_used" not in k}))
+    rng = np.random.default_rng(2)
+    mixed = [rows(n) for n in t if n != "blk.0.attn_gate.weight"]
+    mixed.append(("blk.0.attn_gate.weight", BY_NAME["Q8_0"], [cfg["D"], cfg["nvh"] * 128],
+                  model_blocks(BY_NAME["Q8_0"], cfg["nvh"] * 128, cfg["D"], rng)))
+    refuses("different formats", variant("e.gguf", mixed))
+    short = [rows(n) for n in t if n != "blk.3.attn_v.weight"]
+    short.append(("blk.3.attn_v.weight", t["blk.3.attn_v.weight"].qtype, [cfg["D"], 128],
+                  t["blk.3.attn_v.weight"].data[:t["blk.3.attn_v.weight"].data.nbytes // 2]))
+    refuses("blk.3.attn_v.weight: shape", variant("f.gguf", short))
+    attn_only = [rows(n) for n in t if not n.startswith(("blk.0.", "blk.1.", "blk.2."))]
+    attn_only = [(n.replace("blk.3.", "blk.0."), q, d, x) for n, q, d, x in attn_only]
+    refuses("both gated-DeltaNet and attention", variant("g.gguf", attn_only, dict(meta, **{"qwen3next.block_count": 1})))
+    names = list(t)
+    half = len(names) // 2
+    s1 = variant("s1.gguf", [rows(n) for n in names[:half]])
+    s2 = variant("s2.gguf", [rows(n) for n in names[half:]], {})
+    refuses("more than one shard", p, s2)
+    refuses("missing tensor", s1)
+
+
+def test_reference_binding_lines(libpath):
+    """The reference's own FN.__init__ binding lines (flashnext/fn.py:27-33), run verbatim against this library: every
+    symbol they name exists and takes the argtypes / restypes they set."""
+    import ctypes as C
+    P = np.ctypeslib.ndpointer
+    F32 = P(np.float32, flags="C_CONTIGUOUS")
+    I32 = P(np.int32, flags="C_CONTIGUOUS")
+    U8 = P(np.uint8, flags="C_CONTIGUOUS")
+    d = C.CDLL(libpath)
+    d.fn_error.restype = C.c_char_p
+    d.fn_load.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.c_int]
+    d.fn_forward.argtypes = [I32, C.c_int, C.c_void_p, C.c_void_p]
+    d.fn_debug_layers.argtypes = [C.c_void_p]
+    d.fn_test_dequant.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32]
+    d.fn_test_gemv.argtypes = [C.c_uint32, U8, C.c_int, C.c_int, F32, C.c_int, F32]
+    d.fn_dev_gb.restype = C.c_double
+    d.fn_dev_gb.argtypes = [C.c_int]
+    d.fn_last_ms.restype = C.c_double
+    # the reference's FN methods' calls with nothing loaded: its return values and messages
+    assert d.fn_dev_gb(0) == -1.0 and d.fn_last_ms() == -1.0 and d.fn_n_past() == -1 and d.fn_split() == -1
+    assert d.fn_forward(np.zeros(1, np.int32), 1, None, np.zeros(1, np.int32).ctypes.data) == -1
+    assert d.fn_error() == b"not loaded"
+    assert d.fn_reset() == -1 and d.fn_debug_layers(None) == -1
+    assert d.fn_load(b"/nonexistent.gguf", None, 4096, 0) == -1 and b"No such file" in d.fn_error()

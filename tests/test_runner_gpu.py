@@ -34,7 +34,7 @@ def loaded(fn, tmp_path_factory):
     W = model_weights(cfg, 5)
     p = tmp_path_factory.mktemp("model") / "small.gguf"
     save_model(str(p), cfg, W)
-    fn.load(str(p), max_ctx=MAX_CTX)
+    fn.load(max_ctx=MAX_CTX, shard1=str(p))
     yield cfg, W
     fn.free()
 
@@ -147,7 +147,7 @@ def test_mixed_formats_file(fn, loaded, tmp_path):
     p = str(tmp_path / "mixed.gguf")
     save_model(p, cfg2, W2)
     cfg3, W3, _ = load_model(p)
-    fn.load(p, max_ctx=16)
+    fn.load(max_ctx=16, shard1=p)
     o = OracleModel(cfg3, W3, rope_inv_freq(cfg3["rope_base"]))
     toks = rng.integers(0, cfg["vocab"], 6)
     am, lg = fn.forward(toks, logits=True)
@@ -158,7 +158,7 @@ def test_mixed_formats_file(fn, loaded, tmp_path):
         if top[0] - top[1] > TIE:
             assert int(am[i]) == int(np.argmax(ref))
     with pytest.raises(RuntimeError, match="one format"):  # the batched path stacks q / k / v into one weight
-        fn.load(p, max_ctx=16, batch=2)
+        fn.load(max_ctx=16, shard1=p, batch=2)
 
 
 BATCH_LOGPROB_TOL = 1e-3  # the tensor-core path's stated model-level tolerance (tests/test_batch_gpu.py)
@@ -172,7 +172,7 @@ def test_forward_batch(fn, loaded, tmp_path):
     cfg, W = loaded
     p = str(tmp_path / "small.gguf")
     save_model(p, cfg, W)
-    fn.load(p, max_ctx=24, batch=3)
+    fn.load(max_ctx=24, shard1=p, batch=3)
     rng = np.random.default_rng(29)
     prompts = rng.integers(0, cfg["vocab"], (3, 5))
     oracles = [OracleModel(cfg, W, rope_inv_freq(cfg["rope_base"])) for _ in range(3)]
@@ -237,6 +237,6 @@ def test_not_loaded(fn, loaded, tmp_path):
     with pytest.raises(RuntimeError, match="not loaded"):
         fn.forward_batch(np.zeros((1, 1), np.int32))
     with pytest.raises(RuntimeError):
-        fn.load(str(tmp_path / "missing.gguf"))
+        fn.load(shard1=str(tmp_path / "missing.gguf"))
     with pytest.raises(RuntimeError, match="not loaded"):
         fn.forward([1])
