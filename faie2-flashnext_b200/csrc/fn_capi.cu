@@ -2,6 +2,8 @@
 // the reference (engine/faie2fn.cu:2492-2935) and resident-weight handles for device-pointer callers.
 // Conventions of the reference are kept: int return 0 = ok, -1 = error with the message in fn_error(); the caller
 // owns every host buffer; every fn_test_* / fn_bench_* call is synchronous.
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
@@ -287,6 +289,57 @@ FN_API int fn_test_gemv(uint32_t type, const uint8_t *Wh, int rows, int cols, co
 // GEMV timing on hash-random bytes of a format with the weights cold in L2 (as in a forward, where each weight is
 // read once): `copies` rotating copies whose total exceeds twice the L2, `iters` calls captured in one CUDA graph,
 // one warm-up replay, an L2 flush, then one timed replay. ms per call (engine/faie2fn.cu:2817-2866).
+// Seeded GGUF rows of `type` as the benchmark's synthetic weights: uniform random bytes, the fp16
+// scale fields of every block overwritten with finite |N(0,1)| 1e-3 values (here |u1 + u2 + u3 - 1.5| 2e-3 of three
+// uniforms, a bell-shaped stand-in), BF16 rows as small normal values; x values likewise bell-shaped around 0. A
+// 64-bit linear congruential generator makes the bytes.
+namespace fn {
+struct Lcg {
+    uint64_t s;
+    uint32_t next() {
+        s = s * 6364136223846793005ull + 1442695040888963407ull;
+        return (uint32_t)(s >> 33);
+    }
+    float uni() { return (float)(next() >> 8) * (1.0f / 16777216.0f); }
+    float bell() { return uni() + uni() + uni() - 1.5f; }
+};
+static int scale_offsets(uint32_t t, int *off) {
+    switch (t) {
+        case T_Q4_1: case T_Q5_1: case T_Q4_K: case T_Q5_K: off[0] = 0; off[1] = 2; return 2;
+        case T_Q2_K: off[0] = 80; off[1] = 82; return 2;
+        case T_Q3_K: off[0] = 108; return 1;
+        case T_Q6_K: off[0] = 208; return 1;
+        case T_BF16: return 0;
+        default: off[0] = 0; return 1;
+    }
+}
+static std::vector<uint8_t> bench_rows(uint32_t type, int rows, int cols, uint64_t seed) {
+    const uint64_t rb = row_bytes(type, cols);
+    std::vector<uint8_t> h((size_t)rb * rows);
+    Lcg g{seed};
+    if (type == T_BF16) {
+        for (size_t i = 0; i < h.size() / 2; ++i) {
+            const float v = g.bell() * 0.1f;
+            uint32_t u;
+            std::memcpy(&u, &v, 4);
+            const uint16_t b = (uint16_t)(u >> 16);
+            std::memcpy(&h[2 * i], &b, 2);
+        }
+        return h;
+    }
+    for (auto &b : h) b = (uint8_t)g.next();
+    int qk, tb, off[2];
+    type_info(type, qk, tb);
+    const int nf = scale_offsets(type, off);
+    for (size_t blk = 0; blk < h.size() / tb; ++blk)
+        for (int f = 0; f < nf; ++f) {
+            const __half d = __float2half(fabsf(g.bell()) * 2e-3f);
+            std::memcpy(&h[blk * tb + off[f]], &d, 2);
+        }
+    return h;
+}
+}  // namespace fn
+
 FN_API int fn_bench_gemv(uint32_t type, int rows, int cols, int nt, int iters, float *ms) {
     GemvPlan p;
     if (nt < 1 || nt > 8 || iters < 1) return fail("nt/iters out of range");
@@ -305,11 +358,19 @@ FN_API int fn_bench_gemv(uint32_t type, int rows, int cols, int nt, int iters, f
     FN_CK(cudaMalloc(&x.p, (size_t)nt * cols * 4));
     FN_CK(cudaMalloc(&y.p, (size_t)nt * rows * 4));
     FN_CK(cudaMalloc(&flush.p, flush_n));
-    std::vector<uint8_t> hb(wb);
-    for (size_t i = 0; i < wb; ++i) hb[i] = (uint8_t)((i * 2654435761u) >> 13);
-    FN_CK(cudaMemcpy(W.p, hb.data(), wb, cudaMemcpyHostToDevice));
-    for (int c = 1; c < copies; ++c) FN_CK(cudaMemcpy(W.as<uint8_t>() + wb * c, W.p, wb, cudaMemcpyDeviceToDevice));
-    FN_CK(cudaMemset(x.p, 0, (size_t)nt * cols * 4));
+    {  // one copy of the weights in the engine's layout, then its duplicates; x bell-shaped around 0
+        const std::vector<uint8_t> hb = bench_rows(type, rows, cols, 12345);
+        DevBuf raw;
+        FN_CK(cudaMalloc(&raw.p, hb.size()));
+        FN_CK(cudaMemcpy(raw.p, hb.data(), hb.size(), cudaMemcpyHostToDevice));
+        if (launch_plane_repack(type, raw.as<uint8_t>(), p.rb, W.as<uint8_t>(), p.ldw, rows, cols, 0)) return -1;
+        FN_CK(cudaDeviceSynchronize());
+        for (int c = 1; c < copies; ++c) FN_CK(cudaMemcpy(W.as<uint8_t>() + wb * c, W.p, wb, cudaMemcpyDeviceToDevice));
+        std::vector<float> hx((size_t)nt * cols);
+        Lcg g{777};
+        for (float &v : hx) v = g.bell() * 2.0f;
+        FN_CK(cudaMemcpy(x.p, hx.data(), hx.size() * 4, cudaMemcpyHostToDevice));
+    }
     cudaStream_t st = hook_stream();
     cudaGraph_t g;
     cudaGraphExec_t ge;

@@ -1,4 +1,6 @@
 // C ABI of the MoE layer and the routing hook (declared in include/faie2fn.h).
+#include <cuda.h>
+
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -11,7 +13,7 @@ namespace fn {
 
 struct MoeH {
     MoePlan p;
-    DevBuf gate, up, down, sg, su, sd, act, route;
+    DevBuf gate, up, down, sg, su, sd, act, route, sync;
     MoeWeights w;
     int group = 0;  // expert parallel: the peer group (0: one GPU)
     int e0 = 0;
@@ -56,7 +58,9 @@ static MoeH *moe_build(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
         upload_rows(m->sd, down_type, Wsd, p.rb_down, p.ldw_down, d, ffe, s) ||
         cudaMalloc(&m->act.p, (size_t)MOE_MAXT * (k + 1) * ffe * 4) != cudaSuccess ||
         cudaMemset(m->act.p, 0, (size_t)MOE_MAXT * (k + 1) * ffe * 4) != cudaSuccess ||
-        cudaMalloc(&m->route.p, MOE_ROUTE_WORDS * 4) != cudaSuccess) {
+        cudaMalloc(&m->route.p, MOE_ROUTE_WORDS * 4) != cudaSuccess ||
+        cudaMalloc(&m->sync.p, MOE_SYNC_WORDS * 4) != cudaSuccess ||
+        cudaMemset(m->sync.p, 0, MOE_SYNC_WORDS * 4) != cudaSuccess) {
         delete m;
         if (err().empty()) fail("moe: device allocation failed");
         return nullptr;
@@ -92,7 +96,8 @@ FN_API int fn_test_moe(uint32_t gu_type, uint32_t down_type, int ne, int k, int 
         rc = fail("fn_test_moe: copy failed");
     if (!rc)
         rc = launch_moe(m->p, m->w, lg.as<float>(), ne + 1, xd.as<float>(), m->act.as<float>(), m->route.as<uint32_t>(),
-                        yd.as<float>(), nt, false, sd.as<int>(), wd.as<float>(), true, s);
+                        yd.as<float>(), nt, false, sd.as<int>(), wd.as<float>(), true, s, nullptr, false,
+                        m->sync.as<uint32_t>());
     if (!rc) {
         cudaMemcpyAsync(y, yd.p, (size_t)nt * d * 4, cudaMemcpyDeviceToHost, s);
         if (sel) cudaMemcpyAsync(sel, sd.p, (size_t)nt * k * 4, cudaMemcpyDeviceToHost, s);
@@ -160,7 +165,7 @@ FN_API int fn_moe_run(int h, const float *logits, int ls, const float *x, float 
     if (!m) return fail("fn_moe_run: bad handle");
     if (m->group) return fail("fn_moe_run: an expert-parallel handle runs with fn_moe_ep_run");
     return launch_moe(m->p, m->w, logits, ls, x, m->act.as<float>(), m->route.as<uint32_t>(), y, nt, (acc & 1) != 0,
-                      nullptr, nullptr, true, (cudaStream_t)stream, nullptr, (acc & 2) != 0);
+                      nullptr, nullptr, true, (cudaStream_t)stream, nullptr, (acc & 2) != 0, m->sync.as<uint32_t>());
 }
 
 // Expert-parallel MoE layer on a peer group (one rank per GPU): this rank holds routed experts
@@ -262,17 +267,33 @@ FN_API int fn_bench_route(int variant, int nt, int ks, const float *parth, int i
 // kernel, read by the others) and the activations passed from the gate/up kernel to the down kernel, in a fixed array
 // of device memory that is part of the library image.
 //
-// Limit: nt * (k + 1) * ffe <= FN_MOE_STATIC_ACT_FLOATS (65536 floats, 256 KiB); larger calls are rejected. Every GPU
-// that loads the library holds the array until the process exits. All calls share it, so calls whose kernels overlap
-// on the GPU (two streams, or two host threads) race on it: issue them in one stream. Nothing in it needs to start at
-// zero (each kernel writes every element the next one reads). The first call on a device resolves the array's device
-// address on that device (cudaGetSymbolAddress); make that first call outside stream capture.
+// Limits: 1 <= nt <= 32 tokens and nt * (k + 1) * ffe <= 65536 floats (256 KiB of activations); larger calls are
+// rejected. Every GPU that loads the library holds the array until the process exits. All calls share it, so calls
+// whose kernels overlap on the GPU (two streams, or two host threads) race on it: issue them in one stream. Nothing in
+// it needs to start at zero (each kernel writes every element the next one reads). The first call on a device (and the
+// first after that device's context was re-created, e.g. by cudaDeviceReset) resolves the array's device address in
+// the current context (cudaGetSymbolAddress); make that first call outside stream capture.
 
 namespace fn {
 constexpr size_t kMoeStaticActFloats = 65536;
 // activations, then the routing words
 static __device__ __align__(256) float g_moe_static_act[kMoeStaticActFloats + MOE_ROUTE_WORDS];
-static float *g_moe_static_act_dev[64] = {};  // device address of g_moe_static_act, per device
+// device address of g_moe_static_act per device, and the context it was resolved in
+static float *g_moe_static_act_dev[64] = {};
+static CUcontext g_moe_static_ctx[64] = {};
+// the driver's cuCtxGetCurrent, looked up through the runtime (the library does not link the driver library itself)
+static CUresult current_context(CUcontext *ctx) {
+    using Fn = CUresult (*)(CUcontext *);
+    static Fn f = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (Fn) nullptr;
+        return (Fn)p;
+    }();
+    return f ? f(ctx) : CUDA_ERROR_NOT_FOUND;
+}
 }  // namespace fn
 
 FN_API int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
@@ -281,7 +302,7 @@ FN_API int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int
                                void *stream) {
     MoePlan p;
     if (!plan_moe(p, gu_type, down_type, ne, k, ffe, d)) return fail("fn_moe_layer_static: unsupported types/shape");
-    if (nt < 1 || nt > 8) return fail("fn_moe_layer_static: nt out of range (1..8)");
+    if (nt < 1 || nt > MOE_MAXT) return fail("fn_moe_layer_static: nt out of range (1..32)");
     const size_t need = (size_t)nt * (k + 1) * ffe;
     if (need > kMoeStaticActFloats)
         return fail("fn_moe_layer_static: nt * (k + 1) * ffe = " + std::to_string(need) +
@@ -292,11 +313,15 @@ FN_API int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int
     int dev = 0;
     FN_CK(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail("fn_moe_layer_static: device index out of range");
-    if (!g_moe_static_act_dev[dev]) {
+    CUcontext ctx = nullptr;
+    FN_CK(cudaFree(nullptr));  // makes the device's primary context current (allocates nothing)
+    if (current_context(&ctx) != CUDA_SUCCESS || !ctx) return fail("fn_moe_layer_static: no current CUDA context");
+    if (!g_moe_static_act_dev[dev] || g_moe_static_ctx[dev] != ctx) {
         void *ptr = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&ptr, g_moe_static_act);
         if (e != cudaSuccess) return fail(std::string("fn_moe_layer_static: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
         g_moe_static_act_dev[dev] = (float *)ptr;
+        g_moe_static_ctx[dev] = ctx;
     }
     const MoeWeights w{Wg, Wu, Wd, Wsg, Wsu, Wsd};
     return launch_moe(p, w, logits, ls, x, g_moe_static_act_dev[dev],

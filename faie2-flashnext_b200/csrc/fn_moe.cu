@@ -224,7 +224,7 @@ constexpr size_t kMoeDynSmem = 227 * 1024 - 4 * 1024;
 
 int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act,
                uint32_t *route, float *y, int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s,
-               const MoeEp *ep, bool x_early) {
+               const MoeEp *ep, bool x_early, uint32_t *sync) {
     if (nt < 1 || nt > (ep ? MOE_EP_MAXT : MOE_MAXT)) return fail("moe: nt out of range (1..32, 1..8 expert parallel)");
     if (!route) return fail("moe: no routing scratch");
     int *rsel = (int *)route;
@@ -249,6 +249,11 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         const cudaError_t e = launch_k(k_moe_route, dim3(nt), dim3(ROUTE_THREADS), 0, s, logits, ls, p.ne, p.k, rsel, rw,
                                        sel_out, w_out);
         if (e != cudaSuccess) return fail(std::string("moe route launch: ") + cudaGetErrorString(e));
+    }
+    // ---- the fused form: gate/up and down in one kernel (one token on one GPU)
+    if (settings().moe_var == 2 && nt == 1 && !ep && planes && ls == p.ne + 1) {
+        const int rc = launch_moe_fused(p, w, logits, x, act, rsel, rw, sync, y, acc, x_early, s);
+        if (rc <= 0) return rc;  // launched, or an error; 1: no fused form, the two kernels below
     }
     // ---- gate / up
     {

@@ -49,9 +49,15 @@ struct MoeEp {
 // else GGUF rows at the plan's strides. x_early: x was complete before the kernel before this layer started (the
 // router GEMV's predecessor wrote it), so the gate/up kernel reads it beside the routing kernel.
 constexpr int MOE_ROUTE_WORDS = 2 * MOE_MAXT * 16;  // sel [MOE_MAXT][16] ints, then w [MOE_MAXT][16] floats
+// sync (nullable): MOE_SYNC_WORDS zeroed words of the layer's own, which allow the fused single-kernel form
+// (fn_moe_var(2), one token on one GPU: launch_moe_fused).
+constexpr int MOE_SYNC_WORDS = 32;
 int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int ls, const float *x, float *act,
                uint32_t *route, float *y, int nt, bool acc, int *sel_out, float *w_out, bool planes, cudaStream_t s,
-               const MoeEp *ep = nullptr, bool x_early = false);
+               const MoeEp *ep = nullptr, bool x_early = false, uint32_t *sync = nullptr);
+// the fused form after the routing kernel: 0 launched, 1 no fused form for this layer, -1 error
+int launch_moe_fused(const MoePlan &p, const MoeWeights &w, const float *logits, const float *x, float *act,
+                     const int *rsel, const float *rw, uint32_t *cnt, float *y, bool acc, bool x_early, cudaStream_t s);
 
 // routing alone on split-K partials: logits[t][i] = sum_{j<ks} part[j * kst + t * ts + i] (split order)
 int launch_route(int variant, const float *part, int ks, size_t kst, int ts, int ne, int k, int nt, int *sel, float *w,

@@ -57,9 +57,10 @@ constexpr int XPAD = 36;  // floats per staged x group: 32 values, the two 16-va
 // (an exact power-of-two scaling; the products q * 2^-149 * x * 2^K_t then stay in the normal range) and
 // 2^(149 - K_t) at + 34. nt <= 32. Every thread calls this; it ends with a __syncthreads.
 // nw (an RMSNorm weight, nullable): the values staged are x[t][c] * nw[c], and + 35 of group g holds the sum of the
-// squares of the raw x over the group's 32 values (fixed order) for norm_scale.
+// squares of the raw x over the group's 32 values (fixed order) for norm_scale. cg: x is read through L2 only (data
+// another CTA of the same grid published with a release, after this CTA's acquire).
 __device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int nt, int G, bool denorm,
-                                        const float *nw = nullptr) {
+                                        const float *nw = nullptr, bool cg = false) {
     __shared__ int s_xmax[32];
     if (denorm) {
         if ((int)threadIdx.x < nt) s_xmax[threadIdx.x] = 0;
@@ -94,7 +95,7 @@ __device__ __forceinline__ void stage_x(float *xsm, const float *x, int xs, int 
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            if (!nw) v[q] = src[q];
+            if (!nw) v[q] = cg ? __ldcg(src + q) : src[q];
             *(float4 *)(dst + 16 * h + 4 * q) = v[q];
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[q].x), fabsf(v[q].y)), fmaxf(fabsf(v[q].z), fabsf(v[q].w))));
         }

@@ -113,13 +113,15 @@ class BlockPool:
         return np.concatenate(parts).reshape(rows, row_bytes(self.qtype, cols))
 
 
-def model_weights(cfg: dict, seed: int = 0, pooled: bool = False) -> dict:
+def model_weights(cfg: dict, seed: int = 0, pooled: bool = False, wscale: float = 1e-3) -> dict:
     """Seeded synthetic weights of the config-5 model as GGUF rows (uint8, zero-mean blocks: model_blocks) and fp32
     vectors. DeltaNet projections are stacked as in the reference's load_qw_cat: in = [q | k | v | z] (CONVCH + NVH*128
     rows), ab = [alpha | beta]. The lm_head's scales are 1e-4 (logits of a few units, as a trained head gives).
 
     pooled: the routed experts' tensors are cut from one BlockPool per format and W["layers"] is a generator (each
-    layer made when it is consumed), so the full model never sits in host memory at once."""
+    layer made when it is consumed), so the full model never sits in host memory at once.
+    wscale: the block scale of every layer's quantised projections and experts (the scale field's mean magnitude);
+    1e-3 gives Q4_K elements of rms about 0.13, 2.5e-4 about 0.03, the size of a trained model's weights."""
     rng = np.random.default_rng(seed)
     D = cfg["D"]
     f32 = lambda a: np.asarray(a, np.float32)  # noqa: E731
@@ -128,38 +130,41 @@ def model_weights(cfg: dict, seed: int = 0, pooled: bool = False) -> dict:
     pools = None
     if pooled:
         n = cfg["ne"] * cfg["ffe"] * max(D // TYPES[cfg["gate_up"]][1], 1)
-        pools = (BlockPool(cfg["gate_up"], n + n // 16, rng),
-                 BlockPool(cfg["down"], cfg["ne"] * D * max(cfg["ffe"] // TYPES[cfg["down"]][1], 1) * 17 // 16, rng))
-    gen = (_model_layer(cfg, l, rng, pools) for l in range(cfg["layers"]))
+        pools = (BlockPool(cfg["gate_up"], n + n // 16, rng, wscale),
+                 BlockPool(cfg["down"], cfg["ne"] * D * max(cfg["ffe"] // TYPES[cfg["down"]][1], 1) * 17 // 16, rng,
+                           wscale))
+    gen = (_model_layer(cfg, l, rng, pools, wscale) for l in range(cfg["layers"]))
     W["layers"] = gen if pooled else list(gen)
     return W
 
 
-def _model_layer(cfg: dict, l: int, rng: np.random.Generator, pools) -> dict:
+def _model_layer(cfg: dict, l: int, rng: np.random.Generator, pools, wscale: float = 1e-3) -> dict:
     D, DS, HD = cfg["D"], 128, 256
     nkh, nvh, nh, nkv = cfg["nkh"], cfg["nvh"], cfg["nh"], cfg["nkv"]
     convch = 2 * nkh * DS + nvh * DS
     ne, ffe = cfg["ne"], cfg["ffe"]
-    P = cfg["proj"]
+    P, ws = cfg["proj"], wscale
     f32 = lambda a: np.asarray(a, np.float32)  # noqa: E731
     L = dict(kind=layer_kind(cfg, l), norm1=f32(1 + 0.1 * rng.standard_normal(D)),
              norm2=f32(1 + 0.1 * rng.standard_normal(D)))
     if L["kind"] == "G":
-        L.update(w_in=model_blocks(P, convch + nvh * DS, D, rng), w_ab=model_blocks(P, 2 * nvh, D, rng),
-                 w_out=model_blocks(P, D, nvh * DS, rng), conv_w=f32(rng.standard_normal((convch, 4)) * 0.5),
+        L.update(w_in=model_blocks(P, convch + nvh * DS, D, rng, ws), w_ab=model_blocks(P, 2 * nvh, D, rng, ws),
+                 w_out=model_blocks(P, D, nvh * DS, rng, ws), conv_w=f32(rng.standard_normal((convch, 4)) * 0.5),
                  dt_bias=f32(rng.standard_normal(nvh) * 0.5), ssm_a=f32(-np.exp(rng.standard_normal(nvh) * 0.5)),
                  gnorm=f32(1 + 0.1 * rng.standard_normal(DS)))
     else:
-        L.update(w_q=model_blocks(P, nh * 2 * HD, D, rng), w_k=model_blocks(P, nkv * HD, D, rng),
-                 w_v=model_blocks(P, nkv * HD, D, rng), w_o=model_blocks(P, D, nh * HD, rng),
+        L.update(w_q=model_blocks(P, nh * 2 * HD, D, rng, ws), w_k=model_blocks(P, nkv * HD, D, rng, ws),
+                 w_v=model_blocks(P, nkv * HD, D, rng, ws), w_o=model_blocks(P, D, nh * HD, rng, ws),
                  q_norm=f32(1 + 0.1 * rng.standard_normal(HD)), k_norm=f32(1 + 0.1 * rng.standard_normal(HD)))
     gu, dn = cfg["gate_up"], cfg["down"]
     L["router"] = model_blocks(cfg["router"], ne + 1, D, rng)
     if pools is None:
-        routed = [model_blocks(gu, ne * ffe, D, rng), model_blocks(gu, ne * ffe, D, rng), model_blocks(dn, ne * D, ffe, rng)]
+        routed = [model_blocks(gu, ne * ffe, D, rng, ws), model_blocks(gu, ne * ffe, D, rng, ws),
+                  model_blocks(dn, ne * D, ffe, rng, ws)]
     else:
         routed = [pools[0].take(ne * ffe, D), pools[0].take(ne * ffe, D), pools[1].take(ne * D, ffe)]
-    L["moe"] = routed + [model_blocks(gu, ffe, D, rng), model_blocks(gu, ffe, D, rng), model_blocks(dn, D, ffe, rng)]
+    L["moe"] = routed + [model_blocks(gu, ffe, D, rng, ws), model_blocks(gu, ffe, D, rng, ws),
+                         model_blocks(dn, D, ffe, rng, ws)]
     return L
 
 

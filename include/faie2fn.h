@@ -226,9 +226,10 @@ int fn_gdn_get_state(int h, float *S, float *conv);
  * its own pool, or a decode loop that must not pay cudaFree's device synchronisation). No counterpart in the
  * reference. Everything is a device pointer the caller owns: weights as in fn_test_moe, rows at a stride of
  * row_bytes rounded up to 16, 16-byte aligned; logits [nt][ls] (ls >= ne + 1); x, y [nt][d]. The only scratch (the
- * gate/up -> down activations) is a static 256 KiB device array inside the library: nt * (k + 1) * ffe <= 65536,
- * larger calls fail. All calls share that array, so calls that overlap on the GPU race; keep them in one stream. The
- * first call on a device resolves the array's address there; make it outside stream capture. Allocates nothing. */
+ * gate/up -> down activations) is a static 256 KiB device array inside the library: 1 <= nt <= 32 and
+ * nt * (k + 1) * ffe <= 65536, larger calls fail. All calls share that array, so calls that overlap on the GPU race;
+ * keep them in one stream. The first call on a device (and the first after its context is re-created) resolves the
+ * array's address there; make it outside stream capture. Allocates nothing. */
 int fn_moe_layer_static(uint32_t gu_type, uint32_t down_type, int ne, int k, int ffe, int d, const uint8_t *Wg,
                         const uint8_t *Wu, const uint8_t *Wd, const uint8_t *Wsg, const uint8_t *Wsu, const uint8_t *Wsd,
                         const float *logits, int ls, const float *x, float *y, int nt, void *stream);

@@ -165,6 +165,8 @@ class OracleModel:
             logits_r = L["router"] @ x2
             y, _, _ = M.moe_layer(x2[None], logits_r[None], cfg["k"], *L["experts"])
             h = h + y[0]
+            if getattr(self, "trace", None) is not None:  # the residual after every layer, when asked
+                self.trace.append(h.copy())
         self.pos += 1
         self.h = h
         return self.Hd @ rmsnorm(h, self.W["final_norm"], eps)

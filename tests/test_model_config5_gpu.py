@@ -8,6 +8,12 @@ embedding). Four full-width layers (GGGA: every kind of layer) stand in for the 
 seconds. Teacher-forced: 10 seeded prompt tokens, one step each through the library's decode step. Bars (the north
 star's): every step's log-probabilities within 1e-4 of the oracle's, and the greedy id equal to the oracle's wherever
 its top two logits are more than 1e-3 apart.
+
+The weights are trained-size (model_weights wscale=2.5e-4: quantised elements of rms about 0.03, residual stream of
+norm a few hundred). At the bench's louder synthetic weights (wscale=1e-3, rms about 0.13, residual norm above 1e4)
+the model is conditioned so that the bar lies below float32's own floor: a numpy float32 restatement of the oracle
+(BLAS sgemv) is 2.8e-4 from float64 on this prompt and this engine 1.6e-4, whereas at trained size the float32
+restatement is 2.5e-5 from it.
 """
 
 import numpy as np
@@ -33,7 +39,7 @@ def test_config5_widths_match_oracle(fn):
     cfg = dict(model_config(), layers=4)
     assert (cfg["D"], cfg["nvh"], cfg["nh"], cfg["nkv"], cfg["ne"], cfg["k"], cfg["vocab"]) == (2048, 32, 16, 2, 512, 10,
                                                                                                151936)
-    W = model_weights(cfg, seed=17)
+    W = model_weights(cfg, seed=17, wscale=2.5e-4)
     m = DecodeModel(fn, cfg, W, max_ctx=16, logits=True)
     try:
         o = OracleModel(cfg, W, rope_inv_freq(cfg["rope_base"]))

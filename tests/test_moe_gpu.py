@@ -160,3 +160,60 @@ def test_route_small_logit_collisions_variants_agree(fn):
     s0, w0, _ = fn.bench_route(0, part, MAXT, 1)
     s1, w1, _ = fn.bench_route(1, part, MAXT, 1)
     assert np.array_equal(s0, s1) and np.array_equal(w0.view(np.uint32), w1.view(np.uint32))
+
+
+# ---- the fused single-kernel layer (fn_moe_var(2): gate/up and down with per-slot counters) ----------------------
+@pytest.mark.parametrize("gu,dn,ne,k,ffe,d", [("IQ3_XXS", "Q4_K", 512, 10, 512, 2048), ("IQ3_XXS", "Q4_K", 16, 4, 256, 512),
+                                              ("Q4_K", "Q4_K", 64, 8, 512, 1024), ("IQ2_XXS", "Q4_K", 32, 6, 256, 2048),
+                                              ("Q4_K", "Q6_K", 32, 4, 512, 2048)])
+def test_moe_fused_bit_identical(fn, gu, dn, ne, k, ffe, d):
+    """One token: the fused kernel's output equals the two-kernel layer's bit for bit (the same arithmetic in the same
+    order), over several calls in a row (the counters are zeroed by each call's last CTA), and stays within the
+    float64 bar."""
+    rng = np.random.default_rng(ne + ffe + d)
+    gq, dq = BY_NAME[gu], BY_NAME[dn]
+    W = make_moe(rng, gq, dq, ne, ffe, d)
+    outs = {}
+    try:
+        for var in (0, 2):
+            fn.moe_var(var)
+            rng2 = np.random.default_rng(5)
+            outs[var] = []
+            for _ in range(3):
+                lg = (rng2.standard_normal((1, ne + 1)) * 2).astype(np.float32)
+                x = random_x(1, d, rng2)
+                y, sel, w = fn.moe(gq, dq, ne, k, ffe, d, *W, lg, x)
+                outs[var].append((y, sel, w, lg, x))
+    finally:
+        fn.moe_var(0)
+    for (y0, s0, w0, lg, x), (y2, s2, w2, _, _) in zip(outs[0], outs[2]):
+        assert np.array_equal(s0, s2) and np.array_equal(w0.view(np.uint32), w2.view(np.uint32))
+        assert np.array_equal(y0.view(np.uint32), y2.view(np.uint32))
+        y64, _, _ = oracle(gq, dq, ne, k, ffe, d, W, lg, x)
+        assert np.abs(y2 - y64).max() <= MOE_TOL * np.abs(y64).max()
+
+
+def test_moe_fused_repeated_calls_on_one_handle(fn):
+    """Config 3 through one resident handle, five calls in a row with different tokens: the fused layer (whose last CTA
+    zeroes the per-slot counters for the next call) matches the two-kernel layer bit for bit on every call."""
+    import torch
+    gq, dq, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 512, 10, 512, 2048
+    rng = np.random.default_rng(41)
+    W = make_moe(rng, gq, dq, ne, ffe, d)
+    h = fn.moe_create(gq, dq, ne, k, ffe, d, *W)
+    dev = torch.device("cuda", 0)
+    lg = torch.from_numpy((rng.standard_normal((5, ne + 1)) * 2).astype(np.float32)).to(dev)
+    x = torch.from_numpy(random_x(5, d, rng)).to(dev)
+    ys = {}
+    try:
+        for var in (0, 2):
+            fn.moe_var(var)
+            y = torch.zeros(5, d, device=dev)
+            for i in range(5):
+                fn.moe_run(h, lg[i].data_ptr(), ne + 1, x[i].data_ptr(), y[i].data_ptr(), 1, 0, 0)
+            fn.sync()
+            ys[var] = y.cpu().numpy()
+    finally:
+        fn.moe_var(0)
+        fn.moe_free(h)
+    assert np.array_equal(ys[0].view(np.uint32), ys[2].view(np.uint32))
