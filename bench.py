@@ -1,28 +1,33 @@
-"""Benchmark of the B200 decode hot path: dequant-fused GEMV throughput (the format sweep).
+"""Benchmark of the B200 decode hot path: dequant-fused GEMV throughput (the format sweep) with the
+config-3 MoE layer, at one fixed total workload on 1..N GPUs.
 
-A step is one pass of the format sweep at batch 1: the 13 graded GGUF formats x (2048x4096, 4096x2048, 512x2048)
-(out x in) plus the Q6_K lm_head 151936x2048, 40 GEMVs, each weight read once (385 MB per step, larger than the
-126 MB L2, so every step streams its weights from HBM). Weights are seeded synthetic GGUF blocks (uniform random
-bytes, fp16 scales |N(0,1)|*1e-3), x is N(0,1): the reference's real model tensors are not shipped.
+A step is one batch-1 pass of: the 13 graded GGUF formats x (2048x4096, 4096x2048, 512x2048) (out x in), the
+config-3 MoE layer (512 experts, top-10, width 512, IQ3_XXS gate/up, Q4_K down, shared expert) and the Q6_K lm_head
+151936x2048 with its fused argmax; 400 MB of weights per step, larger than the 126 MB L2, so every step streams its
+weights from HBM. Weights are seeded synthetic GGUF blocks (uniform random bytes, fp16 scales |N(0,1)|*1e-3), x is
+N(0,1), router logits 2 N(0,1): the reference's real model tensors are not shipped.
 
-  value  device-resident throughput: algorithmic bytes (GGUF weight bytes + 4*cols x + 4*rows y per GEMV) of all
-         ranks / the max over ranks of the CUDA-event time of K steps, each step one replay of the sweep captured as
-         CUDA graphs: the 39 independent sweep GEMVs as 8 concurrent chains (programmatic dependent launch inside a
-         chain), then the lm_head
-  e2e    the same metric through the C ABI with host buffers: one fn_w_step_host call per step copies every x in from
-         pinned memory, runs the step's GEMVs and copies every y (the lm_head: its token id) out, inside the timed
-         region
+  value  device-resident throughput: the step's algorithmic bytes (GGUF weight bytes + 4*cols x + 4*rows y per GEMV;
+         the MoE layer: the k routed and the shared experts' rows) / the max over ranks of the CUDA-event time of K
+         steps, each step one replay of the captured CUDA graphs: the 39 independent sweep GEMVs as 8 concurrent
+         chains (programmatic dependent launch inside a chain), the MoE layer, the lm_head
+  e2e    the same metric with host buffers: each step copies every input (the GEMVs' x, the MoE layer's x and router
+         logits) in from pinned memory, runs the step's library launches and copies every output (the GEMVs' y, the
+         MoE output, the token id) out, inside the timed region
   roofline  the dominant kernel (the lm_head GEMV): its algorithmic bytes / its mean CUDA-event duration inside the
          timed region, against the measured HBM copy bandwidth
   cpu_baseline  the reference's CPU path (gguf-py dequant + float64 numpy GEMV) on a bounded row sample, 1 core
 
-`--impl reference` times that CPU path with every host core instead (rank 0 only; other ranks exit 0).
-N > 1 (torchrun): every rank runs the sweep on its own GPU and weights (weak scaling; no data-path collective).
+N > 1 (torchrun, one rank per GPU): the same total step split the north star's way (strong scaling): every GEMV and
+the lm_head by rows (rank g owns rows [g R / N, (g + 1) R / N); the lm_head's argmax is combined in-kernel from the
+ranks' keys over NVLink), the MoE layer by experts (the slot outputs combined in-kernel over NVLink).
+`--impl reference` times the CPU path with every host core instead (rank 0 only; other ranks exit 0).
 `--components` (1 GPU) prints one JSON line per component instead of the bench line: every sweep GEMV alone with cold
 weights (fn_bench_gemv), the tensor-core batched GEMV at 8 and 32 tokens against the CUDA-core batched GEMV, the
 config-3 MoE layer and the config-4 DeltaNet layer step, each timed with CUDA events over a CUDA graph of back-to-back
 calls whose weights alternate between copies (together larger than L2).
-`--workload decode` prints the config-5 decode line instead (tok/s; see run_decode).
+`--workload decode` prints the config-5 decode line instead (tok/s; see run_decode). `--workload kernel` runs one
+kernel family alone for an ncu capture (run_kernel). `--workload lm_head` runs the lm_head alone.
 """
 
 from __future__ import annotations
@@ -465,7 +470,7 @@ def run_reference(args, rank):
     if rank != 0:
         return
     from oracle.ref_path import CPUSweep
-    work = workload()
+    work = workload() + moe3_gemvs()
     cores = os.cpu_count() or 1
     steps, warm = args.steps, args.warmup
     budget = 150.0  # seconds for the whole run
@@ -481,18 +486,369 @@ def run_reference(args, rank):
     s.close()
     total = sum(times)
     gbs = s.bytes * steps / total / 1e9
-    sample = f"every GEMV of the sweep cut to {frac:.4g} of its rows ({s.bytes / 1e6:.1f} MB of GGUF weights per step)"
+    sample = (f"every GEMV of the step (the MoE layer as its 33 expert GEMVs) cut to {frac:.4g} of its rows "
+              f"({s.bytes / 1e6:.1f} MB of GGUF weights per step)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": round(1e3 * total / steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "config2 format sweep (13 formats x 3 shapes + Q6_K lm_head 151936x2048), bs=1",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "config2 format sweep (13 formats x 3 shapes + Q6_K lm_head 151936x2048) + config-3 "
+                               "MoE layer, bs=1",
                    "path": "gguf-py 0.19.0 quants.dequantize -> float64 numpy x . W^T (flashnext/ref_fn.py:44-53, "
                            "flashnext/test_fn_quants.py:34)"},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def run_kernel(args):
+    """`--workload kernel`: one kernel family alone, `steps` eager launches on one stream (PDL as set by FN_PDL) with
+    two weight copies alternating, for ncu captures of a single kernel (-k / -c) from a committed command; prints one
+    JSON line with the mean time per call. --kernel gemv / tc_gemv: --format, --rows, --cols, --tokens; moe: BASELINE
+    config 3 (IQ3_XXS gate/up, Q4_K down, 512 experts, top-10, one token; --moe-var selects the MoE variant); gdn: the
+    config-4 DeltaNet core step."""
+    import torch
+    from fn import FN
+    from synth import BY_NAME, random_blocks
+    f = FN()
+    f.set_device(0)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(3)
+    s = torch.cuda.Stream()
+    cs = s.cuda_stream
+    frees = []
+    if args.kernel in ("gemv", "tc_gemv"):
+        q, r, c, nt = BY_NAME[args.format], args.rows, args.cols, args.tokens
+        if args.warps >= 0:  # the decode step plans its GEMVs with 16 warps per CTA (DecodeModel)
+            f.gemv_tune(args.warps)
+        mk = f.w_create if args.kernel == "gemv" else f.tc_create
+        hs = [mk(q, random_blocks(q, r, c, rng), r, c) for _ in range(2)]
+        frees = [(f.w_free if args.kernel == "gemv" else f.tc_free, h) for h in hs]
+        x = torch.randn(nt, c, device=dev)
+        y = torch.zeros(nt, r, device=dev)
+        call = (lambda i: f.w_gemv(hs[i % 2], x.data_ptr(), c, y.data_ptr(), r, nt, 0, cs)) if args.kernel == "gemv" \
+            else (lambda i: f.tc_gemv(hs[i % 2], x.data_ptr(), c, y.data_ptr(), r, nt, 0, cs))
+        what = {"kernel": args.kernel, "format": args.format, "rows": r, "cols": c, "tokens": nt, "warps": args.warps}
+    elif args.kernel == "moe":
+        gu, dn, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 512, 10, 512, 2048
+        f.moe_var(args.moe_var)
+        hs = [f.moe_create(gu, dn, ne, k, ffe, d, random_blocks(gu, ne * ffe, d, rng), random_blocks(gu, ne * ffe, d, rng),
+                           random_blocks(dn, ne * d, ffe, rng), random_blocks(gu, ffe, d, rng),
+                           random_blocks(gu, ffe, d, rng), random_blocks(dn, d, ffe, rng)) for _ in range(2)]
+        frees = [(f.moe_free, h) for h in hs]
+        lg = torch.randn(ne + 1, device=dev) * 2
+        x = torch.randn(d, device=dev)
+        y = torch.zeros(d, device=dev)
+        call = lambda i: f.moe_run(hs[i % 2], lg.data_ptr(), ne + 1, x.data_ptr(), y.data_ptr(), 1, 2, cs)  # noqa: E731
+        what = {"kernel": "moe", "config": "config3", "moe_var": args.moe_var}
+    else:  # gdn
+        NKH, NVH, DS = 16, 32, 128
+        CONVCH = 2 * NKH * DS + NVH * DS
+        hs = []
+        for _ in range(2):
+            hs.append(f.gdn_create(NKH, NVH, (rng.standard_normal((CONVCH, 4)) * 0.5).astype(np.float32),
+                                   (rng.standard_normal(NVH) * 0.5).astype(np.float32),
+                                   (-np.exp(rng.standard_normal(NVH) * 0.5)).astype(np.float32),
+                                   (1 + 0.1 * rng.standard_normal(DS)).astype(np.float32),
+                                   (rng.standard_normal((NVH, DS, DS)) * 0.02).astype(np.float32),
+                                   rng.standard_normal((3, CONVCH)).astype(np.float32)))
+        frees = [(f.gdn_free, h) for h in hs]
+        qkvz = torch.randn(CONVCH + NVH * DS, device=dev)
+        ab = torch.randn(2 * NVH, device=dev)
+        out = torch.zeros(NVH * DS, device=dev)
+        call = lambda i: f.gdn_run(hs[i % 2], qkvz.data_ptr(), CONVCH, qkvz.data_ptr() + 4 * CONVCH, NVH * DS,  # noqa: E731
+                                   ab.data_ptr(), 2 * NVH, out.data_ptr(), NVH * DS, 1, 1, cs)
+        what = {"kernel": "gdn", "config": "config4 core"}
+    for i in range(max(3, args.warmup)):
+        call(i)
+    f.sync(cs)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for i in range(args.steps):
+        call(i)
+    b.record(s)
+    f.sync(cs)
+    print(json.dumps(dict(what, steps=args.steps, us_per_call=round(a.elapsed_time(b) * 1e3 / args.steps, 3))), flush=True)
+    f.moe_var(0)
+    for fr, h in frees:
+        fr(h)
+
+
+MOE3 = ("IQ3_XXS", "Q4_K", 512, 10, 512, 2048)  # BASELINE config 3: gate/up, down, experts, top-k, width, hidden
+
+
+def moe3_gemvs():
+    """The config-3 MoE layer of one token as the GEMVs it reads (the k routed experts and the shared expert: gate and
+    up over the hidden size, down over the width): the CPU arms' restatement of its weight traffic."""
+    from synth import BY_NAME
+    gu, dn, ne, k, ffe, d = MOE3
+    return [(BY_NAME[gu], ffe, d, gu)] * (2 * (k + 1)) + [(BY_NAME[dn], d, ffe, dn)] * (k + 1)
+
+
+def moe3_bytes():
+    """Algorithmic bytes of one config-3 MoE layer for one token: the k routed experts' and the shared expert's
+    gate, up and down rows, each read once."""
+    from synth import BY_NAME
+    gu, dn, ne, k, ffe, d = MOE3
+    return (k + 1) * (2 * ffe * row_bytes_of(BY_NAME[gu], d) + d * row_bytes_of(BY_NAME[dn], ffe))
+
+
+class SweepStep:
+    """The bench step on this rank: the 39 sweep GEMVs, the config-3 MoE layer (one token) and the lm_head with its
+    fused argmax. One GPU: everything here. N ranks (one per GPU): the north star's partitions at a fixed total
+    workload (strong scaling): every GEMV split by rows (rank g owns rows [g R / N, (g + 1) R / N): each row's sum is
+    the one-GPU sum), the lm_head split by vocabulary rows with its argmax combined in-kernel over NVLink
+    (parallel.LmHeadSplit), the MoE layer split by experts with the slot outputs exchanged in-kernel
+    (fn_moe_ep_create / fn_moe_ep_run). Every input (the GEMVs' x, the MoE layer's x and router logits) is a view of
+    one device buffer X and every output (the GEMVs' y slices, the MoE output, the argmax) of one buffer Y, so a
+    step's host round trip is one copy each way."""
+
+    def __init__(self, f, work, rank, world, group, with_moe=True):
+        import torch
+        from parallel import LmHeadSplit, expert_range, row_range
+        from synth import BY_NAME, random_blocks
+        self.f, self.work, self.world, self.group, self.with_moe = f, work, world, group, with_moe
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gu, dn, ne, k, ffe, d = MOE3
+        self.gu, self.dn = BY_NAME[gu], BY_NAME[dn]
+        # inputs: every GEMV's x, then the MoE layer's x and its router logits (the same values on every rank)
+        xlen = [c for _, _, c, _ in work] + [d, ne + 1]
+        self.xoff = np.concatenate([[0], np.cumsum(xlen)]).astype(int)
+        X = torch.empty(int(self.xoff[-1]), device=dev)
+        for i, n in enumerate(xlen):
+            g = torch.Generator("cuda").manual_seed(i)
+            X[self.xoff[i]:self.xoff[i + 1]] = torch.randn(n, device=dev, generator=g) * (2.0 if i == len(xlen) - 1 else 1.0)
+        self.X = X
+        self.rows = [row_range(r, world, rank) for _, r, _, _ in work]
+        ylen = [r1 - r0 for r0, r1 in self.rows] + [d, 4]  # y slices, the MoE output, the argmax (one int32 slot)
+        self.yoff = np.concatenate([[0], np.cumsum(ylen)]).astype(int)
+        self.Y = torch.zeros(int(self.yoff[-1]), device=dev)
+        self.hs, self.head = [], None
+        self.step_bytes = sum(alg_bytes(q, r, c) for q, r, c, _ in work) + (moe3_bytes() if with_moe else 0)
+        self.head_rows = self.rows[-1][1] - self.rows[-1][0]
+        self.head_bytes = alg_bytes(work[-1][0], self.head_rows, work[-1][2])
+        for i, (q, r, c, name) in enumerate(work):
+            raw = random_blocks(q, r, c, np.random.default_rng(i))  # the same matrix on every rank
+            r0, r1 = self.rows[i]
+            if i == len(work) - 1 and world > 1:
+                self.head = LmHeadSplit(f, group, q, raw, r, c)
+            else:
+                self.hs.append(f.w_create(q, np.ascontiguousarray(raw[r0:r1]), r1 - r0, c))
+            del raw
+        self.moe = 0
+        self.launches_per_step = len(work) + (1 if world > 1 else 0)  # the split lm_head adds its key combine
+        if not with_moe:
+            return
+        rng = np.random.default_rng(77)  # config-3 weights, the same on every rank
+        Wg, Wu = random_blocks(self.gu, ne * ffe, d, rng), random_blocks(self.gu, ne * ffe, d, rng)
+        Wd = random_blocks(self.dn, ne * d, ffe, rng)
+        sh = [random_blocks(self.gu, ffe, d, rng), random_blocks(self.gu, ffe, d, rng), random_blocks(self.dn, d, ffe, rng)]
+        if world > 1:
+            e0, e1 = expert_range(ne, world, rank)
+            self.moe = f.moe_ep_create(self.gu, self.dn, ne, k, ffe, d, group.id, np.ascontiguousarray(Wg[e0 * ffe:e1 * ffe]),
+                                       np.ascontiguousarray(Wu[e0 * ffe:e1 * ffe]), np.ascontiguousarray(Wd[e0 * d:e1 * d]),
+                                       *sh)
+        else:
+            self.moe = f.moe_create(self.gu, self.dn, ne, k, ffe, d, Wg, Wu, Wd, *sh)
+        del Wg, Wu, Wd
+        self.launches_per_step += 3 if world == 1 else 4  # routing, gate/up, down (+ the combine across ranks)
+
+    def x(self, i):
+        return self.X.data_ptr() + 4 * int(self.xoff[i])
+
+    def y(self, i):
+        return self.Y.data_ptr() + 4 * int(self.yoff[i])
+
+    def launch_gemv(self, i, s, early=True):
+        q, r, c, _ = self.work[i]
+        r0, r1 = self.rows[i]
+        if i == len(self.work) - 1:  # the lm_head: logits slice and the vocabulary-wide argmax
+            amax = self.y(len(self.work) + 1)
+            if self.head is not None:
+                self.head.run(self.x(i), c, amax, 1, self.y(i), 2 if early else 0, s)
+            else:
+                self.f.w_gemv_argmax(self.hs[i], self.x(i), c, self.y(i), r, 1, 2 if early else 0, 0, amax, 0, s)
+        else:
+            self.f.w_gemv(self.hs[i], self.x(i), c, self.y(i), r1 - r0, 1, 2 if early else 0, s)
+
+    def launch_moe(self, s):
+        ne, n = MOE3[2], len(self.work)
+        run = self.f.moe_ep_run if self.world > 1 else self.f.moe_run
+        run(self.moe, self.x(n + 1), ne + 1, self.x(n), self.y(n), 1, 0, s)
+
+    def host_buffers(self):
+        """Pinned host copies of X and Y (the e2e path's inputs and outputs)."""
+        import torch
+        return self.X.cpu().pin_memory(), torch.empty(self.Y.numel(), dtype=torch.float32).pin_memory()
+
+    def free(self):
+        for h in self.hs:
+            self.f.w_free(h)
+        if self.head is not None:
+            self.head.close()
+        if self.moe:
+            self.f.moe_free(self.moe)
+
+
+def run_sweep(f, args, rank, world, local, dist):
+    """The default step (SweepStep) on this rank: device-timed value with the inputs resident, then the e2e value with
+    the inputs copied in from pinned host memory and the outputs copied out every step. Returns the JSON line."""
+    import torch
+    from parallel import PeerGroup
+
+    work = workload() if args.workload == "sweep" else workload()[-1:]
+    group = None
+    if world > 1:
+        def gather(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+        group = PeerGroup(f, rank, world, gather, dist.barrier)
+    st = SweepStep(f, work, rank, world, group, with_moe=args.workload == "sweep")
+    n = len(work)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    s0 = stream.cuda_stream
+    # first launches outside capture (kernel attributes, error-word address); every rank makes the same group calls
+    for i in range(n):
+        st.launch_gemv(i, s0, early=False)
+    if st.with_moe:
+        st.launch_moe(s0)
+    f.sync(s0)
+
+    # the sweep's GEMVs are independent (own weights, inputs and outputs): each is launched early (it reads its x
+    # without waiting for the kernel before it, the reference's early-GEMV protocol) and they run as BRANCHES
+    # concurrent chains of one graph (a fork and a join on the capture stream), so several are resident on an SM
+    # at once; the MoE layer and the lm_head with its argmax are graphs of their own on the main stream
+    side = [torch.cuda.Stream() for _ in range(args.branches)]
+    g_small = torch.cuda.CUDAGraph() if n > 1 else None
+    g_moe = torch.cuda.CUDAGraph() if st.with_moe else None
+    g_head = torch.cuda.CUDAGraph()
+    if g_small is not None:
+        with torch.cuda.graph(g_small, stream=stream, capture_error_mode="thread_local"):
+            main_s = torch.cuda.current_stream()
+            for sd in side:
+                sd.wait_stream(main_s)
+            for i in range(n - 1):
+                st.launch_gemv(i, side[i % len(side)].cuda_stream)
+            for sd in side:
+                main_s.wait_stream(sd)
+    if g_moe is not None:
+        with torch.cuda.graph(g_moe, stream=stream, capture_error_mode="thread_local"):
+            st.launch_moe(torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.graph(g_head, stream=stream, capture_error_mode="thread_local"):
+        st.launch_gemv(n - 1, torch.cuda.current_stream().cuda_stream, early=False)
+    graphs = [g for g in (g_small, g_moe, g_head) if g is not None]
+
+    def step():
+        for g in graphs:
+            g.replay()
+
+    def max_over_ranks(v):
+        if dist:
+            t = torch.tensor([v], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return v
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(graphs) + 1)] for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0.record(stream)
+    for k in range(K):
+        ev[k][0].record(stream)
+        for j, g in enumerate(graphs):
+            g.replay()
+            ev[k][j + 1].record(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    seg = [sum(ev[k][j].elapsed_time(ev[k][j + 1]) for k in range(K)) / K for j in range(len(graphs))]
+    head_ms = seg[-1]
+    value = st.step_bytes * K / (ms / 1e3) / 1e9
+
+    # e2e: every step copies all inputs in from pinned host memory, runs the step's library launches (the captured
+    # graphs of the same calls) and copies every output out (the GEMVs' y slices, the MoE output, the token id)
+    xh, yh = st.host_buffers()
+    h2d, d2h = xh.numel() * 4, yh.numel() * 4
+    Ke = max(3, min(K, 200))
+
+    def e2e_step():
+        st.X.copy_(xh, non_blocking=True)
+        step()
+        yh.copy_(st.Y, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(Ke):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b))
+    e2e = st.step_bytes * Ke / (e2e_ms / 1e3) / 1e9
+    yv = yh.numpy()
+    tok = int(yv[-4:].view(np.int32)[0])
+    ok = bool(np.isfinite(yv[:-4]).all()) and 0 <= tok < work[-1][1]
+
+    peak, peak_kind = measured_peak()
+    achieved = st.head_bytes / (head_ms / 1e3) / 1e9
+    traffic = profile_traffic()
+    if traffic is not None:  # the capture is of the whole 151936-row head; a rank's slice reads its share
+        traffic = round(traffic * st.head_rows / work[-1][1])
+    names = (["39 sweep GEMVs"] if g_small is not None else []) + (["config-3 MoE layer"] if g_moe is not None else [])
+    names.append("lm_head" + (" slice + argmax combine" if world > 1 else " + argmax"))
+    part = ("1 GPU" if world == 1 else f"{world} GPUs: every GEMV and the lm_head split by rows (argmax combined "
+            f"in-kernel over NVLink), the MoE layer split by experts (outputs combined in-kernel over NVLink)")
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 format sweep: 13 formats x (2048x4096, 4096x2048, 512x2048) + Q6_K lm_head "
+                               "151936x2048 with fused argmax" + (" + config-3 MoE layer (512 experts, top-10, width "
+                               "512, IQ3_XXS/Q4_K, shared expert)" if st.with_moe else "") + ", bs=1, one fixed "
+                               "total workload split over the GPUs",
+                   "bytes_per_step": st.step_bytes, "l2": "inputs larger than L2 (400 MB of weights per step over "
+                   "all GPUs, each read once per step)", "parallelism": part,
+                   "frac_of_measured_peak": round(value / world / peak, 4)},
+        "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": Ke, "outputs_finite": bool(ok), "path": "pinned host -> device copy of every input, the "
+                "step's library launches (as captured graphs), device -> pinned host copy of every output, per step"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": f"k_gemv<Q6_K> lm_head {st.head_rows}x2048 + fused argmax",
+                     "mean_launch_us": round(head_ms * 1e3, 2), "alg_bytes_per_launch": st.head_bytes},
+        "split_ms_per_step": {k: round(v, 5) for k, v in zip(names, seg)},
+        "gpu_launches": K * st.launches_per_step,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, frac, dt = cpu_baseline_sample(work + (moe3_gemvs() if st.with_moe else []))
+        line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                                "sample": f"every GEMV of the step (the MoE layer as its 33 expert GEMVs) cut to "
+                                          f"{frac:.3g} of its rows, one pass ({dt:.1f} s), gguf-py dequant + float64 "
+                                          f"numpy GEMV, 1 thread"}
+    del graphs, g_small, g_moe, g_head
+    torch.cuda.synchronize()
+    st.free()
+    if group is not None:
+        group.close()
+    return line
 
 
 def main():
@@ -504,9 +860,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--components", action="store_true",
                     help="per-component device times (sweep GEMVs alone, config-3 MoE layer, config-4 DeltaNet layer)")
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "lm_head", "decode"],
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "lm_head", "decode", "kernel"],
                     help="lm_head: only the dominant kernel (the small case the ncu capture profiles); decode: only "
-                         "the config-5 greedy decode (its own line, tok/s)")
+                         "the config-5 greedy decode (its own line, tok/s); kernel: one kernel family alone (--kernel)")
+    ap.add_argument("--kernel", default="gemv", choices=["gemv", "tc_gemv", "moe", "gdn"])
+    ap.add_argument("--format", default="Q4_K")
+    ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--moe-var", type=int, default=0, help="with --kernel moe: the MoE variant (fn_moe_var)")
+    ap.add_argument("--warps", type=int, default=-1,
+                    help="with --kernel gemv: warps per CTA of the plan (fn_gemv_tune; 0 = by weight size)")
     ap.add_argument("--no-decode", action="store_true", help="leave the config-5 decode out of the sweep line")
     ap.add_argument("--branches", type=int, default=8, help="concurrent graph chains of the sweep's independent GEMVs")
     ap.add_argument("--batch", type=int, default=1,
@@ -523,6 +887,9 @@ def main():
     if args.components:
         if rank == 0:
             run_components()
+        return
+    if args.workload == "kernel":
+        run_kernel(args)
         return
     if args.warmup < 3:
         args.warmup = 3
@@ -545,158 +912,7 @@ def main():
             raise SystemExit("--workload decode runs on one GPU")
         print(json.dumps(decode_line(f, args)), flush=True)
         return
-    work = workload() if args.workload == "sweep" else workload()[-1:]
-    hs, xs, ys = [], [], []
-    step_bytes = 0
-    for i, (q, r, c, name) in enumerate(work):
-        rng = np.random.default_rng(1000 * rank + i)
-        raw = random_blocks(q, r, c, rng)
-        hs.append(f.w_create(q, raw, r, c))
-        del raw
-        xs.append(torch.randn(c, device="cuda", generator=torch.Generator("cuda").manual_seed(i)))
-        ys.append(torch.empty(r, device="cuda"))
-        step_bytes += alg_bytes(q, r, c)
-    head_bytes = alg_bytes(*work[-1][:3])
-
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-
-    # the GEMVs of a step are independent, so each is launched early: it reads its x without waiting for the kernel
-    # before it and waits for that kernel only before it exits (the reference's early-GEMV protocol)
-    # the lm_head (last) carries the fused argmax, as in a decode step (lm_head GEMV + k_argmax)
-    amax_d = torch.zeros(8, dtype=torch.int32, device="cuda")
-
-    def launch(idx, s, early=True):
-        q, r, c, _ = work[idx]
-        if idx == len(work) - 1:
-            f.w_gemv_argmax(hs[idx], xs[idx].data_ptr(), c, ys[idx].data_ptr(), r, 1, 2 if early else 0, 0,
-                            amax_d.data_ptr(), 0, s)
-        else:
-            f.w_gemv(hs[idx], xs[idx].data_ptr(), c, ys[idx].data_ptr(), r, 1, 2 if early else 0, s)
-
-    for i in range(len(work)):  # first launches outside capture (kernel attributes, error-word address)
-        launch(i, stream.cuda_stream, early=False)
-    f.sync(stream.cuda_stream)
-
-    # the 39 sweep GEMVs are independent (own weights, inputs and outputs): they run as BRANCHES concurrent chains of
-    # the graph (a fork and a join on the capture stream), so several are resident on an SM at once
-    BRANCHES = args.branches
-    side = [torch.cuda.Stream() for _ in range(BRANCHES)]
-    g_small, g_head = (torch.cuda.CUDAGraph() if len(work) > 1 else None), torch.cuda.CUDAGraph()
-    if g_small is not None:
-        with torch.cuda.graph(g_small, stream=stream, capture_error_mode="thread_local"):
-            main = torch.cuda.current_stream()
-            for sd in side:
-                sd.wait_stream(main)
-            for i in range(len(work) - 1):
-                launch(i, side[i % BRANCHES].cuda_stream)
-            for sd in side:
-                main.wait_stream(sd)
-    with torch.cuda.graph(g_head, stream=stream, capture_error_mode="thread_local"):
-        launch(len(work) - 1, torch.cuda.current_stream().cuda_stream, early=False)
-
-    def step():
-        if g_small is not None:
-            g_small.replay()
-        g_head.replay()
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(local)
-    clocks.start()
-    e0.record(stream)
-    for k in range(K):
-        ev[k][0].record(stream)
-        if g_small is not None:
-            g_small.replay()
-        ev[k][1].record(stream)
-        g_head.replay()
-        ev[k][2].record(stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    if dist:
-        dist.barrier()
-    ms = e0.elapsed_time(e1)
-    head_ms = sum(ev[k][1].elapsed_time(ev[k][2]) for k in range(K)) / K
-    small_ms = sum(ev[k][0].elapsed_time(ev[k][1]) for k in range(K)) / K
-    f.sync(stream.cuda_stream)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * step_bytes * K / (ms / 1e3) / 1e9
-
-    # e2e: through the C ABI with pinned host buffers, host<->device copies inside the timed region
-    # one call per step (fn_w_step_host): every input copied in from pinned host memory, the step's GEMVs, every
-    # output copied out (the lm_head returns its token id, as a decode step does; the other GEMVs their outputs)
-    xh = torch.cat([x.cpu() for x in xs]).pin_memory()
-    yh = torch.empty(sum(w[1] for w in work[:-1]), dtype=torch.float32).pin_memory()
-    ih = torch.zeros(1, dtype=torch.int32).pin_memory()
-    h2d = sum(4 * w[2] for w in work)
-    d2h = sum(4 * w[1] for w in work[:-1]) + 4
-    Ke = max(3, min(K, 200))
-
-    def e2e_step():
-        f.w_step_host(hs, xh.data_ptr(), yh.data_ptr(), len(work) - 1, ih.data_ptr(), stream.cuda_stream)
-        f.sync(stream.cuda_stream)
-
-    for _ in range(3):
-        e2e_step()
-    if dist:
-        dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(Ke):
-        e2e_step()
-    b.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b)
-    if dist:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = world * step_bytes * Ke / (e2e_ms / 1e3) / 1e9
-    ok = bool(np.isfinite(yh.numpy()).all()) and 0 <= int(ih[0]) < work[-1][1]
-    ok = ok and int(ih[0]) == int(amax_d[0].item())  # same x: the host-path token equals the graph's
-
-    peak, peak_kind = measured_peak()
-    achieved = head_bytes / (head_ms / 1e3) / 1e9
-    traffic = profile_traffic()
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 format sweep: 13 formats x (2048x4096, 4096x2048, 512x2048) + Q6_K lm_head "
-                               "151936x2048 with fused argmax, bs=1, 40 GEMVs per step (e2e: the lm_head returns its token id)",
-                   "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (385 MB of weights per step, each "
-                   "read once per step)", "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-                   "frac_of_measured_peak": round(value / world / peak, 4)},
-        "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": Ke, "outputs_finite": bool(ok)},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "k_gemv<Q6_K> lm_head 151936x2048 + fused argmax", "mean_launch_us": round(head_ms * 1e3, 2),
-                     "alg_bytes_per_launch": head_bytes},
-        "split_ms_per_step": {"39 sweep GEMVs": round(small_ms, 5), "lm_head": round(head_ms, 5)},
-        "gpu_launches": K * len(work),
-        "clocks": clk,
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, frac, dt = cpu_baseline_sample(work)
-        line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
-                                "sample": f"every GEMV of the sweep cut to {frac:.3g} of its rows, one pass "
-                                          f"({dt:.1f} s), gguf-py dequant + float64 numpy GEMV, 1 thread"}
-    del g_small, g_head
-    for h in hs:
-        f.w_free(h)
+    line = run_sweep(f, args, rank, world, local, dist)
     if world == 1 and args.workload == "sweep" and not args.no_decode:
         line["decode"] = run_decode(f, args, rank, with_cpu=not args.no_cpu_baseline)
         line["gpu_launches"] += line["decode"]["gpu_launches_per_step"] * (64 + 256 - 1) * line["decode"]["generations"]
