@@ -148,4 +148,24 @@ cudaError_t launch_k(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaSt
     return cudaLaunchKernelEx(&cfg, k, ((P)args)...);
 }
 
+// launch_k for a grid of thread-block clusters of `cluster` CTAs along x (gridDim.x a multiple of it)
+template <typename... P, typename... A>
+cudaError_t launch_kc(void (*k)(P...), dim3 grid, dim3 block, unsigned cluster, size_t smem, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = settings().pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, k, ((P)args)...);
+}
+
 }  // namespace fn

@@ -4,23 +4,34 @@
 // Reference behaviour: k_gdn (engine/faie2fn.cu:1349-1431); value head h reads key head h % NKH (GGUF tiled order,
 // :10-11, 1374); the norm is gated with sigmoid(z) (:1424); softplus(u) = u for u > 20 (:1411).
 //
-// B200 design: CTA h (one per value head) has 512 threads; thread (j, c) = (tid >> 2, tid & 3) owns state column j,
-// key rows [32c, 32c + 32), i.e. 32 fp32 values of S[h] held in registers across all tokens of the launch. The four
-// quarter-column partial dot products (S^T k, S^T q) meet by two xor shuffles inside a warp, in a fixed order. When
+// B200 design: value head h is a cluster of GDN_SPLIT = 4 CTAs of 384 threads; CTA p owns state columns
+// [32p, 32p + 32): thread (jl, c) = (tid >> 2, tid & 3) of the first 128 owns column 32p + jl, key rows [32c, 32c + 32),
+// i.e. 32 fp32 values of S[h] held in registers across all tokens of the launch, so a head's 64 KB state streams
+// through four SMs. The columns are independent up to the gated norm: its sum of squares over the 128 columns is the
+// 16 warp partials (4 per CTA) added in column order through distributed shared memory, so every value equals the
+// one-CTA-per-head arrangement's. Every CTA of a head computes the conv, silu and l2 norm of all 128 q and k channels
+// (the dot products need them all) and only its own 32 value channels. The four quarter-column partial dot products
+// (S^T k, S^T q) meet by two xor shuffles inside a warp, in a fixed order. When
 // the caller says the state was complete before the previous kernel started (in a decode step the layer's previous
 // GDN launch is several kernels back), the state is loaded BEFORE griddepcontrol.wait, so under programmatic
 // dependent launch its HBM read overlaps the projection GEMVs before this kernel; back-to-back launches of one layer
 // load it after the wait. The step's own inputs (qkv, z, ab) are always read after the wait.
 // Conv state: the value channels keep [3][NVH*DS]; every value head keeps its own copy of its key head's q/k conv
 // state ([NVH][3][2][DS]): the value heads sharing a key head would otherwise race on it (one reading the old state
-// while another writes the new one); the copies stay equal.
+// while another writes the new one); the copies stay equal. Inside a head's cluster the CTA that owns a channel's column
+// block writes its history back, after the cluster barrier that follows every other CTA's read of it.
+#include <cooperative_groups.h>
+
 #include "fn_engine.h"
 #include "fn_gdn.h"
+
+namespace cg = cooperative_groups;
 
 namespace fn {
 
 constexpr int GDN_DS = 128;
-constexpr int GDN_THREADS = 4 * GDN_DS;
+constexpr int GDN_SPLIT = 4;                            // CTAs (one cluster) per value head
+constexpr int GDN_THREADS = 3 * GDN_DS;                 // q and k conv channels, then the value channels
 constexpr int KPAD = 36;  // floats per 32-row chunk of the staged q / k (32 + 4: chunk c at bank offset 4c)
 
 struct GdnArgs {
@@ -47,12 +58,16 @@ __device__ __forceinline__ float warp_sum_f(float v) {
     return v;
 }
 
-__global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
-    constexpr int DS = GDN_DS;
-    __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[DS];
-    __shared__ float red_q[4], red_k[4], red_o[16];
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int j = tid >> 2, c = tid & 3;
+__global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {  // clusters of GDN_SPLIT CTAs
+    constexpr int DS = GDN_DS, CW = DS / GDN_SPLIT;  // CW state columns per CTA
+    __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[CW];
+    __shared__ float red_q[4], red_k[4];
+    __shared__ float red_o[2][4];  // this CTA's 4 warp partials of sum o^2, by token parity (read by the cluster)
+    cg::cluster_group cl = cg::this_cluster();
+    const int p = (int)cl.block_rank();  // column block: state columns [CW p, CW (p + 1)) of the value head
+    const int h = blockIdx.x / GDN_SPLIT, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int jl = tid >> 2, c = tid & 3, j = CW * p + jl;  // state threads (tid < 4 CW): column j, rows [32c, 32c + 32)
+    const bool st_thr = tid < 4 * CW;
     const int kh = h % a.nkh, nvd = a.nvh * DS;
     // a batch of independent sequences (gridDim.y > 1, one token each): sequence blockIdx.y's state, conv histories
     // and token row
@@ -60,23 +75,30 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     float *const stS = a.S + (size_t)bq * a.nvh * DS * DS;
     float *const stQK = a.cst_qk + (size_t)bq * a.nvh * 3 * 2 * DS;
     float *const stV = a.cst_v + (size_t)bq * 3 * nvd;
-    // conv roles: threads 0..127 q channel d, 128..255 k channel d, 256..383 v channel d (of this value head)
-    const int role = tid >> 7, d = tid & 127;
-    int ch = -1;
+    // conv roles: threads 0..127 q channel d, 128..255 k channel d (every CTA of the head computes all 256, so each
+    // has the whole normalised q and k; only the owner of d's column block writes its history back), 256..256+CW-1
+    // value channel CW p + d
+    const int role = tid >> 7;
+    int d = tid & 127, ch = -1;
     float *stp = nullptr;
     int sst = 0;  // state stride between the 3 history slots
+    bool own = false;
     if (role == 0) {
         ch = kh * DS + d;
         stp = stQK + (size_t)h * 3 * 2 * DS + d;
         sst = 2 * DS;
+        own = d / CW == p;
     } else if (role == 1) {
         ch = a.nkh * DS + kh * DS + d;
         stp = stQK + (size_t)h * 3 * 2 * DS + DS + d;
         sst = 2 * DS;
-    } else if (role == 2) {
+        own = d / CW == p;
+    } else if (role == 2 && d < CW) {
+        d += CW * p;
         ch = 2 * a.nkh * DS + h * DS + d;
         stp = stV + (size_t)h * DS + d;
         sst = nvd;
+        own = true;
     }
     // ---- state, conv state, parameters: read before griddepcontrol.wait when the state was complete before the
     // previous kernel started (prefetch), else after it (the previous kernel may be this layer's previous step)
@@ -85,8 +107,10 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     float h0 = 0.f, h1 = 0.f, h2 = 0.f;
     float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
     auto load_state = [&]() {
+        if (st_thr) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = Sh[(size_t)(32 * c + i) * DS + j];
+            for (int i = 0; i < 32; ++i) s[i] = Sh[(size_t)(32 * c + i) * DS + j];
+        }
         if (ch >= 0) {
             h0 = stp[0];
             h1 = stp[sst];
@@ -95,7 +119,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
     };
     if (a.prefetch) load_state();
     if (ch >= 0) w = a.conv_w[ch];
-    const float nwj = a.norm_w[j], dtb = a.dt_bias[h], sa = a.ssm_a[h];
+    const float nwj = st_thr ? a.norm_w[j] : 0.f, dtb = a.dt_bias[h], sa = a.ssm_a[h];
     pdl_wait();
     pdl_trigger();
     if (!a.prefetch) {
@@ -124,7 +148,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
             if (role == 0) red_q[warp] = sq;
             else if (role == 1) red_k[warp - 4] = sq;
         }
-        if (role == 2) vs[d] = y;
+        if (role == 2 && ch >= 0) vs[d - CW * p] = y;
         __syncthreads();
         if (role <= 1) {
             const float* r = role == 0 ? red_q : red_k;
@@ -138,57 +162,68 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {
         const float sp = u > 20.0f ? u : log1pf(expf(u));
         const float decay = expf(sp * sa);
         __syncthreads();
-        // kv_j = sum_i S[i][j] k_i over this thread's quarter, then the 4 quarters
-        const float *kq = kn + c * KPAD, *qq = qn + c * KPAD;
-        float kv = 0.f;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-            const float4 kk = *(const float4 *)(kq + i);
-            kv = __fmaf_rn(s[i], kk.x, kv);
-            kv = __fmaf_rn(s[i + 1], kk.y, kv);
-            kv = __fmaf_rn(s[i + 2], kk.z, kv);
-            kv = __fmaf_rn(s[i + 3], kk.w, kv);
-        }
-        kv += __shfl_xor_sync(0xffffffffu, kv, 1);
-        kv += __shfl_xor_sync(0xffffffffu, kv, 2);
-        const float delta = __fmul_rn(__fmaf_rn(-decay, kv, vs[j]), beta);
         float o = 0.f;
+        if (st_thr) {
+            // kv_j = sum_i S[i][j] k_i over this thread's quarter, then the 4 quarters
+            const float *kq = kn + c * KPAD, *qq = qn + c * KPAD;
+            float kv = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-            const float4 kk = *(const float4 *)(kq + i), q4 = *(const float4 *)(qq + i);
-            s[i] = __fmaf_rn(decay, s[i], __fmul_rn(kk.x, delta));
-            s[i + 1] = __fmaf_rn(decay, s[i + 1], __fmul_rn(kk.y, delta));
-            s[i + 2] = __fmaf_rn(decay, s[i + 2], __fmul_rn(kk.z, delta));
-            s[i + 3] = __fmaf_rn(decay, s[i + 3], __fmul_rn(kk.w, delta));
-            o = __fmaf_rn(s[i], q4.x, o);
-            o = __fmaf_rn(s[i + 1], q4.y, o);
-            o = __fmaf_rn(s[i + 2], q4.z, o);
-            o = __fmaf_rn(s[i + 3], q4.w, o);
+            for (int i = 0; i < 32; i += 4) {
+                const float4 kk = *(const float4 *)(kq + i);
+                kv = __fmaf_rn(s[i], kk.x, kv);
+                kv = __fmaf_rn(s[i + 1], kk.y, kv);
+                kv = __fmaf_rn(s[i + 2], kk.z, kv);
+                kv = __fmaf_rn(s[i + 3], kk.w, kv);
+            }
+            kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+            kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+            const float delta = __fmul_rn(__fmaf_rn(-decay, kv, vs[jl]), beta);
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                const float4 kk = *(const float4 *)(kq + i), q4 = *(const float4 *)(qq + i);
+                s[i] = __fmaf_rn(decay, s[i], __fmul_rn(kk.x, delta));
+                s[i + 1] = __fmaf_rn(decay, s[i + 1], __fmul_rn(kk.y, delta));
+                s[i + 2] = __fmaf_rn(decay, s[i + 2], __fmul_rn(kk.z, delta));
+                s[i + 3] = __fmaf_rn(decay, s[i + 3], __fmul_rn(kk.w, delta));
+                o = __fmaf_rn(s[i], q4.x, o);
+                o = __fmaf_rn(s[i + 1], q4.y, o);
+                o = __fmaf_rn(s[i + 2], q4.z, o);
+                o = __fmaf_rn(s[i + 3], q4.w, o);
+            }
+            o += __shfl_xor_sync(0xffffffffu, o, 1);
+            o += __shfl_xor_sync(0xffffffffu, o, 2);
+            o *= 0.08838834764831845f;  // 1 / sqrt(128)
+            // gated RMSNorm over the head's 128 columns: this warp's 8 columns (lanes with c == 0), in lane order
+            const float oo = warp_sum_f(c == 0 ? o * o : 0.f);
+            if (lane == 0) red_o[t & 1][warp] = oo;
         }
-        o += __shfl_xor_sync(0xffffffffu, o, 1);
-        o += __shfl_xor_sync(0xffffffffu, o, 2);
-        o *= 0.08838834764831845f;  // 1 / sqrt(128)
-        // gated RMSNorm over the head's 128 columns (one value per column: lanes with c == 0)
-        const float oo = warp_sum_f(c == 0 ? o * o : 0.f);
-        if (lane == 0) red_o[warp] = oo;
-        __syncthreads();
-        if (c == 0) {
+        // the head's 16 warp partials (4 per CTA of the cluster, CTA p holding columns [32 p, 32 p + 32)), summed in
+        // column order through distributed shared memory
+        cl.sync();
+        if (st_thr && c == 0) {
             float ss = 0.f;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ss += red_o[i];
+            for (int q = 0; q < GDN_SPLIT; ++q) {
+                const float *ro = cl.map_shared_rank(&red_o[t & 1][0], q);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) ss += ro[i];
+            }
             const float r = rsqrtf(ss / DS + 1e-6f);
             const size_t oi = (size_t)h * DS + j;
             outp[(size_t)t * a.os + oi] = o * r * nwj * sigm(zp[(size_t)t * a.zs + oi]);
         }
         __syncthreads();
     }
+    if (st_thr) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) Sh[(size_t)(32 * c + i) * DS + j] = s[i];
-    if (ch >= 0) {
+        for (int i = 0; i < 32; ++i) Sh[(size_t)(32 * c + i) * DS + j] = s[i];
+    }
+    if (ch >= 0 && own) {
         stp[0] = h0;
         stp[sst] = h1;
         stp[2 * sst] = h2;
     }
+    cl.sync();  // no CTA leaves while another may still read its partials
 }
 
 int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs, const float *z, int zs, const float *ab,
@@ -218,7 +253,7 @@ int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs,
     a.nvh = p.nvh;
     a.nt = nt;
     a.prefetch = prefetch_state ? 1 : 0;
-    const cudaError_t e = launch_k(k_gdn, dim3(p.nvh, batch), dim3(GDN_THREADS), 0, s, a);
+    const cudaError_t e = launch_kc(k_gdn, dim3(p.nvh * GDN_SPLIT, batch), dim3(GDN_THREADS), GDN_SPLIT, 0, s, a);
     if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
     return 0;
 }

@@ -45,7 +45,8 @@ void fn_gemv_override(int wpt, int ks, int tb, int warps_per_sm);
  * (all warps' rings), stage KiB (unused by the per-warp rings), CTAs per SM (> 0 sets). No reference counterpart. */
 void fn_gemv_tune(int warps, int ring_kb, int stage_kb, int ctas_per_sm);
 /* MoE layer variant, the reference's A/B switch (engine/faie2fn.cu:2799): 0 (default) = a routing kernel before
- * gate/up, 1 = one token on one GPU routed inside the gate/up and down kernels. */
+ * gate/up, 1 = one token on one GPU routed inside the gate/up and down kernels, 2 = one token on one GPU in one fused
+ * gate/up + down kernel. */
 void fn_moe_var(int v);
 /* The reference's routed-expert launch shapes (engine/faie2fn.cu:2801-2806); the B200 MoE kernels size themselves
  * from the layer's shape and the SM count: accepted and ignored. */
