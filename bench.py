@@ -523,6 +523,7 @@ def run_kernel(args):
         q, r, c, nt = BY_NAME[args.format], args.rows, args.cols, args.tokens
         if args.warps >= 0:  # the decode step plans its GEMVs with 16 warps per CTA (DecodeModel)
             f.gemv_tune(args.warps)
+        f.qmma(args.qmma)
         mk = f.w_create if args.kernel == "gemv" else f.tc_create
         hs = [mk(q, random_blocks(q, r, c, rng), r, c) for _ in range(2)]
         frees = [(f.w_free if args.kernel == "gemv" else f.tc_free, h) for h in hs]
@@ -530,7 +531,8 @@ def run_kernel(args):
         y = torch.zeros(nt, r, device=dev)
         call = (lambda i: f.w_gemv(hs[i % 2], x.data_ptr(), c, y.data_ptr(), r, nt, 0, cs)) if args.kernel == "gemv" \
             else (lambda i: f.tc_gemv(hs[i % 2], x.data_ptr(), c, y.data_ptr(), r, nt, 0, cs))
-        what = {"kernel": args.kernel, "format": args.format, "rows": r, "cols": c, "tokens": nt, "warps": args.warps}
+        what = {"kernel": args.kernel, "format": args.format, "rows": r, "cols": c, "tokens": nt, "warps": args.warps,
+                "qmma": args.qmma}
     elif args.kernel == "moe":
         gu, dn, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 512, 10, 512, 2048
         f.moe_var(args.moe_var)
@@ -869,6 +871,8 @@ def main():
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--moe-var", type=int, default=0, help="with --kernel moe: the MoE variant (fn_moe_var)")
+    ap.add_argument("--qmma", type=int, default=1,
+                    help="with --workload kernel: Q4_K / Q6_K GEMVs on the tensor cores as integer products (fn_qmma)")
     ap.add_argument("--warps", type=int, default=-1,
                     help="with --kernel gemv: warps per CTA of the plan (fn_gemv_tune; 0 = by weight size)")
     ap.add_argument("--no-decode", action="store_true", help="leave the config-5 decode out of the sweep line")

@@ -225,6 +225,9 @@ FN_API void fn_gemv_override(int wpt, int ks, int tb, int warps_per_sm) {
 // (default: measured faster on the config-5 decode step, 2.99 against 3.18 ms per token), 1 = one token on one GPU
 // routed inside the gate/up and down kernels
 FN_API void fn_moe_var(int v) { settings().moe_var = v; }
+// Q4_K / Q6_K GEMVs of 1..4 tokens (rows up to 2048 columns) as exact integer products on the tensor cores (1) or on
+// the CUDA cores (0, the default)
+FN_API void fn_qmma(int on) { settings().qmma = on != 0; }
 // The reference's routed-expert launch shapes (engine/faie2fn.cu:2801-2806). The B200 MoE kernels size their grids
 // and rings from the layer's shape and the SM count, so there is nothing to override: accepted and ignored.
 FN_API void fn_moe_override(int gu_wpt, int gu_tb, int dn_wpt, int dn_tb) {

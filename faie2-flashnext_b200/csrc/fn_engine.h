@@ -67,6 +67,11 @@ struct GemvArgmax {
 // token strides xs, ys (x 16-byte aligned, xs a multiple of 4). early: x was complete before the previous kernel
 // started, so the GEMV does not wait for it before reading x (it waits before it exits). y may be null when am is
 // given (no logits written).
+// the same on the tensor cores as exact integer products (fn_qmma.cu): Q4_K / Q6_K rows of up to 2048 columns,
+// qmma_cap(type, cols) tokens at most (0: not this path)
+int qmma_cap(uint32_t type, int cols);
+int launch_qmma(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
+                bool early, cudaStream_t s, const GemvArgmax *am);
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
                 bool early, cudaStream_t s, const GemvArgmax *am = nullptr);
 
@@ -99,6 +104,7 @@ struct Settings {
     int bench_hot = 0;
     int moe_var = 0;         // MoE layer variant (fn_moe_var): 0 = a routing kernel before gate/up; 1 = one token
                              // on one GPU routed inside the gate/up and down kernels
+    int qmma = 0;            // Q4_K / Q6_K GEMVs of 1..4 tokens as integer tensor-core products (fn_qmma)
 };
 Settings &settings();
 int num_sms();

@@ -174,6 +174,24 @@ size_t plan_weight_bytes(const GemvPlan &p) { return (size_t)p.rows * p.ldw; }
 int launch_gemv(const GemvPlan &p, const uint8_t *W, const float *x, int xs, float *y, int ys, int nt, bool acc,
                 bool early, cudaStream_t s, const GemvArgmax *am) {
     if (nt < 1 || nt > p.ntcap) return fail("gemv: nt out of range for the plan");
+    // Q4_K / Q6_K on the tensor cores (integer products), cap tokens per launch: a token's result is the same in any
+    // batch (a row-split argmax exchange counts calls, so it takes one launch or the CUDA cores)
+    const int cap = settings().qmma ? qmma_cap(p.type, p.cols) : 0;
+    if (cap > 0 && !(am && am->xr && nt > cap)) {
+        for (int t0 = 0; t0 < nt; t0 += cap) {
+            const int n = std::min(cap, nt - t0);
+            GemvArgmax a2;
+            if (am) {
+                a2 = *am;
+                if (a2.index) a2.index += t0;
+                if (a2.key) a2.key += t0;
+            }
+            const int rc = launch_qmma(p, W, x + (size_t)t0 * xs, xs, y ? y + (size_t)t0 * ys : nullptr, ys, n, acc,
+                                       early, s, am ? &a2 : nullptr);
+            if (rc) return rc;
+        }
+        return 0;
+    }
     const size_t smem = gemv_smem(p, nt);
     if (smem > kDynSmem) return fail("gemv: " + std::to_string(nt) + " tokens of " + std::to_string(p.cols) +
                                        " columns do not fit in shared memory");

@@ -151,7 +151,9 @@ struct MoeCombineArgs {
 __global__ void __launch_bounds__(256) k_moe_ep_combine(const MoeCombineArgs a) {
     __shared__ float wsel[16];
     __shared__ int s_ok;
-    const int t = blockIdx.x, tid = threadIdx.x, ks = a.k + 1;
+    // CTA (chunk, t): rows [chunk d / gridDim.x, (chunk + 1) d / gridDim.x) of token t
+    const int t = blockIdx.y, tid = threadIdx.x, ks = a.k + 1;
+    const int i0 = (int)((long long)blockIdx.x * a.d / gridDim.x), i1 = (int)((long long)(blockIdx.x + 1) * a.d / gridDim.x);
     // the routing weights and logits were complete before the gate/up kernel two launches back passed its wait
     if (tid < a.k) wsel[tid] = a.rw[t * 16 + tid];
     pdl_wait();
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(256) k_moe_ep_combine(const MoeCombineArgs a) 
     if (s_ok) {
         const float *dp = a.dpart + ((size_t)(c & 1u) * MOE_EP_MAXT + t) * ks * a.d;
         const float sg = sigm(a.logits[(size_t)t * a.ls + a.ne]);
-        for (int i = tid; i < a.d; i += blockDim.x) {
+        for (int i = i0 + tid; i < i1; i += blockDim.x) {
             float acc = 0.0f;
             for (int q = 0; q < a.k; ++q) acc = __fmaf_rn(wsel[q], dp[(size_t)q * a.d + i], acc);
             const float v = __fmaf_rn(sg, dp[(size_t)a.k * a.d + i], acc);
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(256) k_moe_ep_combine(const MoeCombineArgs a) 
     if (tid == 0) {
         uint32_t tk;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(tk) : "l"(a.calls + 2) : "memory");
-        if (tk == gridDim.x - 1) {
+        if (tk == gridDim.x * gridDim.y - 1) {
             a.calls[0] = c + 1;
             a.calls[1] = expect;
             a.calls[2] = 0u;
@@ -382,7 +384,7 @@ int launch_moe(const MoePlan &p, const MoeWeights &w, const float *logits, int l
         if (ep) {  // ---- expert parallel: combine the ranks' slot outputs on every rank
             MoeCombineArgs c{logits, rw, ls, p.ne, p.k, p.d, nt, E.n, E.dpart[E.rank], E.counters[E.rank], E.calls,
                              (uint32_t)(chunks * nt), y, acc ? 1 : 0, dev_error_ptr()};
-            e = launch_k(k_moe_ep_combine, dim3(nt), dim3(256), 0, s, c);
+            e = launch_k(k_moe_ep_combine, dim3(std::max(1, std::min(16, p.d / 128)), nt), dim3(256), 0, s, c);
             if (e != cudaSuccess) return fail(std::string("moe combine launch: ") + cudaGetErrorString(e));
         }
     }

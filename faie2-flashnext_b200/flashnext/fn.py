@@ -37,7 +37,7 @@ EXPORTS = [
     "fn_tc_create", "fn_tc_free", "fn_tc_gemv", "fn_test_tc_gemv", "fn_bench_tc_gemv",
     "fn_embed_batch", "fn_rmsnorm_rows", "fn_attn_decode_batch", "fn_step_advance_batch", "fn_gdn_create_batch",
     "fn_gdn_run_batch", "fn_w_weights", "fn_w_prefetch_after", "fn_moe_prefetch_after", "fn_w_norm", "fn_moe_norm",
-    "fn_gemv_tune", "fn_moe_var", "fn_moe_override",
+    "fn_gemv_tune", "fn_moe_var", "fn_qmma", "fn_moe_override",
     "fn_decoder_create", "fn_decoder_free", "fn_decoder_step", "fn_decoder_launches",
     "fn_load", "fn_forward", "fn_reset", "fn_free", "fn_debug_layers", "fn_use_graphs", "fn_n_past", "fn_last_ms",
     "fn_dev_gb", "fn_split", "fn_model_dims",
@@ -74,6 +74,7 @@ class FN:
         d.fn_gemv_override.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
         d.fn_gemv_tune.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
         d.fn_moe_var.argtypes = [C.c_int]
+        d.fn_qmma.argtypes = [C.c_int]
         d.fn_moe_override.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
         d.fn_gemv_waves.argtypes = [C.c_int]
         d.fn_gemv_plan.argtypes = [C.c_uint32, C.c_int, C.c_int, I32]
@@ -512,6 +513,10 @@ class FN:
     def moe_var(self, v):
         """MoE variant (engine/faie2fn.cu:2799): 0 = a routing kernel, 1 = routed inside the expert kernels."""
         self.d.fn_moe_var(v)
+
+    def qmma(self, on):
+        """Q4_K / Q6_K GEMVs of 1..4 tokens on the tensor cores as exact integer products (1) or not (0, default)."""
+        self.d.fn_qmma(1 if on else 0)
 
     def sync(self, stream=0):
         self.check(self.d.fn_sync(C.c_void_p(stream)))

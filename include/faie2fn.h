@@ -48,6 +48,9 @@ void fn_gemv_tune(int warps, int ring_kb, int stage_kb, int ctas_per_sm);
  * gate/up, 1 = one token on one GPU routed inside the gate/up and down kernels, 2 = one token on one GPU in one fused
  * gate/up + down kernel. */
 void fn_moe_var(int v);
+/* Q4_K / Q6_K GEMVs of 1..4 tokens with rows of up to 2048 columns: 1 = exact integer products on the tensor cores
+ * (tcgen05.mma kind::i8), 0 (default) = the CUDA-core GEMV. No reference counterpart (this build's A/B switch). */
+void fn_qmma(int on);
 /* The reference's routed-expert launch shapes (engine/faie2fn.cu:2801-2806); the B200 MoE kernels size themselves
  * from the layer's shape and the SM count: accepted and ignored. */
 void fn_moe_override(int gu_wpt, int gu_tb, int dn_wpt, int dn_tb);
