@@ -398,6 +398,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) k_qmma(const __grid_constant__ 
                 bool ok = true;
                 if (c == 0) ok = wt(&sfull[tile & 1], (uint32_t)(tile >> 1) & 1u);
                 ok = ok && wt(&mdone[tb], (uint32_t)(p / QM_NBUF) & 1u);
+                ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: all lanes or none
                 qm_fence_after();
                 const bool valid = ok && tile * QM_M + row < nrow;
                 const uint8_t *srow = S + (size_t)(tile & 1) * QM_M * a.srs + (size_t)row * a.srs;
