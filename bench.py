@@ -506,7 +506,7 @@ def run_kernel(args):
     """`--workload kernel`: one kernel family alone, `steps` eager launches on one stream (PDL as set by FN_PDL) with
     two weight copies alternating, for ncu captures of a single kernel (-k / -c) from a committed command; prints one
     JSON line with the mean time per call. --kernel gemv / tc_gemv: --format, --rows, --cols, --tokens; moe: BASELINE
-    config 3 (IQ3_XXS gate/up, Q4_K down, 512 experts, top-10, one token; --moe-var selects the MoE variant); gdn: the
+    config 3 (IQ3_XXS gate/up, Q4_K down, 512 experts, top-10, --tokens tokens; --moe-var selects the MoE variant); gdn: the
     config-4 DeltaNet core step."""
     import torch
     from fn import FN
@@ -523,7 +523,7 @@ def run_kernel(args):
         q, r, c, nt = BY_NAME[args.format], args.rows, args.cols, args.tokens
         if args.warps >= 0:  # the decode step plans its GEMVs with 16 warps per CTA (DecodeModel)
             f.gemv_tune(args.warps)
-        f.qmma(args.qmma)
+        f.qmma(1 if args.qmma is None else args.qmma)
         mk = f.w_create if args.kernel == "gemv" else f.tc_create
         hs = [mk(q, random_blocks(q, r, c, rng), r, c) for _ in range(2)]
         frees = [(f.w_free if args.kernel == "gemv" else f.tc_free, h) for h in hs]
@@ -532,7 +532,7 @@ def run_kernel(args):
         call = (lambda i: f.w_gemv(hs[i % 2], x.data_ptr(), c, y.data_ptr(), r, nt, 0, cs)) if args.kernel == "gemv" \
             else (lambda i: f.tc_gemv(hs[i % 2], x.data_ptr(), c, y.data_ptr(), r, nt, 0, cs))
         what = {"kernel": args.kernel, "format": args.format, "rows": r, "cols": c, "tokens": nt, "warps": args.warps,
-                "qmma": args.qmma}
+                "qmma": 1 if args.qmma is None else args.qmma}
     elif args.kernel == "moe":
         gu, dn, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 512, 10, 512, 2048
         f.moe_var(args.moe_var)
@@ -540,11 +540,12 @@ def run_kernel(args):
                            random_blocks(dn, ne * d, ffe, rng), random_blocks(gu, ffe, d, rng),
                            random_blocks(gu, ffe, d, rng), random_blocks(dn, d, ffe, rng)) for _ in range(2)]
         frees = [(f.moe_free, h) for h in hs]
-        lg = torch.randn(ne + 1, device=dev) * 2
-        x = torch.randn(d, device=dev)
-        y = torch.zeros(d, device=dev)
-        call = lambda i: f.moe_run(hs[i % 2], lg.data_ptr(), ne + 1, x.data_ptr(), y.data_ptr(), 1, 2, cs)  # noqa: E731
-        what = {"kernel": "moe", "config": "config3", "moe_var": args.moe_var}
+        nt = args.tokens
+        lg = torch.randn(nt, ne + 1, device=dev) * 2
+        x = torch.randn(nt, d, device=dev)
+        y = torch.zeros(nt, d, device=dev)
+        call = lambda i: f.moe_run(hs[i % 2], lg.data_ptr(), ne + 1, x.data_ptr(), y.data_ptr(), nt, 2, cs)  # noqa: E731
+        what = {"kernel": "moe", "config": "config3", "moe_var": args.moe_var, "tokens": nt}
     else:  # gdn
         NKH, NVH, DS = 16, 32, 128
         CONVCH = 2 * NKH * DS + NVH * DS
@@ -871,8 +872,9 @@ def main():
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--moe-var", type=int, default=0, help="with --kernel moe: the MoE variant (fn_moe_var)")
-    ap.add_argument("--qmma", type=int, default=1,
-                    help="with --workload kernel: Q4_K / Q6_K GEMVs on the tensor cores as integer products (fn_qmma)")
+    ap.add_argument("--qmma", type=int, default=None,
+                    help="Q4_K / Q6_K GEMVs of up to 2048 columns on the tensor cores as integer products (fn_qmma); "
+                         "default: on for --workload kernel, the library's default elsewhere")
     ap.add_argument("--warps", type=int, default=-1,
                     help="with --kernel gemv: warps per CTA of the plan (fn_gemv_tune; 0 = by weight size)")
     ap.add_argument("--no-decode", action="store_true", help="leave the config-5 decode out of the sweep line")
@@ -911,6 +913,8 @@ def main():
 
     f = FN()
     f.set_device(local)
+    if args.qmma is not None:
+        f.qmma(args.qmma)
     if args.workload == "decode":
         if world > 1:
             raise SystemExit("--workload decode runs on one GPU")
