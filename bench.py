@@ -535,7 +535,7 @@ def run_kernel(args):
                 "qmma": 1 if args.qmma is None else args.qmma}
     elif args.kernel == "moe":
         gu, dn, ne, k, ffe, d = BY_NAME["IQ3_XXS"], BY_NAME["Q4_K"], 512, 10, 512, 2048
-        f.moe_var(args.moe_var)
+        f.moe_var(args.moe_var or 0)
         hs = [f.moe_create(gu, dn, ne, k, ffe, d, random_blocks(gu, ne * ffe, d, rng), random_blocks(gu, ne * ffe, d, rng),
                            random_blocks(dn, ne * d, ffe, rng), random_blocks(gu, ffe, d, rng),
                            random_blocks(gu, ffe, d, rng), random_blocks(dn, d, ffe, rng)) for _ in range(2)]
@@ -545,7 +545,7 @@ def run_kernel(args):
         x = torch.randn(nt, d, device=dev)
         y = torch.zeros(nt, d, device=dev)
         call = lambda i: f.moe_run(hs[i % 2], lg.data_ptr(), ne + 1, x.data_ptr(), y.data_ptr(), nt, 2, cs)  # noqa: E731
-        what = {"kernel": "moe", "config": "config3", "moe_var": args.moe_var, "tokens": nt}
+        what = {"kernel": "moe", "config": "config3", "moe_var": args.moe_var or 0, "tokens": nt}
     else:  # gdn
         NKH, NVH, DS = 16, 32, 128
         CONVCH = 2 * NKH * DS + NVH * DS
@@ -871,7 +871,8 @@ def main():
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=1)
-    ap.add_argument("--moe-var", type=int, default=0, help="with --kernel moe: the MoE variant (fn_moe_var)")
+    ap.add_argument("--moe-var", type=int, default=None,
+                    help="the MoE variant (fn_moe_var; default: 0 with --kernel moe, the library's default elsewhere)")
     ap.add_argument("--qmma", type=int, default=None,
                     help="Q4_K / Q6_K GEMVs of up to 2048 columns on the tensor cores as integer products (fn_qmma); "
                          "default: on for --workload kernel, the library's default elsewhere")
@@ -915,6 +916,8 @@ def main():
     f.set_device(local)
     if args.qmma is not None:
         f.qmma(args.qmma)
+    if args.moe_var is not None:
+        f.moe_var(args.moe_var)
     if args.workload == "decode":
         if world > 1:
             raise SystemExit("--workload decode runs on one GPU")

@@ -1,34 +1,45 @@
 // Batched decode GEMV on the 5th-generation tensor cores (tcgen05): y[t][r] = W[r] . x[t] for t < nt <= 32 tokens.
 //
 // At batch 8..32 the quantised GEMV becomes a dense contraction (rows x cols x nt), so this path dequantises each
-// weight tile once into shared memory and lets tcgen05.mma multiply it by all tokens at once, where the CUDA-core GEMV
-// would repeat the FMA work per token (its batched form, k_gemv<.., NT = 8, ..>, runs 8 tokens per call). The
-// reference has no batched path (its k_tgemv takes nt <= 8 on CUDA cores, engine/faie2fn.cu:734-955); the operator
-// contract is the same as fn_w_gemv's.
+// weight tile once and lets tcgen05.mma multiply it by all tokens at once, where the CUDA-core GEMV would repeat the
+// FMA work per token (its batched form, k_gemv<.., NT = 8, ..>, runs 8 tokens per call). The reference has no batched
+// path (its k_tgemv takes nt <= 8 on CUDA cores, engine/faie2fn.cu:734-955); the operator contract is the same as
+// fn_w_gemv's.
 //
 // Precision: the tensor cores take bf16 operands, so every weight value v (the exact GGUF dequantisation, load_group) and
-// every x value is split into v_hi = bf16(v) and v_lo = bf16(v - v_hi), and each 16-deep step runs three MMAs,
-// hi*hi + hi*lo + lo*hi, accumulated in fp32 in tensor memory: each product keeps about 16 mantissa bits (the lo*lo
-// term is below 2^-16 of it), so y is within about 3e-5 of float64, relative to max |y| (the stated tolerance is 1e-4).
+// every x value is split into v_hi = bf16(v) and v_lo = bf16(v - v_hi), and the products hi*hi + hi*lo + lo*hi are
+// accumulated in fp32 in tensor memory: each keeps about 16 mantissa bits (the lo*lo term is below 2^-16 of it), so y
+// is within about 3e-5 of float64, relative to max |y| (the stated tolerance is 1e-4). BF16 weights are exact in bf16
+// (v_lo = 0), so they take one MMA per step.
 //
-// Layout and schedule, per CTA (256 threads; one 128-row tile of W and a K range of its columns; CTAs split K when
-// there are fewer tiles than SMs, the last CTA of a tile adding the partials in split order, so y is deterministic):
-//   * K is walked in chunks of 128 columns, two chunk buffers in shared memory. For a chunk, warps decode the tile's
-//     128 x 128 values (one lane per row and 32-value group, stored as whole 16-byte core-matrix rows, so the 8 lanes
-//     of a store phase fill one core matrix) into A_hi / A_lo and
-//     stage x's N x 128 values into B_hi / B_lo, all in the tensor cores' canonical K-major layout without swizzle:
-//     8-row x 16-byte core matrices, the 8-row groups 128 bytes apart (SBO), the 8-column groups a whole M (or N)
-//     extent apart (LBO).
-//   * one thread issues the chunk's 8 x 3 MMAs (M = 128, N = 16 or 32, K = 16 each) and commits them to the buffer's
-//     mbarrier; the warps then decode the next chunk into the other buffer while the tensor cores work, and wait for a
-//     buffer's commit before they overwrite it.
-//   * the accumulator (128 lanes x N fp32 columns of tensor memory) is read by warps 0-3 (lane 32w + l = row
-//     32w + l) with tcgen05.ld and stored to y (or to the split's partial).
-// Every wait is bounded: a wait that runs out records DEV_WAIT_TIMEOUT, the CTA still waits (bounded) for the MMAs it
-// issued, frees its tensor memory and returns.
+// Weights on the device: GGUF rows cut into raw chunks of 256 columns (128 for the formats whose 256 columns exceed
+// 240 bytes), each chunk padded to a 16-byte multiple and stored tile-major (a chunk of a tile's 128 rows is one
+// contiguous run, one bulk copy), so that a chunk starts on a block boundary and a 16-byte boundary (a K-quant block's
+// fields then sit 16-byte aligned in shared memory).
+//
+// One CTA per SM streams its tiles (128 rows) chunk by chunk; warps meet only at mbarriers (no block barrier in the
+// loop), and every wait parks the warp in the hardware (try_wait with a suspend-time hint):
+//   * one lane issues the raw chunk copies into a ring of up to 8 slots (100-200 KB in flight per SM);
+//   * 16 decoder warps turn a step's 128 columns (4 groups of 32) into bf16 hi / lo and store them straight into
+//     tensor memory (tcgen05.st; warp w holds lanes 32 (w % 4) .. and group w / 4), which the MMAs read as their A
+//     operand, so the weights never pass through shared memory after the copy;
+//   * one warp copies each step's x columns of every token into a 4-slot fp32 staging ring (one 512-byte bulk copy per
+//     token, one token per lane), and 4 warps convert them into the B operand: x_hi of the N tokens, then x_lo, as
+//     2 N rows in the canonical K-major layout without swizzle (8-row x 16-byte core matrices, 8-row groups 128 bytes
+//     apart, 8-column groups 2 N x 16 bytes apart);
+//   * one lane issues two MMAs per 16-deep step (M = 128, K = 16): A_hi [x_hi | x_lo] with N = 2 npad, and A_lo x_hi
+//     with N = npad (the operand's first npad rows), into a tile's accumulators in tensor memory (double-buffered
+//     across tiles), and commits them to the buffers' mbarriers; an MMA costs about the same at N = 32 as at N = 64,
+//     so the x halves share one instruction;
+//   * 4 warps read a finished tile's accumulators (tcgen05.ld), add A_hi x_hi + A_hi x_lo + A_lo x_hi in that order
+//     and store y (or the split's partial) while the next tile runs.
+// Matrices with fewer tiles than SMs split K instead (one tile per CTA); the tile's last CTA adds the partials in split
+// order (release / acquire ticket), so y is deterministic. Every wait is bounded: a wait that runs out records
+// DEV_WAIT_TIMEOUT, the CTA waits (bounded) for the copies and MMAs it issued, frees its tensor memory and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -38,45 +49,44 @@
 namespace fn {
 
 constexpr int TC_M = 128;       // rows per tile (one MMA's M)
-constexpr int TC_KC = 128;      // columns per chunk
-constexpr int TC_THREADS = 512;
+constexpr int TC_KC = 128;      // columns per decode step (4 groups of 32, 8 MMA steps of 16)
 constexpr int TC_NMAX = 32;     // tokens per call
-constexpr int TC_TMEM_COLS = 32;
+constexpr int TC_DEC = 16;      // decoder warps: tensor-memory lane quarter w % 4, group w / 4 of a step
+constexpr int TC_XW = 4;        // warps staging x (the B operand)
+constexpr int TC_EPI = 4;       // read-back warps, one per tensor-memory lane quarter
+constexpr int W_X0 = TC_DEC, W_EPI0 = W_X0 + TC_XW, W_COPY = W_EPI0 + TC_EPI, W_XCOPY = W_COPY + 1, W_MMA = W_XCOPY + 1;
+constexpr int TC_THREADS = 32 * (W_MMA + 1);  // 864
+constexpr int TC_RS_MAX = 8;                  // raw chunk slots at most
+constexpr int TC_XS = 4;                      // x staging slots (fp32, every token's 128 columns of a step)
+// tensor memory: A buffers [2][hi 64 | lo 64 columns] (bf16 pairs, 128 values of a row), then per tile parity the
+// accumulators D1 (A_hi [x_hi | x_lo]: 2 N columns) and D2 (A_lo x_hi: N columns), 128 columns per parity
+constexpr uint32_t TC_TA = 0, TC_TACC = 256, TC_TMEM_COLS = 512;
+// shared memory: mbarriers, B buffers [2] (x_hi tokens then x_lo tokens: 2 N x 128 bf16, sized for N = 32), x staging
+// [TC_XS][32 tokens]
+// (rows of 128 fp32 padded to 528 bytes: the converting threads read 8 tokens' rows without bank conflicts), then the
+// raw ring
+constexpr uint32_t TC_B_BUF = 2 * TC_NMAX * TC_KC * 2;
+constexpr uint32_t TC_XROW = TC_KC * 4 + 16, TC_XSLOT = TC_NMAX * TC_XROW;
+constexpr uint32_t TC_B_OFF = 1024, TC_X_OFF = TC_B_OFF + 2 * TC_B_BUF, TC_RAW_OFF = TC_X_OFF + TC_XS * TC_XSLOT;
+constexpr size_t TC_SMEM_MAX = 227 * 1024 - 2048;  // less the static shared memory
 
 static size_t tc_align(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct TcArgs {
-    CUtensorMap tmap;  // W as a 2-D byte array [rows][ldw]; box: 128 rows x raw_stride bytes
-    const uint8_t *W;  // GGUF rows at stride ldw
-    uint32_t ldw;
-    int rows, cols;
+    const uint8_t *W;  // tile-major: raw chunk c of tile T = 128 rows x wbytes at (T * nr + c) * 128 * wbytes
+    int rows, nt, npad;  // npad: the MMA's N (16 or 32)
     const float *x;
     int xs;
     float *y;
-    int ys, nt, npad;  // npad: the MMA's N (16 or 32)
-    int acc;           // 1: y += W x (the residual add of a projection)
-    int chunks_per_split, splits;
+    int ys, acc;       // acc 1: y += W x (the residual add of a projection)
+    int tiles, nr, spr;  // tiles of the matrix; raw chunks per row; decode steps per raw chunk (1 or 2)
+    int splits, nr_split;  // K splits (then one tile per CTA), raw chunks per split
+    int rs;            // raw ring slots
+    uint32_t wbytes;   // bytes of a padded raw chunk of a row (16-byte multiple)
     float *part;        // [splits][32][rows] when splits > 1
     uint32_t *tickets;  // [tiles], zero between launches
-    uint32_t raw_stride;  // bytes per row of a raw chunk slot (16-byte multiple): the TMA box width
     uint32_t *err;
 };
-
-// shared memory (bytes): per buffer A_hi, A_lo [16 k-cores][16 m-groups][128 B], B_hi, B_lo [16 k-cores][N/8][128 B]
-constexpr uint32_t TC_A_BYTES = TC_M * TC_KC * 2;        // 32 KiB
-constexpr uint32_t TC_B_BYTES = TC_NMAX * TC_KC * 2;     // 8 KiB at N = 32
-constexpr uint32_t TC_BUF_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;
-constexpr uint32_t TC_BARS = 2 * TC_BUF_BYTES;           // 4 mbarriers: MMA done per buffer, raw chunk landed per slot
-constexpr uint32_t TC_RAW = TC_BARS + 128;              // two raw chunk slots of 128 rows x raw_stride
-constexpr size_t TC_SMEM_MAX = 227 * 1024 - 1024;       // less the static shared memory
-
-// bytes [start, end) of a row that chunk c (columns 128 c .. 128 c + 127) decodes from: whole blocks, widened to
-// 16-byte boundaries for the bulk copy (the row stride is a 16-byte multiple, so end <= the stride)
-__host__ __device__ inline void tc_chunk_bytes(int c, int qk, int tb, uint32_t &start, uint32_t &end) {
-    const uint32_t b0 = (uint32_t)(c * TC_KC / qk), b1 = (uint32_t)(((c + 1) * TC_KC + qk - 1) / qk);
-    start = (b0 * (uint32_t)tb) & ~15u;
-    end = (b1 * (uint32_t)tb + 15u) & ~15u;
-}
 
 // sm_100 shared-memory matrix descriptor: start address, leading / stride byte offsets (>> 4), version 1, no swizzle
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -87,11 +97,13 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
-__device__ __forceinline__ void umma_bf16(uint32_t dtmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+// D (+)= A B with A in tensor memory (row i in lane i, two bf16 per 32-bit column along K) and B in shared memory
+__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t dtmem, uint32_t atmem, uint64_t b, uint32_t idesc,
+                                                 uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dtmem),
+        "r"(atmem), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -101,6 +113,32 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void async_proxy_fence() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait on a phase that parks the warp in the hardware until the phase completes (try_wait with a suspend-time
+// hint), so waiting roles take no issue slots from the decoders; gives up after about a second of the global timer.
+__device__ __forceinline__ uint64_t tc_now() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool mbar_park(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (;;) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(20000u)
+            : "memory");
+        if (done) return true;
+        const uint64_t t = tc_now();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > 1000000000ull) return false;
+    }
+}
 
 // 16 consecutive fp32 columns of this warp's 32 tensor-memory lanes
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -115,6 +153,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 16 consecutive 32-bit columns into this warp's 32 tensor-memory lanes (one row per lane)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
 // the bf16 pair (hi, lo) of 4 values as two 8-byte words
 __device__ __forceinline__ void split4(float a, float b, float c, float d, uint2 &hi, uint2 &lo) {
@@ -125,68 +173,137 @@ __device__ __forceinline__ void split4(float a, float b, float c, float d, uint2
     lo = make_uint2(*(const uint32_t *)&l01, *(const uint32_t *)&l23);
 }
 
-// One 32-value group of a staged raw row, as load_group (the same values, bit for bit). Q4_K blocks sit 16-byte
-// aligned in a row, so their header and quants are read with four 16-byte shared-memory loads; the other formats go
-// through load_group.
-template <uint32_t TY> __device__ __forceinline__ auto tc_load(const uint8_t *row, int g, const uint32_t *grid) {
-    if constexpr (TY == T_Q4_K) {
+// two values as bf16 hi / lo words: hi = bf16(v), lo = bf16(v - hi) (v - hi is exact in fp32: one FMA by -1)
+__device__ __forceinline__ void split2(float2 v, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    const uint32_t hw = *(const uint32_t *)&h;
+    const float2 hf = make_float2(__uint_as_float(hw << 16), __uint_as_float(hw & 0xFFFF0000u));
+    const float2 d = __ffma2_rn(hf, make_float2(-1.0f, -1.0f), v);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(d.x, d.y);
+    hi = hw;
+    lo = *(const uint32_t *)&l;
+}
+// bytes k, k+1 of w (unsigned) as the floats 2^23 + byte
+__device__ __forceinline__ float2 tc_mag2(uint32_t w, int k) {
+    return make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u + k)),
+                       __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441u + k)));
+}
+// values v = A (q - off) (+ B) of the four unsigned codes q of word w, as split words 2i, 2i + 1 of hi / lo; the
+// same two float32 roundings as gguf-py ((A q) then + B), B = -0 where a format has no offset
+template <bool HAS_B>
+__device__ __forceinline__ void tc_word(uint32_t w, float off, float A, float B, uint32_t *hi, uint32_t *lo) {
+    const float2 mo = make_float2(-(8388608.0f + off), -(8388608.0f + off)), a2 = make_float2(A, A);
+    float2 v01 = __fmul2_rn(a2, __fadd2_rn(tc_mag2(w, 0), mo)), v23 = __fmul2_rn(a2, __fadd2_rn(tc_mag2(w, 2), mo));
+    if constexpr (HAS_B) {
+        v01 = __fadd2_rn(v01, make_float2(B, B));
+        v23 = __fadd2_rn(v23, make_float2(B, B));
+    }
+    split2(v01, hi[0], lo[0]);
+    split2(v23, hi[1], lo[1]);
+}
+
+// Group g of a staged raw chunk as 16 hi and 16 lo words (values 2i, 2i + 1 in word i). Q4_K and Q6_K decode their
+// 16-byte-aligned block fields directly (the values of load_group, bit for bit); the other formats go through
+// load_group.
+template <uint32_t TY>
+__device__ __forceinline__ void tc_group_words(const uint8_t *row, int g, const uint32_t *grid, uint32_t (&hi)[16],
+                                               uint32_t (&lo)[16]) {
+    if constexpr (TY == T_Q6_K) {
+        // a 256-column chunk is one block: ql [128] at 0, qh [64] at 128, int8 scales [16] at 192, fp16 d at 208
+        const int s = g & 7, H = s >> 2, sp = s & 3;
+        const uint4 l0 = *(const uint4 *)(row + 64 * H + 32 * (sp & 1)), l1 = *(const uint4 *)(row + 64 * H + 32 * (sp & 1) + 16);
+        const uint4 h0 = *(const uint4 *)(row + 128 + 32 * H), h1 = *(const uint4 *)(row + 144 + 32 * H);
+        const uint32_t sc = u16_at(row + 192 + 2 * s);
+        const float d = f16_at(row + 208);
+        const float A0 = __fmul_rn(d, (float)(int8_t)(sc & 255u)), A1 = __fmul_rn(d, (float)(int8_t)(sc >> 8));
+        const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const int lsh = 4 * (sp >> 1), hsh = 2 * sp;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t th = (hsh <= 4 ? hw[i] << (4 - hsh) : hw[i] >> (hsh - 4)) & 0x30303030u;
+            tc_word<false>(((lw[i] >> lsh) & LOW4) | th, 32.0f, i < 4 ? A0 : A1, 0.0f, hi + 2 * i, lo + 2 * i);
+        }
+    } else if constexpr (TY == T_Q4_K) {
         const uint8_t *blk = row + (g >> 3) * 144;
         const int s = g & 7;
         const uint4 h = *(const uint4 *)blk;  // d, dmin | the 12 packed scale and min bytes
         uint32_t sc, mn;
         kq_scale_min(s, h.y, h.z, h.w, sc, mn);
-        Codes32 c;
-        c.a[0] = c.a[1] = __fmul_rn(f16_of(h.x, 0), __uint2float_rn(sc));
-        c.b[0] = c.b[1] = -__fmul_rn(f16_of(h.x, 1), __uint2float_rn(mn));
+        const float A = __fmul_rn(f16_of(h.x, 0), __uint2float_rn(sc)), B = -__fmul_rn(f16_of(h.x, 1), __uint2float_rn(mn));
         const uint4 q0 = *(const uint4 *)(blk + 16 + 32 * (s >> 1)), q1 = *(const uint4 *)(blk + 32 + 32 * (s >> 1));
         const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         const int sh = 4 * (s & 1);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) c.q[i] = (qw[i] >> sh) & LOW4;
-        return c;
+        for (int i = 0; i < 8; ++i) tc_word<true>((qw[i] >> sh) & LOW4, 0.0f, A, B, hi + 2 * i, lo + 2 * i);
     } else {
-        return load_group<TY>(row, g, grid);
+        const auto G = load_group<TY>(row, g, grid);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 v = G.quad(4 * k);
+            split2(make_float2(v.x, v.y), hi[2 * k], lo[2 * k]);
+            split2(make_float2(v.z, v.w), hi[2 * k + 1], lo[2 * k + 1]);
+        }
     }
 }
 
 template <uint32_t TY>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant__ TcArgs a) {
+    constexpr bool EXACT = TY == T_BF16;  // weights exact in bf16: no lo part, one MMA per step
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ uint32_t s_tmem;
-    __shared__ int s_fail, s_last;
-    uint64_t *mbars = (uint64_t *)(sm + TC_BARS);      // [2]: the MMAs reading buffer b are complete
-    uint64_t *rbars = mbars + 2;                       // [2]: raw chunk slot s has landed
+    __shared__ volatile int s_fail;
+    __shared__ int s_last;
+    uint64_t *rfull = (uint64_t *)sm, *rempty = rfull + TC_RS_MAX, *aready = rempty + TC_RS_MAX, *afree = aready + 2,
+             *bready = afree + 2, *bfree = bready + 2, *accdone = bfree + 2, *accfree = accdone + 2,
+             *xfull = accfree + 2, *xempty = xfull + TC_XS;
+    uint8_t *Bs = sm + TC_B_OFF, *xst = sm + TC_X_OFF, *raw = sm + TC_RAW_OFF;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tile = blockIdx.x, split = blockIdx.y, row0 = tile * TC_M;
-    const int nchunks = a.cols / TC_KC;
-    const int c0 = split * a.chunks_per_split, c1 = min(nchunks, c0 + a.chunks_per_split);
-    const int nrow = min(TC_M, a.rows - row0);
-    const uint32_t n = (uint32_t)a.npad, bbytes = n * TC_KC * 2;  // B bytes per hi / lo
-    const uint32_t idesc = umma_idesc_bf16(TC_M, a.npad);
-    const uint32_t *grid = dev_grid<TY>();
-    constexpr int QK = Gguf<TY>::qk, TB = Gguf<TY>::bytes;
-
-    // the raw bytes of chunk c of the tile's rows into slot sl: one 2-D tensor copy of the box (128 rows x raw_stride
-    // bytes from byte column st, a 16-byte multiple; rows past the matrix and bytes past the stride read as zero)
-    auto issue_raw = [&](int c, int sl) {
-        if (tid != 0) return;
-        uint32_t st, en;
-        tc_chunk_bytes(c, QK, TB, st, en);
-        uint64_t *bar = &rbars[sl];
-        mbar_arrive_tx(bar, (uint32_t)TC_M * a.raw_stride);
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
-            ::"r"(smem_u32(sm + TC_RAW + (size_t)sl * TC_M * a.raw_stride)), "l"(&a.tmap), "r"((int)st), "r"(row0),
-            "r"(smem_u32(bar))
-            : "memory");
+    // this CTA's work: tiles [t0, t1), raw chunks [c0, c1) of each of their rows
+    int t0, t1, c0, c1, split = 0;
+    if (a.splits > 1) {
+        t0 = blockIdx.x / a.splits;
+        t1 = t0 + 1;
+        split = blockIdx.x - t0 * a.splits;
+        c0 = split * a.nr_split;
+        c1 = min(a.nr, c0 + a.nr_split);
+    } else {
+        t0 = (int)((long long)blockIdx.x * a.tiles / gridDim.x);
+        t1 = (int)((long long)(blockIdx.x + 1) * a.tiles / gridDim.x);
+        c0 = 0;
+        c1 = a.nr;
+    }
+    const int nrc = c1 - c0, ntile = t1 - t0, NI = ntile * nrc, NS = NI * a.spr, sps = nrc * a.spr;
+    const uint32_t n = (uint32_t)a.npad;
+    // a bounded wait that gives up at once when another role already failed
+    auto wt = [&](uint64_t *bar, uint32_t par) {
+        if (s_fail) return false;
+        if (mbar_park(bar, par)) return true;
+        s_fail = 1;
+        return false;
     };
 
     if (tid == 0) {
-        for (int q = 0; q < 4; ++q) mbar_init(&mbars[q], 1);
+        for (int i = 0; i < TC_RS_MAX; ++i) {
+            mbar_init(&rfull[i], 1);
+            mbar_init(&rempty[i], TC_DEC);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&aready[i], TC_DEC);
+            mbar_init(&afree[i], 1);
+            mbar_init(&bready[i], TC_XW);
+            mbar_init(&bfree[i], 1);
+            mbar_init(&accdone[i], 1);
+            mbar_init(&accfree[i], TC_EPI);
+        }
+        for (int i = 0; i < TC_XS; ++i) {
+            mbar_init(&xfull[i], 1);
+            mbar_init(&xempty[i], TC_XW);
+        }
         mbar_fence_init();
         s_fail = 0;
     }
-    if (warp == 0) {  // tensor memory: TC_TMEM_COLS fp32 columns x 128 lanes
+    if (warp == W_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&s_tmem)),
                      "r"(TC_TMEM_COLS)
                      : "memory");
@@ -196,196 +313,259 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_gemv(const __grid_constant
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    // the weights are read-only: the first two chunks' copies fly before the wait for the previous kernel
-    if (c0 < c1) issue_raw(c0, 0);
-    if (c0 + 1 < c1) issue_raw(c0 + 1, 1);
+    int n_raw = 0, n_mma = 0, n_x = 0;  // raw chunks / steps / x steps issued by the copy, MMA and x-copy lanes
 
-    pdl_wait();
-    pdl_trigger();
-    const float *x = after_wait(a.x);
-    // x: one (token, 8-column group) item per thread (n * 16 <= 512 items); the next chunk's values are loaded into
-    // registers while this chunk is decoded
-    const int xt = tid % (int)n, xkc = tid / (int)n;
-    const bool xitem = tid < (int)n * (TC_KC / 8), xlive = xitem && xt < a.nt;
-    auto load_x = [&](int c, float4 &p, float4 &q) {
-        if (xlive) {
-            const float4 *src = (const float4 *)(x + (size_t)xt * a.xs + c * TC_KC + xkc * 8);
-            p = src[0];
-            q = src[1];
-        }
-    };
-    float4 xp = make_float4(0.f, 0.f, 0.f, 0.f), xq = xp, np_ = xp, nq_ = xp;
-    if (c0 < c1) load_x(c0, xp, xq);
+    if (warp == W_COPY) {
+        // ---- raw chunk copies, tile-major; the weights are read-only, so the first ring's copies go before the wait
+        // for the previous kernel; every lane then takes part in the wait and the trigger
+        auto issue = [&](int i) {
+            const int sl = i % a.rs;
+            if (i >= a.rs && !wt(&rempty[sl], (uint32_t)((i / a.rs) - 1) & 1u)) return false;
+            mbar_arrive_tx(&rfull[sl], (uint32_t)TC_M * a.wbytes);
+            bulk_g2s(raw + (size_t)sl * TC_M * a.wbytes,
+                     a.W + ((size_t)(t0 + i / nrc) * a.nr + c0 + i % nrc) * TC_M * a.wbytes, (uint32_t)TC_M * a.wbytes,
+                     &rfull[sl]);
+            n_raw = i + 1;
+            return true;
+        };
+        const int first = min(NI, a.rs);
+        if (lane == 0)
+            for (int i = 0; i < first; ++i) issue(i);
+        __syncwarp();
+        pdl_wait();
+        pdl_trigger();
+        if (lane == 0)
+            for (int i = first; i < NI && !s_fail; ++i)
+                if (!issue(i)) break;
+    } else {
+        pdl_wait();
+        pdl_trigger();
+    }
 
-    int issued = 0;  // chunks whose MMAs were issued (the commit of chunk i arrives on mbars[i & 1])
-    for (int c = c0; c < c1; ++c) {
-        const int i = c - c0, b = i & 1;
-        uint8_t *buf = sm + b * TC_BUF_BYTES;
-        uint8_t *Ahi = buf, *Alo = buf + TC_A_BYTES, *Bhi = buf + 2 * TC_A_BYTES, *Blo = Bhi + bbytes;
-        // the slot of chunk i + 1 held chunk i - 1, decoded before the barrier that ended that chunk's staging
-        if (i >= 1 && c + 1 < c1) issue_raw(c + 1, (i + 1) & 1);
-        bool ok = mbar_wait(&rbars[i & 1], (uint32_t)(i >> 1) & 1u);
-        if (i >= 2) ok = ok && mbar_wait(&mbars[b], (uint32_t)((i - 2) >> 1) & 1u);  // chunk i - 2 read this buffer
-        if (!ok) s_fail = 1;
-        __syncthreads();
-        if (s_fail) break;
-        if (c + 1 < c1) load_x(c + 1, np_, nq_);
-        // weights: one (row, group of 32) per thread, a warp on 32 consecutive rows, decoded from the raw slot (the
-        // row pointer is shifted so that the decoder's block offsets of this chunk land in the slot)
-        uint32_t st, en;
-        tc_chunk_bytes(c, QK, TB, st, en);
-        const uint8_t *raw = sm + TC_RAW + (size_t)(i & 1) * TC_M * a.raw_stride;
-        for (int it = tid; it < TC_M * (TC_KC / 32); it += TC_THREADS) {
-            const int r = it & (TC_M - 1), gl = it >> 7;
-            const uint32_t roff = (uint32_t)(r >> 3) * 128u + (uint32_t)(r & 7) * 16u;
-            if (r < nrow) {
-                const uint8_t *rp = raw + (size_t)r * a.raw_stride - st;
-                // the group's values as four 16-byte core-matrix rows each of hi and lo: the 8 lanes of a store
-                // phase write one core matrix's 128 contiguous bytes (no bank conflict)
-                const auto G = tc_load<TY>(rp, c * (TC_KC / 32) + gl, grid);
+    if (warp < TC_DEC) {
+        // ---- decode: group gl of every step, rows 32 q + lane, into A buffer j & 1 of tensor memory
+        const int q = warp & 3, gl = warp >> 2, r = 32 * q + lane;
+        const uint32_t *grid = dev_grid<TY>();
+        for (int j = 0; j < NS; ++j) {
+            const int i = j / a.spr, sub = j - i * a.spr, sl = i % a.rs, b = j & 1;
+            bool ok = true;
+            if (sub == 0) ok = wt(&rfull[sl], (uint32_t)(i / a.rs) & 1u);
+            if (ok && j >= 2) ok = wt(&afree[b], (uint32_t)((j >> 1) - 1) & 1u);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-collective
+            if (ok) {
+                const int tile = t0 + i / nrc;
+                uint32_t hi[16], lo[16];
+                if (tile * TC_M + r < a.rows) {
+                    tc_group_words<TY>(raw + ((size_t)sl * TC_M + r) * a.wbytes, sub * 4 + gl, grid, hi, lo);
+                } else {  // rows past the matrix: zeros (their accumulator lanes are never read)
 #pragma unroll
-                for (int kc = 0; kc < 4; ++kc) {
-                    uint2 h0, l0, h1, l1;
-                    const float4 p = G.quad(8 * kc), q = G.quad(8 * kc + 4);
-                    split4(p.x, p.y, p.z, p.w, h0, l0);
-                    split4(q.x, q.y, q.z, q.w, h1, l1);
-                    const uint32_t off = (uint32_t)(gl * 4 + kc) * (TC_M * 16u) + roff;
-                    *(uint4 *)(Ahi + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
-                    *(uint4 *)(Alo + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+                    for (int k = 0; k < 16; ++k) hi[k] = lo[k] = 0u;
                 }
-            } else {
-#pragma unroll
-                for (int kc = 0; kc < 4; ++kc) {
-                    const uint32_t off = (uint32_t)(gl * 4 + kc) * (TC_M * 16u) + roff;
-                    *(uint4 *)(Ahi + off) = make_uint4(0, 0, 0, 0);
-                    *(uint4 *)(Alo + off) = make_uint4(0, 0, 0, 0);
-                }
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TC_TA + (uint32_t)b * 128u + 16u * (uint32_t)gl;
+                tmem_st16(ta, hi);
+                if constexpr (!EXACT) tmem_st16(ta + 64u, lo);
+                tmem_wait_st();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                tc_arrive(&aready[b]);
+                if (sub == a.spr - 1) tc_arrive(&rempty[sl]);
             }
         }
-        // x: this thread's (token, 8-column group); tokens >= nt are zero
-        if (xitem) {
-            const uint32_t off = (uint32_t)xkc * (n * 16u) + (uint32_t)(xt >> 3) * 128u + (uint32_t)(xt & 7) * 16u;
-            uint2 h0, l0, h1, l1;
-            split4(xp.x, xp.y, xp.z, xp.w, h0, l0);
-            split4(xq.x, xq.y, xq.z, xq.w, h1, l1);
-            *(uint4 *)(Bhi + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
-            *(uint4 *)(Blo + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
-        }
-        xp = np_;
-        xq = nq_;
-        async_proxy_fence();  // the generic-proxy stores (and reads of the raw slot) ordered before async-proxy use
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            // descriptors of step 0; a 16-deep step moves the start address by two core-matrix columns (the address
-            // field is address >> 4 in the low 14 bits, and shared addresses stay below 2^18, so adding cannot carry)
-            uint64_t dah = umma_desc(smem_u32(Ahi), TC_M * 16u, 128u), dal = umma_desc(smem_u32(Alo), TC_M * 16u, 128u);
-            uint64_t dbh = umma_desc(smem_u32(Bhi), n * 16u, 128u), dbl = umma_desc(smem_u32(Blo), n * 16u, 128u);
-            const uint64_t ainc = 2u * TC_M * 16u >> 4, binc = 2u * n * 16u >> 4;
+    } else if (warp < W_EPI0) {
+        // ---- x: the step's columns of every token (staged fp32 by the x copies) as bf16 hi / lo into B buffer j & 1;
+        // a thread's items are (token t, 8-column group kc) = xi + 128 m; tokens >= nt are zero
+        constexpr int XI = TC_NMAX * (TC_KC / 8) / (32 * TC_XW);  // items per thread at N = 32
+        const int xi = tid - 32 * W_X0, nitems = (int)n * (TC_KC / 8);
+        for (int j = 0; j < NS; ++j) {
+            const int b = j & 1, xsl = j % TC_XS;
+            bool ok = wt(&xfull[xsl], (uint32_t)(j / TC_XS) & 1u);
+            if (ok && j >= 2) ok = wt(&bfree[b], (uint32_t)((j >> 1) - 1) & 1u);
+            if (ok) {
+                uint8_t *Bb = Bs + (size_t)b * TC_B_BUF;
+                const uint8_t *xs_ = xst + (size_t)xsl * TC_XSLOT;
 #pragma unroll
-            for (int j = 0; j < TC_KC / 16; ++j) {  // 16-deep steps: two 8-column core matrices each
-                umma_bf16(tmem, dah, dbh, idesc, (i > 0 || j > 0) ? 1u : 0u);
-                umma_bf16(tmem, dah, dbl, idesc, 1u);
-                umma_bf16(tmem, dal, dbh, idesc, 1u);
-                dah += ainc;
-                dal += ainc;
-                dbh += binc;
-                dbl += binc;
-            }
-            umma_commit(&mbars[b]);
-        }
-        ++issued;
-    }
-    // the last commit covers every MMA this CTA issued; raw copies still in flight (a wait ran out) land first
-    if (issued > 0) {
-        const int i = issued - 1;
-        if (!mbar_wait(&mbars[i & 1], (uint32_t)(i >> 1) & 1u) && tid == 0) s_fail = 1;
-    }
-    if (s_fail && tid == 0) {
-        const int n_issued_raw = min(c1 - c0, issued + 2);
-        for (int q = issued; q < n_issued_raw; ++q) mbar_wait(&rbars[q & 1], (uint32_t)(q >> 1) & 1u, 1u << 16);
-    }
-    tc_fence_after();
-    __syncthreads();
-    const bool ok = !s_fail && issued > 0;
-    if (ok && warp < 4) {  // accumulator rows 32 w + lane -> y or this split's partial
-        const int r = row0 + warp * 32 + lane;
-        for (int c = 0; c < a.npad; c += 16) {
-            float v[16];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-            if (r < a.rows)
-#pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    const int t = c + q;
+                for (int m = 0; m < XI; ++m) {
+                    const int it = xi + 32 * TC_XW * m, t = it % (int)n, kc = it / (int)n;
+                    if (it >= nitems) break;
+                    float4 p = make_float4(0.f, 0.f, 0.f, 0.f), p2 = p;
                     if (t < a.nt) {
-                        if (a.splits == 1) {
-                            float *o = a.y + (size_t)t * a.ys + r;
-                            *o = a.acc ? __fadd_rn(*o, v[q]) : v[q];
-                        }
-                        else a.part[((size_t)split * TC_NMAX + t) * a.rows + r] = v[q];
+                        const float4 *src = (const float4 *)(xs_ + (size_t)t * TC_XROW + 32 * kc);
+                        p = src[0];
+                        p2 = src[1];
                     }
+                    uint2 h0, l0, h1, l1;
+                    split4(p.x, p.y, p.z, p.w, h0, l0);
+                    split4(p2.x, p2.y, p2.z, p2.w, h1, l1);
+                    // K-major, 2 N rows: 8-column groups 2 N x 16 bytes apart, 8-row groups 128 bytes apart
+                    const uint32_t kofs = (uint32_t)kc * (2u * n * 16u), tl = (uint32_t)t + n;
+                    *(uint4 *)(Bb + kofs + (uint32_t)(t >> 3) * 128u + (uint32_t)(t & 7) * 16u) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+                    *(uint4 *)(Bb + kofs + (tl >> 3) * 128u + (tl & 7) * 16u) = make_uint4(l0.x, l0.y, l1.x, l1.y);
                 }
+            }
+            async_proxy_fence();  // the generic-proxy stores before the tensor cores read them
+            __syncwarp();
+            if (lane == 0) {
+                tc_arrive(&bready[b]);
+                tc_arrive(&xempty[xsl]);
+            }
+        }
+    } else if (warp == W_XCOPY) {
+        // ---- x copies: step j's 128 columns of each of the nt tokens (one 512-byte bulk copy per token), TC_XS steps
+        // ahead of the conversion
+        // (lane t issues token t's copy after lane 0 set the slot's expected bytes)
+        const float *x = after_wait(a.x);
+        for (int j = 0; j < NS; ++j) {
+            const int xsl = j % TC_XS, i = j / a.spr, sub = j - i * a.spr;
+            bool ok = !s_fail;
+            if (ok && j >= TC_XS) ok = wt(&xempty[xsl], (uint32_t)((j / TC_XS) - 1) & 1u);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const int col0 = (c0 + i % nrc) * (a.spr * TC_KC) + sub * TC_KC;
+            if (lane == 0) mbar_arrive_tx(&xfull[xsl], (uint32_t)a.nt * (TC_KC * 4));
+            __syncwarp();
+            if (lane < a.nt)
+                bulk_g2s(xst + (size_t)xsl * TC_XSLOT + (size_t)lane * TC_XROW, x + (size_t)lane * a.xs + col0, TC_KC * 4,
+                         &xfull[xsl]);
+            n_x = j + 1;
+        }
+    } else if (warp < W_COPY) {
+        // ---- read-back: tile k's accumulator (lanes = its rows) -> y or this split's partial
+        const int q = warp & 3, rl = 32 * q + lane;
+        for (int k = 0; k < ntile; ++k) {
+            const int ab = k & 1;
+            bool ok = wt(&accdone[ab], (uint32_t)(k >> 1) & 1u);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+            tc_fence_after();
+            const int r = (t0 + k) * TC_M + rl;
+            if (ok) {
+                for (int c = 0; c < a.npad; c += 16) {
+                    // y = A_hi x_hi + A_hi x_lo + A_lo x_hi, added in that order
+                    const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + TC_TACC + (uint32_t)ab * 128u + (uint32_t)c;
+                    float v[16], w[16];
+                    tmem_ld16(tb, v);
+                    tmem_ld16(tb + n, w);
+#pragma unroll
+                    for (int qq = 0; qq < 16; ++qq) v[qq] += w[qq];
+                    if constexpr (!EXACT) {
+                        tmem_ld16(tb + 2u * n, w);
+#pragma unroll
+                        for (int qq = 0; qq < 16; ++qq) v[qq] += w[qq];
+                    }
+                    if (r < a.rows)
+#pragma unroll
+                        for (int qq = 0; qq < 16; ++qq) {
+                            const int t = c + qq;
+                            if (t < a.nt) {
+                                if (a.splits == 1) {
+                                    float *o = a.y + (size_t)t * a.ys + r;
+                                    *o = a.acc ? __fadd_rn(*o, v[qq]) : v[qq];
+                                } else {
+                                    a.part[((size_t)split * TC_NMAX + t) * a.rows + r] = v[qq];
+                                }
+                            }
+                        }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc_arrive(&accfree[ab]);
+        }
+        if (a.splits > 1) __threadfence();  // this split's partials, before the tile's ticket below
+    } else if (warp == W_MMA) {
+        // ---- MMAs: step j reads A buffer j & 1 and B buffer j & 1 into tile k's accumulator k & 1
+        if (lane == 0) {
+            // one MMA A_hi [x_hi | x_lo] (N = 2 npad) and one A_lo x_hi (N = npad, the operand's first npad rows) per
+            // 16-deep step: few, wide MMAs (an MMA's issue costs about the same at N = 32 as at N = 64)
+            const uint32_t id2 = umma_idesc_bf16(TC_M, 2 * a.npad), id1 = umma_idesc_bf16(TC_M, a.npad);
+            const uint32_t bbase = smem_u32(Bs);
+            const uint64_t binc = (2u * 2u * n * 16u) >> 4;  // a 16-deep step: two core-matrix columns of 2 N rows
+            for (int j = 0; j < NS; ++j) {
+                const int b = j & 1, k = j / sps, js = j - k * sps;
+                if (!wt(&aready[b], (uint32_t)(j >> 1) & 1u) || !wt(&bready[b], (uint32_t)(j >> 1) & 1u)) break;
+                if (js == 0 && k >= 2 && !wt(&accfree[k & 1], (uint32_t)((k >> 1) - 1) & 1u)) break;
+                tc_fence_after();
+                const uint32_t d1 = tmem + TC_TACC + (uint32_t)(k & 1) * 128u, d2 = d1 + 2u * n;
+                const uint32_t ah = tmem + TC_TA + (uint32_t)b * 128u, al = ah + 64u;
+                uint64_t db = umma_desc(bbase + (uint32_t)b * TC_B_BUF, 2u * n * 16u, 128u);
+#pragma unroll
+                for (int ks = 0; ks < TC_KC / 16; ++ks) {
+                    const uint32_t acc = (js > 0 || ks > 0) ? 1u : 0u;
+                    umma_bf16_tmem_a(d1, ah + 8u * ks, db, id2, acc);
+                    if constexpr (!EXACT) umma_bf16_tmem_a(d2, al + 8u * ks, db, id1, acc);
+                    db += binc;
+                }
+                umma_commit(&afree[b]);
+                umma_commit(&bfree[b]);
+                if (js == sps - 1) umma_commit(&accdone[k & 1]);
+                n_mma = j + 1;
+            }
+        }
+    }
+
+    // ---- wind down: what this CTA issued completes before its shared and tensor memory are released
+    if (s_fail) {
+        if (warp == W_COPY && lane == 0) {
+            dev_fail(a.err, DEV_WAIT_TIMEOUT);
+            for (int k = max(0, n_raw - a.rs); k < n_raw; ++k) mbar_wait(&rfull[k % a.rs], (uint32_t)(k / a.rs) & 1u, 1u << 16);
+        }
+        if (warp == W_XCOPY && lane == 0)
+            for (int k = max(0, n_x - TC_XS); k < n_x; ++k) mbar_wait(&xfull[k % TC_XS], (uint32_t)(k / TC_XS) & 1u, 1u << 16);
+        if (warp == W_MMA && lane == 0 && n_mma > 0) {  // the last commit covers every MMA issued before it
+            const int j = n_mma - 1;
+            mbar_wait(&afree[j & 1], (uint32_t)(j >> 1) & 1u, 1u << 16);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == W_MMA) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
     }
-    if (!ok) {
-        if (tid == 0 && s_fail) dev_fail(a.err, DEV_WAIT_TIMEOUT);
-        return;
-    }
     if (a.splits == 1) return;
-    // split K: the tile's last CTA adds the partials in split order (release / acquire ticket)
-    __threadfence();
-    __syncthreads();
+    // ---- split K (one tile per CTA): the tile's last CTA adds the partials in split order (release / acquire
+    // ticket); every thread takes up to 5 of the tile's 128 x 32 outputs and has all of their splits' loads in flight
     if (tid == 0) {
         uint32_t tk;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(tk) : "l"(a.tickets + tile) : "memory");
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(tk) : "l"(a.tickets + t0) : "memory");
         s_last = tk == (uint32_t)a.splits - 1;
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // each thread's outputs (token t = it / 128, row it % 128; up to 8 of them): the splits added in order, one split's
-    // loads of all its outputs in flight at once
-    constexpr int PER = TC_NMAX * TC_M / TC_THREADS;
-    float sum[PER];
+    constexpr int PER = (TC_M * TC_NMAX + TC_THREADS - 1) / TC_THREADS, SPL = 8;
+    float v[PER][SPL];
 #pragma unroll
-    for (int m = 0; m < PER; ++m) sum[m] = 0.0f;
-    for (int q = 0; q < a.splits; ++q) {
-        float v[PER];
+    for (int m = 0; m < PER; ++m) {
+        const int o = tid + TC_THREADS * m, t = o / TC_M, r = t0 * TC_M + (o % TC_M);
+        const bool live = o < TC_M * TC_NMAX && t < a.nt && r < a.rows;
 #pragma unroll
-        for (int m = 0; m < PER; ++m) {
-            const int it = tid + m * TC_THREADS, t = it / TC_M, r = row0 + (it % TC_M);
-            v[m] = t < a.nt && r < a.rows ? __ldcg(a.part + ((size_t)q * TC_NMAX + t) * a.rows + r) : 0.0f;
-        }
-#pragma unroll
-        for (int m = 0; m < PER; ++m) sum[m] += v[m];
+        for (int p = 0; p < SPL; ++p)
+            v[m][p] = live && p < a.splits ? __ldcg(a.part + ((size_t)p * TC_NMAX + t) * a.rows + r) : 0.0f;
     }
 #pragma unroll
     for (int m = 0; m < PER; ++m) {
-        const int it = tid + m * TC_THREADS, t = it / TC_M, r = row0 + (it % TC_M);
-        if (t < a.nt && r < a.rows) {
-            float *o = a.y + (size_t)t * a.ys + r;
-            *o = a.acc ? __fadd_rn(*o, sum[m]) : sum[m];
+        const int o = tid + TC_THREADS * m, t = o / TC_M, r = t0 * TC_M + (o % TC_M);
+        if (o < TC_M * TC_NMAX && t < a.nt && r < a.rows && !s_fail) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int p = 0; p < SPL; ++p)
+                if (p < a.splits) sum += v[m][p];
+            float *dst = a.y + (size_t)t * a.ys + r;
+            *dst = a.acc ? __fadd_rn(*dst, sum) : sum;
         }
     }
-    if (tid == 0) a.tickets[tile] = 0u;
+    if (tid == 0) a.tickets[t0] = 0u;
 }
 
-// ---- resident weights for the tensor-core path: GGUF rows at a 16-byte stride, plus the split-K scratch --------------
+// ---- resident weights for the tensor-core path: padded raw chunks, plus the split-K scratch -------------------------
 
 struct TcH {
-    CUtensorMap tmap;
     uint32_t type = 0;
-    int rows = 0, cols = 0, dev = 0, splits = 1, chunks_per_split = 1;
-    uint32_t raw_stride = 0;
+    int rows = 0, cols = 0, dev = 0, tiles = 0, nr = 0, spr = 1, splits = 1, nr_split = 1, rs = 2, grid = 1;
+    uint32_t wbytes = 0, cb = 0;  // padded / GGUF bytes of a raw chunk of a row
     size_t smem = 0;
     uint64_t rb = 0;
-    uint32_t ldw = 0;
     DevBuf W, part, tickets;
 };
 static std::vector<TcH *> g_tc;
@@ -396,26 +576,34 @@ static TcH *tc_get(int h) {
     return h >= 1 && h <= (int)g_tc.size() ? g_tc[h - 1] : nullptr;
 }
 
+// raw chunk width: 256 columns where its bytes fit a 240-byte box (a K-quant block, eight 32-value blocks), else 128
 static int tc_plan(TcH &w) {
-    const int tiles = (w.rows + TC_M - 1) / TC_M, nchunks = w.cols / TC_KC;
     int qk = 0, tb = 0;
     type_info(w.type, qk, tb);
-    uint32_t mx = 0;
-    for (int c = 0; c < nchunks; ++c) {
-        uint32_t st, en;
-        tc_chunk_bytes(c, qk, tb, st, en);
-        mx = std::max(mx, en - st);
+    auto bytes = [&](int c) { return (uint64_t)(c / qk) * (uint64_t)tb; };
+    int rc = 0;
+    if (w.cols % 256 == 0 && 256 % qk == 0 && bytes(256) <= 240) rc = 256;
+    else if (w.cols % 128 == 0 && 128 % qk == 0 && bytes(128) <= 256) rc = 128;
+    if (!rc) return fail("tc: unsupported type or shape (cols a multiple of 128, 256 for 256-value blocks)");
+    w.spr = rc / TC_KC;
+    w.nr = w.cols / rc;
+    w.cb = (uint32_t)bytes(rc);
+    w.wbytes = (uint32_t)tc_align(w.cb, 16);
+    const size_t slot = (size_t)TC_M * w.wbytes;
+    w.rs = (int)std::min<size_t>(TC_RS_MAX, (TC_SMEM_MAX - TC_RAW_OFF) / slot);
+    if (w.rs < 2) return fail("tc: rows too wide for the raw chunk ring");
+    w.smem = TC_RAW_OFF + (size_t)w.rs * slot;
+    w.tiles = (w.rows + TC_M - 1) / TC_M;
+    const int nsm = num_sms();
+    if (w.tiles < nsm) {  // fewer tiles than SMs: split K (at most 8 partials per row)
+        w.splits = std::max(1, std::min(std::min(8, nsm / w.tiles), w.nr));
+        w.nr_split = (w.nr + w.splits - 1) / w.splits;
+        w.splits = (w.nr + w.nr_split - 1) / w.nr_split;  // no empty split
+    } else {
+        w.splits = 1;
+        w.nr_split = w.nr;
     }
-    // the TMA box is one raw chunk of every row: an odd number of 16-byte units keeps a warp's 16-byte reads of its 32
-    // rows free of bank conflicts where that fits; a box row is at most 256 bytes
-    w.raw_stride = mx + ((mx / 16) % 2 == 0 && mx + 16 <= 256 && (size_t)TC_RAW + 2ull * TC_M * (mx + 16) <= TC_SMEM_MAX
-                             ? 16 : 0);
-    w.smem = (size_t)TC_RAW + 2ull * TC_M * w.raw_stride;
-    if (w.smem > TC_SMEM_MAX || w.raw_stride > 256) return fail("tc: rows too wide for the raw chunk slots");
-    const int target = std::max(1, std::min(8, num_sms() / tiles));  // one CTA per SM; at most 8 partials per row
-    w.splits = std::max(1, std::min(nchunks, target));
-    w.chunks_per_split = (nchunks + w.splits - 1) / w.splits;
-    w.splits = (nchunks + w.chunks_per_split - 1) / w.chunks_per_split;  // no empty split
+    w.grid = w.splits > 1 ? w.tiles * w.splits : std::min(w.tiles, nsm);
     return 0;
 }
 
@@ -423,50 +611,33 @@ int launch_tc_gemv(const TcH &w, const float *x, int xs, float *y, int ys, int n
     if (nt < 1 || nt > TC_NMAX) return fail("tc gemv: nt out of range (1..32)");
     if (((uintptr_t)x & 15) || (xs & 3)) return fail("tc gemv: x must be 16-byte aligned, xs % 4 == 0");
     TcArgs a;
-    a.tmap = w.tmap;
     a.W = w.W.as<uint8_t>();
-    a.ldw = w.ldw;
     a.rows = w.rows;
-    a.cols = w.cols;
+    a.nt = nt;
+    a.npad = nt <= 16 ? 16 : 32;
     a.x = x;
     a.xs = xs;
     a.y = y;
     a.ys = ys;
-    a.nt = nt;
-    a.npad = nt <= 16 ? 16 : 32;
     a.acc = acc ? 1 : 0;
-    a.chunks_per_split = w.chunks_per_split;
+    a.tiles = w.tiles;
+    a.nr = w.nr;
+    a.spr = w.spr;
     a.splits = w.splits;
+    a.nr_split = w.nr_split;
+    a.rs = w.rs;
+    a.wbytes = w.wbytes;
     a.part = w.part.as<float>();
     a.tickets = w.tickets.as<uint32_t>();
-    a.raw_stride = w.raw_stride;
     a.err = dev_error_ptr();
-    const dim3 grid((w.rows + TC_M - 1) / TC_M, w.splits);
     cudaError_t e = cudaSuccess;
     const bool known = dispatch_type(w.type, [&]<uint32_t TY>() {
         e = allow_max_dynamic_smem(k_tc_gemv<TY>);
-        if (e == cudaSuccess) e = launch_k(k_tc_gemv<TY>, grid, dim3(TC_THREADS), w.smem, s, a);
+        if (e == cudaSuccess) e = launch_k(k_tc_gemv<TY>, dim3(w.grid), dim3(TC_THREADS), w.smem, s, a);
     });
     if (!known) return fail("tc gemv: unsupported type");
     if (e != cudaSuccess) return fail(std::string("tc gemv launch: ") + cudaGetErrorString(e));
     return 0;
-}
-
-// the driver's tensor-map encoder, looked up through the runtime (the library links no driver symbol, so it loads on a
-// machine without a GPU driver)
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-static EncodeTiled encode_tiled() {
-    static EncodeTiled f = [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (EncodeTiled) nullptr;
-        return (EncodeTiled)p;
-    }();
-    return f;
 }
 
 static TcH *tc_build(uint32_t type, const uint8_t *Wh, int rows, int cols) {
@@ -480,33 +651,30 @@ static TcH *tc_build(uint32_t type, const uint8_t *Wh, int rows, int cols) {
     w->rows = rows;
     w->cols = cols;
     w->rb = rb;
-    w->ldw = (uint32_t)tc_align(rb, 16);
     cudaGetDevice(&w->dev);
     if (tc_plan(*w)) {
         delete w;
         return nullptr;
     }
-    const int tiles = (rows + TC_M - 1) / TC_M;
-    if (cudaMalloc(&w->W.p, (size_t)w->ldw * rows) != cudaSuccess ||
-        cudaMemcpy2D(w->W.p, w->ldw, Wh, rb, rb, rows, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMalloc(&w->part.p, (size_t)w->splits * TC_NMAX * rows * 4) != cudaSuccess ||
-        cudaMalloc(&w->tickets.p, (size_t)tiles * 4) != cudaSuccess ||
-        cudaMemset(w->tickets.p, 0, (size_t)tiles * 4) != cudaSuccess) {
+    // tile-major padded raw chunks: chunk c of tile T holds its 128 rows' GGUF bytes of columns [c rc, (c + 1) rc) at
+    // a row stride of wbytes (zeros after each row's bytes and for rows past the matrix), at (T nr + c) 128 wbytes, so
+    // a chunk is one contiguous bulk copy
+    const size_t chunk = (size_t)TC_M * w->wbytes, total = (size_t)w->tiles * w->nr * chunk;
+    std::vector<uint8_t> host(total, 0);
+    for (int r = 0; r < rows; ++r) {
+        const int T = r / TC_M, rr = r % TC_M;
+        for (int c = 0; c < w->nr; ++c)
+            std::memcpy(host.data() + ((size_t)T * w->nr + c) * chunk + (size_t)rr * w->wbytes, Wh + (size_t)r * rb + (size_t)c * w->cb,
+                        w->cb);
+    }
+    bool ok = cudaMalloc(&w->W.p, total) == cudaSuccess &&
+              cudaMemcpy(w->W.p, host.data(), total, cudaMemcpyHostToDevice) == cudaSuccess;
+    ok = ok && cudaMalloc(&w->part.p, (size_t)w->splits * TC_NMAX * rows * 4) == cudaSuccess &&
+         cudaMalloc(&w->tickets.p, (size_t)w->tiles * 4) == cudaSuccess &&
+         cudaMemset(w->tickets.p, 0, (size_t)w->tiles * 4) == cudaSuccess;
+    if (!ok) {
         delete w;
         fail("tc: device allocation / copy failed");
-        return nullptr;
-    }
-    // W as a 2-D byte tensor: dims {ldw, rows}, row stride ldw (a 16-byte multiple, base 256-byte aligned)
-    const cuuint64_t dims[2] = {w->ldw, (cuuint64_t)rows}, strides[1] = {w->ldw};
-    const cuuint32_t box[2] = {w->raw_stride, (cuuint32_t)TC_M}, es[2] = {1, 1};
-    const EncodeTiled enc = encode_tiled();
-    const CUresult cr = enc ? enc(&w->tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->W.p, dims, strides, box, es,
-                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)
-                            : CUDA_ERROR_NOT_FOUND;
-    if (cr != CUDA_SUCCESS) {
-        delete w;
-        fail("tc: tensor map encoding failed (" + std::to_string((int)cr) + ")");
         return nullptr;
     }
     return w;
