@@ -133,6 +133,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     return false;
 }
 
+// The global nanosecond timer.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait for the phase of `parity` that parks the thread in the hardware until the phase completes (try_wait with
+// a suspend-time hint) instead of re-issuing polls, so waiting warps leave their scheduler's issue slots to the
+// working ones; false after about a second of the global timer.
+__device__ __forceinline__ bool mbar_park(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (;;) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(20000u)
+            : "memory");
+        if (done) return true;
+        const uint64_t t = global_ns();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > 1000000000ull) return false;
+    }
+}
+
 // bulk (non-tensor) copy global -> shared, completing `bytes` of transactions on `bar`. dst, src 16-byte aligned,
 // bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -116,30 +116,6 @@ __device__ __forceinline__ void async_proxy_fence() { asm volatile("fence.proxy.
 __device__ __forceinline__ void tc_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
-// Bounded wait on a phase that parks the warp in the hardware until the phase completes (try_wait with a suspend-time
-// hint), so waiting roles take no issue slots from the decoders; gives up after about a second of the global timer.
-__device__ __forceinline__ uint64_t tc_now() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ bool mbar_park(uint64_t *bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    uint64_t t0 = 0;
-    for (;;) {
-        uint32_t done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity), "r"(20000u)
-            : "memory");
-        if (done) return true;
-        const uint64_t t = tc_now();
-        if (t0 == 0) t0 = t;
-        else if (t - t0 > 1000000000ull) return false;
-    }
-}
-
 // 16 consecutive fp32 columns of this warp's 32 tensor-memory lanes
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
