@@ -413,6 +413,16 @@ def run_decode_batch(f, args, batch):
     m.capture(s)
     prompts = np.random.default_rng(0).integers(0, cfg["vocab"], (batch, n_prompt))
     m.generate(prompts, 16, s)  # warm-up
+    if args.profile_steps:  # the launch list of a few eager steps (an NVTX range "decode_steps" for ncu)
+        torch.cuda.nvtx.range_push("decode_steps")
+        for _ in range(args.profile_steps):
+            m.launch_step(s.cuda_stream)
+        f.sync(s.cuda_stream)
+        torch.cuda.nvtx.range_pop()
+        n = m.launches_per_step()
+        m.free()
+        return {"batch": batch, "profile_steps": args.profile_steps, "gpu_launches_per_step": n,
+                "build_s": round(time.perf_counter() - t0, 1)}
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     clocks.start()
@@ -432,6 +442,8 @@ def decode_line(f, args):
     """`--workload decode`: the config-5 decode as its own bench line (tok/s)."""
     if args.batch > 1:
         d = run_decode_batch(f, args, args.batch)
+        if args.profile_steps:
+            return d
         return {"metric": METRIC, "value": d["tok_s"], "unit": "tok/s", "n_gpus": 1, "steps": 256, "warmup": 16,
                 "ms_per_step": d["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32 (bf16 hi/lo tensor-core products)", "data": "synthetic",
@@ -883,7 +895,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1,
                     help="with --workload decode: that many sequences at once on the tensor-core path (2..32)")
     ap.add_argument("--profile-steps", type=int, default=0,
-                    help="with --workload decode: run this many eager decode steps in an NVTX range and exit")
+                    help="with --workload decode (any --batch): run this many eager decode steps in an NVTX range and exit")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -907,6 +919,9 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL carries only host plumbing here (handle exchange, barriers, the max over ranks): no NVLink multicast
+        # objects are needed, and none are bound to the ranks' memory
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
 
     from fn import FN

@@ -58,7 +58,10 @@ __device__ __forceinline__ float warp_sum_f(float v) {
     return v;
 }
 
-__global__ void __launch_bounds__(GDN_THREADS, 1) k_gdn(const GdnArgs a) {  // clusters of GDN_SPLIT CTAs
+// MINB CTAs per SM: 1 for one sequence (one wave of nvh * GDN_SPLIT CTAs, registers unconstrained), 2 for a batch of
+// sequences (nvh * GDN_SPLIT CTAs per sequence: two resident per SM halve the waves, at 80 registers a thread)
+template <int MINB>
+__global__ void __launch_bounds__(GDN_THREADS, MINB) k_gdn(const GdnArgs a) {  // clusters of GDN_SPLIT CTAs
     constexpr int DS = GDN_DS, CW = DS / GDN_SPLIT;  // CW state columns per CTA
     __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[CW];
     __shared__ float red_q[4], red_k[4];
@@ -253,7 +256,8 @@ int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs,
     a.nvh = p.nvh;
     a.nt = nt;
     a.prefetch = prefetch_state ? 1 : 0;
-    const cudaError_t e = launch_kc(k_gdn, dim3(p.nvh * GDN_SPLIT, batch), dim3(GDN_THREADS), GDN_SPLIT, 0, s, a);
+    const cudaError_t e = batch > 1 ? launch_kc(k_gdn<2>, dim3(p.nvh * GDN_SPLIT, batch), dim3(GDN_THREADS), GDN_SPLIT, 0, s, a)
+                                    : launch_kc(k_gdn<1>, dim3(p.nvh * GDN_SPLIT, batch), dim3(GDN_THREADS), GDN_SPLIT, 0, s, a);
     if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
     return 0;
 }
