@@ -4,7 +4,7 @@
 // Reference behaviour: k_gdn (engine/faie2fn.cu:1349-1431); value head h reads key head h % NKH (GGUF tiled order,
 // :10-11, 1374); the norm is gated with sigmoid(z) (:1424); softplus(u) = u for u > 20 (:1411).
 //
-// B200 design: value head h is a cluster of GDN_SPLIT = 4 CTAs of 384 threads; CTA p owns state columns
+// B200 design (one sequence): value head h is a cluster of GDN_SPLIT = 4 CTAs of 384 threads; CTA p owns state columns
 // [32p, 32p + 32): thread (jl, c) = (tid >> 2, tid & 3) of the first 128 owns column 32p + jl, key rows [32c, 32c + 32),
 // i.e. 32 fp32 values of S[h] held in registers across all tokens of the launch, so a head's 64 KB state streams
 // through four SMs. The columns are independent up to the gated norm: its sum of squares over the 128 columns is the
@@ -30,8 +30,9 @@ namespace cg = cooperative_groups;
 namespace fn {
 
 constexpr int GDN_DS = 128;
-constexpr int GDN_SPLIT = 4;                            // CTAs (one cluster) per value head
-constexpr int GDN_THREADS = 3 * GDN_DS;                 // q and k conv channels, then the value channels
+constexpr int GDN_SPLIT = 4;                            // CTAs (one cluster) per value head of one sequence
+// threads: the q, k and value conv channels (3 DS), and 4 per state column of the CTA (4 DS / SPLIT), whichever is more
+constexpr int gdn_threads(int split) { return 3 * GDN_DS > 4 * GDN_DS / split ? 3 * GDN_DS : 4 * GDN_DS / split; }
 constexpr int KPAD = 36;  // floats per 32-row chunk of the staged q / k (32 + 4: chunk c at bank offset 4c)
 
 struct GdnArgs {
@@ -58,17 +59,19 @@ __device__ __forceinline__ float warp_sum_f(float v) {
     return v;
 }
 
-// MINB CTAs per SM: 1 for one sequence (one wave of nvh * GDN_SPLIT CTAs, registers unconstrained), 2 for a batch of
-// sequences (nvh * GDN_SPLIT CTAs per sequence: two resident per SM halve the waves, at 80 registers a thread)
-template <int MINB>
-__global__ void __launch_bounds__(GDN_THREADS, MINB) k_gdn(const GdnArgs a) {  // clusters of GDN_SPLIT CTAs
-    constexpr int DS = GDN_DS, CW = DS / GDN_SPLIT;  // CW state columns per CTA
+// SPLIT CTAs per value head: 4 (a cluster) for one sequence, whose head's state then streams through four SMs; 1 for a
+// batch of sequences (one 512-thread CTA per head and sequence: the batch fills the GPU, and no cluster barriers). The
+// gated norm adds the same warp partials in the same column order either way, so the results are the same bits.
+template <int SPLIT>
+__global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) {  // clusters of SPLIT CTAs
+    constexpr int DS = GDN_DS, CW = DS / SPLIT;  // CW state columns per CTA
+    constexpr int NSW = 4 * CW / 32;             // warps holding state
     __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[CW];
     __shared__ float red_q[4], red_k[4];
-    __shared__ float red_o[2][4];  // this CTA's 4 warp partials of sum o^2, by token parity (read by the cluster)
+    __shared__ float red_o[2][NSW];  // this CTA's warp partials of sum o^2, by token parity (read by the cluster)
     cg::cluster_group cl = cg::this_cluster();
-    const int p = (int)cl.block_rank();  // column block: state columns [CW p, CW (p + 1)) of the value head
-    const int h = blockIdx.x / GDN_SPLIT, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int p = SPLIT > 1 ? (int)cl.block_rank() : 0;  // column block: state columns [CW p, CW (p + 1)) of the head
+    const int h = blockIdx.x / SPLIT, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int jl = tid >> 2, c = tid & 3, j = CW * p + jl;  // state threads (tid < 4 CW): column j, rows [32c, 32c + 32)
     const bool st_thr = tid < 4 * CW;
     const int kh = h % a.nkh, nvd = a.nvh * DS;
@@ -200,16 +203,17 @@ __global__ void __launch_bounds__(GDN_THREADS, MINB) k_gdn(const GdnArgs a) {  /
             const float oo = warp_sum_f(c == 0 ? o * o : 0.f);
             if (lane == 0) red_o[t & 1][warp] = oo;
         }
-        // the head's 16 warp partials (4 per CTA of the cluster, CTA p holding columns [32 p, 32 p + 32)), summed in
-        // column order through distributed shared memory
-        cl.sync();
+        // the head's 16 warp partials (NSW per CTA of the cluster, CTA p holding columns [CW p, CW (p + 1))), summed in
+        // column order (through distributed shared memory when the head spans a cluster)
+        if constexpr (SPLIT > 1) cl.sync();
+        else __syncthreads();
         if (st_thr && c == 0) {
             float ss = 0.f;
 #pragma unroll
-            for (int q = 0; q < GDN_SPLIT; ++q) {
-                const float *ro = cl.map_shared_rank(&red_o[t & 1][0], q);
+            for (int q = 0; q < SPLIT; ++q) {
+                const float *ro = SPLIT > 1 ? cl.map_shared_rank(&red_o[t & 1][0], q) : &red_o[t & 1][0];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) ss += ro[i];
+                for (int i = 0; i < NSW; ++i) ss += ro[i];
             }
             const float r = rsqrtf(ss / DS + 1e-6f);
             const size_t oi = (size_t)h * DS + j;
@@ -226,7 +230,7 @@ __global__ void __launch_bounds__(GDN_THREADS, MINB) k_gdn(const GdnArgs a) {  /
         stp[sst] = h1;
         stp[2 * sst] = h2;
     }
-    cl.sync();  // no CTA leaves while another may still read its partials
+    if constexpr (SPLIT > 1) cl.sync();  // no CTA leaves while another may still read its partials
 }
 
 int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs, const float *z, int zs, const float *ab,
@@ -256,8 +260,9 @@ int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs,
     a.nvh = p.nvh;
     a.nt = nt;
     a.prefetch = prefetch_state ? 1 : 0;
-    const cudaError_t e = batch > 1 ? launch_kc(k_gdn<2>, dim3(p.nvh * GDN_SPLIT, batch), dim3(GDN_THREADS), GDN_SPLIT, 0, s, a)
-                                    : launch_kc(k_gdn<1>, dim3(p.nvh * GDN_SPLIT, batch), dim3(GDN_THREADS), GDN_SPLIT, 0, s, a);
+    const cudaError_t e = batch > 1 ? launch_k(k_gdn<1>, dim3(p.nvh, batch), dim3(gdn_threads(1)), 0, s, a)
+                                    : launch_kc(k_gdn<GDN_SPLIT>, dim3(p.nvh * GDN_SPLIT, 1), dim3(gdn_threads(GDN_SPLIT)),
+                                                GDN_SPLIT, 0, s, a);
     if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
     return 0;
 }
