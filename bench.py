@@ -13,7 +13,8 @@ N(0,1), router logits 2 N(0,1): the reference's real model tensors are not shipp
          chains (programmatic dependent launch inside a chain), the MoE layer, the lm_head
   e2e    the same metric with host buffers: each step copies every input (the GEMVs' x, the MoE layer's x and router
          logits) in from pinned memory, runs the step's library launches and copies every output (the GEMVs' y, the
-         MoE output, the token id) out, inside the timed region
+         MoE output, the token id) out, inside the timed region; two input / output buffer pairs alternate so the
+         copies overlap the neighbouring steps' kernels
   roofline  the dominant kernel (the lm_head GEMV): its algorithmic bytes / its mean CUDA-event duration inside the
          timed region, against the measured HBM copy bandwidth
   cpu_baseline  the reference's CPU path (gguf-py dequant + float64 numpy GEMV) on a bounded row sample, 1 core
@@ -636,10 +637,12 @@ class SweepStep:
             g = torch.Generator("cuda").manual_seed(i)
             X[self.xoff[i]:self.xoff[i + 1]] = torch.randn(n, device=dev, generator=g) * (2.0 if i == len(xlen) - 1 else 1.0)
         self.X = X
+        self.buf = 0  # which input / output buffer pair the launches use (the e2e pipeline alternates two)
         self.rows = [row_range(r, world, rank) for _, r, _, _ in work]
         ylen = [r1 - r0 for r0, r1 in self.rows] + [d, 4]  # y slices, the MoE output, the argmax (one int32 slot)
         self.yoff = np.concatenate([[0], np.cumsum(ylen)]).astype(int)
         self.Y = torch.zeros(int(self.yoff[-1]), device=dev)
+        self.X2, self.Y2 = self.X.clone(), torch.zeros_like(self.Y)  # the second pair
         self.hs, self.head = [], None
         self.step_bytes = sum(alg_bytes(q, r, c) for q, r, c, _ in work) + (moe3_bytes() if with_moe else 0)
         self.head_rows = self.rows[-1][1] - self.rows[-1][0]
@@ -670,11 +673,15 @@ class SweepStep:
         del Wg, Wu, Wd
         self.launches_per_step += 3 if world == 1 else 4  # routing, gate/up, down (+ the combine across ranks)
 
+    def bufs(self, b):
+        """Input and output buffers of pair b (0: the device-timed step's; 1: the e2e pipeline's second pair)."""
+        return (self.X, self.Y) if b == 0 else (self.X2, self.Y2)
+
     def x(self, i):
-        return self.X.data_ptr() + 4 * int(self.xoff[i])
+        return self.bufs(self.buf)[0].data_ptr() + 4 * int(self.xoff[i])
 
     def y(self, i):
-        return self.Y.data_ptr() + 4 * int(self.yoff[i])
+        return self.bufs(self.buf)[1].data_ptr() + 4 * int(self.yoff[i])
 
     def launch_gemv(self, i, s, early=True):
         q, r, c, _ = self.work[i]
@@ -738,24 +745,34 @@ def run_sweep(f, args, rank, world, local, dist):
     # concurrent chains of one graph (a fork and a join on the capture stream), so several are resident on an SM
     # at once; the MoE layer and the lm_head with its argmax are graphs of their own on the main stream
     side = [torch.cuda.Stream() for _ in range(args.branches)]
-    g_small = torch.cuda.CUDAGraph() if n > 1 else None
-    g_moe = torch.cuda.CUDAGraph() if st.with_moe else None
-    g_head = torch.cuda.CUDAGraph()
-    if g_small is not None:
-        with torch.cuda.graph(g_small, stream=stream, capture_error_mode="thread_local"):
-            main_s = torch.cuda.current_stream()
-            for sd in side:
-                sd.wait_stream(main_s)
-            for i in range(n - 1):
-                st.launch_gemv(i, side[i % len(side)].cuda_stream)
-            for sd in side:
-                main_s.wait_stream(sd)
-    if g_moe is not None:
-        with torch.cuda.graph(g_moe, stream=stream, capture_error_mode="thread_local"):
-            st.launch_moe(torch.cuda.current_stream().cuda_stream)
-    with torch.cuda.graph(g_head, stream=stream, capture_error_mode="thread_local"):
-        st.launch_gemv(n - 1, torch.cuda.current_stream().cuda_stream, early=False)
-    graphs = [g for g in (g_small, g_moe, g_head) if g is not None]
+
+    def capture(b):
+        """The step's graphs (sweep, MoE layer, lm_head) over input / output buffer pair b."""
+        st.buf = b
+        g_small = torch.cuda.CUDAGraph() if n > 1 else None
+        g_moe = torch.cuda.CUDAGraph() if st.with_moe else None
+        g_head = torch.cuda.CUDAGraph()
+        if g_small is not None:
+            with torch.cuda.graph(g_small, stream=stream, capture_error_mode="thread_local"):
+                main_s = torch.cuda.current_stream()
+                for sd in side:
+                    sd.wait_stream(main_s)
+                for i in range(n - 1):
+                    st.launch_gemv(i, side[i % len(side)].cuda_stream)
+                for sd in side:
+                    main_s.wait_stream(sd)
+        if g_moe is not None:
+            with torch.cuda.graph(g_moe, stream=stream, capture_error_mode="thread_local"):
+                st.launch_moe(torch.cuda.current_stream().cuda_stream)
+        with torch.cuda.graph(g_head, stream=stream, capture_error_mode="thread_local"):
+            st.launch_gemv(n - 1, torch.cuda.current_stream().cuda_stream, early=False)
+        st.buf = 0
+        return [g for g in (g_small, g_moe, g_head) if g is not None]
+
+    graphs = capture(0)
+    sets = [graphs, capture(1)]  # the second over buffer pair 1, which holds the same inputs
+    g_small = graphs[0] if n > 1 else None
+    g_moe = graphs[1 if n > 1 else 0] if st.with_moe else None
 
     def step():
         for g in graphs:
@@ -768,8 +785,9 @@ def run_sweep(f, args, rank, world, local, dist):
             return float(t.item())
         return v
 
-    for _ in range(args.warmup):
-        step()
+    for w in range(args.warmup):
+        for g in sets[w & 1]:
+            g.replay()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -779,13 +797,24 @@ def run_sweep(f, args, rank, world, local, dist):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
     clocks.start()
+    # `value`: K steps timed by events at the ends only, the two graph sets alternating and each step ordered after the
+    # previous one through an event, as in the e2e pipeline below (measured on 2 GPUs: 2160 -> 2256 GB/s; no change on
+    # one); then the same K steps again with an event between the graphs, for the per-component split and the
+    # lm_head's launch time (the events between graphs add small gaps)
+    evs = [torch.cuda.Event(), torch.cuda.Event()]
     e0.record(stream)
+    for k in range(K):
+        if k >= 1:
+            stream.wait_event(evs[(k - 1) & 1])
+        for g in sets[k & 1]:
+            g.replay()
+        evs[k & 1].record(stream)
+    e1.record(stream)
     for k in range(K):
         ev[k][0].record(stream)
         for j, g in enumerate(graphs):
             g.replay()
             ev[k][j + 1].record(stream)
-    e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
@@ -794,29 +823,52 @@ def run_sweep(f, args, rank, world, local, dist):
     value = st.step_bytes * K / (ms / 1e3) / 1e9
 
     # e2e: every step copies all inputs in from pinned host memory, runs the step's library launches (the captured
-    # graphs of the same calls) and copies every output out (the GEMVs' y slices, the MoE output, the token id)
+    # graphs of the same calls) and copies every output out (the GEMVs' y slices, the MoE output, the token id). Two
+    # input / output buffer pairs alternate, with a copy stream each way, so a step's copies overlap the kernels of the
+    # steps beside it: step k's input copy waits for step k - 2's kernels (the same input buffer), its kernels for that
+    # copy and for step k - 2's output copy (the same output buffer), its output copy for its kernels.
     xh, yh = st.host_buffers()
     h2d, d2h = xh.numel() * 4, yh.numel() * 4
     Ke = max(3, min(K, 200))
+    pairs = [st.bufs(0), st.bufs(1)]
+    yhs = [yh, torch.empty_like(yh).pin_memory()]
+    cs_in, cs_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in, ev_done, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
 
-    def e2e_step():
-        st.X.copy_(xh, non_blocking=True)
-        step()
-        yh.copy_(st.Y, non_blocking=True)
-        stream.synchronize()
+    def e2e_run(nsteps, start, end):
+        start.record(stream)
+        cs_in.wait_event(start)
+        cs_out.wait_event(start)
+        for k in range(nsteps):
+            bb = k & 1
+            X, Y = pairs[bb]
+            if k >= 2:
+                cs_in.wait_event(ev_done[bb])
+            with torch.cuda.stream(cs_in):
+                X.copy_(xh, non_blocking=True)
+            ev_in[bb].record(cs_in)
+            stream.wait_event(ev_in[bb])
+            if k >= 2:
+                stream.wait_event(ev_out[bb])
+            for g in sets[bb]:
+                g.replay()
+            ev_done[bb].record(stream)
+            cs_out.wait_event(ev_done[bb])
+            with torch.cuda.stream(cs_out):
+                yhs[bb].copy_(Y, non_blocking=True)
+            ev_out[bb].record(cs_out)
+        stream.wait_stream(cs_out)
+        end.record(stream)
+        torch.cuda.synchronize()
 
-    for _ in range(3):
-        e2e_step()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_run(4, a, b)  # warm-up
     if dist:
         dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(Ke):
-        e2e_step()
-    b.record(stream)
-    torch.cuda.synchronize()
+    e2e_run(Ke, a, b)
     e2e_ms = max_over_ranks(a.elapsed_time(b))
     e2e = st.step_bytes * Ke / (e2e_ms / 1e3) / 1e9
+    yh = yhs[(Ke - 1) & 1]
     yv = yh.numpy()
     tok = int(yv[-4:].view(np.int32)[0])
     ok = bool(np.isfinite(yv[:-4]).all()) and 0 <= tok < work[-1][1]
@@ -843,13 +895,15 @@ def run_sweep(f, args, rank, world, local, dist):
                    "frac_of_measured_peak": round(value / world / peak, 4)},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": Ke, "outputs_finite": bool(ok), "path": "pinned host -> device copy of every input, the "
-                "step's library launches (as captured graphs), device -> pinned host copy of every output, per step"},
+                "step's library launches (as captured graphs), device -> pinned host copy of every output, per step; "
+                "two input / output buffer pairs alternate with a copy stream each way, so the copies overlap the "
+                "neighbouring steps' kernels"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": f"k_gemv<Q6_K> lm_head {st.head_rows}x2048 + fused argmax",
                      "mean_launch_us": round(head_ms * 1e3, 2), "alg_bytes_per_launch": st.head_bytes},
         "split_ms_per_step": {k: round(v, 5) for k, v in zip(names, seg)},
-        "gpu_launches": K * st.launches_per_step,
+        "gpu_launches": 2 * K * st.launches_per_step,  # the value pass and the split pass
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -858,7 +912,7 @@ def run_sweep(f, args, rank, world, local, dist):
                                 "sample": f"every GEMV of the step (the MoE layer as its 33 expert GEMVs) cut to "
                                           f"{frac:.3g} of its rows, one pass ({dt:.1f} s), gguf-py dequant + float64 "
                                           f"numpy GEMV, 1 thread"}
-    del graphs, g_small, g_moe, g_head
+    del graphs, sets, g_small, g_moe
     torch.cuda.synchronize()
     st.free()
     if group is not None:
