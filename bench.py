@@ -520,7 +520,7 @@ def run_kernel(args):
     two weight copies alternating, for ncu captures of a single kernel (-k / -c) from a committed command; prints one
     JSON line with the mean time per call. --kernel gemv / tc_gemv: --format, --rows, --cols, --tokens; moe: BASELINE
     config 3 (IQ3_XXS gate/up, Q4_K down, 512 experts, top-10, --tokens tokens; --moe-var selects the MoE variant); gdn: the
-    config-4 DeltaNet core step."""
+    config-4 DeltaNet core step (--tokens B > 1: a batch of B sequences, one token each)."""
     import torch
     from fn import FN
     from synth import BY_NAME, random_blocks
@@ -559,6 +559,21 @@ def run_kernel(args):
         y = torch.zeros(nt, d, device=dev)
         call = lambda i: f.moe_run(hs[i % 2], lg.data_ptr(), ne + 1, x.data_ptr(), y.data_ptr(), nt, 2, cs)  # noqa: E731
         what = {"kernel": "moe", "config": "config3", "moe_var": args.moe_var or 0, "tokens": nt}
+    elif args.tokens > 1:  # gdn, a batch of --tokens sequences at one token each (the batched decode's core)
+        NKH, NVH, DS, B = 16, 32, 128, args.tokens
+        CONVCH = 2 * NKH * DS + NVH * DS
+        hs = [f.gdn_create_batch(NKH, NVH, (rng.standard_normal((CONVCH, 4)) * 0.5).astype(np.float32),
+                                 (rng.standard_normal(NVH) * 0.5).astype(np.float32),
+                                 (-np.exp(rng.standard_normal(NVH) * 0.5)).astype(np.float32),
+                                 (1 + 0.1 * rng.standard_normal(DS)).astype(np.float32), B) for _ in range(2)]
+        frees = [(f.gdn_free, h) for h in hs]
+        qkvz = torch.randn(B, CONVCH + NVH * DS, device=dev)
+        ab = torch.randn(B, 2 * NVH, device=dev)
+        out = torch.zeros(B, NVH * DS, device=dev)
+        rs = CONVCH + NVH * DS
+        call = lambda i: f.gdn_run_batch(hs[i % 2], qkvz.data_ptr(), rs, qkvz.data_ptr() + 4 * CONVCH, rs,  # noqa: E731
+                                         ab.data_ptr(), 2 * NVH, out.data_ptr(), NVH * DS, 1, cs)
+        what = {"kernel": "gdn", "config": f"config4 core, a batch of {B} sequences", "tokens": B}
     else:  # gdn
         NKH, NVH, DS = 16, 32, 128
         CONVCH = 2 * NKH * DS + NVH * DS
