@@ -69,10 +69,17 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
     __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[CW];
     __shared__ float red_q[4], red_k[4];
     __shared__ float red_o[2][NSW];  // this CTA's warp partials of sum o^2, by token parity (read by the cluster)
+    // one CTA per head: the 4 row-quarter partials of S^T k and S^T q per column, and o^2 per column
+    __shared__ float red_kv[SPLIT == 1 ? 4 * DS : 1], red_qo[SPLIT == 1 ? 4 * DS : 1], red_sq[SPLIT == 1 ? DS : 1];
     cg::cluster_group cl = cg::this_cluster();
     const int p = SPLIT > 1 ? (int)cl.block_rank() : 0;  // column block: state columns [CW p, CW (p + 1)) of the head
     const int h = blockIdx.x / SPLIT, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int jl = tid >> 2, c = tid & 3, j = CW * p + jl;  // state threads (tid < 4 CW): column j, rows [32c, 32c + 32)
+    // state threads (tid < 4 CW): column j, rows [32c, 32c + 32). A cluster CTA gives a column's 4 quarters to
+    // adjacent lanes (their partials meet by xor shuffles); one CTA per head puts a warp's lanes on 32 consecutive
+    // columns of one quarter, so each state load and store of a warp is one 128-byte line (the partials then meet in
+    // shared memory, added in the same order)
+    const int jl = SPLIT == 1 ? 32 * (warp & 3) + lane : tid >> 2, c = SPLIT == 1 ? warp >> 2 : tid & 3;
+    const int j = CW * p + jl;
     const bool st_thr = tid < 4 * CW;
     const int kh = h % a.nkh, nvd = a.nvh * DS;
     // a batch of independent sequences (gridDim.y > 1, one token each): sequence blockIdx.y's state, conv histories
@@ -181,8 +188,14 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
                 kv = __fmaf_rn(s[i + 2], kk.z, kv);
                 kv = __fmaf_rn(s[i + 3], kk.w, kv);
             }
-            kv += __shfl_xor_sync(0xffffffffu, kv, 1);
-            kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+            if constexpr (SPLIT == 1) {  // every thread holds state here: the barrier is reached by all
+                red_kv[c * DS + jl] = kv;
+                __syncthreads();
+                kv = (red_kv[jl] + red_kv[DS + jl]) + (red_kv[2 * DS + jl] + red_kv[3 * DS + jl]);
+            } else {  // lanes c = 0..3: ((p0 + p1) + (p2 + p3)) in every lane
+                kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+                kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+            }
             const float delta = __fmul_rn(__fmaf_rn(-decay, kv, vs[jl]), beta);
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
@@ -196,12 +209,22 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
                 o = __fmaf_rn(s[i + 2], q4.z, o);
                 o = __fmaf_rn(s[i + 3], q4.w, o);
             }
-            o += __shfl_xor_sync(0xffffffffu, o, 1);
-            o += __shfl_xor_sync(0xffffffffu, o, 2);
+            if constexpr (SPLIT == 1) {
+                red_qo[c * DS + jl] = o;
+                __syncthreads();
+                o = (red_qo[jl] + red_qo[DS + jl]) + (red_qo[2 * DS + jl] + red_qo[3 * DS + jl]);
+            } else {
+                o += __shfl_xor_sync(0xffffffffu, o, 1);
+                o += __shfl_xor_sync(0xffffffffu, o, 2);
+            }
             o *= 0.08838834764831845f;  // 1 / sqrt(128)
-            // gated RMSNorm over the head's 128 columns: this warp's 8 columns (lanes with c == 0), in lane order
-            const float oo = warp_sum_f(c == 0 ? o * o : 0.f);
-            if (lane == 0) red_o[t & 1][warp] = oo;
+            if constexpr (SPLIT == 1) {
+                if (c == 0) red_sq[jl] = o * o;
+            } else {
+                // gated RMSNorm over the head's 128 columns: this warp's 8 columns (lanes with c == 0), in lane order
+                const float oo = warp_sum_f(c == 0 ? o * o : 0.f);
+                if (lane == 0) red_o[t & 1][warp] = oo;
+            }
         }
         // the head's 16 warp partials (NSW per CTA of the cluster, CTA p holding columns [CW p, CW (p + 1))), summed in
         // column order (through distributed shared memory when the head spans a cluster)
@@ -209,11 +232,21 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
         else __syncthreads();
         if (st_thr && c == 0) {
             float ss = 0.f;
+            if constexpr (SPLIT == 1) {
+                // the cluster form's sum: per block of 8 columns the xor-16 / 8 / 4 butterfly over its lanes 0, 4, ..,
+                // 28, i.e. ((q0 + q4) + (q2 + q6)) + ((q1 + q5) + (q3 + q7)), then the 16 blocks in column order
 #pragma unroll
-            for (int q = 0; q < SPLIT; ++q) {
-                const float *ro = SPLIT > 1 ? cl.map_shared_rank(&red_o[t & 1][0], q) : &red_o[t & 1][0];
+                for (int b = 0; b < DS / 8; ++b) {
+                    const float *q8 = red_sq + 8 * b;
+                    ss += ((q8[0] + q8[4]) + (q8[2] + q8[6])) + ((q8[1] + q8[5]) + (q8[3] + q8[7]));
+                }
+            } else {
 #pragma unroll
-                for (int i = 0; i < NSW; ++i) ss += ro[i];
+                for (int q = 0; q < SPLIT; ++q) {
+                    const float *ro = cl.map_shared_rank(&red_o[t & 1][0], q);
+#pragma unroll
+                    for (int i = 0; i < NSW; ++i) ss += ro[i];
+                }
             }
             const float r = rsqrtf(ss / DS + 1e-6f);
             const size_t oi = (size_t)h * DS + j;
