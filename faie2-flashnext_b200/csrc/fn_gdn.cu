@@ -51,6 +51,7 @@ struct GdnArgs {
     int os;
     int nkh, nvh, nt;
     int prefetch;  // 1: the state was complete before the previous kernel started, so it is read before the wait
+    uint32_t *err;  // device error word (a bounded wait that ran out)
 };
 
 __device__ __forceinline__ float warp_sum_f(float v) {
@@ -63,7 +64,7 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 // batch of sequences (one 512-thread CTA per head and sequence: the batch fills the GPU, and no cluster barriers). The
 // gated norm adds the same warp partials in the same column order either way, so the results are the same bits.
 template <int SPLIT>
-__global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) {  // clusters of SPLIT CTAs
+__global__ void __launch_bounds__(gdn_threads(SPLIT), SPLIT == 1 ? 2 : 1) k_gdn(const GdnArgs a) {  // clusters of SPLIT CTAs
     constexpr int DS = GDN_DS, CW = DS / SPLIT;  // CW state columns per CTA
     constexpr int NSW = 4 * CW / 32;             // warps holding state
     __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[CW];
@@ -71,6 +72,10 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
     __shared__ float red_o[2][NSW];  // this CTA's warp partials of sum o^2, by token parity (read by the cluster)
     // one CTA per head: the 4 row-quarter partials of S^T k and S^T q per column, and o^2 per column
     __shared__ float red_kv[SPLIT == 1 ? 4 * DS : 1], red_qo[SPLIT == 1 ? 4 * DS : 1], red_sq[SPLIT == 1 ? DS : 1];
+    // one CTA per head: the head's whole state (64 KiB, dynamic shared memory) arrives by one bulk copy on st_bar, so
+    // the load is a single request to the copy engine instead of 32 scalar loads per thread
+    extern __shared__ __align__(128) float st_sm[];
+    __shared__ __align__(8) uint64_t st_bar;
     cg::cluster_group cl = cg::this_cluster();
     const int p = SPLIT > 1 ? (int)cl.block_rank() : 0;  // column block: state columns [CW p, CW (p + 1)) of the head
     const int h = blockIdx.x / SPLIT, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -115,14 +120,33 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
     }
     // ---- state, conv state, parameters: read before griddepcontrol.wait when the state was complete before the
     // previous kernel started (prefetch), else after it (the previous kernel may be this layer's previous step)
-    float s[32];
+    float s[SPLIT == 1 ? 1 : 32];
     float *Sh = stS + (size_t)h * DS * DS;
     float h0 = 0.f, h1 = 0.f, h2 = 0.f;
     float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (SPLIT == 1) {
+        if (tid == 0) {
+            mbar_init(&st_bar, 1);
+            mbar_fence_init();
+        }
+        __syncthreads();
+    }
+    bool st_ok = true;  // the state copy landed within the wait's bound
+    // this thread's state value i (row 32c + i of column j): in registers for a cluster CTA, in the staged shared
+    // copy for one CTA per head (two CTAs then share an SM, so one's copy overlaps the other's arithmetic)
+    auto sv = [&](int i) -> float & {
+        if constexpr (SPLIT == 1) return st_sm[(32 * c + i) * DS + jl];
+        else return s[i];
+    };
     auto load_state = [&]() {
-        if (st_thr) {
+        if constexpr (SPLIT == 1) {
+            if (tid == 0) {
+                mbar_arrive_tx(&st_bar, DS * DS * 4);
+                bulk_g2s(st_sm, Sh, DS * DS * 4, &st_bar);
+            }
+        } else if (st_thr) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s[i] = Sh[(size_t)(32 * c + i) * DS + j];
+            for (int i = 0; i < 32; ++i) sv(i) = Sh[(size_t)(32 * c + i) * DS + j];
         }
         if (ch >= 0) {
             h0 = stp[0];
@@ -176,6 +200,12 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
         const float decay = expf(sp * sa);
         __syncthreads();
         float o = 0.f;
+        if constexpr (SPLIT == 1) {
+            if (t == 0) {  // the state copy landed: this thread's 32 values of column j (a warp reads 32 consecutive words)
+                st_ok = mbar_park(&st_bar, 0);
+                if (!st_ok) dev_fail(a.err, DEV_WAIT_TIMEOUT);
+            }
+        }
         if (st_thr) {
             // kv_j = sum_i S[i][j] k_i over this thread's quarter, then the 4 quarters
             const float *kq = kn + c * KPAD, *qq = qn + c * KPAD;
@@ -183,10 +213,10 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
                 const float4 kk = *(const float4 *)(kq + i);
-                kv = __fmaf_rn(s[i], kk.x, kv);
-                kv = __fmaf_rn(s[i + 1], kk.y, kv);
-                kv = __fmaf_rn(s[i + 2], kk.z, kv);
-                kv = __fmaf_rn(s[i + 3], kk.w, kv);
+                kv = __fmaf_rn(sv(i), kk.x, kv);
+                kv = __fmaf_rn(sv(i + 1), kk.y, kv);
+                kv = __fmaf_rn(sv(i + 2), kk.z, kv);
+                kv = __fmaf_rn(sv(i + 3), kk.w, kv);
             }
             if constexpr (SPLIT == 1) {  // every thread holds state here: the barrier is reached by all
                 red_kv[c * DS + jl] = kv;
@@ -200,14 +230,14 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
                 const float4 kk = *(const float4 *)(kq + i), q4 = *(const float4 *)(qq + i);
-                s[i] = __fmaf_rn(decay, s[i], __fmul_rn(kk.x, delta));
-                s[i + 1] = __fmaf_rn(decay, s[i + 1], __fmul_rn(kk.y, delta));
-                s[i + 2] = __fmaf_rn(decay, s[i + 2], __fmul_rn(kk.z, delta));
-                s[i + 3] = __fmaf_rn(decay, s[i + 3], __fmul_rn(kk.w, delta));
-                o = __fmaf_rn(s[i], q4.x, o);
-                o = __fmaf_rn(s[i + 1], q4.y, o);
-                o = __fmaf_rn(s[i + 2], q4.z, o);
-                o = __fmaf_rn(s[i + 3], q4.w, o);
+                sv(i) = __fmaf_rn(decay, sv(i), __fmul_rn(kk.x, delta));
+                sv(i + 1) = __fmaf_rn(decay, sv(i + 1), __fmul_rn(kk.y, delta));
+                sv(i + 2) = __fmaf_rn(decay, sv(i + 2), __fmul_rn(kk.z, delta));
+                sv(i + 3) = __fmaf_rn(decay, sv(i + 3), __fmul_rn(kk.w, delta));
+                o = __fmaf_rn(sv(i), q4.x, o);
+                o = __fmaf_rn(sv(i + 1), q4.y, o);
+                o = __fmaf_rn(sv(i + 2), q4.z, o);
+                o = __fmaf_rn(sv(i + 3), q4.w, o);
             }
             if constexpr (SPLIT == 1) {
                 red_qo[c * DS + jl] = o;
@@ -256,7 +286,7 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
     }
     if (st_thr) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) Sh[(size_t)(32 * c + i) * DS + j] = s[i];
+        for (int i = 0; i < 32; ++i) Sh[(size_t)(32 * c + i) * DS + j] = sv(i);
     }
     if (ch >= 0 && own) {
         stp[0] = h0;
@@ -264,6 +294,8 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), 1) k_gdn(const GdnArgs a) 
         stp[2 * sst] = h2;
     }
     if constexpr (SPLIT > 1) cl.sync();  // no CTA leaves while another may still read its partials
+    if constexpr (SPLIT == 1)
+        if (!st_ok) (void)mbar_park(&st_bar, 0);  // a copy past the first bound: let it land (bounded) before exiting
 }
 
 int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs, const float *z, int zs, const float *ab,
@@ -293,7 +325,12 @@ int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs,
     a.nvh = p.nvh;
     a.nt = nt;
     a.prefetch = prefetch_state ? 1 : 0;
-    const cudaError_t e = batch > 1 ? launch_k(k_gdn<1>, dim3(p.nvh, batch), dim3(gdn_threads(1)), 0, s, a)
+    a.err = dev_error_ptr();
+    if (batch > 1) {
+        const cudaError_t e = allow_max_dynamic_smem(k_gdn<1>);
+        if (e != cudaSuccess) return fail(std::string("gdn attributes: ") + cudaGetErrorString(e));
+    }
+    const cudaError_t e = batch > 1 ? launch_k(k_gdn<1>, dim3(p.nvh, batch), dim3(gdn_threads(1)), GDN_DS * GDN_DS * 4, s, a)
                                     : launch_kc(k_gdn<GDN_SPLIT>, dim3(p.nvh * GDN_SPLIT, 1), dim3(gdn_threads(GDN_SPLIT)),
                                                 GDN_SPLIT, 0, s, a);
     if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
