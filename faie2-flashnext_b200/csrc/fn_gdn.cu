@@ -284,7 +284,19 @@ __global__ void __launch_bounds__(gdn_threads(SPLIT), SPLIT == 1 ? 2 : 1) k_gdn(
         }
         __syncthreads();
     }
-    if (st_thr) {
+    if constexpr (SPLIT == 1) {
+        // the updated state leaves shared memory by one bulk store: every writer orders its shared-memory writes
+        // before the copy engine's reads (proxy fence + barrier); the CTA exits once the engine has read them
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(Sh), "r"(smem_u32(st_sm)),
+                         "r"(DS * DS * 4)
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+        }
+    } else if (st_thr) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) Sh[(size_t)(32 * c + i) * DS + j] = sv(i);
     }
