@@ -63,8 +63,10 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 // SPLIT CTAs per value head: 4 (a cluster) for one sequence, whose head's state then streams through four SMs; 1 for a
 // batch of sequences (one 512-thread CTA per head and sequence: the batch fills the GPU, and no cluster barriers). The
 // gated norm adds the same warp partials in the same column order either way, so the results are the same bits.
-template <int SPLIT>
-__global__ void __launch_bounds__(gdn_threads(SPLIT), SPLIT == 1 ? 2 : 1) k_gdn(const GdnArgs a) {  // clusters of SPLIT CTAs
+// MINB: CTAs per SM the registers must allow (one CTA per head: 2 at 64 registers, or 3 at 40 for batches whose CTAs
+// fill three per SM; the shared-memory state allows three)
+template <int SPLIT, int MINB = 1>
+__global__ void __launch_bounds__(gdn_threads(SPLIT), MINB) k_gdn(const GdnArgs a) {  // clusters of SPLIT CTAs
     constexpr int DS = GDN_DS, CW = DS / SPLIT;  // CW state columns per CTA
     constexpr int NSW = 4 * CW / 32;             // warps holding state
     __shared__ __align__(16) float qn[4 * KPAD], kn[4 * KPAD], vs[CW];
@@ -338,11 +340,14 @@ int launch_gdn(const GdnParams &p, const GdnState &st, const float *qkv, int qs,
     a.nt = nt;
     a.prefetch = prefetch_state ? 1 : 0;
     a.err = dev_error_ptr();
+    // a batch: three CTAs per SM once they fill three per SM (32 sequences x 32 heads: 31.4 us against 33.7 at two),
+    // else two (8 x 32: 7.8 us against 9.6 at three, which leaves SMs idle)
+    void (*kb)(const GdnArgs) = p.nvh * batch >= 3 * num_sms() ? k_gdn<1, 3> : k_gdn<1, 2>;
     if (batch > 1) {
-        const cudaError_t e = allow_max_dynamic_smem(k_gdn<1>);
+        const cudaError_t e = allow_max_dynamic_smem(kb);
         if (e != cudaSuccess) return fail(std::string("gdn attributes: ") + cudaGetErrorString(e));
     }
-    const cudaError_t e = batch > 1 ? launch_k(k_gdn<1>, dim3(p.nvh, batch), dim3(gdn_threads(1)), GDN_DS * GDN_DS * 4, s, a)
+    const cudaError_t e = batch > 1 ? launch_k(kb, dim3(p.nvh, batch), dim3(gdn_threads(1)), GDN_DS * GDN_DS * 4, s, a)
                                     : launch_kc(k_gdn<GDN_SPLIT>, dim3(p.nvh * GDN_SPLIT, 1), dim3(gdn_threads(GDN_SPLIT)),
                                                 GDN_SPLIT, 0, s, a);
     if (e != cudaSuccess) return fail(std::string("gdn launch: ") + cudaGetErrorString(e));
