@@ -20,6 +20,13 @@
 // state ([NVH][3][2][DS]): the value heads sharing a key head would otherwise race on it (one reading the old state
 // while another writes the new one); the copies stay equal. Inside a head's cluster the CTA that owns a channel's column
 // block writes its history back, after the cluster barrier that follows every other CTA's read of it.
+//
+// B200 design (a batch of sequences, one token each): one 512-thread CTA per (value head, sequence), no cluster. The
+// head's 64 KB state arrives in shared memory by one bulk copy (before griddepcontrol.wait under the same condition as
+// above), is updated there and leaves by one bulk store, so a CTA needs 64 registers (40 at three CTAs per SM) and
+// several CTAs share an SM, one's copy overlapping another's arithmetic. A warp's lanes take 32 consecutive columns of
+// one 32-row quarter (conflict-free shared-memory rows); the quarter partials meet in shared memory in the order the
+// xor shuffles give, and the gated norm adds the same partials in the same order, so the values are the same bits.
 #include <cooperative_groups.h>
 
 #include "fn_engine.h"
